@@ -1,0 +1,232 @@
+/*
+ * lbx.h — C ABI of the B200 (sm_100a) LittleBit kernels.
+ *
+ * Every pointer is a caller-owned DEVICE buffer unless the comment says "host".
+ * Every call is stream-ordered on the given cudaStream_t, performs no host
+ * synchronisation and no device allocation, and returns an int status:
+ *   LBX_OK (0), LBX_EINVAL (1, bad argument/shape), LBX_EUNSUPPORTED (2),
+ *   LBX_ECUDA (3, a CUDA launch error; text in lbx_last_error).
+ * No C++ exception crosses this boundary.  The reference's native op library
+ * (patches/littlebit_cpu_optimized.cpp, TORCH_LIBRARY at :2321-2377) raised
+ * TORCH_CHECK errors instead; the Python layer turns a non-zero status into a
+ * RuntimeError carrying lbx_last_error(), so callers see the same exception type.
+ *
+ * Bit-packing contract (quantization/utils/binary_packer.py:4-50): a {-1,+1}
+ * matrix [R, C] is stored as int32 words [R, ceil(C/32)], bit j of word w is
+ * column 32*w + j (LSB first), bit 1 <=> -1, pad columns are +1 (bit 0).
+ */
+#ifndef LBX_H
+#define LBX_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LBX_OK 0
+#define LBX_EINVAL 1
+#define LBX_EUNSUPPORTED 2
+#define LBX_ECUDA 3
+
+/* element types for activations */
+#define LBX_F32 0
+#define LBX_BF16 1
+
+/* largest token batch one linear launch handles; larger batches are split
+ * by the host into independent launches (tokens never interact in a linear). */
+#define LBX_MAX_TOKENS 16
+/* largest number of projections sharing one input in a single launch */
+#define LBX_MAX_PROJ 3
+
+/* One LittleBit branch: y_b = u1 ⊙ U_sign·(mid ⊙ V_sign·(v2 ⊙ x)).
+ * Reference: quantization/modules/littlebit.py:114-121 (_compute_forward),
+ * runtime keys convert_hf_to_runtime.py:47-57 (u_sign_rt, v_sign_rt, u1, v2,
+ * mid = v1*u2). */
+typedef struct lbx_branch {
+  const int32_t *v_sign; /* [rank, ceil(in/32)]; NULL => reuse branch 0's V-stage */
+  const float *v2;       /* [in]   (NULL when v_sign is NULL)                     */
+  const float *mid;      /* [rank] v1*u2                                          */
+  const int32_t *u_sign; /* [out, ceil(rank/32)]                                  */
+  const float *u1;       /* [out]                                                 */
+  int32_t rank;
+} lbx_branch;
+
+/* One LittleBitLinear (littlebit.py:95-112): main branch, optional residual
+ * branch (littlebit.py:104-107, or the shared-factor residual of
+ * littlespec_ref/littlebit_itq_spec.py:298-309 when br[1].v_sign == NULL),
+ * optional bias. */
+typedef struct lbx_proj {
+  int32_t in_features;
+  int32_t out_features;
+  int32_t n_branches; /* 1 or 2 */
+  int32_t _pad;
+  lbx_branch br[2];
+  const float *bias; /* [out] or NULL */
+} lbx_proj;
+
+/* Input transform applied while the kernel stages x (fused, no extra pass). */
+#define LBX_PRO_NONE 0
+#define LBX_PRO_RMSNORM 1 /* x <- x * rsqrt(mean(x^2)+eps) * norm_w              */
+#define LBX_PRO_SILU_MUL 2 /* x <- silu(x) * x2   (cpp:1117-1170 silu_mul)        */
+
+/* Output mode. */
+#define LBX_EPI_STORE 0 /* y  = linear(x)                                        */
+#define LBX_EPI_ADD 1   /* y += linear(x)   (residual stream update, fp32 only)  */
+
+typedef struct lbx_linear_args {
+  int32_t n_proj;      /* 1..LBX_MAX_PROJ projections sharing the input x      */
+  int32_t n_tokens;    /* k tokens (rows of x)                                 */
+  int32_t x_dtype;     /* LBX_F32 / LBX_BF16                                   */
+  int32_t y_dtype;     /* LBX_F32 / LBX_BF16                                   */
+  int32_t prologue;    /* LBX_PRO_*                                            */
+  int32_t epilogue;    /* LBX_EPI_*                                            */
+  float eps;           /* RMSNorm epsilon                                      */
+  int32_t use_pdl;     /* launch with programmatic dependent launch            */
+  const void *x;       /* [k, in] row-major                                    */
+  const void *x2;      /* [k, in] second input of LBX_PRO_SILU_MUL             */
+  const float *norm_w; /* [in] RMSNorm weight of LBX_PRO_RMSNORM               */
+  void *y[LBX_MAX_PROJ];   /* per projection [k, out] row-major                */
+  int64_t y_ld[LBX_MAX_PROJ]; /* row stride (elements) of each y; 0 => out    */
+} lbx_linear_args;
+
+/* Bytes of device scratch one lbx_linear / lbx_linear_verify call needs. */
+size_t lbx_linear_workspace_size(const lbx_proj *projs /* host */, int32_t n_proj,
+                                 int32_t n_tokens);
+
+/* Batch-1 LittleBitLinear.  Replaces littlebit_cpu_ops::littlebit_linear
+ * (patches/littlebit_cpu_optimized.cpp:598-701) and the inline projection
+ * lb_linear_i2_inline (cpp:1320-1369); fp32-accurate, no int8 activation loss. */
+int lbx_linear(const lbx_proj *projs /* host */, const lbx_linear_args *a /* host */,
+               void *ws, size_t ws_bytes, cudaStream_t stream);
+
+/* Batch-k verify LittleBitLinear: one packed-weight read for all k tokens.
+ * Each token's result is bit-identical to lbx_linear on that token alone.
+ * Replaces the serial per-token projection loop of full_forward_batch
+ * (cpp:1942-1946).  Same arguments as lbx_linear with a->n_tokens = k. */
+int lbx_linear_verify(const lbx_proj *projs, const lbx_linear_args *a, void *ws,
+                      size_t ws_bytes, cudaStream_t stream);
+
+/* ---- bit packing (quantization/utils/binary_packer.py) ------------------ */
+/* binary_packer (binary_packer.py:4-50): int8 ±1 [rows, cols] -> int32 words.
+ * Entries other than -1/+1 set *bad_count (device int, may be NULL). */
+int lbx_pack_signs(const int8_t *signs, int64_t rows, int64_t cols, int32_t *packed,
+                   int32_t *bad_count, cudaStream_t stream);
+/* binary_unpacker (binary_packer.py:53-97): int32 words -> int8 ±1. */
+int lbx_unpack_signs(const int32_t *packed, int64_t rows, int64_t cols, int8_t *signs,
+                     cudaStream_t stream);
+/* pack_weights (littlebit.py:307-320): sign(w) with 0 -> +1 (functions/binary.py:7-10),
+ * then binary_packer, straight from a float/bf16 latent factor. */
+int lbx_pack_signs_from_float(const void *w, int32_t w_dtype, int64_t rows, int64_t cols,
+                              int32_t *packed, cudaStream_t stream);
+
+/* ---- decoder pieces ------------------------------------------------------ */
+/* embedding_lookup (cpp:973-996): out[i,:] = float(table[ids[i],:]); bf16 table. */
+int lbx_embed(const uint16_t *table_bf16, const int64_t *ids, int32_t n, int32_t hidden,
+              int32_t vocab, float *out, cudaStream_t stream);
+/* rms_norm (cpp:998-1052), n rows. out may alias x. */
+int lbx_rmsnorm(const float *x, const float *w, int32_t n, int32_t hidden, float eps,
+                float *out, cudaStream_t stream);
+/* silu_mul (cpp:1117-1170): out = g*sigmoid(g)*u, exact expf. */
+int lbx_silu_mul(const float *g, const float *u, int64_t n, float *out, cudaStream_t stream);
+/* HF Llama rotary embedding (rotate_half convention), in place on
+ * x [n, heads, head_dim] at positions pos[n]. Missing in the reference CPU
+ * path (it applies none); the GPU/HF path applies it. */
+int lbx_rope(float *x, const int32_t *pos, int32_t n, int32_t heads, int32_t head_dim,
+             float theta, cudaStream_t stream);
+
+/* Decode attention over a bf16 KV cache with fused RoPE and KV write.
+ * Replaces fused_attention (cpp:1172-1301) and the causal loop of
+ * full_forward_batch (cpp:1963-2021).  q/k_new/v_new are the raw projection
+ * outputs [n, heads*d] / [n, kv_heads*d] fp32 (row strides q_ld / kv_ld).
+ * New token i is rotated with position pos[i] and written to cache slot
+ * prefix_len + i.  Query i sees cache slots [0, prefix_len) plus the new slots
+ * prefix_len + j with bit j of tree_mask[i] set (its tree ancestors and
+ * itself) or, when tree_mask == NULL, j <= i (causal).  GQA: query head h
+ * reads kv head h / (heads / kv_heads) (cpp:1238).  Caches are
+ * [kv_heads, max_seq, head_dim] bf16; head_dim even and <= 128; n <= 64. */
+typedef struct lbx_attn_args {
+  int32_t n;
+  int32_t heads, kv_heads, head_dim, max_seq;
+  int32_t prefix_len;
+  float scale, theta;
+  int32_t use_pdl;
+  const float *q; int64_t q_ld;
+  const float *k_new; const float *v_new; int64_t kv_ld;
+  const int32_t *pos;        /* [n] rotary positions */
+  const uint64_t *tree_mask; /* [n] or NULL          */
+  uint16_t *k_cache; uint16_t *v_cache;
+  float *out;                /* [n, heads*d]         */
+} lbx_attn_args;
+size_t lbx_attn_workspace_size(const lbx_attn_args *a);
+int lbx_attn_decode(const lbx_attn_args *a, void *ws, size_t ws_bytes, cudaStream_t stream);
+
+/* Fused final RMSNorm + lm_head (bf16 [vocab, hidden]) + argmax.
+ * Replaces dense_gemv_f32 (cpp:1054-1115) + the argmax of generate_token
+ * (cpp:2306-2314).  x [n, hidden] fp32 is the pre-norm hidden state when
+ * norm_w != NULL.  logits [n, vocab] fp32 may be NULL; argmax_out [n] int64
+ * takes the lowest index among equal maxima (torch.argmax order). */
+size_t lbx_lmhead_workspace_size(int32_t n, int32_t vocab);
+int lbx_lmhead_argmax(const float *x, const float *norm_w, float eps, int32_t n,
+                      int32_t hidden, const uint16_t *w_bf16, int32_t vocab, float *logits,
+                      int64_t *argmax_out, void *ws, size_t ws_bytes, int32_t use_pdl,
+                      cudaStream_t stream);
+
+/* Greedy chain acceptance (speculative_decoding.py:315-330, 356-363):
+ * draft[k], target_argmax[k+1] -> out[0] = accepted count a, out[1] = the
+ * token appended after them (target_argmax[a]). */
+int lbx_accept_greedy_chain(const int64_t *draft, const int64_t *target_argmax, int32_t k,
+                            int64_t *out, cudaStream_t stream);
+/* Greedy tree acceptance (tree_utils.py:182-214 on the gather of
+ * speculative_decoding.py:541-554): cand [L, D+1] token ids (-1 pad),
+ * node_argmax [T] argmax of each tree node's logits, retrieve [L, D+1] node
+ * indices (-1 pad) -> out[0] = best leaf row, out[1] = accept length,
+ * out[2] = bonus token, out[3..3+D) = accepted node indices. */
+int lbx_accept_greedy_tree(const int64_t *cand, const int64_t *node_argmax,
+                           const int64_t *retrieve, int32_t L, int32_t D1, int64_t *out,
+                           cudaStream_t stream);
+
+/* ---- whole decoder step (cpp:1522-1840 full_forward, 1846-2079
+ *      full_forward_batch, 2256-2317 generate_token) ----------------------- */
+typedef struct lbx_layer {
+  const float *ln1; /* input_layernorm  [hidden] */
+  const float *ln2; /* post_attention_layernorm [hidden] */
+  lbx_proj proj[7]; /* q, k, v, o, gate, up, down (cpp:1307-1317 order) */
+  uint16_t *k_cache; uint16_t *v_cache; /* [kv_heads, max_seq, head_dim] bf16 */
+} lbx_layer;
+
+typedef struct lbx_model {
+  int32_t n_layers, hidden, intermediate, heads, kv_heads, head_dim, vocab, max_seq;
+  float rms_eps, rope_theta, attn_scale;
+  int32_t use_pdl;
+  const uint16_t *embed;   /* [vocab, hidden] bf16 */
+  const float *final_norm; /* [hidden] */
+  const uint16_t *lm_head; /* [vocab, hidden] bf16, may be NULL for hidden-only */
+  const lbx_layer *layers; /* host array [n_layers] */
+} lbx_model;
+
+size_t lbx_forward_workspace_size(const lbx_model *m /* host */, int32_t n_tokens);
+/* n tokens at cache slots start..start+n-1 (rotary positions pos[] or, when
+ * pos == NULL, the slots).  tree_mask as in lbx_attn_args (NULL = causal).
+ * hidden_out [n, hidden] receives the final-RMSNorm output (may be NULL);
+ * logits [n, vocab] / argmax [n] as in lbx_lmhead_argmax (may be NULL). */
+int lbx_forward(const lbx_model *m, const int64_t *tokens, int32_t n, int32_t start,
+                const int32_t *pos, const uint64_t *tree_mask, float *hidden_out,
+                float *logits, int64_t *argmax_out, void *ws, size_t ws_bytes,
+                cudaStream_t stream);
+
+/* ---- diagnostics --------------------------------------------------------- */
+/* Copies the last host-side error text of the calling thread. */
+int lbx_last_error(char *buf, size_t n);
+/* Device error word written by bounded waits that ran out (0 = none). */
+int lbx_device_error(int32_t *out_host, cudaStream_t stream);
+int lbx_clear_device_error(cudaStream_t stream);
+/* Library version / build arch string (host). */
+const char *lbx_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LBX_H */

@@ -1,0 +1,167 @@
+"""CUDA LittleBitLinear and bit packing vs the CPU oracle (seeded inputs).
+
+Bars: packed words bit-exact; per-layer outputs within rtol 1e-3 of the fp64
+restatement of LittleBitLinear._compute_forward (abs floor 1e-4 x max|y|);
+a token's output bit-identical whatever verify batch it is computed in.
+"""
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_linear_close, oracle_branches, rel_err
+from oracle import littlebit as olb
+from oracle import packing as opk
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from littlebit_b200 import ops as o
+
+    o.clear_device_error()
+    yield o
+    torch.cuda.synchronize()
+    assert o.device_error() == 0
+
+
+def _gen(seed):
+    return torch.Generator().manual_seed(seed)
+
+
+@pytest.mark.parametrize("shape", [(2, 40), (5, 33), (3, 1), (16, 1840), (4096, 208), (208, 4096),
+                                   (7, 64), (0, 5)])
+def test_pack_bitexact(ops, shape):
+    g = _gen(1)
+    s = (torch.randint(0, 2, shape, generator=g, dtype=torch.int8) * 2 - 1)
+    p = ops.binary_packer(s.to(DEV)).cpu().numpy()
+    ref = opk.binary_packer(s.numpy()) if shape[0] else np.zeros((0, (shape[1] + 31) // 32), np.int32)
+    assert np.array_equal(p, ref)
+    u = ops.binary_unpacker(torch.from_numpy(ref).to(DEV), shape).cpu().numpy()
+    assert np.array_equal(u, s.numpy())
+
+
+def test_pack_golden(ops, golden):
+    gd = golden("packing")
+    for n in sorted({k.rsplit("_", 1)[0] for k in gd.files}):
+        s = torch.from_numpy(gd[f"{n}_signs"]).to(DEV)
+        assert np.array_equal(ops.binary_packer(s).cpu().numpy(), gd[f"{n}_packed"]), n
+
+
+def test_pack_from_float_sign_convention(ops):
+    w = torch.tensor([[0.0, -0.0, -1.5, 2.0, -1e-30] + [1.0] * 30], device=DEV)
+    p = ops.pack_signs_from_float(w).cpu().numpy()
+    ref = opk.binary_packer(opk.sign(w.cpu().numpy()).astype(np.int8))
+    assert np.array_equal(p, ref)
+    pb = ops.pack_signs_from_float(w.bfloat16()).cpu().numpy()
+    assert np.array_equal(pb, ref)
+
+
+def test_pack_rejects(ops):
+    with pytest.raises(TypeError):
+        ops.binary_packer(torch.ones(2, 3, dtype=torch.int32, device=DEV))
+    with pytest.raises(RuntimeError):
+        ops.binary_packer(torch.ones(2, 3, dtype=torch.int8))  # CPU tensor: no CPU path
+
+
+def _layer(ops, in_f, out_f, ranks, seed, shared=False, bias=False):
+    from littlebit_b200 import synthetic as syn
+
+    g = _gen(seed)
+    brs = syn.layer(in_f, out_f, ranks, g, shared_residual=shared)
+    b = torch.randn(out_f, generator=g) if bias else None
+    return brs, b, syn.to_packed_linear(in_f, out_f, brs, DEV, bias=b)
+
+
+def _ref(x, brs, in_f, out_f, bias=None):
+    return olb.linear_forward(x.double().numpy(), oracle_branches(brs), in_f, out_f,
+                              bias=None if bias is None else bias.numpy())
+
+
+@pytest.mark.parametrize("case", [
+    ("c1", 4096, 4096, [208], 1, torch.float32),
+    ("c2_k1", 4096, 4096, [208, 1840], 1, torch.bfloat16),
+    ("c2_k5", 4096, 4096, [208, 1840], 5, torch.bfloat16),
+    ("c2_k8", 4096, 4096, [208, 1840], 8, torch.bfloat16),
+    ("down", 11008, 4096, [280], 3, torch.float32),
+    ("gate", 4096, 11008, [280], 2, torch.float32),
+    ("odd_rank", 256, 128, [40, 8], 4, torch.float32),
+    ("k16", 512, 256, [184], 16, torch.float32),
+    ("k20", 512, 256, [96], 20, torch.float32),
+    ("tiny", 128, 16, [8], 1, torch.float32),
+])
+def test_linear_matches_oracle(ops, case):
+    name, in_f, out_f, ranks, k, dt = case
+    brs, _, lay = _layer(ops, in_f, out_f, ranks, seed=sum(map(ord, name)))
+    x = torch.randn(k, in_f, generator=_gen(7)).to(dt)
+    y = ops.lb_linear(lay, x.to(DEV)).cpu()
+    ref = _ref(x.float(), brs, in_f, out_f)
+    assert_linear_close(y.numpy(), ref)
+    assert rel_err(y.numpy(), ref) < 2e-4
+
+
+def test_linear_shared_residual_and_bias(ops):
+    brs, b, lay = _layer(ops, 1024, 512, [96, 96], seed=3, shared=True, bias=True)
+    x = torch.randn(3, 1024, generator=_gen(8))
+    y = ops.lb_linear(lay, x.to(DEV)).cpu().numpy()
+    assert_linear_close(y, _ref(x, brs, 1024, 512, bias=b))
+
+
+def test_verify_batch_bit_identical_to_batch1(ops):
+    brs, _, lay = _layer(ops, 4096, 4096, [208, 1840], seed=4)
+    x = torch.randn(8, 4096, generator=_gen(9)).bfloat16().to(DEV)
+    yk = ops.lb_linear(lay, x)
+    for i in range(8):
+        y1 = ops.lb_linear(lay, x[i:i + 1])
+        assert torch.equal(y1[0], yk[i]), i
+    y5 = ops.lb_linear(lay, x[2:7])
+    assert torch.equal(y5, yk[2:7])
+
+
+def test_prologues_epilogues_groups(ops):
+    from littlebit_b200 import _lib as L
+
+    g = _gen(12)
+    H, I, k = 512, 768, 3
+    layers = [_layer(ops, H, o, [64], seed=20 + i) for i, o in enumerate((H, 256, 256))]
+    x = torch.randn(k, H, generator=g)
+    w = (1 + 0.1 * torch.randn(H, generator=g)).abs()
+    outs = [torch.empty(k, l[2].out_features, device=DEV) for l in layers]
+    ops.linear_group([l[2] for l in layers], x.to(DEV), outs, prologue=L.LBX_PRO_RMSNORM,
+                     norm_w=w.to(DEV), eps=1e-6)
+    xn = x.double() / torch.sqrt((x.double() ** 2).mean(-1, keepdim=True) + 1e-6) * w.double()
+    for (brs, _, lay), o in zip(layers, outs):
+        assert_linear_close(o.cpu().numpy(), _ref(xn, brs, H, lay.out_features))
+    # SiLU-mul prologue + residual-add epilogue (the down projection)
+    brs, _, dn = _layer(ops, I, H, [80], seed=30)
+    gt, up = torch.randn(k, I, generator=g), torch.randn(k, I, generator=g)
+    res = torch.randn(k, H, generator=g)
+    y = res.clone().to(DEV)
+    ops.linear_group([dn], gt.to(DEV), [y], prologue=L.LBX_PRO_SILU_MUL, x2=up.to(DEV),
+                     epilogue=L.LBX_EPI_ADD)
+    a = torch.nn.functional.silu(gt.double()) * up.double()
+    assert_linear_close(y.cpu().numpy() - res.numpy(), _ref(a, brs, I, H), atol_frac=2e-4)
+
+
+def test_reference_schema_littlebit_linear(ops):
+    from littlebit_b200 import synthetic as syn
+
+    g = _gen(13)
+    b = syn.branch(256, 384, 40, g)
+    x = torch.randn(2, 256, generator=g)
+    y = ops.littlebit_linear(x.to(DEV), b["v2"][None].to(DEV), b["v_sign"].to(DEV), 256,
+                             b["mid"][None].to(DEV), b["u_sign"].to(DEV), 40, b["u1"][None].to(DEV))
+    assert_linear_close(y.cpu().numpy(), _ref(x, [b], 256, 384))
+    with pytest.raises(RuntimeError):  # shape checks as cpp:608-634
+        ops.littlebit_linear(x.to(DEV), b["v2"][None].to(DEV), b["v_sign"].to(DEV), 255,
+                             b["mid"][None].to(DEV), b["u_sign"].to(DEV), 40, b["u1"][None].to(DEV))
+
+
+def test_unsupported_shapes_raise(ops):
+    from littlebit_b200 import synthetic as syn
+
+    brs = syn.layer(96, 64, [16], _gen(1))  # in_features not a multiple of 128
+    lay = syn.to_packed_linear(96, 64, brs, DEV)
+    with pytest.raises(RuntimeError, match="unsupported"):
+        ops.lb_linear(lay, torch.randn(1, 96, device=DEV))
