@@ -1,0 +1,393 @@
+"""Benchmark: LittleBitLinear GB/s vs HBM peak on the BASELINE config-2 layer.
+
+Workload (per GPU): the 4096->4096 LittleBitLinear with a draft branch of
+rank 208 and a residual branch of rank 1840 (independent V_R), random packed
+±1 factors and |N(1,0.1)| scales, bf16 activations.  One STEP is a chain of
+POOL distinct layer instances (x_{i+1} = y_i, like a deep stack), so each
+step streams POOL x 2.28 MB of packed weights — 128 layers = 292 MB, more
+than twice the 126 MB L2, so every step reads the weights from HBM (no L2
+flush needed).  A step is one CUDA graph replay (2 kernels per layer, chained
+with programmatic dependent launch).
+
+value   = algorithmic bytes of all layers of all ranks / max-over-ranks time
+          (packed bits without word padding + fp32 scales + activations in/out)
+e2e     = the same metric through the C-ABI call per layer with pinned HOST
+          x/y: every layer copies its input host->device and its output
+          device->host inside the timed region
+roofline: the linear (V+U kernel pair) is the dominant kernel; achieved =
+          bytes per layer call / mean layer time; peak = MEASURED_PEAKS.json
+cpu_baseline: the reference's own C++ op (oracle/_ref, littlebit_linear from
+          patches/littlebit_cpu_optimized.cpp) on the host cores, a bounded
+          sample of the same layer.
+
+    python bench.py [--gpus N --steps K --warmup W --tokens k --impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "LittleBitLinear GB/s vs HBM peak; spec-decode tokens/s, Llama-2-7B shape"
+IN_F = OUT_F = 4096
+RANKS = [208, 1840]
+
+
+def layer_bytes(k: int) -> tuple[int, int]:
+    """(algorithmic bytes per layer call, packed-weight bytes) for k bf16 tokens."""
+    packed = sum((r * IN_F + 7) // 8 + (OUT_F * r + 7) // 8 for r in RANKS)
+    scales = sum(4 * (IN_F + r + OUT_F) for r in RANKS)
+    act = 2 * k * IN_F + 2 * k * OUT_F
+    return packed + scales + act, packed
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_from_profiles(k: int):
+    f = ROOT / "profiles" / f"linear_c2_k{k}.md"
+    if not f.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch\s*=\s*([0-9]+)", f.read_text())
+    return int(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            if len(r) >= 9:
+                for nm, v in zip(names, r[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_init():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        return dist.get_rank(), ws, int(os.environ.get("LOCAL_RANK", "0"))
+    return 0, 1, 0
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v: float, ws: int) -> float:
+    if ws == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# reference arm / CPU baseline: the reference's own C++ op on host cores
+# ---------------------------------------------------------------------------
+def cpu_reference(k: int, budget_s: float, nlayers: int = 4):
+    from oracle import build_ref  # CPU baseline leg only
+
+    if not build_ref.load():
+        return None
+    from littlebit_b200 import synthetic as syn
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    threads = torch.get_num_threads()
+    g = torch.Generator().manual_seed(0)
+    layers = [syn.layer(IN_F, OUT_F, RANKS, g) for _ in range(nlayers)]
+    op = torch.ops.littlebit_cpu_ops.littlebit_linear
+    x = torch.randn(k, IN_F, generator=g).bfloat16().float()
+
+    def run(lay, xin):
+        y = None
+        for b in lay:  # main + residual branch, summed (littlebit.py:104-107)
+            yb = op(xin, b["v2"][None], b["v_sign"], IN_F, b["mid"][None], b["u_sign"], b["rank"],
+                    b["u1"][None])
+            y = yb if y is None else y + yb
+        return y.bfloat16().float()
+
+    for i in range(5):  # warm-up (benchmark_models_cpu.py:31-77 uses 5)
+        x = run(layers[i % nlayers], x)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    i = 0
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        x = run(layers[i % nlayers], x)
+        times.append(time.perf_counter() - t0)
+        i += 1
+    b, _ = layer_bytes(k)
+    med = statistics.median(times)
+    return {"gbs": b / med / 1e9, "sec_per_layer": med, "threads": threads, "calls": len(times),
+            "sample": f"{len(times)} calls of littlebit_linear x2 branches (r={RANKS}) on {nlayers} "
+                      f"distinct layers, k={k}, median per layer"}
+
+
+def run_reference(args):
+    rank, ws, _ = dist_init()
+    if rank != 0:
+        return 0
+    t0 = time.perf_counter()
+    res = cpu_reference(args.tokens, budget_s=max(2.0, 2.0 * args.steps / 10))
+    if res is None:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "reference C++ op not built (oracle/_ref missing: run oracle/build_ref.py)"}))
+        return 0
+    b, _ = layer_bytes(args.tokens)
+    val = res["gbs"]
+    out = {
+        "metric": METRIC, "impl": "reference", "value": round(val, 4), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": res["calls"], "warmup": 5,
+        "ms_per_step": round(res["sec_per_layer"] * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8xsign/fp32 (W1A8)", "data": "synthetic",
+        "config": {"workload": f"C2 4096->4096 LittleBitLinear r={RANKS[0]}+{RANKS[1]}, k={args.tokens}, "
+                               "reference CPU op per layer", "tokens": args.tokens},
+        "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": res["threads"],
+                         "kind": "reference", "sample": res["sample"]},
+        "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": round(time.perf_counter() - t0, 2),
+    }
+    print(json.dumps(out))
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def build_pool(P: int, device, seed: int):
+    """P distinct C2 layers generated on the device (random words == Bernoulli(0.5) signs)."""
+    from littlebit_b200.ops import Branch, PackedLinear
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    pool = []
+    for _ in range(P):
+        brs = []
+        for r in RANKS:
+            def words(rows, cols):
+                w = torch.randint(-(2 ** 31), 2 ** 31, (rows, (cols + 31) // 32), generator=g,
+                                  device=device, dtype=torch.int64)
+                if cols % 32:
+                    w[:, -1] &= (1 << (cols % 32)) - 1
+                return w.to(torch.int32)
+            sc = lambda n: (1 + 0.1 * torch.randn(n, generator=g, device=device)).abs()
+            brs.append(Branch(words(r, IN_F), sc(IN_F), sc(r), words(OUT_F, r), sc(OUT_F), r))
+        pool.append(PackedLinear(IN_F, OUT_F, brs))
+    return pool
+
+
+def run_ours(args):
+    from littlebit_b200 import ops
+
+    rank, ws, lrank = dist_init()
+    torch.cuda.set_device(lrank)
+    dev = torch.device("cuda", lrank)
+    k, P = args.tokens, args.pool
+    pool = build_pool(P, dev, seed=1234 + rank)
+    arrs = [ops.projs_array([p]) for p in pool]
+    wsb = torch.zeros(ops.linear_workspace_bytes([pool[0]], k), dtype=torch.uint8, device=dev)
+    acts = [torch.randn(k, IN_F, device=dev).bfloat16()] + \
+           [torch.empty(k, OUT_F, device=dev, dtype=torch.bfloat16) for _ in range(P)]
+    stream = torch.cuda.Stream(dev)
+
+    def step():
+        for i in range(P):
+            ops.linear_group([pool[i]], acts[i], [acts[i + 1]], use_pdl=args.pdl, ws=wsb, arr=arrs[i])
+
+    # eager warm-up, then capture one step as a graph
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    ops.clear_device_error()
+
+    sampler = ClockSampler(lrank)
+    sampler.start()
+    time.sleep(0.3)
+    barrier(ws)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(ws)
+    clocks = sampler.stop()
+    t_ms = e0.elapsed_time(e1)
+    t_ms = max_over_ranks(t_ms, ws)
+    assert ops.device_error() == 0, "device error word set during the bench"
+    if not torch.isfinite(acts[-1].float()).all():
+        raise RuntimeError("non-finite output in the layer chain")
+
+    b_layer, packed = layer_bytes(k)
+    total_bytes = b_layer * P * args.steps * ws
+    value = total_bytes / (t_ms * 1e-3) / 1e9
+    per_launch_s = t_ms * 1e-3 / (P * args.steps)
+    peak, peak_kind = peaks()
+    achieved = b_layer / per_launch_s / 1e9
+
+    # ---- e2e: per-layer host round trip through pinned buffers
+    hx = torch.empty(k, IN_F, dtype=torch.bfloat16).pin_memory()
+    hx.copy_(acts[0].cpu())
+    hys = [torch.empty(k, OUT_F, dtype=torch.bfloat16).pin_memory() for _ in range(P)]
+    dx = torch.empty(k, IN_F, device=dev, dtype=torch.bfloat16)
+    dy = torch.empty(k, OUT_F, device=dev, dtype=torch.bfloat16)
+
+    def e2e_step():
+        src = hx
+        for i in range(P):
+            dx.copy_(src, non_blocking=True)
+            ops.linear_group([pool[i]], dx, [dy], use_pdl=False, ws=wsb, arr=arrs[i])
+            hys[i].copy_(dy, non_blocking=True)
+            src = hys[i]
+
+    with torch.cuda.stream(stream):
+        e2e_step()
+    torch.cuda.synchronize()
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2, stream=stream):
+        e2e_step()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            g2.replay()
+    torch.cuda.synchronize()
+    barrier(ws)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            g2.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    t2 = max_over_ranks(e0.elapsed_time(e1), ws)
+    e2e_val = b_layer * P * args.steps * ws / (t2 * 1e-3) / 1e9
+
+    # ---- CPU baseline (rank 0, N=1 only)
+    cpu = None
+    if ws == 1 and not args.no_cpu:
+        r = cpu_reference(k, budget_s=args.cpu_seconds)
+        if r is not None:
+            cpu = {"value": round(r["gbs"], 4), "unit": "GB/s", "cores": r["threads"],
+                   "kind": "reference", "sample": r["sample"]}
+
+    if rank == 0:
+        traffic = traffic_from_profiles(k)
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "s8 digits x packed sign bits, int32 acc (bf16 in/out)", "data": "synthetic",
+            "config": {"workload": f"C2 4096->4096 LittleBitLinear r={RANKS[0]}+{RANKS[1]} (independent "
+                                   f"V_R), k={k} bf16 tokens, chain of {P} distinct layers per step",
+                       "tokens": k, "pool_layers": P,
+                       "pool_mb": round(P * (packed + sum(4 * (IN_F + r + OUT_F) for r in RANKS)) / 1e6, 1),
+                       "l2": "weight pool > 2x L2 (126 MB): no flush needed",
+                       "parallelism": f"dp{ws} (independent replicas)", "pdl": bool(args.pdl)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": b_layer,
+                         "launch": "one lbx_linear call (V-stage + U-stage kernels)",
+                         "mean_launch_us": round(per_launch_s * 1e6, 3)},
+            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": 2 * k * IN_F * P, "d2h_bytes_per_step": 2 * k * OUT_F * P,
+                    "ms_per_step": round(t2 / args.steps, 4)},
+            "cpu_baseline": cpu,
+            "gpu_launches": 2 * P * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(out))
+    if ws > 1:
+        import torch.distributed as dist
+        del graph, g2
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--pool", type=int, default=128)
+    ap.add_argument("--pdl", type=int, default=1)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    return run_reference(args) if args.impl == "reference" else run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

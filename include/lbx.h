@@ -92,7 +92,11 @@ typedef struct lbx_linear_args {
   int64_t y_ld[LBX_MAX_PROJ]; /* row stride (elements) of each y; 0 => out    */
 } lbx_linear_args;
 
-/* Bytes of device scratch one lbx_linear / lbx_linear_verify call needs. */
+/* Bytes of device scratch one lbx_linear / lbx_linear_verify call needs.
+ * The workspace must be zero-filled once when it is allocated: it holds a few
+ * bookkeeping words (per-token maxima, a CTA counter) that every call expects
+ * at zero and leaves at zero when it completes.  Calls sharing a workspace must
+ * be ordered on one stream. */
 size_t lbx_linear_workspace_size(const lbx_proj *projs /* host */, int32_t n_proj,
                                  int32_t n_tokens);
 
@@ -207,6 +211,7 @@ typedef struct lbx_model {
   const lbx_layer *layers; /* host array [n_layers] */
 } lbx_model;
 
+/* Workspace of lbx_forward: zero-filled once at allocation, like lbx_linear's. */
 size_t lbx_forward_workspace_size(const lbx_model *m /* host */, int32_t n_tokens);
 /* n tokens at cache slots start..start+n-1 (rotary positions pos[] or, when
  * pos == NULL, the slots).  tree_mask as in lbx_attn_args (NULL = causal).

@@ -238,8 +238,7 @@ extern "C" int lbx_attn_decode(const lbx_attn_args *a, void *ws, size_t ws_bytes
                        (size_t)p.R * ACH) * 4;
   static bool attr_done = false;
   if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(attn_chunk_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaError_t e = allow_max_smem(attn_chunk_kernel);
     if (e != cudaSuccess) return cuda_status(e, "attn smem attribute");
     attr_done = true;
   }

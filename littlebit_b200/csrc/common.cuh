@@ -42,6 +42,27 @@ inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 
 // unit (lbx_all.cu), so this is the single definition.
 __device__ int g_lbx_device_error = 0;
 
+// Allow a kernel the largest dynamic shared memory the device grants a block
+// (opt-in limit minus the kernel's static shared memory).  Returns that size.
+template <typename Kern>
+cudaError_t allow_max_smem(Kern k, size_t *granted = nullptr) {
+  int dev = 0, optin = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  cudaFuncAttributes fa;
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, k);
+  if (e != cudaSuccess) return e;
+  const int dyn = optin - (int)fa.sharedSizeBytes;
+  if (granted) *granted = (size_t)dyn;
+  return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+}
+
+// Phase probes: no-ops in the library build.  A profiling build may define
+// LBX_PROBE(id) to record a timestamp at each phase boundary of a kernel.
+#ifndef LBX_PROBE
+#define LBX_PROBE(id) ((void)0)
+#endif
+
 // Launch with optional programmatic dependent launch (PDL).
 template <typename Kern, typename... Args>
 cudaError_t launch(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,

@@ -4,22 +4,26 @@
 // Reference: quantization/modules/littlebit.py:95-121 (fp32 semantics) and
 // patches/littlebit_cpu_optimized.cpp:598-701 (packed-word CPU kernel).
 //
-// One call = two kernels chained with programmatic dependent launch:
-//   V-stage  t = V_sign·a,  a = v2 ⊙ prologue(x);  z_b = mid_b ⊙ t  -> scratch
-//   U-stage  y = Σ_b u1_b ⊙ U_b·z_b
-// Both stages are "sign matrix × activation" contractions done on the int8
-// tensor cores:
-//   * activations are quantised to 16-bit integers (two int8 digits) with a
-//     per-token scale (per 1024-column chunk in the V-stage, per vector in the
-//     U-stage), so Σ_j s_j·q_j is computed EXACTLY in int32;
-//   * a sign word is expanded in registers with one prmt per 4 signs into
-//     int8 0/−1 (= −bit), giving Σ_j (−b_j)·digit_j from mma.m16n8k32.s8;
+// One call = two kernels chained with programmatic dependent launch (PDL):
+//   V-stage  CTA = 16 rank rows x all of K, warp = 256-column blocks:
+//            z_b = mid_b ⊙ (V_sign · a) [⊙ rsqrt(mean x^2 + eps) for a fused
+//            RMSNorm],  a = v2 ⊙ prologue(x);  blocks summed in fixed order
+//   U-stage  CTA = ut 16-row output tiles, its 16 warps split tiles x ranks:
+//            y = Σ_b u1_b ⊙ U_b · z_b (+ bias)
+// Both contractions run on the int8 tensor cores:
+//   * activations are quantised to 16-bit integers (two int8 digits); the
+//     V-stage uses one scale per token per 256 columns, the U-stage one per
+//     token per branch, so every Σ_j s_j·q_j inside a scale block is EXACT;
+//   * a sign word is expanded in registers by one prmt per 4 signs into int8
+//     0/−1 (= −bit), and mma.m16n8k32.s8 gives D = Σ_j (−b_j)·digit_j;
 //   * Σ_j s_j q_j = Σ_j q_j + 2·(256·D_hi + D_lo).
-// Integer accumulation makes every token's result independent of how many
-// tokens share the launch (verify batch == batch 1, bit for bit).
+// Block results are combined in a fixed order, so a token's output does not
+// depend on how many tokens share the launch (verify batch == batch 1, bit for
+// bit) and repeated calls are deterministic.
 //
-// Weights are prefetched with cp.async.bulk into shared memory BEFORE
-// griddepcontrol.wait, so their HBM latency overlaps the preceding kernel.
+// All weights of a CTA (sign words and scale vectors) are prefetched with
+// cp.async.bulk into shared memory BEFORE griddepcontrol.wait, so their HBM
+// latency overlaps the preceding kernel.
 
 #include <algorithm>
 
@@ -27,9 +31,15 @@
 
 namespace lbx {
 
-constexpr int CH_WORDS = 32;  // words per V-stage chunk (1024 columns)
-constexpr int VWARPS = 4;     // warps per V-stage CTA (split the chunks)
-constexpr int UWARPS_MAX = 8; // warps per U-stage CTA (one 16-row tile each)
+constexpr int PASS_WORDS = 128; // V-stage staging pass: 4096 columns (512 threads x 8)
+constexpr int BLK_WORDS = 8;    // V-stage scale block: 256 columns (one warp)
+constexpr int VWARPS = 16;
+constexpr int VTHREADS = VWARPS * 32;
+constexpr int TBATCH = 2;       // tokens whose x loads are issued together in staging
+constexpr int VCAP_MAX = 12288; // leading v2/norm_w columns prefetched into shared memory
+constexpr int UWARPS = 16;      // warp (tile, split): ut row tiles x (16/ut) rank splits
+constexpr int UTHREADS = UWARPS * 32;
+constexpr int UT_MAX = 8;
 
 // activation buffer: act[W][slot][col] uint32, word stride 8*ncols+8
 __host__ __device__ inline int act_ws(int ncols) { return 8 * ncols + 8; }
@@ -42,17 +52,20 @@ struct VSeg {
   const int32_t *v_sign; // [rank, Wv]
   const float *v2;       // [K]
   const float *mid0;     // [rank]
-  const float *mid1;     // [rank] shared-V residual, or nullptr
-  float *z0;             // [k, rank]
-  float *z1;             // [k, rank] or nullptr
+  const float *mid1;     // [rank] (shared-V residual) or nullptr
+  float *z0;             // [k][rank]
+  float *z1;             // [k][rank] or nullptr
+  int *zmax0;            // [k] running max |z0| (float bits), zero before the call
+  int *zmax1;            // [k] or nullptr
   int rank;
-  int tile0;             // first CTA index of this segment
+  int tile0;             // first CTA (16-row tile) of this segment
 };
 
 struct VParams {
   VSeg seg[2 * LBX_MAX_PROJ];
   int nseg;
-  int K, Wv, pitch, nch;
+  int K, Wv, vpitch;
+  int vcap;              // columns of v2 / norm_w staged in shared memory
   int k, ncols;
   int xdt, prologue;
   float eps;
@@ -64,7 +77,8 @@ struct VParams {
 struct USeg {
   const int32_t *u_sign[2];
   const float *u1[2];
-  const float *z[2];
+  const float *z[2];     // [k][rank] from the V-stage
+  const int *zmax[2];    // [k] max |z| per token (float bits) from the V-stage
   int rank[2];
   int words[2];   // ceil(rank/32)
   int pitch[2];   // smem row pitch (words)
@@ -80,25 +94,33 @@ struct USeg {
 struct UParams {
   USeg seg[LBX_MAX_PROJ];
   int nseg;
-  int k, ncols, ydt, epi, uwarps;
+  int k, ncols, ydt, epi;
+  int ut;             // row tiles per CTA (warps split the ranks 16/ut ways)
   int act_words[2];   // max over projections of 4*ceil(words/4)
-  int wtile_words;    // per-warp weight region (words)
+  int wtile_words;    // per-tile weight region (words)
+  int *zmax_all;      // all zmax words of this call (reset by the last CTA)
+  int nzmax;
+  unsigned *ticket;   // CTA completion counter (zero before and after the call)
 };
 
 // ---------------------------------------------------------------------------
 // shared contraction: one warp, rows g and g+8 of a 16-row sign tile
 // ---------------------------------------------------------------------------
-// Consumes `ngroups` groups of 4 words.  Thread (g,q) reads word 4G+q of its two
+// Consumes groups [g0, g1) of 4 words.  Thread (g,q) reads word 4G+q of its two
 // rows; its 8 prmt expansions feed 4 MMA k-steps.  The activation layout puts,
 // for word w, slot s=(h*4+j), column c, the 4 digits of reduction positions
 // 32w+16h+j+{0,4,8,12} into one uint32, matching the A-fragment bytes.
+// Even and odd groups accumulate into separate registers (two independent
+// MMA dependency chains), summed exactly at the end.
 template <int NCB>
 LBX_DEV void sign_mma(int (&acc)[NCB][4], const uint32_t *rowg, const uint32_t *rowg8,
-                      const uint32_t *act, int ws, int ncols, int ngroups, int lane) {
+                      const uint32_t *act, int ws, int ncols, int g0, int g1, int lane) {
   const int q = lane & 3;
   const int n8 = lane >> 2;
-#pragma unroll 2
-  for (int G = 0; G < ngroups; ++G) {
+  int acc2[NCB][4];
+#pragma unroll
+  for (int cb = 0; cb < NCB; ++cb) acc2[cb][0] = acc2[cb][1] = acc2[cb][2] = acc2[cb][3] = 0;
+  auto group = [&](int G, int (&ac)[NCB][4]) {
     const int w = 4 * G + q;
     const uint32_t wa = rowg[w];
     const uint32_t wb = rowg8[w];
@@ -119,10 +141,20 @@ LBX_DEV void sign_mma(int (&acc)[NCB][4], const uint32_t *rowg, const uint32_t *
           b0 = aw[slot * ncols + col];
           b1 = aw[(slot + 1) * ncols + col];
         }
-        mma_s8(acc[cb], a0, a1, a2, a3, b0, b1);
+        mma_s8(ac[cb], a0, a1, a2, a3, b0, b1);
       }
     }
+  };
+  int G = g0;
+  for (; G + 1 < g1; G += 2) {
+    group(G, acc);
+    group(G + 1, acc2);
   }
+  if (G < g1) group(G, acc);
+#pragma unroll
+  for (int cb = 0; cb < NCB; ++cb)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[cb][e] += acc2[cb][e];
 }
 
 LBX_DEV uint32_t pack4(int a, int b, int c, int d) {
@@ -130,207 +162,331 @@ LBX_DEV uint32_t pack4(int a, int b, int c, int d) {
          ((uint32_t)(d & 255) << 24);
 }
 
+// activations (written by the preceding kernel): L2 loads
+LBX_DEV void load8(const void *p, int dtype, int64_t i, float (&v)[8]) {
+  if (dtype == LBX_F32) {
+    const float4 *s = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(p) + i);
+    const float4 a = __ldcg(s), b = __ldcg(s + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 u = __ldcg(reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(p) + i));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      v[2 * e] = __uint_as_float(w[e] << 16);
+      v[2 * e + 1] = __uint_as_float(w[e] & 0xFFFF0000u);
+    }
+  }
+}
+
+LBX_DEV void load8f(const float *p, float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4 *>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// partial-sum loads of data written by the preceding kernel: L2 only
+LBX_DEV void load8cg(const float *p, float (&v)[8]) {
+  const float4 a = __ldcg(reinterpret_cast<const float4 *>(p));
+  const float4 b = __ldcg(reinterpret_cast<const float4 *>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
 // ---------------------------------------------------------------------------
 // V-stage
 // ---------------------------------------------------------------------------
-LBX_DEV float v_input(const VParams &p, const float *v2, int tok, int pos, float *xsq) {
-  const int64_t i = (int64_t)tok * p.K + pos;
-  float x = load_act(p.x, p.xdt, i);
-  float a;
-  if (p.prologue == LBX_PRO_RMSNORM) {
-    if (xsq) *xsq += x * x;
-    a = x * __ldg(p.norm_w + pos);
-  } else if (p.prologue == LBX_PRO_SILU_MUL) {
-    const float u = load_act(p.x2, p.xdt, i);
-    a = (x / (1.0f + expf(-x))) * u;
-  } else {
-    a = x;
-  }
-  return a * __ldg(v2 + pos);
-}
-
 template <int NCB>
-__global__ void __launch_bounds__(VWARPS * 32) vstage_kernel(const __grid_constant__ VParams p) {
+__global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_constant__ VParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ float s_inv[VWARPS][LBX_MAX_TOKENS];
+  __shared__ int s_sq[VWARPS][LBX_MAX_TOKENS];
+  __shared__ float s_ssq[VWARPS][LBX_MAX_TOKENS];
+  __shared__ __align__(16) float s_mid[2][16];
+  __shared__ int s_zmax[2][LBX_MAX_TOKENS];
+  __shared__ __align__(8) uint64_t bar;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, q = lane & 3;
 
-  // locate segment / tile
   int s = 0;
   while (s + 1 < p.nseg && (int)blockIdx.x >= p.seg[s + 1].tile0) ++s;
   const VSeg &sg = p.seg[s];
   const int row0 = ((int)blockIdx.x - sg.tile0) * 16;
-  const int rows = min(16, sg.rank - row0);
+  const int rows = min(16, sg.rank - row0);  // 8 or 16 (ranks are multiples of 8)
+  const bool rms = p.prologue == LBX_PRO_RMSNORM;
 
   const int ws = act_ws(p.ncols);
-  uint32_t *wbuf = reinterpret_cast<uint32_t *>(smem_raw);           // 16 x pitch
-  uint32_t *actb = wbuf + 16 * p.pitch;                               // VWARPS x 32 x ws
-  float *red = reinterpret_cast<float *>(actb + VWARPS * CH_WORDS * ws); // VWARPS x 16 x k
-  float *ssq = red + VWARPS * 16 * p.k;                               // VWARPS x k
-  uint64_t *bar = reinterpret_cast<uint64_t *>(ssq + VWARPS * LBX_MAX_TOKENS + 2);
-  bar = reinterpret_cast<uint64_t *>((reinterpret_cast<uintptr_t>(bar) + 7) & ~uintptr_t(7));
+  uint32_t *wbuf = reinterpret_cast<uint32_t *>(smem_raw);           // 16 x vpitch
+  float *sv2 = reinterpret_cast<float *>(wbuf + 16 * p.vpitch);       // vcap
+  float *snw = sv2 + p.vcap;                                          // vcap (RMSNorm)
+  uint32_t *act = reinterpret_cast<uint32_t *>(snw + (rms ? p.vcap : 0)); // PASS_WORDS x ws
+  float *red = reinterpret_cast<float *>(act + PASS_WORDS * ws);      // [16][16 rows][k]
 
+  // weights of this CTA (sign rows, v2, norm_w, mid) do not depend on the
+  // preceding kernel: start their copies before waiting for it
+  const int vcap = p.vcap;  // leading columns of v2 / norm_w held in shared memory
+  LBX_PROBE(0);
   if (tid == 0) {
-    mbar_init(bar, 1);
+    mbar_init(&bar, 1);
     fence_mbar_init();
+    uint32_t bytes = (uint32_t)rows * p.Wv * 4u + (uint32_t)vcap * 4u * (rms ? 2u : 1u) +
+                     (uint32_t)rows * 4u * (sg.mid1 ? 2u : 1u);
+    mbar_arrive_expect_tx(&bar, bytes);
   }
+  if (tid < VWARPS * LBX_MAX_TOKENS) (&s_ssq[0][0])[tid] = 0.f;
+  if (tid < 2 * LBX_MAX_TOKENS) (&s_zmax[0][0])[tid] = 0;
   __syncthreads();
-  // weight prefetch (independent of the preceding kernel)
-  if (warp == 0) {
-    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)rows * p.Wv * 4u);
-    __syncwarp();
-    if (lane < rows)
-      bulk_g2s(wbuf + lane * p.pitch, sg.v_sign + (int64_t)(row0 + lane) * p.Wv,
-               (uint32_t)p.Wv * 4u, bar);
-  }
+  if (tid < rows)
+    bulk_g2s(wbuf + tid * p.vpitch, sg.v_sign + (int64_t)(row0 + tid) * p.Wv, (uint32_t)p.Wv * 4u,
+             &bar);
+  else if (tid == 16)
+    bulk_g2s(sv2, sg.v2, (uint32_t)vcap * 4u, &bar);
+  else if (tid == 17 && rms)
+    bulk_g2s(snw, p.norm_w, (uint32_t)vcap * 4u, &bar);
+  else if (tid == 18)
+    bulk_g2s(s_mid[0], sg.mid0 + row0, (uint32_t)rows * 4u, &bar);
+  else if (tid == 19 && sg.mid1)
+    bulk_g2s(s_mid[1], sg.mid1 + row0, (uint32_t)rows * 4u, &bar);
   pdl_trigger();
   pdl_wait();
+  LBX_PROBE(1);
 
-  uint32_t *act = actb + warp * CH_WORDS * ws;
+  // thread t stages columns 8*(t%4)..+8 of word t/4 of each 128-word pass;
+  // warp w = one 256-column scale block
+  const int W = tid >> 2, qq = tid & 3;
+  const int hh = qq >> 1;
+  const bool low = (qq & 1) == 0;  // my digits are bytes 0,1 (else 2,3) of the slot words
   float tacc[NCB][2];
 #pragma unroll
   for (int cb = 0; cb < NCB; ++cb) tacc[cb][0] = tacc[cb][1] = 0.f;
-  float xsq_tok = 0.f;  // lane-partial sum of squares for token `lane` (RMSNorm)
-  bool have_w = false;
   bool ok = true;
-
-  __shared__ float s_inv[VWARPS][LBX_MAX_TOKENS];
-  __shared__ int s_sq[VWARPS][LBX_MAX_TOKENS];
-
-  for (int c = warp; c < p.nch; c += VWARPS) {
-    const int base = c * CH_WORDS * 32;
-    const int cwords = min(CH_WORDS, p.Wv - c * CH_WORDS);
-    // ---- stage this chunk: per token absmax, then digits
-    for (int t = 0; t < p.k; ++t) {
-      float amax = 0.f, sq = 0.f;
-      for (int i = lane; i < cwords * 32; i += 32) {
-        const float a = v_input(p, sg.v2, t, base + i, &sq);
-        amax = fmaxf(amax, fabsf(a));
-      }
-      amax = warp_max(amax);
-      if (p.prologue == LBX_PRO_RMSNORM) {
-        sq = warp_sum(sq);
-        if (lane == t) xsq_tok += sq;
-      }
-      const float sc = amax > 0.f ? QMAX / amax : 0.f;
-      int sqi = 0;
-      for (int it = 0; it < CH_WORDS / 4; ++it) {
-        const int W = it * 4 + (lane >> 3);
-        const int slot = lane & 7;
-        const int hh = slot >> 2, jj = slot & 3;
-        int hi[4], lo[4];
+  const int npass = (p.Wv + PASS_WORDS - 1) / PASS_WORDS;
+  for (int pass = 0; pass < npass; ++pass) {
+    const int pw0 = pass * PASS_WORDS;
+    const int pwords = min(PASS_WORDS, p.Wv - pw0);
+    const bool wvalid = W < pwords;
+    const int64_t col = (int64_t)(pw0 + W) * 32 + 8 * qq;
+    const bool silu = p.prologue == LBX_PRO_SILU_MUL;
+    float hw[8];
+    for (int t0 = 0; t0 < p.k; t0 += TBATCH) {
+      // issue the loads of a batch of tokens before using any of them
+      float xv[TBATCH][8], uv[TBATCH][8];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          int qv = 0;
-          if (W < cwords) {
-            const float a = v_input(p, sg.v2, t, base + 32 * W + 16 * hh + jj + 4 * e, nullptr);
-            qv = __float2int_rn(a * sc);
-          }
-          sqi += qv;
-          split_digits(qv, hi[e], lo[e]);
+      for (int j = 0; j < TBATCH; ++j) {
+        if (wvalid && t0 + j < p.k) {
+          load8(p.x, p.xdt, (int64_t)(t0 + j) * p.K + col, xv[j]);
+          if (silu) load8(p.x2, p.xdt, (int64_t)(t0 + j) * p.K + col, uv[j]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) xv[j][i] = uv[j][i] = 0.f;
         }
-        act[W * ws + slot * p.ncols + 2 * t] = pack4(hi[0], hi[1], hi[2], hi[3]);
-        act[W * ws + slot * p.ncols + 2 * t + 1] = pack4(lo[0], lo[1], lo[2], lo[3]);
       }
-      sqi = warp_sum_i(sqi);
-      if (lane == 0) {
-        s_inv[warp][t] = amax / QMAX;
-        s_sq[warp][t] = sqi;
-      }
-    }
-    __syncwarp();
-    if (!have_w) {
-      ok = mbar_wait_bounded(bar, 0, 0x101);
-      have_w = true;
-    }
-    if (!ok) break;
-    int acc[NCB][4];
+      if (t0 == 0) {
+        if (pass == 0) {
+          ok = mbar_wait_bounded(&bar, 0, 0x101);
+          LBX_PROBE(2);
+        }
+        if (!wvalid) {
 #pragma unroll
-    for (int cb = 0; cb < NCB; ++cb) acc[cb][0] = acc[cb][1] = acc[cb][2] = acc[cb][3] = 0;
-    sign_mma<NCB>(acc, wbuf + g * p.pitch + c * CH_WORDS, wbuf + (g + 8) * p.pitch + c * CH_WORDS,
-                  act, ws, p.ncols, cwords / 4, lane);
+          for (int i = 0; i < 8; ++i) hw[i] = 0.f;
+        } else if (col < vcap) {
+          const float4 *v4 = reinterpret_cast<const float4 *>(sv2 + col);
+          const float4 a0 = v4[0], a1 = v4[1];
+          hw[0] = a0.x; hw[1] = a0.y; hw[2] = a0.z; hw[3] = a0.w;
+          hw[4] = a1.x; hw[5] = a1.y; hw[6] = a1.z; hw[7] = a1.w;
+          if (rms) {
+            const float4 *n4 = reinterpret_cast<const float4 *>(snw + col);
+            const float4 b0 = n4[0], b1 = n4[1];
+            hw[0] *= b0.x; hw[1] *= b0.y; hw[2] *= b0.z; hw[3] *= b0.w;
+            hw[4] *= b1.x; hw[5] *= b1.y; hw[6] *= b1.z; hw[7] *= b1.w;
+          }
+        } else {  // columns beyond the shared-memory copy (very wide inputs)
+          load8f(sg.v2 + col, hw);
+          if (rms) {
+            float nw[8];
+            load8f(p.norm_w + col, nw);
 #pragma unroll
-    for (int cb = 0; cb < NCB; ++cb) {
-      const int t = cb * 4 + q;
-      if (t < p.k) {
-        const int sq = s_sq[warp][t];
-        const float inv = s_inv[warp][t];
-        tacc[cb][0] += __int2float_rn(sq + 2 * (256 * acc[cb][0] + acc[cb][1])) * inv;
-        tacc[cb][1] += __int2float_rn(sq + 2 * (256 * acc[cb][2] + acc[cb][3])) * inv;
+            for (int i = 0; i < 8; ++i) hw[i] *= nw[i];
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < TBATCH; ++j) {
+        const int t = t0 + j;
+        if (t >= p.k) break;  // uniform across the CTA
+        float a[8];
+        float sq2 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float xx = xv[j][i];
+          if (silu) {
+            a[i] = (xx / (1.0f + expf(-xx))) * uv[j][i] * hw[i];
+          } else {
+            sq2 = fmaf(xx, xx, sq2);
+            a[i] = xx * hw[i];
+          }
+        }
+        float m = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(a[i]));
+        m = __int_as_float(__reduce_max_sync(0xffffffffu, __float_as_int(m)));
+        const float sc = m > 0.f ? QMAX / m : 0.f;
+        int hi[8], lo[8], sqi = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int qv = __float2int_rn(a[i] * sc);
+          sqi += qv;
+          split_digits(qv, hi[i], lo[i]);
+        }
+        // 16-bit halves of the 4 slot words (h, j): bytes = columns j and j+4
+        uint32_t H[2], L[2];
+#pragma unroll
+        for (int jp = 0; jp < 2; ++jp) {
+          const int j0 = 2 * jp, j1 = 2 * jp + 1;
+          H[jp] = ((hi[j0] & 255) | ((hi[j0 + 4] & 255) << 8)) |
+                  (((hi[j1] & 255) | ((hi[j1 + 4] & 255) << 8)) << 16);
+          L[jp] = ((lo[j0] & 255) | ((lo[j0 + 4] & 255) << 8)) |
+                  (((lo[j1] & 255) | ((lo[j1 + 4] & 255) << 8)) << 16);
+        }
+        const uint32_t PH0 = __shfl_xor_sync(0xffffffffu, H[0], 1);
+        const uint32_t PH1 = __shfl_xor_sync(0xffffffffu, H[1], 1);
+        const uint32_t PL0 = __shfl_xor_sync(0xffffffffu, L[0], 1);
+        const uint32_t PL1 = __shfl_xor_sync(0xffffffffu, L[1], 1);
+        uint32_t *aw = act + W * ws + 2 * t;
+        if (low) {  // slots j = 0, 1: my half low, partner's high
+          aw[(4 * hh + 0) * p.ncols] = (H[0] & 0xFFFFu) | (PH0 << 16);
+          aw[(4 * hh + 0) * p.ncols + 1] = (L[0] & 0xFFFFu) | (PL0 << 16);
+          aw[(4 * hh + 1) * p.ncols] = (H[0] >> 16) | (PH0 & 0xFFFF0000u);
+          aw[(4 * hh + 1) * p.ncols + 1] = (L[0] >> 16) | (PL0 & 0xFFFF0000u);
+        } else {    // slots j = 2, 3: partner's half low, mine high
+          aw[(4 * hh + 2) * p.ncols] = (PH1 & 0xFFFFu) | (H[1] << 16);
+          aw[(4 * hh + 2) * p.ncols + 1] = (PL1 & 0xFFFFu) | (L[1] << 16);
+          aw[(4 * hh + 3) * p.ncols] = (PH1 >> 16) | (H[1] & 0xFFFF0000u);
+          aw[(4 * hh + 3) * p.ncols + 1] = (PL1 >> 16) | (L[1] & 0xFFFF0000u);
+        }
+        sqi = __reduce_add_sync(0xffffffffu, sqi);
+        if (rms) sq2 = warp_sum(sq2);
+        if (lane == 0) {
+          s_inv[warp][t] = m / QMAX;
+          s_sq[warp][t] = sqi;
+          s_ssq[warp][t] += sq2;
+        }
       }
     }
-    __syncwarp();
+    __syncthreads();
+    LBX_PROBE(3);
+    // MMA: warp w contracts its own 256-column block of this pass
+    if (ok && BLK_WORDS * warp < pwords) {
+      int acc[NCB][4];
+#pragma unroll
+      for (int cb = 0; cb < NCB; ++cb) acc[cb][0] = acc[cb][1] = acc[cb][2] = acc[cb][3] = 0;
+      const int wb = pw0 + BLK_WORDS * warp;
+      const int ng = min(BLK_WORDS, pwords - BLK_WORDS * warp) / 4;
+      sign_mma<NCB>(acc, wbuf + g * p.vpitch + wb, wbuf + (g + 8) * p.vpitch + wb,
+                    act + BLK_WORDS * warp * ws, ws, p.ncols, 0, ng, lane);
+#pragma unroll
+      for (int cb = 0; cb < NCB; ++cb) {
+        const int t = cb * 4 + q;
+        if (t < p.k) {
+          const int sq = s_sq[warp][t];
+          const float inv = s_inv[warp][t];
+          tacc[cb][0] += __int2float_rn(sq + 2 * (256 * acc[cb][0] + acc[cb][1])) * inv;
+          tacc[cb][1] += __int2float_rn(sq + 2 * (256 * acc[cb][2] + acc[cb][3])) * inv;
+        }
+      }
+    }
+    __syncthreads();
   }
-  // if this warp had no chunk it never waited; make sure the copy landed
-  // before the CTA exits (shared memory must not be released under a copy).
-  if (!have_w) ok = mbar_wait_bounded(bar, 0, 0x102);
-
-  // ---- cross-warp reduction in fixed warp order
+  // ---- fixed-order reduction over the 16 warps, then scales
+  float *rw = red + warp * 16 * p.k;
 #pragma unroll
   for (int cb = 0; cb < NCB; ++cb) {
     const int t = cb * 4 + q;
     if (t < p.k) {
-      red[(warp * 16 + g) * p.k + t] = tacc[cb][0];
-      red[(warp * 16 + g + 8) * p.k + t] = tacc[cb][1];
+      rw[g * p.k + t] = tacc[cb][0];
+      rw[(g + 8) * p.k + t] = tacc[cb][1];
     }
   }
-  if (p.prologue == LBX_PRO_RMSNORM && lane < p.k) ssq[warp * LBX_MAX_TOKENS + lane] = xsq_tok;
   __syncthreads();
+  LBX_PROBE(4);
   if (!ok) return;
-  for (int i = tid; i < rows * p.k; i += blockDim.x) {
-    const int rr = i / p.k, t = i % p.k;
+  for (int i = tid; i < rows * p.k; i += VTHREADS) {
+    const int rr = i / p.k, t = i - rr * p.k;
     float v = 0.f;
 #pragma unroll
     for (int w = 0; w < VWARPS; ++w) v += red[(w * 16 + rr) * p.k + t];
-    if (p.prologue == LBX_PRO_RMSNORM) {
+    if (rms) {
       float s2 = 0.f;
 #pragma unroll
-      for (int w = 0; w < VWARPS; ++w) s2 += ssq[w * LBX_MAX_TOKENS + t];
+      for (int w = 0; w < VWARPS; ++w) s2 += s_ssq[w][t];
       v *= rsqrtf(s2 / (float)p.K + p.eps);
     }
-    const int r = row0 + rr;
-    sg.z0[(int64_t)t * sg.rank + r] = __ldg(sg.mid0 + r) * v;
-    if (sg.z1) sg.z1[(int64_t)t * sg.rank + r] = __ldg(sg.mid1 + r) * v;
+    const float z0 = s_mid[0][rr] * v;
+    sg.z0[(int64_t)t * sg.rank + row0 + rr] = z0;
+    atomicMax(&s_zmax[0][t], __float_as_int(fabsf(z0)));
+    if (sg.z1) {
+      const float z1 = s_mid[1][rr] * v;
+      sg.z1[(int64_t)t * sg.rank + row0 + rr] = z1;
+      atomicMax(&s_zmax[1][t], __float_as_int(fabsf(z1)));
+    }
   }
+  __syncthreads();
+  if (tid < p.k) {
+    atomicMax(sg.zmax0 + tid, s_zmax[0][tid]);
+    if (sg.z1) atomicMax(sg.zmax1 + tid, s_zmax[1][tid]);
+  }
+  LBX_PROBE(5);
 }
 
 // ---------------------------------------------------------------------------
 // U-stage
 // ---------------------------------------------------------------------------
 template <int NCB>
-__global__ void __launch_bounds__(UWARPS_MAX * 32) ustage_kernel(const __grid_constant__ UParams p) {
+__global__ void __launch_bounds__(UTHREADS, 2) ustage_kernel(const __grid_constant__ UParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ float s_inv[2][LBX_MAX_TOKENS];
+  __shared__ float s_scale[2][LBX_MAX_TOKENS];
+  __shared__ int s_sq[2][LBX_MAX_TOKENS];
+  __shared__ __align__(8) uint64_t bars[UT_MAX];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, q = lane & 3;
-  const int nthreads = blockDim.x;
+  const int ut = p.ut, nsplit = UWARPS / ut;
+  const int tile = warp % ut, split = warp / ut;
 
   int s = 0;
   while (s + 1 < p.nseg && (int)blockIdx.x >= p.seg[s + 1].cta0) ++s;
   const USeg &sg = p.seg[s];
-  const int n0 = ((int)blockIdx.x - sg.cta0) * (16 * p.uwarps) + 16 * warp;
+  const int n0 = ((int)blockIdx.x - sg.cta0) * (16 * ut) + 16 * tile;
   const bool active = n0 < sg.out;
 
   const int ws = act_ws(p.ncols);
   uint32_t *act0 = reinterpret_cast<uint32_t *>(smem_raw);
   uint32_t *act1 = act0 + p.act_words[0] * ws;
-  uint32_t *wt = act1 + p.act_words[1] * ws;                 // uwarps x wtile_words
-  uint64_t *bars = reinterpret_cast<uint64_t *>(wt + p.uwarps * p.wtile_words);
-  __shared__ float s_inv[2][LBX_MAX_TOKENS];
-  __shared__ int s_sq[2][LBX_MAX_TOKENS];
+  int *xch = reinterpret_cast<int *>(act1 + p.act_words[1] * ws);     // [warps][32][2*NCB*4]
+  uint32_t *wt = reinterpret_cast<uint32_t *>(xch + UWARPS * 32 * 8 * NCB);  // ut x wtile_words
+  float *su1 = reinterpret_cast<float *>(wt + ut * p.wtile_words);    // ut x 48 (u1_0, u1_1, bias)
 
-  uint32_t *mywt0 = wt + warp * p.wtile_words;
+  uint32_t *mywt0 = wt + tile * p.wtile_words;
   uint32_t *mywt1 = mywt0 + 16 * sg.pitch[0] + 4;
+  float *myu1 = su1 + tile * 48;
+  const int r0 = sg.rank[0], r1 = sg.nbr > 1 ? sg.rank[1] : 0;
 
-  if (lane == 0) {
-    mbar_init(bars + warp, 1);
+  LBX_PROBE(10);
+  if (tid < ut) {
+    mbar_init(bars + tid, 1);
     fence_mbar_init();
   }
   if (tid < 2 * LBX_MAX_TOKENS) (&s_sq[0][0])[tid] = 0;
   __syncthreads();
-  if (active) {
+  // weights (signs, u1, bias of each tile) do not depend on the preceding
+  // kernel: start their copies before waiting for it
+  if (active && split == 0) {
     uint32_t bytes = 0;
-    for (int b = 0; b < sg.nbr; ++b) bytes += 16u * sg.words[b] * 4u;
-    if (lane == 0) mbar_arrive_expect_tx(bars + warp, bytes);
+    for (int b = 0; b < sg.nbr; ++b) bytes += 16u * sg.words[b] * 4u + 64u;
+    if (sg.bias) bytes += 64u;
+    if (lane == 0) mbar_arrive_expect_tx(bars + tile, bytes);
     __syncwarp();
     for (int b = 0; b < sg.nbr; ++b) {
       uint32_t *dst = b == 0 ? mywt0 : mywt1;
@@ -338,70 +494,126 @@ __global__ void __launch_bounds__(UWARPS_MAX * 32) ustage_kernel(const __grid_co
       if (sg.perrow[b]) {
         if (lane < 16)
           bulk_g2s(dst + lane * sg.pitch[b], src + (int64_t)lane * sg.words[b],
-                   (uint32_t)sg.words[b] * 4u, bars + warp);
+                   (uint32_t)sg.words[b] * 4u, bars + tile);
       } else if (lane == 0) {
-        bulk_g2s(dst, src, 16u * sg.words[b] * 4u, bars + warp);
+        bulk_g2s(dst, src, 16u * sg.words[b] * 4u, bars + tile);
       }
+      if (lane == 16 + b) bulk_g2s(myu1 + 16 * b, sg.u1[b] + n0, 64u, bars + tile);
     }
+    if (lane == 18 && sg.bias) bulk_g2s(myu1 + 32, sg.bias + n0, 64u, bars + tile);
   }
   pdl_trigger();
   pdl_wait();
+  LBX_PROBE(11);
 
-  // ---- stage z_b as 16-bit digits with one scale per token
-  for (int b = 0; b < sg.nbr; ++b) {
-    const float *z = sg.z[b];
-    const int r = sg.rank[b];
-    for (int t = warp; t < p.k; t += p.uwarps) {
-      float m = 0.f;
-      for (int i = lane; i < r; i += 32) m = fmaxf(m, fabsf(z[(int64_t)t * r + i]));
-      m = warp_max(m);
-      if (lane == 0) s_inv[b][t] = m / QMAX;
-    }
+  // ---- per-(branch, token) scale from the V-stage maxima, 16-bit digits of z
+  if (tid < 2 * p.k) {
+    const int b = tid / p.k, t = tid - b * p.k;
+    const float m = (b < sg.nbr) ? __int_as_float(__ldcg(sg.zmax[b] + t)) : 0.f;
+    s_inv[b][t] = m / QMAX;
+    s_scale[b][t] = m > 0.f ? QMAX / m : 0.f;
   }
   __syncthreads();
-  for (int b = 0; b < sg.nbr; ++b) {
-    const float *z = sg.z[b];
-    const int r = sg.rank[b];
-    const int nw = 4 * ((sg.words[b] + 3) / 4);
-    uint32_t *act = b == 0 ? act0 : act1;
-    const int items = nw * 8 * p.k;
-    for (int i = tid; i < items; i += nthreads) {
-      const int t = i / (nw * 8);
-      const int rem = i - t * nw * 8;
-      const int W = rem >> 3, slot = rem & 7;
+  LBX_PROBE(12);
+  {
+    // items (t, b, W, slot): each (t, b) segment is a multiple of 32 items, so a
+    // warp's 32 items always share (t, b) and reduce with one redux
+    const int nw0 = 4 * ((sg.words[0] + 3) / 4);
+    const int nw1 = sg.nbr > 1 ? 4 * ((sg.words[1] + 3) / 4) : 0;
+    const int per = (nw0 + nw1) * 8;
+    const int total = p.k * per;
+    for (int base = warp * 32; base < total; base += UTHREADS) {
+      const int i = base + lane;
+      const int t = i / per, rem = i - t * per;
+      const int b = rem < nw0 * 8 ? 0 : 1;
+      const int rr = b ? rem - nw0 * 8 : rem;
+      const int W = rr >> 3, slot = rr & 7;
       const int hh = slot >> 2, jj = slot & 3;
-      const float inv = s_inv[b][t];
-      const float sc = inv > 0.f ? 1.0f / inv : 0.f;
-      int hi[4], lo[4], sq = 0;
+      const int r = b ? r1 : r0;
+      const float *zrow = sg.z[b] + (int64_t)t * r;
+      const float sc = s_scale[b][t];
+      float zv[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int pos = 32 * W + 16 * hh + jj + 4 * e;
-        int qv = 0;
-        if (pos < r) qv = __float2int_rn(z[(int64_t)t * r + pos] * sc);
+        zv[e] = pos < r ? __ldcg(zrow + pos) : 0.f;
+      }
+      int hi[4], lo[4], sq = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int qv = __float2int_rn(zv[e] * sc);
         sq += qv;
         split_digits(qv, hi[e], lo[e]);
       }
-      act[W * ws + slot * p.ncols + 2 * t] = pack4(hi[0], hi[1], hi[2], hi[3]);
-      act[W * ws + slot * p.ncols + 2 * t + 1] = pack4(lo[0], lo[1], lo[2], lo[3]);
-      atomicAdd(&s_sq[b][t], sq);
+      uint32_t *aw = (b ? act1 : act0) + W * ws + 2 * t;
+      aw[slot * p.ncols] = pack4(hi[0], hi[1], hi[2], hi[3]);
+      aw[slot * p.ncols + 1] = pack4(lo[0], lo[1], lo[2], lo[3]);
+      sq = __reduce_add_sync(0xffffffffu, sq);
+      if (lane == 0) atomicAdd(&s_sq[b][t], sq);
     }
   }
   __syncthreads();
 
+  LBX_PROBE(13);
   bool ok = true;
-  if (active) ok = mbar_wait_bounded(bars + warp, 0, 0x201);
-  if (!active || !ok) return;
+  if (active) ok = mbar_wait_bounded(bars + tile, 0, 0x201);
+  LBX_PROBE(14);
 
   int acc0[NCB][4], acc1[NCB][4];
 #pragma unroll
   for (int cb = 0; cb < NCB; ++cb)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc0[cb][e] = acc1[cb][e] = 0;
-  sign_mma<NCB>(acc0, mywt0 + g * sg.pitch[0], mywt0 + (g + 8) * sg.pitch[0], act0, ws, p.ncols,
-                (sg.words[0] + 3) / 4, lane);
-  if (sg.nbr > 1)
-    sign_mma<NCB>(acc1, mywt1 + g * sg.pitch[1], mywt1 + (g + 8) * sg.pitch[1], act1, ws,
-                  p.ncols, (sg.words[1] + 3) / 4, lane);
+  // this warp's share of the flattened (branch, group) list
+  const int ng0 = (sg.words[0] + 3) / 4, ng1 = sg.nbr > 1 ? (sg.words[1] + 3) / 4 : 0;
+  const int ngt = ng0 + ng1;
+  const int ga = (split * ngt) / nsplit, gb = ((split + 1) * ngt) / nsplit;
+  if (active && ok) {
+    if (ga < ng0)
+      sign_mma<NCB>(acc0, mywt0 + g * sg.pitch[0], mywt0 + (g + 8) * sg.pitch[0], act0, ws,
+                    p.ncols, ga, min(gb, ng0), lane);
+    if (gb > ng0)
+      sign_mma<NCB>(acc1, mywt1 + g * sg.pitch[1], mywt1 + (g + 8) * sg.pitch[1], act1, ws,
+                    p.ncols, max(ga, ng0) - ng0, gb - ng0, lane);
+  }
+  if (nsplit > 1) {
+    int *xw = xch + (warp * 32 + lane) * (8 * NCB);
+    if (split > 0) {
+#pragma unroll
+      for (int cb = 0; cb < NCB; ++cb)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          xw[cb * 4 + e] = acc0[cb][e];
+          xw[4 * NCB + cb * 4 + e] = acc1[cb][e];
+        }
+    }
+    __syncthreads();
+    if (split == 0) {
+      for (int sp = 1; sp < nsplit; ++sp) {
+        const int *xr = xch + ((sp * ut + tile) * 32 + lane) * (8 * NCB);
+#pragma unroll
+        for (int cb = 0; cb < NCB; ++cb)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            acc0[cb][e] += xr[cb * 4 + e];
+            acc1[cb][e] += xr[4 * NCB + cb * 4 + e];
+          }
+      }
+    }
+  }
+  LBX_PROBE(15);
+  // the last CTA to get here clears the call's bookkeeping words for the next call
+  // (every CTA has read its scales before this point)
+  if (tid == 0) {
+    __threadfence();
+    const unsigned done = atomicAdd(p.ticket, 1u);
+    if (done == gridDim.x - 1) {
+      for (int i = 0; i < p.nzmax; ++i) p.zmax_all[i] = 0;
+      *p.ticket = 0u;
+      __threadfence();
+    }
+  }
+  if (!active || !ok || split != 0) return;
 
 #pragma unroll
   for (int cb = 0; cb < NCB; ++cb) {
@@ -409,15 +621,16 @@ __global__ void __launch_bounds__(UWARPS_MAX * 32) ustage_kernel(const __grid_co
     if (t >= p.k) continue;
 #pragma unroll
     for (int hrow = 0; hrow < 2; ++hrow) {
-      const int n = n0 + g + 8 * hrow;
-      float v = __ldg(sg.u1[0] + n) *
+      const int nl = g + 8 * hrow;
+      const int n = n0 + nl;
+      float v = myu1[nl] *
                 (__int2float_rn(s_sq[0][t] + 2 * (256 * acc0[cb][2 * hrow] + acc0[cb][2 * hrow + 1])) *
                  s_inv[0][t]);
       if (sg.nbr > 1)
-        v += __ldg(sg.u1[1] + n) *
+        v += myu1[16 + nl] *
              (__int2float_rn(s_sq[1][t] + 2 * (256 * acc1[cb][2 * hrow] + acc1[cb][2 * hrow + 1])) *
               s_inv[1][t]);
-      if (sg.bias) v += __ldg(sg.bias + n);
+      if (sg.bias) v += myu1[32 + nl];
       const int64_t off = (int64_t)t * sg.y_ld + n;
       if (p.ydt == LBX_F32) {
         float *y = reinterpret_cast<float *>(sg.y) + off;
@@ -433,11 +646,15 @@ __global__ void __launch_bounds__(UWARPS_MAX * 32) ustage_kernel(const __grid_co
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-static size_t z_bytes(const lbx_proj *projs, int n_proj, int k) {
-  size_t tot = 0;
+constexpr size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// scratch: [bookkeeping: zmax words + CTA ticket] then z of every (projection, branch)
+constexpr size_t WS_HDR = al256((2 * LBX_MAX_PROJ * LBX_MAX_TOKENS + 1) * sizeof(int));
+
+static size_t ws_bytes_for(const lbx_proj *projs, int n_proj, int k) {
+  size_t tot = WS_HDR;
   for (int i = 0; i < n_proj; ++i)
-    for (int b = 0; b < projs[i].n_branches; ++b)
-      tot += (((size_t)projs[i].br[b].rank * k * 4) + 255) & ~(size_t)255;
+    for (int b = 0; b < projs[i].n_branches; ++b) tot += al256((size_t)k * projs[i].br[b].rank * 4);
   return tot;
 }
 
@@ -455,12 +672,13 @@ static int validate(const lbx_proj *projs, int n_proj) {
     LBX_CHECK_ARG(pr.n_branches == 1 || pr.n_branches == 2, "n_branches must be 1 or 2");
     for (int b = 0; b < pr.n_branches; ++b) {
       const lbx_branch &br = pr.br[b];
-      LBX_CHECK_ARG(br.rank > 0, "rank must be positive");
+      LBX_CHECK_SUP(br.rank > 0 && br.rank % 8 == 0, "rank must be a positive multiple of 8 (got %d)",
+                    br.rank);
       LBX_CHECK_ARG(br.mid && br.u_sign && br.u1, "branch %d: mid/u_sign/u1 required", b);
-      LBX_CHECK_ARG(aligned16(br.u_sign), "u_sign must be 16-byte aligned");
+      LBX_CHECK_ARG(aligned16(br.u_sign) && aligned16(br.mid), "u_sign/mid must be 16-byte aligned");
       if (br.v_sign) {
         LBX_CHECK_ARG(br.v2, "branch %d: v2 required with v_sign", b);
-        LBX_CHECK_ARG(aligned16(br.v_sign), "v_sign must be 16-byte aligned");
+        LBX_CHECK_ARG(aligned16(br.v_sign) && aligned16(br.v2), "v_sign/v2 must be 16-byte aligned");
       } else {
         LBX_CHECK_ARG(b == 1 && pr.br[0].v_sign && br.rank == pr.br[0].rank,
                       "a shared-V branch must be the residual with the main branch's rank");
@@ -468,13 +686,6 @@ static int validate(const lbx_proj *projs, int n_proj) {
     }
   }
   return LBX_OK;
-}
-
-static size_t vstage_smem(int Wv, int ncols, int k) {
-  const int pitch = row_pitch(Wv);
-  size_t b = (size_t)16 * pitch * 4 + (size_t)VWARPS * CH_WORDS * act_ws(ncols) * 4 +
-             (size_t)VWARPS * 16 * k * 4 + (size_t)VWARPS * LBX_MAX_TOKENS * 4 + 8 + 16;
-  return b;
 }
 
 static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, int k, void *ws,
@@ -485,24 +696,30 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
   const int ncb = (ncols + 7) / 8;
   const int esz_x = a->x_dtype == LBX_F32 ? 4 : 2;
   const int esz_y = a->y_dtype == LBX_F32 ? 4 : 2;
+  const int Wv = K / 32;
+  const bool rms = a->prologue == LBX_PRO_RMSNORM;
 
-  // z scratch layout
+  // scratch: bookkeeping, then z of every (projection, branch), [k][rank]
+  int *zmax_all = reinterpret_cast<int *>(ws);
+  unsigned *ticket = reinterpret_cast<unsigned *>(zmax_all + 2 * LBX_MAX_PROJ * LBX_MAX_TOKENS);
   float *zp[LBX_MAX_PROJ][2] = {};
+  int *zm[LBX_MAX_PROJ][2] = {};
   {
-    uint8_t *w = reinterpret_cast<uint8_t *>(ws);
+    uint8_t *w = reinterpret_cast<uint8_t *>(ws) + WS_HDR;
     for (int i = 0; i < n_proj; ++i)
       for (int b = 0; b < projs[i].n_branches; ++b) {
         zp[i][b] = reinterpret_cast<float *>(w);
-        w += (((size_t)projs[i].br[b].rank * k * 4) + 255) & ~(size_t)255;
+        zm[i][b] = zmax_all + (2 * i + b) * LBX_MAX_TOKENS;
+        w += al256((size_t)k * projs[i].br[b].rank * 4);
       }
   }
 
   // ---------------- V-stage
   VParams vp = {};
   vp.K = K;
-  vp.Wv = K / 32;
-  vp.pitch = row_pitch(vp.Wv);
-  vp.nch = (vp.Wv + CH_WORDS - 1) / CH_WORDS;
+  vp.Wv = Wv;
+  vp.vpitch = row_pitch(Wv);
+  vp.vcap = std::min(K, VCAP_MAX);
   vp.k = k;
   vp.ncols = ncols;
   vp.xdt = a->x_dtype;
@@ -511,7 +728,7 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
   vp.x = reinterpret_cast<const uint8_t *>(a->x) + (size_t)tok0 * K * esz_x;
   vp.x2 = a->x2 ? reinterpret_cast<const uint8_t *>(a->x2) + (size_t)tok0 * K * esz_x : nullptr;
   vp.norm_w = a->norm_w;
-  int tiles = 0;
+  int vtiles = 0;
   for (int i = 0; i < n_proj; ++i) {
     const lbx_proj &pr = projs[i];
     for (int b = 0; b < pr.n_branches; ++b) {
@@ -521,17 +738,19 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
       sg.v2 = pr.br[b].v2;
       sg.mid0 = pr.br[b].mid;
       sg.z0 = zp[i][b];
+      sg.zmax0 = zm[i][b];
       sg.rank = pr.br[b].rank;
       if (b == 0 && pr.n_branches == 2 && !pr.br[1].v_sign) {
         sg.mid1 = pr.br[1].mid;
         sg.z1 = zp[i][1];
+        sg.zmax1 = zm[i][1];
       }
-      sg.tile0 = tiles;
-      tiles += (sg.rank + 15) / 16;
+      sg.tile0 = vtiles;
+      vtiles += (sg.rank + 15) / 16;
     }
   }
-  const size_t vsmem = vstage_smem(vp.Wv, ncols, k);
-  LBX_CHECK_SUP(vsmem <= 227 * 1024, "V-stage needs %zu bytes of shared memory", vsmem);
+  const size_t vsmem = (size_t)16 * vp.vpitch * 4 + (size_t)vp.vcap * 4 * (rms ? 2 : 1) +
+                       (size_t)PASS_WORDS * act_ws(ncols) * 4 + (size_t)VWARPS * 16 * k * 4;
 
   // ---------------- U-stage
   UParams up = {};
@@ -539,7 +758,7 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
   up.ncols = ncols;
   up.ydt = a->y_dtype;
   up.epi = a->epilogue;
-  int maxw[2] = {0, 0}, maxtile = 0;
+  int maxw[2] = {0, 0}, maxtile = 0, tiles = 0;
   for (int i = 0; i < n_proj; ++i) {
     const lbx_proj &pr = projs[i];
     USeg &sg = up.seg[i];
@@ -554,6 +773,7 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
       sg.u_sign[b] = pr.br[b].u_sign;
       sg.u1[b] = pr.br[b].u1;
       sg.z[b] = zp[i][b];
+      sg.zmax[b] = zm[i][b];
       sg.rank[b] = pr.br[b].rank;
       sg.words[b] = (pr.br[b].rank + 31) / 32;
       sg.perrow[b] = (sg.words[b] % 4) == 0;
@@ -562,37 +782,60 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
       tw += 16 * sg.pitch[b] + 4;
     }
     maxtile = std::max(maxtile, tw);
+    tiles += pr.out_features / 16;
   }
   up.act_words[0] = maxw[0];
   up.act_words[1] = maxw[1];
   up.wtile_words = (maxtile + 3) & ~3;
-  int uw = UWARPS_MAX;
-  size_t usmem = 0;
-  for (; uw >= 1; uw >>= 1) {
-    usmem = (size_t)(maxw[0] + maxw[1]) * act_ws(ncols) * 4 + (size_t)uw * up.wtile_words * 4 +
-            (size_t)uw * 8 + 16;
-    if (usmem <= 227 * 1024) break;
+  up.zmax_all = zmax_all;
+  up.nzmax = 2 * LBX_MAX_PROJ * LBX_MAX_TOKENS;
+  up.ticket = ticket;
+
+  cudaError_t e;
+  // once per process, before any graph capture
+  static size_t vmax = 0, umax = 0;
+  if (!vmax) {
+    size_t m = 0;
+    size_t v_ = (size_t)-1, u_ = (size_t)-1;
+    for (auto kk : {vstage_kernel<1>, vstage_kernel<2>, vstage_kernel<4>}) {
+      e = allow_max_smem(kk, &m);
+      if (e != cudaSuccess) return cuda_status(e, "vstage smem attribute");
+      v_ = std::min(v_, m);
+    }
+    for (auto kk : {ustage_kernel<1>, ustage_kernel<2>, ustage_kernel<4>}) {
+      e = allow_max_smem(kk, &m);
+      if (e != cudaSuccess) return cuda_status(e, "ustage smem attribute");
+      u_ = std::min(u_, m);
+    }
+    umax = u_;
+    vmax = v_;
   }
-  LBX_CHECK_SUP(uw >= 1, "U-stage needs too much shared memory (rank too large for k=%d)", k);
-  up.uwarps = uw;
+  LBX_CHECK_SUP(vsmem <= vmax, "V-stage needs %zu bytes of shared memory (max %zu)", vsmem, vmax);
+  // row tiles per CTA: enough CTAs to cover the SMs, within shared memory; the
+  // remaining warps of a CTA split the ranks of its tiles
+  int ut = UT_MAX;
+  while (ut > 1 && tiles / ut < 120) ut >>= 1;
+  size_t usmem = 0;
+  for (; ut >= 1; ut >>= 1) {
+    usmem = (size_t)(maxw[0] + maxw[1]) * act_ws(ncols) * 4 + (size_t)UWARPS * 32 * 8 * ncb * 4 +
+            (size_t)ut * up.wtile_words * 4 + (size_t)ut * 48 * 4;
+    if (usmem <= umax) break;
+  }
+  LBX_CHECK_SUP(ut >= 1, "U-stage needs too much shared memory (rank too large for k=%d)", k);
+  up.ut = ut;
   int ctas = 0;
   for (int i = 0; i < n_proj; ++i) {
     up.seg[i].cta0 = ctas;
-    ctas += (projs[i].out_features + 16 * uw - 1) / (16 * uw);
+    ctas += (projs[i].out_features + 16 * ut - 1) / (16 * ut);
   }
   up.nseg = n_proj;
 
   const bool pdl = a->use_pdl != 0;
-  cudaError_t e;
   auto vk = ncb == 1 ? vstage_kernel<1> : ncb == 2 ? vstage_kernel<2> : vstage_kernel<4>;
   auto uk = ncb == 1 ? ustage_kernel<1> : ncb == 2 ? ustage_kernel<2> : ustage_kernel<4>;
-  e = cudaFuncSetAttribute(vk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vsmem);
-  if (e != cudaSuccess) return cuda_status(e, "vstage smem attribute");
-  e = cudaFuncSetAttribute(uk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)usmem);
-  if (e != cudaSuccess) return cuda_status(e, "ustage smem attribute");
-  e = launch(vk, dim3(tiles), dim3(VWARPS * 32), vsmem, stream, pdl, vp);
+  e = launch(vk, dim3(vtiles), dim3(VTHREADS), vsmem, stream, pdl, vp);
   if (e != cudaSuccess) return cuda_status(e, "vstage launch");
-  e = launch(uk, dim3(ctas), dim3(uw * 32), usmem, stream, pdl, up);
+  e = launch(uk, dim3(ctas), dim3(UTHREADS), usmem, stream, pdl, up);
   if (e != cudaSuccess) return cuda_status(e, "ustage launch");
   return LBX_OK;
 }
@@ -603,7 +846,7 @@ extern "C" size_t lbx_linear_workspace_size(const lbx_proj *projs, int32_t n_pro
                                             int32_t n_tokens) {
   if (!projs || n_proj < 1 || n_proj > LBX_MAX_PROJ || n_tokens < 1) return 0;
   const int k = n_tokens < LBX_MAX_TOKENS ? n_tokens : LBX_MAX_TOKENS;
-  return lbx::z_bytes(projs, n_proj, k);
+  return lbx::ws_bytes_for(projs, n_proj, k);
 }
 
 extern "C" int lbx_linear_verify(const lbx_proj *projs, const lbx_linear_args *a, void *ws,
@@ -616,8 +859,10 @@ extern "C" int lbx_linear_verify(const lbx_proj *projs, const lbx_linear_args *a
   LBX_CHECK_ARG(a->x, "x is NULL");
   LBX_CHECK_ARG(a->x_dtype == LBX_F32 || a->x_dtype == LBX_BF16, "bad x_dtype");
   LBX_CHECK_ARG(a->y_dtype == LBX_F32 || a->y_dtype == LBX_BF16, "bad y_dtype");
+  LBX_CHECK_ARG(aligned16(a->x) && (!a->x2 || aligned16(a->x2)), "x/x2 must be 16-byte aligned");
   LBX_CHECK_ARG(a->prologue >= LBX_PRO_NONE && a->prologue <= LBX_PRO_SILU_MUL, "bad prologue");
-  LBX_CHECK_ARG(a->prologue != LBX_PRO_RMSNORM || a->norm_w, "RMSNorm prologue needs norm_w");
+  LBX_CHECK_ARG(a->prologue != LBX_PRO_RMSNORM || (a->norm_w && aligned16(a->norm_w)),
+                "RMSNorm prologue needs a 16-byte aligned norm_w");
   LBX_CHECK_ARG(a->prologue != LBX_PRO_SILU_MUL || a->x2, "SiLU-mul prologue needs x2");
   LBX_CHECK_ARG(a->epilogue == LBX_EPI_STORE || (a->epilogue == LBX_EPI_ADD && a->y_dtype == LBX_F32),
                 "bad epilogue (ADD needs fp32 y)");

@@ -173,7 +173,7 @@ extern "C" int lbx_lmhead_argmax(const float *x, const float *norm_w, float eps,
   static bool attr_done = false;
   if (!attr_done) {
     for (auto k : {lmhead_kernel<1>, lmhead_kernel<2>, lmhead_kernel<4>, lmhead_kernel<8>}) {
-      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      cudaError_t e = allow_max_smem(k);
       if (e != cudaSuccess) return cuda_status(e, "lmhead smem attribute");
     }
     attr_done = true;

@@ -50,15 +50,18 @@ def _dt(t: torch.Tensor) -> int:
 
 
 class Workspace:
-    """A growable device scratch buffer (one per device and purpose)."""
+    """A growable device scratch buffer (one per device and purpose).
+
+    Zero-filled when (re)allocated: the kernels keep small bookkeeping words in
+    the workspace that must start at zero and are left at zero by every call."""
 
     def __init__(self, device: torch.device):
         self.device = device
-        self.buf = torch.empty(0, dtype=torch.uint8, device=device)
+        self.buf = torch.zeros(0, dtype=torch.uint8, device=device)
 
     def get(self, nbytes: int) -> torch.Tensor:
         if self.buf.numel() < nbytes:
-            self.buf = torch.empty(max(nbytes, 2 * self.buf.numel()), dtype=torch.uint8,
+            self.buf = torch.zeros(max(nbytes, 2 * self.buf.numel()), dtype=torch.uint8,
                                    device=self.device)
         return self.buf
 

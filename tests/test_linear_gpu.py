@@ -165,3 +165,29 @@ def test_unsupported_shapes_raise(ops):
     lay = syn.to_packed_linear(96, 64, brs, DEV)
     with pytest.raises(RuntimeError, match="unsupported"):
         ops.lb_linear(lay, torch.randn(1, 96, device=DEV))
+
+
+def test_pdl_chain_matches_unchained(ops):
+    # a chain of layers launched back to back with programmatic dependent launch
+    # must equal the same layers run one at a time
+    layers = [_layer(ops, 1024, 1024, [96, 256], seed=40 + i)[2] for i in range(6)]
+    x0 = torch.randn(3, 1024, generator=_gen(41)).bfloat16().to(DEV)
+    acts = [x0] + [torch.empty(3, 1024, dtype=torch.bfloat16, device=DEV) for _ in layers]
+    for i, l in enumerate(layers):
+        ops.linear_group([l], acts[i], [acts[i + 1]], use_pdl=True)
+    y = x0
+    for i, l in enumerate(layers):
+        y2 = torch.empty_like(y)
+        ops.linear_group([l], y, [y2], use_pdl=False)
+        torch.cuda.synchronize()
+        assert torch.equal(y2, acts[i + 1]), i
+        y = y2
+
+
+def test_c2_k16(ops):
+    brs, _, lay = _layer(ops, 4096, 4096, [208, 1840], seed=77)
+    x = torch.randn(16, 4096, generator=_gen(78)).bfloat16()
+    y = ops.lb_linear(lay, x.to(DEV)).cpu()
+    assert_linear_close(y.numpy(), _ref(x.float(), brs, 4096, 4096))
+    y1 = ops.lb_linear(lay, x[5:6].to(DEV)).cpu()
+    assert torch.equal(y1[0], y[5])
