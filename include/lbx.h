@@ -113,6 +113,24 @@ int lbx_linear(const lbx_proj *projs /* host */, const lbx_linear_args *a /* hos
 int lbx_linear_verify(const lbx_proj *projs, const lbx_linear_args *a, void *ws,
                       size_t ws_bytes, cudaStream_t stream);
 
+/* lbx_linear_verify for callers that cannot allocate device memory.  No
+ * counterpart in the reference (its CPU op allocated its own scratch): this
+ * entry point is for code that must not call cudaMalloc or hand the library a
+ * buffer — e.g. work recorded while a CUDA graph is captured in a mode that
+ * forbids allocation, or a host application that owns every device
+ * allocation.  The scratch is a fixed module-level device array of
+ * lbx_linear_noalloc_max_bytes() bytes (1 MiB) that every GPU loading the
+ * library holds until exit; calls needing more scratch than that are rejected
+ * with LBX_EUNSUPPORTED.  No cudaMalloc, cudaFree or allocating library
+ * routine is called.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress), so make that first call before any stream
+ * capture.  All calls share the array and it keeps the previous call's
+ * contents: each call clears the words that must start at zero, and calls
+ * whose work overlaps on the GPU (different streams, or different host
+ * threads on one device) race on it — order them on one stream. */
+int lbx_linear_noalloc(const lbx_proj *projs, const lbx_linear_args *a, cudaStream_t stream);
+size_t lbx_linear_noalloc_max_bytes(void);
+
 /* ---- bit packing (quantization/utils/binary_packer.py) ------------------ */
 /* binary_packer (binary_packer.py:4-50): int8 ±1 [rows, cols] -> int32 words.
  * Entries other than -1/+1 set *bad_count (device int, may be NULL). */

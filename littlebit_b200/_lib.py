@@ -77,6 +77,8 @@ _SIGNATURES = {
     "lbx_linear_workspace_size": (c_size_t, [POINTER(Proj), c_int32, c_int32]),
     "lbx_linear": (c_int, [POINTER(Proj), POINTER(LinearArgs), c_void_p, c_size_t, c_void_p]),
     "lbx_linear_verify": (c_int, [POINTER(Proj), POINTER(LinearArgs), c_void_p, c_size_t, c_void_p]),
+    "lbx_linear_noalloc": (c_int, [POINTER(Proj), POINTER(LinearArgs), c_void_p]),
+    "lbx_linear_noalloc_max_bytes": (c_size_t, []),
     "lbx_pack_signs": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "lbx_unpack_signs": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
     "lbx_pack_signs_from_float": (c_int, [c_void_p, c_int32, c_int64, c_int64, c_void_p, c_void_p]),

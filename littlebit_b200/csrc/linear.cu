@@ -881,3 +881,62 @@ extern "C" int lbx_linear(const lbx_proj *projs, const lbx_linear_args *a, void 
                           size_t ws_bytes, cudaStream_t stream) {
   return lbx_linear_verify(projs, a, ws, ws_bytes, stream);
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant: the scratch lives in a fixed device array
+// ---------------------------------------------------------------------------
+// Some callers cannot hand the library device memory: code that runs while a
+// CUDA graph is being captured in a mode that forbids allocation, a host
+// application that owns every device allocation through its own pool, or a
+// plugin without access to any allocator.  lbx_linear_noalloc runs the same two
+// kernels as lbx_linear_verify with its scratch in this module-level array.
+// Device code could name the array directly; host code cannot (there the name
+// is only a host-side stand-in), so its device address is fetched once per
+// device with cudaGetSymbolAddress.
+
+#include <mutex>
+
+namespace lbx {
+constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(1) << 20;  // 1 MiB, held by every GPU that loads the library
+static __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+constexpr int NOALLOC_MAX_DEVICES = 64;
+static void *g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
+static std::mutex g_noalloc_mu;
+}  // namespace lbx
+
+extern "C" size_t lbx_linear_noalloc_max_bytes(void) { return lbx::NOALLOC_SCRATCH_BYTES; }
+
+extern "C" int lbx_linear_noalloc(const lbx_proj *projs, const lbx_linear_args *a,
+                                  cudaStream_t stream) {
+  using namespace lbx;
+  LBX_CHECK_ARG(a, "args is NULL");
+  int rc = validate(projs, a->n_proj);
+  if (rc) return rc;
+  LBX_CHECK_ARG(a->n_tokens >= 1, "n_tokens must be >= 1");
+  const size_t need = lbx_linear_workspace_size(projs, a->n_proj, a->n_tokens);
+  LBX_CHECK_SUP(need <= NOALLOC_SCRATCH_BYTES,
+                "lbx_linear_noalloc: this call needs %zu bytes of scratch but the fixed buffer holds "
+                "%zu; use lbx_linear with a caller-provided workspace",
+                need, NOALLOC_SCRATCH_BYTES);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "lbx_linear_noalloc: cudaGetDevice");
+  LBX_CHECK_SUP(dev >= 0 && dev < NOALLOC_MAX_DEVICES, "lbx_linear_noalloc: device %d out of range",
+                dev);
+  void *scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {  // first call on this device: resolve the array's device address
+      void *p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (e != cudaSuccess) return cuda_status(e, "lbx_linear_noalloc: cudaGetSymbolAddress");
+      g_noalloc_ptr[dev] = p;
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  // the bookkeeping words must start at zero; clear them rather than trusting
+  // whatever an earlier (possibly failed) call left behind
+  e = cudaMemsetAsync(scratch, 0, WS_HDR, stream);
+  if (e != cudaSuccess) return cuda_status(e, "lbx_linear_noalloc: clear scratch");
+  return lbx_linear_verify(projs, a, scratch, NOALLOC_SCRATCH_BYTES, stream);
+}
