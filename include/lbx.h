@@ -172,9 +172,11 @@ int lbx_rope(float *x, const int32_t *pos, int32_t n, int32_t heads, int32_t hea
 typedef struct lbx_attn_args {
   int32_t n;
   int32_t heads, kv_heads, head_dim, max_seq;
-  int32_t prefix_len;
+  int32_t prefix_len;         /* cached slots; with prefix_dev: an upper bound */
   float scale, theta;
   int32_t use_pdl;
+  const int32_t *prefix_dev;  /* device copy of the cached-slot count, or NULL:
+                                 lets one CUDA graph replay at any position */
   const float *q; int64_t q_ld;
   const float *k_new; const float *v_new; int64_t kv_ld;
   const int32_t *pos;        /* [n] rotary positions */
@@ -232,13 +234,25 @@ typedef struct lbx_model {
 /* Workspace of lbx_forward: zero-filled once at allocation, like lbx_linear's. */
 size_t lbx_forward_workspace_size(const lbx_model *m /* host */, int32_t n_tokens);
 /* n tokens at cache slots start..start+n-1 (rotary positions pos[] or, when
- * pos == NULL, the slots).  tree_mask as in lbx_attn_args (NULL = causal).
- * hidden_out [n, hidden] receives the final-RMSNorm output (may be NULL);
- * logits [n, vocab] / argmax [n] as in lbx_lmhead_argmax (may be NULL). */
+ * pos == NULL, the slots).  With start_dev != NULL the slot offset is read
+ * from device memory and `start` is only an upper bound (for CUDA graphs that
+ * replay at varying positions; pos must then be given).  tree_mask as in
+ * lbx_attn_args (NULL = causal).  hidden_out [n, hidden] receives the
+ * final-RMSNorm output (may be NULL); logits [n, vocab] / argmax [n] as in
+ * lbx_lmhead_argmax (may be NULL). */
 int lbx_forward(const lbx_model *m, const int64_t *tokens, int32_t n, int32_t start,
-                const int32_t *pos, const uint64_t *tree_mask, float *hidden_out,
-                float *logits, int64_t *argmax_out, void *ws, size_t ws_bytes,
-                cudaStream_t stream);
+                const int32_t *start_dev, const int32_t *pos, const uint64_t *tree_mask,
+                float *hidden_out, float *logits, int64_t *argmax_out, void *ws,
+                size_t ws_bytes, cudaStream_t stream);
+
+/* Move KV rows inside the caches of every layer: for i < n, slot dst[i] <- slot
+ * src[i] (all sources are read before any destination is written), used to
+ * compact an accepted tree path into consecutive slots after tree
+ * verification.  k_caches / v_caches: DEVICE arrays of n_layers cache pointers
+ * ([kv_heads, max_seq, head_dim] bf16 each); n <= 64. */
+int lbx_kv_move(uint16_t *const *k_caches, uint16_t *const *v_caches, int32_t n_layers,
+                int32_t kv_heads, int32_t max_seq, int32_t head_dim, const int32_t *src,
+                const int32_t *dst, int32_t n, cudaStream_t stream);
 
 /* ---- diagnostics --------------------------------------------------------- */
 /* Copies the last host-side error text of the calling thread. */

@@ -46,7 +46,7 @@ class AttnArgs(ctypes.Structure):
     _fields_ = [
         ("n", c_int32), ("heads", c_int32), ("kv_heads", c_int32), ("head_dim", c_int32),
         ("max_seq", c_int32), ("prefix_len", c_int32), ("scale", c_float), ("theta", c_float),
-        ("use_pdl", c_int32),
+        ("use_pdl", c_int32), ("prefix_dev", c_void_p),
         ("q", c_void_p), ("q_ld", c_int64),
         ("k_new", c_void_p), ("v_new", c_void_p), ("kv_ld", c_int64),
         ("pos", c_void_p), ("tree_mask", c_void_p),
@@ -97,7 +97,9 @@ _SIGNATURES = {
                                        c_void_p, c_void_p]),
     "lbx_forward_workspace_size": (c_size_t, [POINTER(Model), c_int32]),
     "lbx_forward": (c_int, [POINTER(Model), c_void_p, c_int32, c_int32, c_void_p, c_void_p,
-                            c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+                            c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "lbx_kv_move": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p,
+                            c_void_p, c_int32, c_void_p]),
     "lbx_last_error": (c_int, [c_char_p, c_size_t]),
     "lbx_device_error": (c_int, [POINTER(c_int32), c_void_p]),
     "lbx_clear_device_error": (c_int, [c_void_p]),

@@ -26,6 +26,7 @@ constexpr int AMAX_ROWS = 64; // query rows (tokens x GQA group) per launch
 
 struct AttnParams {
   int n, heads, kvh, d, max_seq, prefix, rep, R, nchunk;
+  const int32_t *prefix_dev;  // actual cached-slot count (prefix is then a bound)
   float scale, theta;
   const float *q; int64_t q_ld;
   const float *k_new; const float *v_new; int64_t kv_ld;
@@ -45,9 +46,9 @@ LBX_DEV void rope_cs_a(int pos, int i, int d, float theta, float &c, float &s) {
   s = (float)sd;
 }
 
-LBX_DEV bool visible(const AttnParams &p, int i, int slot) {
-  if (slot < p.prefix) return true;
-  const int j = slot - p.prefix;
+LBX_DEV bool visible(const AttnParams &p, int prefix, int i, int slot) {
+  if (slot < prefix) return true;
+  const int j = slot - prefix;
   if (j >= p.n) return false;
   if (p.tree) return (p.tree[i] >> j) & 1ull;
   return j <= i;
@@ -65,6 +66,13 @@ __global__ void __launch_bounds__(ATHREADS) attn_chunk_kernel(const __grid_const
 
   pdl_trigger();
   pdl_wait();
+  const int prefix = p.prefix_dev ? __ldcg(p.prefix_dev) : p.prefix;
+  const int total = prefix + p.n;
+  const int64_t pbase = ((int64_t)h * p.nchunk + c) * p.R;
+  if (c * ACH >= total) {  // chunk past the live sequence: an empty partial
+    for (int r = tid; r < p.R; r += ATHREADS) p.part_ml[pbase + r] = make_float2(-INFINITY, 0.f);
+    return;
+  }
 
   // queries of this kv head's group, rotated
   for (int e = tid; e < p.R * half; e += ATHREADS) {
@@ -78,19 +86,18 @@ __global__ void __launch_bounds__(ATHREADS) attn_chunk_kernel(const __grid_const
     Qs[r * d + j + half] = x2 * cs + x1 * sn;
   }
   // keys / values of this chunk
-  const int total = p.prefix + p.n;
   const int64_t cache_base = (int64_t)h * p.max_seq * d;
   for (int e = tid; e < ACH * half; e += ATHREADS) {
     const int jj = e / half, j = e - jj * half;
     const int slot = c * ACH + jj;
     float k1 = 0.f, k2 = 0.f, v1 = 0.f, v2 = 0.f;
-    if (slot < p.prefix) {
+    if (slot < prefix) {
       const uint16_t *kr = p.kc + cache_base + (int64_t)slot * d;
       const uint16_t *vr = p.vc + cache_base + (int64_t)slot * d;
       k1 = bf16_to_f32(kr[j]); k2 = bf16_to_f32(kr[j + half]);
       v1 = bf16_to_f32(vr[j]); v2 = bf16_to_f32(vr[j + half]);
     } else if (slot < total) {
-      const int i = slot - p.prefix;
+      const int i = slot - prefix;
       const float *kr = p.k_new + (int64_t)i * p.kv_ld + (int64_t)h * d;
       const float *vr = p.v_new + (int64_t)i * p.kv_ld + (int64_t)h * d;
       float cs, sn;
@@ -114,7 +121,7 @@ __global__ void __launch_bounds__(ATHREADS) attn_chunk_kernel(const __grid_const
     const int i = r / p.rep;
     const int slot = c * ACH + jj;
     float sc = -INFINITY;
-    if (visible(p, i, slot)) {
+    if (visible(p, prefix, i, slot)) {
       const float *qr = Qs + r * d;
       const float *kr = Ks + jj * (d + 1);
       float a = 0.f;
@@ -127,7 +134,6 @@ __global__ void __launch_bounds__(ATHREADS) attn_chunk_kernel(const __grid_const
 
   // chunk-local softmax numerators
   const int warp = tid >> 5, lane = tid & 31;
-  const int64_t pbase = ((int64_t)h * p.nchunk + c) * p.R;
   for (int r = warp; r < p.R; r += ATHREADS / 32) {
     const float s0 = P[r * ACH + lane], s1 = P[r * ACH + lane + 32];
     const float m = warp_max(fmaxf(s0, s1));
@@ -160,17 +166,17 @@ __global__ void attn_combine_kernel(const __grid_constant__ AttnParams p) {
   pdl_trigger();
   pdl_wait();
   float M = -INFINITY;
-  for (int c = 0; c < p.nchunk; ++c) M = fmaxf(M, p.part_ml[((int64_t)h * p.nchunk + c) * p.R + r].x);
+  for (int c = 0; c < p.nchunk; ++c) M = fmaxf(M, __ldcg(p.part_ml + ((int64_t)h * p.nchunk + c) * p.R + r).x);
   const int i = r / p.rep, qh = h * p.rep + (r - i * p.rep);
   for (int t = threadIdx.x; t < d; t += blockDim.x) {
     float L = 0.f, O = 0.f;
     for (int c = 0; c < p.nchunk; ++c) {
       const int64_t b = ((int64_t)h * p.nchunk + c) * p.R + r;
-      const float2 ml = p.part_ml[b];
+      const float2 ml = __ldcg(p.part_ml + b);
       if (ml.x == -INFINITY) continue;
       const float w = expf(ml.x - M);
       L = fmaf(w, ml.y, L);
-      O = fmaf(w, p.part_o[b * d + t], O);
+      O = fmaf(w, __ldcg(p.part_o + b * d + t), O);
     }
     p.out[(int64_t)i * p.heads * d + (int64_t)qh * d + t] = L > 0.f ? O / L : 0.f;
   }
@@ -198,6 +204,7 @@ static void attn_fill(const lbx_attn_args *a, AttnParams &p) {
   p.kc = a->k_cache;
   p.vc = a->v_cache;
   p.out = a->out;
+  p.prefix_dev = a->prefix_dev;
 }
 
 }  // namespace lbx

@@ -31,14 +31,8 @@ static FwdLayout fwd_layout(const lbx_model *m, int n) {
                KV = (size_t)m->kv_heads * m->head_dim;
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off += al(bytes); return o; };
-  L.x = take((size_t)n * H * 4);
-  L.q = take((size_t)n * Q * 4);
-  L.kk = take((size_t)n * KV * 4);
-  L.vv = take((size_t)n * KV * 4);
-  L.att = take((size_t)n * Q * 4);
-  L.gate = take((size_t)n * I * 4);
-  L.up = take((size_t)n * I * 4);
-  L.pos = take((size_t)n * 4);
+  // the linear scratch comes first: its bookkeeping words (kept at zero between
+  // calls) must sit at the same offset whatever n a call uses
   size_t lin = 0;
   for (int l = 0; l < m->n_layers; ++l) {
     const lbx_proj *pr = m->layers[l].proj;
@@ -49,6 +43,14 @@ static FwdLayout fwd_layout(const lbx_model *m, int n) {
   }
   L.lin_bytes = lin;
   L.lin = take(lin);
+  L.x = take((size_t)n * H * 4);
+  L.q = take((size_t)n * Q * 4);
+  L.kk = take((size_t)n * KV * 4);
+  L.vv = take((size_t)n * KV * 4);
+  L.att = take((size_t)n * Q * 4);
+  L.gate = take((size_t)n * I * 4);
+  L.up = take((size_t)n * I * 4);
+  L.pos = take((size_t)n * 4);
   lbx_attn_args aa = {};
   aa.n = n;
   aa.heads = m->heads;
@@ -63,9 +65,28 @@ static FwdLayout fwd_layout(const lbx_model *m, int n) {
   return L;
 }
 
-__global__ void iota_kernel(int32_t *pos, int start, int n) {
+__global__ void iota_kernel(int32_t *pos, int start, const int32_t *start_dev, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) pos[i] = start + i;
+  if (i < n) pos[i] = (start_dev ? *start_dev : start) + i;
+}
+
+// every (layer, kv head, k|v) row block: stage all source rows, then write
+__global__ void kv_move_kernel(uint16_t *const *kc, uint16_t *const *vc, int kvh, int max_seq, int d,
+                               const int32_t *src, const int32_t *dst, int n) {
+  extern __shared__ uint16_t rows[];  // n x d
+  const int layer = blockIdx.x / (2 * kvh);
+  const int rem = blockIdx.x - layer * 2 * kvh;
+  const int h = rem >> 1;
+  uint16_t *base = ((rem & 1) ? vc[layer] : kc[layer]) + (int64_t)h * max_seq * d;
+  for (int e = threadIdx.x; e < n * d; e += blockDim.x) {
+    const int i = e / d, t = e - i * d;
+    rows[e] = base[(int64_t)src[i] * d + t];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < n * d; e += blockDim.x) {
+    const int i = e / d, t = e - i * d;
+    base[(int64_t)dst[i] * d + t] = rows[e];
+  }
 }
 
 }  // namespace lbx
@@ -75,10 +96,25 @@ extern "C" size_t lbx_forward_workspace_size(const lbx_model *m, int32_t n_token
   return lbx::fwd_layout(m, n_tokens).total;
 }
 
+extern "C" int lbx_kv_move(uint16_t *const *k_caches, uint16_t *const *v_caches, int32_t n_layers,
+                           int32_t kv_heads, int32_t max_seq, int32_t head_dim, const int32_t *src,
+                           const int32_t *dst, int32_t n, cudaStream_t stream) {
+  using namespace lbx;
+  LBX_CHECK_ARG(n >= 0 && n <= 64, "n must be in [0,64]");
+  if (n == 0) return LBX_OK;
+  LBX_CHECK_ARG(k_caches && v_caches && src && dst, "NULL pointer");
+  LBX_CHECK_ARG(n_layers > 0 && kv_heads > 0 && head_dim > 0 && max_seq > 0, "bad shape");
+  const size_t smem = (size_t)n * head_dim * 2;
+  LBX_CHECK_SUP(smem <= 48 * 1024, "too many rows to move at once");
+  kv_move_kernel<<<n_layers * 2 * kv_heads, 256, smem, stream>>>(k_caches, v_caches, kv_heads, max_seq,
+                                                                  head_dim, src, dst, n);
+  return cuda_status(cudaGetLastError(), "kv_move launch");
+}
+
 extern "C" int lbx_forward(const lbx_model *m, const int64_t *tokens, int32_t n, int32_t start,
-                           const int32_t *pos, const uint64_t *tree_mask, float *hidden_out,
-                           float *logits, int64_t *argmax_out, void *ws, size_t ws_bytes,
-                           cudaStream_t stream) {
+                           const int32_t *start_dev, const int32_t *pos, const uint64_t *tree_mask,
+                           float *hidden_out, float *logits, int64_t *argmax_out, void *ws,
+                           size_t ws_bytes, cudaStream_t stream) {
   using namespace lbx;
   LBX_CHECK_ARG(m && m->layers, "model is NULL");
   LBX_CHECK_ARG(n >= 1 && tokens, "need n >= 1 tokens");
@@ -105,7 +141,7 @@ extern "C" int lbx_forward(const lbx_model *m, const int64_t *tokens, int32_t n,
   int rc = lbx_embed(m->embed, tokens, n, m->hidden, m->vocab, x, stream);
   if (rc) return rc;
   if (!pos) {
-    iota_kernel<<<(n + 127) / 128, 128, 0, stream>>>(posb, start, n);
+    iota_kernel<<<(n + 127) / 128, 128, 0, stream>>>(posb, start, start_dev, n);
     rc = cuda_status(cudaGetLastError(), "iota launch");
     if (rc) return rc;
     pos = posb;
@@ -137,6 +173,7 @@ extern "C" int lbx_forward(const lbx_model *m, const int64_t *tokens, int32_t n,
     aa.head_dim = m->head_dim;
     aa.max_seq = m->max_seq;
     aa.prefix_len = start;
+    aa.prefix_dev = start_dev;
     aa.scale = m->attn_scale;
     aa.theta = m->rope_theta;
     aa.use_pdl = pdl;

@@ -693,7 +693,10 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
   const int n_proj = a->n_proj;
   const int K = projs[0].in_features;
   const int ncols = 2 * k;
-  const int ncb = (ncols + 7) / 8;
+  // MMA column blocks the launched kernel is instantiated for (1, 2 or 4); every
+  // size below must use this, not the bare ceil(ncols/8)
+  const int ncb_need = (ncols + 7) / 8;
+  const int ncb = ncb_need <= 1 ? 1 : ncb_need <= 2 ? 2 : 4;
   const int esz_x = a->x_dtype == LBX_F32 ? 4 : 2;
   const int esz_y = a->y_dtype == LBX_F32 ? 4 : 2;
   const int Wv = K / 32;

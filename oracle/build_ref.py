@@ -2,7 +2,7 @@
 timed CPU baseline only — never part of the product).
 
 Compiles patches/littlebit_cpu_optimized.cpp straight from the read-only
-reference checkout (LITTLESPEC_REF, default /root/reference) as a torch
+reference checkout (LITTLESPEC_REF, default REF below) as a torch
 extension.  -mavx2 -mfma instead of -march=native so the .so built here also
 runs on the GPU box's host CPU; libgomp is linked from gcc's own directory
 because the bare -lgomp of the reference's recipe does not resolve with this

@@ -1,7 +1,7 @@
 """Generate the golden vectors that pin the oracle to the reference.
 
 Runs ONLY where the reference checkout is available (read-only, imported from
-LITTLESPEC_REF, default /root/reference); the resulting .npz files are
+LITTLESPEC_REF, default REF below); the resulting .npz files are
 committed and the tests never import the reference.
 
     python tests/golden/make_golden.py

@@ -87,6 +87,8 @@ def _ref(x, brs, in_f, out_f, bias=None):
     ("down", 11008, 4096, [280], 3, torch.float32),
     ("gate", 4096, 11008, [280], 2, torch.float32),
     ("odd_rank", 256, 128, [40, 8], 4, torch.float32),
+    ("k9", 512, 256, [184, 96], 9, torch.float32),
+    ("k12", 1024, 512, [64, 40], 12, torch.bfloat16),
     ("k16", 512, 256, [184], 16, torch.float32),
     ("k20", 512, 256, [96], 20, torch.float32),
     ("tiny", 128, 16, [8], 1, torch.float32),
