@@ -237,6 +237,108 @@ def build_pool(P: int, device, seed: int):
     return pool
 
 
+# ---------------------------------------------------------------------------
+# decode: spec-decode tokens/s on the Llama-2-7B shape
+# ---------------------------------------------------------------------------
+def _ranks_at(shape, eff_bit):
+    from littlebit_b200.littlebit import LittleBitLinear
+
+    H, I = shape.hidden_size, shape.intermediate_size
+    qd = shape.num_attention_heads * shape.head_dim
+    kvd = shape.num_key_value_heads * shape.head_dim
+    dims = {"q_proj": (H, qd), "k_proj": (H, kvd), "v_proj": (H, kvd), "o_proj": (qd, H),
+            "gate_proj": (H, I), "up_proj": (H, I), "down_proj": (I, H)}
+    out = {}
+    for nm, (a, b) in dims.items():
+        f = LittleBitLinear._estimate_split_dim(a, b, eff_bit, False)
+        out[nm] = LittleBitLinear._finalize_split_dim(f, 1024, 8)
+    return out
+
+
+def run_decode(args, dev, rank, ws):
+    """Greedy decode on the Llama-2-7B shape: 0.1-bit draft
+    (ranks of littlebit.py:50-93 at eff_bit 0.1), target = draft + an independent
+    0.9-bit residual branch per projection (~1.0 BPW).  128-token uniform-random
+    prompt, 256 new tokens; target-only greedy, chain speculation (gamma 4) and
+    depth-4 binary-tree speculation, each checked token-identical to target-only.
+    Weights: |N(1,0.1)| scales times unit-gain constants (mid / sqrt(in),
+    u1 / sqrt(rank)); the residual's u1 is further scaled by res_scale so that the
+    draft agrees with the target often enough for speculation to matter."""
+    from littlebit_b200.cuda_models import CudaDraftModel, CudaTargetModel
+    from littlebit_b200.model import LLAMA2_7B, LittleBitDecoder, synthetic_runtime_state
+    from littlebit_b200.speculative_decoding import (autoregressive_generate, speculative_decode,
+                                                     speculative_decode_tree)
+    from littlebit_b200.tree_utils import binary_tree_choices, generate_tree_buffers
+
+    shape = LLAMA2_7B
+    r_d, r_r = _ranks_at(shape, 0.1), _ranks_at(shape, 0.9)
+    ranks = {k: [r_d[k], r_r[k]] for k in r_d}
+    st = synthetic_runtime_state(shape, ranks, seed=77 + rank, device=dev, unit_gain=True)
+    for k in list(st):
+        if k.endswith(".u1_r"):
+            st[k] = st[k] * args.res_scale
+    max_seq = args.prompt + args.new_tokens + 64
+    dec = LittleBitDecoder(shape, st, device=dev, max_seq=max_seq)
+    del st
+    tgt = CudaTargetModel.from_decoder(dec)
+    drf = CudaDraftModel.from_target(tgt)
+    draft_only = CudaTargetModel.from_decoder(drf.dec)
+    ids = torch.randint(0, shape.vocab_size, (1, args.prompt),
+                        generator=torch.Generator().manual_seed(1000 + rank)).to(dev)
+    tb = generate_tree_buffers(binary_tree_choices(4, 2), device=dev)
+    n = args.new_tokens
+
+    def timed(fn):
+        barrier(ws)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        out = fn()
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        return out, max_over_ranks(dt, ws)
+
+    # warm-up: one short pass of each loop (graph capture, smem attributes)
+    autoregressive_generate(draft_only, ids, None, max_new_tokens=8, eos_token_id=-1)
+    autoregressive_generate(tgt, ids, None, max_new_tokens=8, eos_token_id=-1)
+    speculative_decode(drf, tgt, ids, None, max_new_tokens=8, draft_length=4, eos_token_id=-1)
+    speculative_decode_tree(drf, tgt, ids, None, max_new_tokens=8, tree_buffers=tb, top_k=2, eos_token_id=-1)
+    (dr, _), t_draft = timed(lambda: autoregressive_generate(draft_only, ids, None, max_new_tokens=n,
+                                                              eos_token_id=-1))
+    (ar, _), t_ar = timed(lambda: autoregressive_generate(tgt, ids, None, max_new_tokens=n, eos_token_id=-1))
+    (sp, sst), t_sp = timed(lambda: speculative_decode(drf, tgt, ids, None, max_new_tokens=n, draft_length=4,
+                                                       eos_token_id=-1))
+    (tr, tst), t_tr = timed(lambda: speculative_decode_tree(drf, tgt, ids, None, max_new_tokens=n,
+                                                            tree_buffers=tb, top_k=2, eos_token_id=-1))
+    n_tr = tr.shape[1] - ids.shape[1]
+    if n_tr > n:  # the tree loop may overshoot max_new_tokens (speculative_decoding.py:560-566)
+        ar_long, _ = autoregressive_generate(tgt, ids, None, max_new_tokens=n_tr, eos_token_id=-1)
+    else:
+        ar_long = ar
+    chain_ok = sp.tolist() == ar.tolist()
+    tree_ok = tr.tolist() == ar_long[:, :tr.shape[1]].tolist()
+    if not (chain_ok and tree_ok):
+        raise RuntimeError(f"speculative output differs from target-only greedy (chain {chain_ok}, tree {tree_ok})")
+    packed = dec.packed_bytes()
+    return {
+        "workload": f"Llama-2-7B shape (32 layers, hidden 4096, MLP 11008, vocab 32000), "
+                    f"{args.prompt}-token random prompt, {n} greedy tokens, batch 1 per GPU",
+        "unit": "tokens/s", "aggregate_over_gpus": ws,
+        "draft_ranks_0p1bit": r_d, "residual_ranks_0p9bit": r_r, "residual_scale": args.res_scale,
+        "target_packed_mb": round(packed / 1e6, 1),
+        "draft_greedy": round(n * ws / t_draft, 2),
+        "target_greedy": round(n * ws / t_ar, 2),
+        "spec_chain_gamma4": {"tokens_per_s": round(n * ws / t_sp, 2),
+                              "acceptance_rate": round(sst["acceptance_rate"], 4),
+                              "mean_acceptance_length": round(sst["mean_acceptance_length"], 3),
+                              "num_steps": sst["num_steps"], "token_identical": chain_ok},
+        "spec_tree_d4b2": {"tokens_per_s": round(n_tr * ws / t_tr, 2),
+                           "acceptance_rate": round(tst["acceptance_rate"], 4),
+                           "mean_acceptance_length": round(tst["mean_acceptance_length"], 3),
+                           "num_steps": tst["num_steps"], "tokens": n_tr, "token_identical": tree_ok},
+        "timing": "wall clock around each whole generate call (host syncs included), max over ranks",
+    }
+
+
 def run_ours(args):
     from littlebit_b200 import ops
 
@@ -338,6 +440,8 @@ def run_ours(args):
             cpu = {"value": round(r["gbs"], 4), "unit": "GB/s", "cores": r["threads"],
                    "kind": "reference", "sample": r["sample"]}
 
+    decode = run_decode(args, dev, rank, ws) if args.decode else None
+
     if rank == 0:
         traffic = traffic_from_profiles(k)
         out = {
@@ -361,6 +465,7 @@ def run_ours(args):
                     "h2d_bytes_per_step": 2 * k * IN_F * P, "d2h_bytes_per_step": 2 * k * OUT_F * P,
                     "ms_per_step": round(t2 / args.steps, 4)},
             "cpu_baseline": cpu,
+            "decode": decode,
             "gpu_launches": 2 * P * args.steps,
             "clocks": clocks,
         }
@@ -383,6 +488,10 @@ def main():
     ap.add_argument("--pdl", type=int, default=1)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--decode", type=int, default=1, help="also run the 7B-shape decode section")
+    ap.add_argument("--prompt", type=int, default=128)
+    ap.add_argument("--new-tokens", type=int, default=256)
+    ap.add_argument("--res-scale", type=float, default=0.08)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -168,7 +168,12 @@ int lbx_rope(float *x, const int32_t *pos, int32_t n, int32_t heads, int32_t hea
  * prefix_len + j with bit j of tree_mask[i] set (its tree ancestors and
  * itself) or, when tree_mask == NULL, j <= i (causal).  GQA: query head h
  * reads kv head h / (heads / kv_heads) (cpp:1238).  Caches are
- * [kv_heads, max_seq, head_dim] bf16; head_dim even and <= 128; n <= 64. */
+ * [kv_heads, max_seq, head_dim] bf16; head_dim even and <= 128; n <= 64.
+ * A query's keys are the cached prefix, then its visible new tokens in index
+ * order (a tree's ancestors precede their descendants, as in
+ * generate_tree_buffers); the arithmetic follows that order, so a tree node's
+ * output is bit-identical to decoding its path as a causal sequence.
+ * theta <= 0 applies no rotation (the reference CPU runtime applies none). */
 typedef struct lbx_attn_args {
   int32_t n;
   int32_t heads, kv_heads, head_dim, max_seq;
@@ -239,7 +244,9 @@ size_t lbx_forward_workspace_size(const lbx_model *m /* host */, int32_t n_token
  * replay at varying positions; pos must then be given).  tree_mask as in
  * lbx_attn_args (NULL = causal).  hidden_out [n, hidden] receives the
  * final-RMSNorm output (may be NULL); logits [n, vocab] / argmax [n] as in
- * lbx_lmhead_argmax (may be NULL). */
+ * lbx_lmhead_argmax (may be NULL).  n <= 64 with tree_mask or start_dev; a
+ * longer causal run at a host-given start proceeds in steps of 64 tokens
+ * (the workspace is sized for min(n, 64)). */
 int lbx_forward(const lbx_model *m, const int64_t *tokens, int32_t n, int32_t start,
                 const int32_t *start_dev, const int32_t *pos, const uint64_t *tree_mask,
                 float *hidden_out, float *logits, int64_t *argmax_out, void *ws,

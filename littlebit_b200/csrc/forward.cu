@@ -18,6 +18,8 @@
 
 namespace lbx {
 
+constexpr int FWD_MAX_TOKENS = 64;  // tokens per step (attention and tree-mask width)
+
 struct FwdLayout {
   size_t x, q, kk, vv, att, gate, up, pos, lin, attn, lm, total;
   size_t lin_bytes, attn_bytes, lm_bytes;
@@ -93,7 +95,7 @@ __global__ void kv_move_kernel(uint16_t *const *kc, uint16_t *const *vc, int kvh
 
 extern "C" size_t lbx_forward_workspace_size(const lbx_model *m, int32_t n_tokens) {
   if (!m || !m->layers || n_tokens < 1) return 0;
-  return lbx::fwd_layout(m, n_tokens).total;
+  return lbx::fwd_layout(m, n_tokens < lbx::FWD_MAX_TOKENS ? n_tokens : lbx::FWD_MAX_TOKENS).total;
 }
 
 extern "C" int lbx_kv_move(uint16_t *const *k_caches, uint16_t *const *v_caches, int32_t n_layers,
@@ -111,17 +113,12 @@ extern "C" int lbx_kv_move(uint16_t *const *k_caches, uint16_t *const *v_caches,
   return cuda_status(cudaGetLastError(), "kv_move launch");
 }
 
-extern "C" int lbx_forward(const lbx_model *m, const int64_t *tokens, int32_t n, int32_t start,
-                           const int32_t *start_dev, const int32_t *pos, const uint64_t *tree_mask,
-                           float *hidden_out, float *logits, int64_t *argmax_out, void *ws,
-                           size_t ws_bytes, cudaStream_t stream) {
-  using namespace lbx;
-  LBX_CHECK_ARG(m && m->layers, "model is NULL");
-  LBX_CHECK_ARG(n >= 1 && tokens, "need n >= 1 tokens");
-  LBX_CHECK_ARG(start >= 0 && start + n <= m->max_seq, "start + n exceeds max_seq");
-  LBX_CHECK_ARG(m->heads % m->kv_heads == 0, "heads must be a multiple of kv_heads");
-  LBX_CHECK_ARG(m->embed && m->final_norm, "embed/final_norm required");
-  LBX_CHECK_ARG(!(logits || argmax_out) || m->lm_head, "lm_head required for logits/argmax");
+namespace lbx {
+// one step of n <= FWD_MAX_TOKENS tokens (checked by the caller)
+static int forward_chunk(const lbx_model *m, const int64_t *tokens, int32_t n, int32_t start,
+                         const int32_t *start_dev, const int32_t *pos, const uint64_t *tree_mask,
+                         float *hidden_out, float *logits, int64_t *argmax_out, void *ws,
+                         size_t ws_bytes, cudaStream_t stream) {
   const FwdLayout L = fwd_layout(m, n);
   LBX_CHECK_ARG(ws && ws_bytes >= L.total, "workspace too small (%zu < %zu)", ws_bytes, L.total);
   uint8_t *w = reinterpret_cast<uint8_t *>(ws);
@@ -224,6 +221,34 @@ extern "C" int lbx_forward(const lbx_model *m, const int64_t *tokens, int32_t n,
   if (logits || argmax_out) {
     rc = lbx_lmhead_argmax(x, m->final_norm, m->rms_eps, n, m->hidden, m->lm_head, m->vocab,
                            logits, argmax_out, lm_ws, L.lm_bytes, pdl, stream);
+    if (rc) return rc;
+  }
+  return LBX_OK;
+}
+}  // namespace lbx
+
+extern "C" int lbx_forward(const lbx_model *m, const int64_t *tokens, int32_t n, int32_t start,
+                           const int32_t *start_dev, const int32_t *pos, const uint64_t *tree_mask,
+                           float *hidden_out, float *logits, int64_t *argmax_out, void *ws,
+                           size_t ws_bytes, cudaStream_t stream) {
+  using namespace lbx;
+  LBX_CHECK_ARG(m && m->layers, "model is NULL");
+  LBX_CHECK_ARG(n >= 1 && tokens, "need n >= 1 tokens");
+  LBX_CHECK_ARG(start >= 0 && start + n <= m->max_seq, "start + n exceeds max_seq");
+  LBX_CHECK_ARG(m->heads % m->kv_heads == 0, "heads must be a multiple of kv_heads");
+  LBX_CHECK_ARG(m->embed && m->final_norm, "embed/final_norm required");
+  LBX_CHECK_ARG(!(logits || argmax_out) || m->lm_head, "lm_head required for logits/argmax");
+  LBX_CHECK_ARG(n <= FWD_MAX_TOKENS || (!tree_mask && !start_dev),
+                "more than %d tokens only as a causal run at a host-given start", FWD_MAX_TOKENS);
+  const size_t need = fwd_layout(m, n < FWD_MAX_TOKENS ? n : FWD_MAX_TOKENS).total;
+  LBX_CHECK_ARG(ws && ws_bytes >= need, "workspace too small (%zu < %zu)", ws_bytes, need);
+  // a long causal run is a sequence of steps of FWD_MAX_TOKENS tokens
+  for (int a = 0; a < n; a += FWD_MAX_TOKENS) {
+    const int c = n - a < FWD_MAX_TOKENS ? n - a : FWD_MAX_TOKENS;
+    const int rc = forward_chunk(m, tokens + a, c, start + a, start_dev, pos ? pos + a : nullptr, tree_mask,
+                                 hidden_out ? hidden_out + (int64_t)a * m->hidden : nullptr,
+                                 logits ? logits + (int64_t)a * m->vocab : nullptr,
+                                 argmax_out ? argmax_out + a : nullptr, ws, ws_bytes, stream);
     if (rc) return rc;
   }
   return LBX_OK;

@@ -8,6 +8,11 @@ namespace lbx {
 // cos/sin of pos * theta^(-2i/d), evaluated in double precision (HF Llama's
 // LlamaRotaryEmbedding computes the same angle in fp32).
 LBX_DEV void rope_cs(int pos, int i, int d, float theta, float &c, float &s) {
+  if (!(theta > 0.f)) {  // theta <= 0: no rotation (the reference CPU runtime applies none)
+    c = 1.f;
+    s = 0.f;
+    return;
+  }
   const double inv = pow((double)theta, -2.0 * (double)i / (double)d);
   double sd, cd;
   sincos((double)pos * inv, &sd, &cd);

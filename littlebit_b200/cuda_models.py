@@ -130,9 +130,13 @@ class _GraphCache:
 
 
 def _bound(pos: int, extra: int, max_seq: int) -> int:
-    """Upper bound of the cached-slot count a graph is captured for (attention grid)."""
-    b = ((pos + extra + 256) // 256) * 256
-    return min(b, max_seq - extra)
+    """Upper bound of the cached-slot count a graph is captured for (it sizes the
+    attention grid; chunks past the live length exit at once).  Power-of-two
+    buckets from 512 keep the number of captured graphs logarithmic."""
+    b = 512
+    while b < pos + extra + 1:
+        b *= 2
+    return max(pos, min(b, max_seq - extra))
 
 
 class CudaDraftModel:
@@ -174,7 +178,7 @@ class CudaDraftModel:
         dev = self.device
         self.tok_buf = torch.zeros(65, dtype=torch.int64, device=dev)
         self.start_buf = torch.zeros(64, dtype=torch.int32, device=dev)
-        self.pos_buf = torch.zeros(64, dtype=torch.int32, device=dev)
+        self.iota = torch.arange(64, dtype=torch.int32, device=dev)
         self.logits_buf = torch.zeros(64, self._vocab_size, dtype=torch.float32, device=dev)
         self._graphs = _GraphCache()
         self._stream = torch.cuda.Stream(dev)
@@ -254,16 +258,13 @@ class CudaDraftModel:
         def seq():
             for i in range(k):
                 dec.step(self.tok_buf[i:i + 1], bound, start_dev=self.start_buf[i:i + 1],
-                         pos=self.pos_buf[i:i + 1], argmax=self.tok_buf[i + 1:i + 2])
+                         argmax=self.tok_buf[i + 1:i + 2])
         return self._graphs.get(("draft", k, bound), seq, self._stream)
 
     def draft_on_device(self, P: int, k: int):
         """Greedy-draft k tokens: tok_buf[0] holds the token at slot P (already set on
         the device); tok_buf[1..k] receive the drafts.  No host synchronisation."""
-        idx = torch.arange(k, dtype=torch.int32)
-        hostv = torch.cat([P + idx, P + idx]).pin_memory()
-        self.start_buf[:k].copy_(hostv[:k], non_blocking=True)
-        self.pos_buf[:k].copy_(hostv[k:], non_blocking=True)
+        torch.add(self.iota[:k], P, out=self.start_buf[:k])
         if self.use_graphs:
             bound = _bound(P, k, self.max_seq_len)
             g = self._draft_graph(k, bound)
@@ -370,7 +371,7 @@ class CudaTargetModel:
         self.h_buf = [torch.zeros(64, H, dtype=torch.float32, device=dev) for _ in decs]
         self.am_buf = torch.zeros(64, dtype=torch.int64, device=dev)
         self.start_buf = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.pos_buf = torch.zeros(64, dtype=torch.int32, device=dev)
+        self.vtok = torch.zeros(64, dtype=torch.int64, device=dev)
         self._graphs = _GraphCache()
         self._stream = torch.cuda.Stream(dev)
         self._lm_ws = torch.zeros(int(lib().lbx_lmhead_workspace_size(64, self._vocab_size)),
@@ -442,20 +443,19 @@ class CudaTargetModel:
             u.pos = upto
         self._cached_tokens = list(ids[:upto])
 
-    def _verify_graph(self, tokens: torch.Tensor, n: int, bound: int):
+    def _verify_graph(self, n: int, bound: int):
+        # positions come from start_buf on the device (slots start..start+n-1)
         def seq():
-            self._step(tokens[:n], bound, argmax=self.am_buf[:n], start_dev=self.start_buf,
-                       pos=self.pos_buf[:n])
-        return self._graphs.get(("verify", n, bound, tokens.data_ptr()), seq, self._stream)
+            self._step(self.vtok[:n], bound, argmax=self.am_buf[:n], start_dev=self.start_buf)
+        return self._graphs.get(("verify", n, bound), seq, self._stream)
 
     def verify_on_device(self, tokens: torch.Tensor, P: int, n: int) -> torch.Tensor:
         """Target argmax [n] for tokens[0..n) at slots P.. (no host sync)."""
-        hostv = torch.cat([torch.tensor([P], dtype=torch.int32),
-                           P + torch.arange(n, dtype=torch.int32)]).pin_memory()
-        self.start_buf.copy_(hostv[:1], non_blocking=True)
-        self.pos_buf[:n].copy_(hostv[1:], non_blocking=True)
+        self.start_buf.fill_(P)
         if self.use_graphs:
-            g = self._verify_graph(tokens, n, _bound(P, n, self.max_seq_len))
+            if tokens.data_ptr() != self.vtok.data_ptr():
+                self.vtok[:n].copy_(tokens[:n])
+            g = self._verify_graph(n, _bound(P, n, self.max_seq_len))
             self._stream.wait_stream(torch.cuda.current_stream())
             g.replay()
             torch.cuda.current_stream().wait_stream(self._stream)

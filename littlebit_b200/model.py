@@ -202,8 +202,6 @@ class LittleBitDecoder:
         n = int(tokens.numel())
         if start + n > self.max_seq:
             raise RuntimeError(f"KV cache full: {start}+{n} > max_seq {self.max_seq}")
-        if start_dev is not None and pos is None:
-            raise RuntimeError("pos is required with start_dev")
         ws = self.workspace(n)
         L.check(lib().lbx_forward(ctypes.byref(self._model), _p(tokens), n, int(start), _p(start_dev),
                                   _p(pos), _p(tree_mask), _p(hidden), _p(logits), _p(argmax), _p(ws),

@@ -62,7 +62,11 @@ def rms_norm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
 
 
 def rope(x: np.ndarray, pos: np.ndarray, theta: float) -> np.ndarray:
-    """HF rotate_half RoPE on x [n, heads, d] at positions pos [n] (float64 angles)."""
+    """HF rotate_half RoPE on x [n, heads, d] at positions pos [n] (float64 angles).
+    theta <= 0 applies no rotation, as the reference's CPU runtime does
+    (patches/littlebit_cpu_optimized.cpp:1522-2079 has no rotary step)."""
+    if not theta > 0:
+        return x
     d = x.shape[-1]
     half = d // 2
     inv = theta ** (-2.0 * np.arange(half, dtype=np.float64) / d)
@@ -149,3 +153,49 @@ class OracleDecoder:
 
     def logits(self, x: np.ndarray) -> np.ndarray:
         return self.final_hidden(x) @ self.lm_head.T
+
+
+def _np(t):
+    """torch tensor or array -> numpy (bf16 tensors widen to float32 exactly)."""
+    if hasattr(t, "detach"):
+        t = t.detach().cpu()
+        return t.float().numpy() if t.is_floating_point() else t.numpy()
+    return np.asarray(t)
+
+
+def _proj_prefix(layer: int, name: str) -> str:
+    grp = "self_attn" if name in ("q_proj", "k_proj", "v_proj", "o_proj") else "mlp"
+    return f"model.layers.{layer}.{grp}.{name}"
+
+
+def from_runtime_state(state, n_layers: int, hidden: int, intermediate: int, heads: int,
+                       kv_heads: int, vocab: int, rms_eps: float = 1e-6, rope_theta: float = 10000.0,
+                       max_seq: int = 256, include_residual: bool = True,
+                       kv_bf16: bool = True) -> "OracleDecoder":
+    """OracleDecoder over a state dict in the runtime checkpoint layout
+    (convert_hf_to_runtime.py:47-77 keys: ``*.v_sign_rt``, ``*.u_sign_rt``, ``v2``,
+    ``mid``, ``u1`` and the ``_r`` residual set; a residual without its own
+    ``v_sign_r_rt`` shares the main branch's V)."""
+    layers = []
+    for i in range(n_layers):
+        projs = []
+        for nm in PROJ_NAMES:
+            p = _proj_prefix(i, nm)
+            r = int(_np(state[f"{p}.v_sign_rt_shape"])[0])
+            br = [RtBranch(_np(state[f"{p}.v_sign_rt"]), _np(state[f"{p}.v2"]).reshape(-1),
+                           _np(state[f"{p}.mid"]).reshape(-1), _np(state[f"{p}.u_sign_rt"]),
+                           _np(state[f"{p}.u1"]).reshape(-1), r)]
+            if include_residual and f"{p}.u_sign_r_rt" in state:
+                rr = int(_np(state[f"{p}.u_sign_r_rt_shape"])[1])
+                shared = f"{p}.v_sign_r_rt" not in state
+                br.append(RtBranch(None if shared else _np(state[f"{p}.v_sign_r_rt"]),
+                                   None if shared else _np(state[f"{p}.v2_r"]).reshape(-1),
+                                   _np(state[f"{p}.mid_r"]).reshape(-1), _np(state[f"{p}.u_sign_r_rt"]),
+                                   _np(state[f"{p}.u1_r"]).reshape(-1), rr))
+            projs.append(br)
+        layers.append(OracleLayer(_np(state[f"model.layers.{i}.input_layernorm.weight"]),
+                                  _np(state[f"model.layers.{i}.post_attention_layernorm.weight"]), projs))
+    cfg = DecoderConfig(n_layers, hidden, intermediate, heads, kv_heads, vocab, rms_eps, rope_theta, max_seq)
+    return OracleDecoder(cfg, _np(state["model.embed_tokens.weight"]), _np(state["model.norm.weight"]),
+                         _np(state["lm_head.weight"]) if "lm_head.weight" in state else None, layers,
+                         kv_bf16=kv_bf16)

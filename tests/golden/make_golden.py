@@ -18,6 +18,7 @@ Records, from the reference's own Python code:
                 with deterministic table-driven models (speculative_decoding.py)
   hf_llama.npz  HF LlamaForCausalLM + apply_littlebit_patch logits of a tiny
                 model (the reference's GPU/HF model path)
+  ref_schemas.json  the reference's littlebit_cpu_ops op schemas (cpp:2321-2377)
 """
 from __future__ import annotations
 
@@ -240,11 +241,24 @@ def gen_hf_llama():
     np.savez_compressed(HERE / "hf_llama.npz", **out)
 
 
+def gen_schemas():
+    """The op schemas of the reference's TORCH_LIBRARY block
+    (patches/littlebit_cpu_optimized.cpp:2321-2377), read as text."""
+    import re
+
+    src = (REF / "patches" / "littlebit_cpu_optimized.cpp").read_text()
+    block = src[src.index("TORCH_LIBRARY(littlebit_cpu_ops"):]
+    block = block[:block.index("TORCH_LIBRARY_IMPL")]
+    defs = re.findall(r'm\.def\(\s*((?:"[^"]*"\s*)+)\)', block)
+    schemas = ["".join(re.findall(r'"([^"]*)"', d)) for d in defs]
+    (HERE / "ref_schemas.json").write_text(json.dumps(schemas, indent=1) + "\n")
+
+
 if __name__ == "__main__":
     ap_ = argparse.ArgumentParser()
     ap_.add_argument("--only", default="")
     a = ap_.parse_args()
-    for fn in (gen_packing, gen_linear, gen_convert, gen_tree, gen_spec, gen_hf_llama):
+    for fn in (gen_packing, gen_linear, gen_convert, gen_tree, gen_spec, gen_hf_llama, gen_schemas):
         if a.only and a.only not in fn.__name__:
             continue
         fn()

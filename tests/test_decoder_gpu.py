@@ -1,18 +1,17 @@
 """The native decoder step (lbx_forward) vs the CPU oracle decoder.
 
 Same seeded runtime-layout weights on both sides; the oracle keeps keys and
-values rounded to bf16 like the B200 cache.  Bars: logits within 2e-3 of the
-largest |logit| (int16-quantised activations, fp32 elsewhere, compounded over
-the layers); greedy tokens equal wherever the oracle's top-2 margin exceeds
-that tolerance; a token's logits bit-identical whether prefilled alone or in a
-batch (the property that makes greedy speculative decoding token-identical).
+values rounded to bf16 like the B200 cache.  Bars: logits within 1e-2 of the
+largest |logit| (basis in ``_close``); greedy tokens equal wherever the
+oracle's top-2 margin exceeds that tolerance; a token's logits bit-identical
+whether prefilled alone or in a batch (the property that makes greedy
+speculative decoding token-identical).
 """
 import numpy as np
 import pytest
 import torch
 
 from oracle import decoder as od
-from oracle.littlebit import RtBranch
 
 pytestmark = pytest.mark.gpu
 
@@ -23,32 +22,9 @@ TINY_RANKS = {"q_proj": [64, 32], "k_proj": [32, 16], "v_proj": [32, 16], "o_pro
 
 
 def oracle_from_state(shape, st, max_seq, include_residual=True):
-    from littlebit_b200.model import PROJ_NAMES, proj_prefix
-
-    n = lambda t: t.float().numpy() if t.is_floating_point() else t.numpy()
-    layers = []
-    for i in range(shape.num_hidden_layers):
-        projs = []
-        for nm in PROJ_NAMES:
-            p = proj_prefix(i, nm)
-            r = int(st[f"{p}.v_sign_rt_shape"][0])
-            br = [RtBranch(n(st[f"{p}.v_sign_rt"]), n(st[f"{p}.v2"]).reshape(-1), n(st[f"{p}.mid"]).reshape(-1),
-                           n(st[f"{p}.u_sign_rt"]), n(st[f"{p}.u1"]).reshape(-1), r)]
-            if include_residual and f"{p}.u_sign_r_rt" in st:
-                rr = int(st[f"{p}.u_sign_r_rt_shape"][1])
-                shared = f"{p}.v_sign_r_rt" not in st
-                br.append(RtBranch(None if shared else n(st[f"{p}.v_sign_r_rt"]),
-                                   None if shared else n(st[f"{p}.v2_r"]).reshape(-1),
-                                   n(st[f"{p}.mid_r"]).reshape(-1), n(st[f"{p}.u_sign_r_rt"]),
-                                   n(st[f"{p}.u1_r"]).reshape(-1), rr))
-            projs.append(br)
-        layers.append(od.OracleLayer(n(st[f"model.layers.{i}.input_layernorm.weight"]),
-                                     n(st[f"model.layers.{i}.post_attention_layernorm.weight"]), projs))
-    cfg = od.DecoderConfig(shape.num_hidden_layers, shape.hidden_size, shape.intermediate_size,
-                           shape.num_attention_heads, shape.num_key_value_heads, shape.vocab_size,
-                           shape.rms_norm_eps, shape.rope_theta, max_seq)
-    return od.OracleDecoder(cfg, n(st["model.embed_tokens.weight"]), n(st["model.norm.weight"]),
-                            n(st["lm_head.weight"]), layers, kv_bf16=True)
+    return od.from_runtime_state(st, shape.num_hidden_layers, shape.hidden_size, shape.intermediate_size,
+                                 shape.num_attention_heads, shape.num_key_value_heads, shape.vocab_size,
+                                 shape.rms_norm_eps, shape.rope_theta, max_seq, include_residual)
 
 
 @pytest.fixture(scope="module")
@@ -114,24 +90,32 @@ def test_batch_invariance_bitwise(tiny):
         assert torch.equal(one[0], full[i]), i
 
 
-def test_tree_mask_matches_path_decode(tiny):
+@pytest.mark.parametrize("tree", ["small", "binary_d4"])
+def test_tree_mask_matches_path_decode(tiny, tree):
+    """A tree node's logits are bit-identical to decoding its root-to-node path
+    as a plain causal sequence: the property that keeps tree speculation
+    token-identical to target-only greedy decoding."""
     from littlebit_b200.model import LittleBitDecoder
-    from littlebit_b200.tree_utils import generate_tree_buffers
+    from littlebit_b200.tree_utils import binary_tree_choices, generate_tree_buffers
 
     shape, st = tiny
     m = LittleBitDecoder(shape, st, max_seq=256)
-    ids = torch.randint(0, shape.vocab_size, (40,), generator=torch.Generator().manual_seed(3))
-    tb = generate_tree_buffers([[0], [1], [0, 0], [0, 1], [1, 0], [0, 0, 0]], device="cpu")
+    ids = torch.randint(0, shape.vocab_size, (64,), generator=torch.Generator().manual_seed(3))
+    choices = [[0], [1], [0, 0], [0, 1], [1, 0], [0, 0, 0]] if tree == "small" else binary_tree_choices(4, 2)
+    tb = generate_tree_buffers(choices, device="cpu")
     T = tb["tree_len"]
     mask = tb["tree_attn_mask"][0, 0]
-    nodes = ids[19:19 + T]
+    P = 19 if tree == "small" else 50  # the big tree straddles the 64-key chunk boundary
+    nodes = ids[:T]
     tmask = [int(sum(1 << j for j in range(T) if mask[i, j])) for i in range(T)]
-    pos = 19 + tb["tree_position_ids"]
-    m.forward_tokens(ids[:19], 0)
-    lt = m.forward_tokens(nodes, 19, pos=pos, tree_mask=tmask)["logits"].cpu().numpy()
+    tmask = [v - (1 << 64) if v >= (1 << 63) else v for v in tmask]
+    pos = P + tb["tree_position_ids"]
+    prompt = torch.randint(0, shape.vocab_size, (P,), generator=torch.Generator().manual_seed(7))
+    m.forward_tokens(prompt, 0)
+    lt = m.forward_tokens(nodes, P, pos=pos, tree_mask=tmask)["logits"].cpu()
     for i in range(T):
         path = [j for j in range(T) if mask[i, j]]
         m2 = LittleBitDecoder(shape, st, max_seq=256)
-        m2.forward_tokens(ids[:19], 0)
-        ref = m2.forward_tokens(nodes[path], 19)["logits"][-1].cpu().numpy()
-        np.testing.assert_allclose(lt[i], ref, rtol=0, atol=1e-4 * np.abs(ref).max())
+        m2.forward_tokens(prompt, 0)
+        ref = m2.forward_tokens(nodes[path], P)["logits"][-1].cpu()
+        assert torch.equal(lt[i], ref), (i, float((lt[i] - ref).abs().max()))
