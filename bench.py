@@ -339,6 +339,51 @@ def run_decode(args, dev, rank, ws):
     }
 
 
+# ---------------------------------------------------------------------------
+# row-sharded 8192 -> 28672 LittleBitLinear (N > 1)
+# ---------------------------------------------------------------------------
+def run_row_shard(args, dev, rank, ws, reps: int = 200):
+    """BASELINE config 5's GEMV sweep point at this world size: U rows split over
+    the ranks, V replicated, one NCCL all-gather of the y slices per call.
+    GB/s counts the whole layer's algorithmic bytes once per call."""
+    import torch.distributed as dist
+    from littlebit_b200 import synthetic
+    from littlebit_b200.sharded import RowShardedLinear
+
+    K, N, r = 8192, 28672, 616
+    g = torch.Generator().manual_seed(4242)
+    full = synthetic.to_packed_linear(K, N, synthetic.layer(K, N, [r], g), dev)
+    sh = RowShardedLinear(full, ws, rank)
+    x = torch.randn(1, K, generator=g).to(dev)
+    part = sh.local_forward(x)
+    gat = torch.empty(ws, 1, N // ws, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for _ in range(5):
+            fn()
+        barrier(ws)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1) / reps * 1e3, ws)
+
+    t_local = timed(lambda: sh.local_forward(x, part))
+    t_ag = timed(lambda: dist.all_gather_into_tensor(gat, part))
+    t_all = timed(lambda: (sh.local_forward(x, part), dist.all_gather_into_tensor(gat, part)))
+    alg = (r * K + 7) // 8 + (N * r + 7) // 8 + 4 * (K + r + N) + 4 * K + 4 * N
+    return {"workload": f"LittleBitLinear {K}->{N} r={r}, k=1 fp32, U rows split over {ws} GPUs, "
+                        f"V replicated, NCCL all-gather of y",
+            "us_per_call": round(t_all, 3), "local_kernel_us": round(t_local, 3),
+            "allgather_us": round(t_ag, 3), "allgather_bytes_per_rank": 4 * N // ws,
+            "gbs_whole_layer": round(alg / (t_all * 1e-6) / 1e9, 2), "algorithmic_bytes": alg,
+            "timing": f"CUDA events over {reps} calls, max over ranks"}
+
+
 def run_ours(args):
     from littlebit_b200 import ops
 
@@ -441,6 +486,7 @@ def run_ours(args):
                    "kind": "reference", "sample": r["sample"]}
 
     decode = run_decode(args, dev, rank, ws) if args.decode else None
+    row_shard = run_row_shard(args, dev, rank, ws) if ws > 1 else None
 
     if rank == 0:
         traffic = traffic_from_profiles(k)
@@ -466,6 +512,7 @@ def run_ours(args):
                     "ms_per_step": round(t2 / args.steps, 4)},
             "cpu_baseline": cpu,
             "decode": decode,
+            "row_shard": row_shard,
             "gpu_launches": 2 * P * args.steps,
             "clocks": clocks,
         }
