@@ -25,6 +25,7 @@ cpu_baseline: the reference's own C++ op (oracle/_ref, littlebit_linear from
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import re
@@ -393,88 +394,82 @@ def run_ours(args):
     k, P = args.tokens, args.pool
     pool = build_pool(P, dev, seed=1234 + rank)
     arrs = [ops.projs_array([p]) for p in pool]
-    wsb = torch.zeros(ops.linear_workspace_bytes([pool[0]], k), dtype=torch.uint8, device=dev)
+    arr_all = ops.projs_array(pool)
     acts = [torch.randn(k, IN_F, device=dev).bfloat16()] + \
            [torch.empty(k, OUT_F, device=dev, dtype=torch.bfloat16) for _ in range(P)]
+    ptrs = (ctypes.c_void_p * (P + 1))(*[t.data_ptr() for t in acts])
+    wsb = torch.zeros(ops.linear_workspace_bytes([pool[0]], k), dtype=torch.uint8, device=dev)
+    wsc = torch.zeros(int(ops.lib().lbx_linear_chain_workspace_size(arr_all, P, k)), dtype=torch.uint8,
+                      device=dev)
     stream = torch.cuda.Stream(dev)
 
-    def step():
+    def step_kernels():  # one V-stage + one U-stage grid per layer, chained with PDL
         for i in range(P):
             ops.linear_group([pool[i]], acts[i], [acts[i + 1]], use_pdl=args.pdl, ws=wsb, arr=arrs[i])
 
-    # eager warm-up, then capture one step as a graph
-    with torch.cuda.stream(stream):
-        step()
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        step()
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            graph.replay()
-    torch.cuda.synchronize()
-    ops.clear_device_error()
+    def step_program():  # the whole chain as one persistent program
+        ops.linear_chain(pool, acts, ws=wsc, arr=arr_all, ptrs=ptrs)
 
+    def timed_graph(fn):
+        with torch.cuda.stream(stream):
+            fn()  # eager warm-up (builds the program, sets kernel attributes)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            fn()
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                graph.replay()
+        torch.cuda.synchronize()
+        ops.clear_device_error()
+        barrier(ws)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(ws)
+        out = max_over_ranks(e0.elapsed_time(e1), ws)
+        del graph
+        return out
+
+    main_fn = step_program if args.exec == "program" else step_kernels
     sampler = ClockSampler(lrank)
     sampler.start()
     time.sleep(0.3)
-    barrier(ws)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for _ in range(args.steps):
-            graph.replay()
-        e1.record(stream)
-    torch.cuda.synchronize()
-    barrier(ws)
+    t_ms = timed_graph(main_fn)
     clocks = sampler.stop()
-    t_ms = e0.elapsed_time(e1)
-    t_ms = max_over_ranks(t_ms, ws)
     assert ops.device_error() == 0, "device error word set during the bench"
     if not torch.isfinite(acts[-1].float()).all():
         raise RuntimeError("non-finite output in the layer chain")
+    y_main = acts[-1].clone()
+    t_other = timed_graph(step_kernels if args.exec == "program" else step_program)
+    if not torch.equal(acts[-1], y_main):
+        raise RuntimeError("program and kernel paths disagree")
 
     b_layer, packed = layer_bytes(k)
     total_bytes = b_layer * P * args.steps * ws
     value = total_bytes / (t_ms * 1e-3) / 1e9
+    other_gbs = total_bytes / (t_other * 1e-3) / 1e9
     per_launch_s = t_ms * 1e-3 / (P * args.steps)
     peak, peak_kind = peaks()
     achieved = b_layer / per_launch_s / 1e9
 
-    # ---- e2e: per-layer host round trip through pinned buffers
+    # ---- e2e: the chain through the C-ABI call with pinned HOST input/output:
+    # every step copies x host->device, runs the chain, copies y device->host
     hx = torch.empty(k, IN_F, dtype=torch.bfloat16).pin_memory()
     hx.copy_(acts[0].cpu())
-    hys = [torch.empty(k, OUT_F, dtype=torch.bfloat16).pin_memory() for _ in range(P)]
-    dx = torch.empty(k, IN_F, device=dev, dtype=torch.bfloat16)
-    dy = torch.empty(k, OUT_F, device=dev, dtype=torch.bfloat16)
+    hy = torch.empty(k, OUT_F, dtype=torch.bfloat16).pin_memory()
 
     def e2e_step():
-        src = hx
-        for i in range(P):
-            dx.copy_(src, non_blocking=True)
-            ops.linear_group([pool[i]], dx, [dy], use_pdl=False, ws=wsb, arr=arrs[i])
-            hys[i].copy_(dy, non_blocking=True)
-            src = hys[i]
+        acts[0].copy_(hx, non_blocking=True)
+        main_fn()
+        hy.copy_(acts[-1], non_blocking=True)
 
-    with torch.cuda.stream(stream):
-        e2e_step()
-    torch.cuda.synchronize()
-    g2 = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g2, stream=stream):
-        e2e_step()
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            g2.replay()
-    torch.cuda.synchronize()
-    barrier(ws)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for _ in range(args.steps):
-            g2.replay()
-        e1.record(stream)
-    torch.cuda.synchronize()
-    t2 = max_over_ranks(e0.elapsed_time(e1), ws)
+    t2 = timed_graph(e2e_step)
     e2e_val = b_layer * P * args.steps * ws / (t2 * 1e-3) / 1e9
 
     # ---- CPU baseline (rank 0, N=1 only)
@@ -489,7 +484,7 @@ def run_ours(args):
     row_shard = run_row_shard(args, dev, rank, ws) if ws > 1 else None
 
     if rank == 0:
-        traffic = traffic_from_profiles(k)
+        traffic = traffic_from_profiles(k) if args.exec == "kernels" else None
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 4),
@@ -500,26 +495,29 @@ def run_ours(args):
                        "tokens": k, "pool_layers": P,
                        "pool_mb": round(P * (packed + sum(4 * (IN_F + r + OUT_F) for r in RANKS)) / 1e6, 1),
                        "l2": "weight pool > 2x L2 (126 MB): no flush needed",
-                       "parallelism": f"dp{ws} (independent replicas)", "pdl": bool(args.pdl)},
+                       "parallelism": f"dp{ws} (independent replicas)",
+                       "exec": ("one persistent cooperative program per step (lbx_linear_chain)"
+                                if args.exec == "program" else "two kernels per layer, PDL-chained")},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": b_layer,
-                         "launch": "one lbx_linear call (V-stage + U-stage kernels)",
+                         "launch": "one LittleBit layer (V-stage + U-stage units)",
                          "mean_launch_us": round(per_launch_s * 1e6, 3)},
+            "other_exec_gbs": round(other_gbs, 2),
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
-                    "h2d_bytes_per_step": 2 * k * IN_F * P, "d2h_bytes_per_step": 2 * k * OUT_F * P,
-                    "ms_per_step": round(t2 / args.steps, 4)},
+                    "h2d_bytes_per_step": 2 * k * IN_F, "d2h_bytes_per_step": 2 * k * OUT_F,
+                    "ms_per_step": round(t2 / args.steps, 4),
+                    "path": "pinned host x -> chain via the C ABI -> pinned host y, each step"},
             "cpu_baseline": cpu,
             "decode": decode,
             "row_shard": row_shard,
-            "gpu_launches": 2 * P * args.steps,
+            "gpu_launches": (1 if args.exec == "program" else 2 * P) * args.steps,
             "clocks": clocks,
         }
         print(json.dumps(out))
     if ws > 1:
         import torch.distributed as dist
-        del graph, g2
         dist.destroy_process_group()
     return 0
 
@@ -533,6 +531,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--pool", type=int, default=128)
     ap.add_argument("--pdl", type=int, default=1)
+    ap.add_argument("--exec", default="kernels", choices=["program", "kernels"],
+                    help="program: each step is one persistent launch; kernels: one grid per stage")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--decode", type=int, default=1, help="also run the 7B-shape decode section")

@@ -168,7 +168,7 @@ int lbx_rope(float *x, const int32_t *pos, int32_t n, int32_t heads, int32_t hea
  * prefix_len + j with bit j of tree_mask[i] set (its tree ancestors and
  * itself) or, when tree_mask == NULL, j <= i (causal).  GQA: query head h
  * reads kv head h / (heads / kv_heads) (cpp:1238).  Caches are
- * [kv_heads, max_seq, head_dim] bf16; head_dim even and <= 128; n <= 64.
+ * [kv_heads, max_seq, head_dim] bf16; head_dim a multiple of 4, <= 128; n <= 64.
  * A query's keys are the cached prefix, then its visible new tokens in index
  * order (a tree's ancestors precede their descendants, as in
  * generate_tree_buffers); the arithmetic follows that order, so a tree node's
@@ -188,9 +188,17 @@ typedef struct lbx_attn_args {
   const uint64_t *tree_mask; /* [n] or NULL          */
   uint16_t *k_cache; uint16_t *v_cache;
   float *out;                /* [n, heads*d]         */
+  const float *rope_cs;      /* [n][head_dim/2] (cos, sin) pairs from
+                                lbx_rope_table for pos[], or NULL: computed
+                                in the kernel (same values)               */
 } lbx_attn_args;
+/* Workspace: zero-filled once at allocation (it holds self-resetting tickets). */
 size_t lbx_attn_workspace_size(const lbx_attn_args *a);
 int lbx_attn_decode(const lbx_attn_args *a, void *ws, size_t ws_bytes, cudaStream_t stream);
+/* (cos, sin) of pos[i] * theta^(-2j/head_dim), j < head_dim/2, evaluated in
+ * double and rounded to float: out [n][head_dim/2][2].  theta <= 0 gives (1, 0). */
+int lbx_rope_table(const int32_t *pos, int32_t n, int32_t head_dim, float theta, float *out,
+                   cudaStream_t stream);
 
 /* Fused final RMSNorm + lm_head (bf16 [vocab, hidden]) + argmax.
  * Replaces dense_gemv_f32 (cpp:1054-1115) + the argmax of generate_token
@@ -217,6 +225,16 @@ int lbx_accept_greedy_tree(const int64_t *cand, const int64_t *node_argmax,
                            const int64_t *retrieve, int32_t L, int32_t D1, int64_t *out,
                            cudaStream_t stream);
 
+/* Chain of single-projection LittleBit layers as one persistent program:
+ * acts[i+1] = layer_i(acts[i]) for i < n_layers, n_tokens rows each, all
+ * activations of one dtype (LBX_F32 / LBX_BF16).  Same numerics as calling
+ * lbx_linear layer by layer.  The workspace (zero-filled once) is shared by
+ * the layers; the program is built on the first call with these pointers,
+ * outside stream capture. */
+size_t lbx_linear_chain_workspace_size(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens);
+int lbx_linear_chain(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens, int32_t dtype,
+                     void *const *acts, void *ws, size_t ws_bytes, cudaStream_t stream);
+
 /* ---- whole decoder step (cpp:1522-1840 full_forward, 1846-2079
  *      full_forward_batch, 2256-2317 generate_token) ----------------------- */
 typedef struct lbx_layer {
@@ -234,7 +252,21 @@ typedef struct lbx_model {
   const float *final_norm; /* [hidden] */
   const uint16_t *lm_head; /* [vocab, hidden] bf16, may be NULL for hidden-only */
   const lbx_layer *layers; /* host array [n_layers] */
+  int32_t exec_mode;       /* LBX_EXEC_*: how lbx_forward runs a step */
+  int32_t _pad2;
 } lbx_model;
+
+/* lbx_forward execution: the kernel path launches one grid per op (chained
+ * with programmatic dependent launch); a persistent program runs the whole
+ * step (n <= LBX_MAX_TOKENS) as one cooperative launch with grid barriers
+ * between phases.  Both compute the same bits.  AUTO selects the kernel path,
+ * the faster of the two on B200 at present.  A program is built and uploaded
+ * on the first call of each (model, n, cached length / 64, outputs,
+ * workspace) combination, which must happen outside stream capture; later
+ * calls may be captured. */
+#define LBX_EXEC_AUTO 0
+#define LBX_EXEC_KERNELS 1
+#define LBX_EXEC_PROGRAM 2
 
 /* Workspace of lbx_forward: zero-filled once at allocation, like lbx_linear's. */
 size_t lbx_forward_workspace_size(const lbx_model *m /* host */, int32_t n_tokens);

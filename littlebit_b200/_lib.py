@@ -17,6 +17,7 @@ LBX_MAX_TOKENS = 16
 LBX_MAX_PROJ = 3
 LBX_PRO_NONE, LBX_PRO_RMSNORM, LBX_PRO_SILU_MUL = 0, 1, 2
 LBX_EPI_STORE, LBX_EPI_ADD = 0, 1
+LBX_EXEC_AUTO, LBX_EXEC_KERNELS, LBX_EXEC_PROGRAM = 0, 1, 2
 
 
 class Branch(ctypes.Structure):
@@ -51,6 +52,7 @@ class AttnArgs(ctypes.Structure):
         ("k_new", c_void_p), ("v_new", c_void_p), ("kv_ld", c_int64),
         ("pos", c_void_p), ("tree_mask", c_void_p),
         ("k_cache", c_void_p), ("v_cache", c_void_p), ("out", c_void_p),
+        ("rope_cs", c_void_p),
     ]
 
 
@@ -70,6 +72,7 @@ class Model(ctypes.Structure):
         ("use_pdl", c_int32),
         ("embed", c_void_p), ("final_norm", c_void_p), ("lm_head", c_void_p),
         ("layers", POINTER(Layer)),
+        ("exec_mode", c_int32), ("_pad2", c_int32),
     ]
 
 
@@ -88,6 +91,7 @@ _SIGNATURES = {
     "lbx_rope": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_float, c_void_p]),
     "lbx_attn_workspace_size": (c_size_t, [POINTER(AttnArgs)]),
     "lbx_attn_decode": (c_int, [POINTER(AttnArgs), c_void_p, c_size_t, c_void_p]),
+    "lbx_rope_table": (c_int, [c_void_p, c_int32, c_int32, c_float, c_void_p, c_void_p]),
     "lbx_lmhead_workspace_size": (c_size_t, [c_int32, c_int32]),
     "lbx_lmhead_argmax": (c_int, [c_void_p, c_void_p, c_float, c_int32, c_int32, c_void_p,
                                   c_int32, c_void_p, c_void_p, c_void_p, c_size_t, c_int32,
@@ -95,6 +99,9 @@ _SIGNATURES = {
     "lbx_accept_greedy_chain": (c_int, [c_void_p, c_void_p, c_int32, c_void_p, c_void_p]),
     "lbx_accept_greedy_tree": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int32,
                                        c_void_p, c_void_p]),
+    "lbx_linear_chain_workspace_size": (c_size_t, [POINTER(Proj), c_int32, c_int32]),
+    "lbx_linear_chain": (c_int, [POINTER(Proj), c_int32, c_int32, c_int32, POINTER(c_void_p), c_void_p,
+                                 c_size_t, c_void_p]),
     "lbx_forward_workspace_size": (c_size_t, [POINTER(Model), c_int32]),
     "lbx_forward": (c_int, [POINTER(Model), c_void_p, c_int32, c_int32, c_void_p, c_void_p,
                             c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),

@@ -21,7 +21,7 @@ namespace lbx {
 constexpr int FWD_MAX_TOKENS = 64;  // tokens per step (attention and tree-mask width)
 
 struct FwdLayout {
-  size_t x, q, kk, vv, att, gate, up, pos, lin, attn, lm, total;
+  size_t tk, sw, x, q, kk, vv, att, gate, up, pos, rope, lin, attn, lm, total;
   size_t lin_bytes, attn_bytes, lm_bytes;
 };
 
@@ -33,8 +33,11 @@ static FwdLayout fwd_layout(const lbx_model *m, int n) {
                KV = (size_t)m->kv_heads * m->head_dim;
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off += al(bytes); return o; };
-  // the linear scratch comes first: its bookkeeping words (kept at zero between
-  // calls) must sit at the same offset whatever n a call uses
+  // the attention tickets and the linear scratch come first: their bookkeeping
+  // words (kept at zero between calls) must sit at the same offset whatever n
+  // a call uses
+  L.tk = take(attn_ticket_bytes(m->kv_heads));
+  L.sw = take(16);
   size_t lin = 0;
   for (int l = 0; l < m->n_layers; ++l) {
     const lbx_proj *pr = m->layers[l].proj;
@@ -53,13 +56,14 @@ static FwdLayout fwd_layout(const lbx_model *m, int n) {
   L.gate = take((size_t)n * I * 4);
   L.up = take((size_t)n * I * 4);
   L.pos = take((size_t)n * 4);
+  L.rope = take((size_t)n * m->head_dim * 4);
   lbx_attn_args aa = {};
   aa.n = n;
   aa.heads = m->heads;
   aa.kv_heads = m->kv_heads;
   aa.head_dim = m->head_dim;
   aa.prefix_len = m->max_seq - n;
-  L.attn_bytes = lbx_attn_workspace_size(&aa);
+  L.attn_bytes = attn_partial_bytes(&aa, nullptr);
   L.attn = take(L.attn_bytes);
   L.lm_bytes = lbx_lmhead_workspace_size(n, m->vocab);
   L.lm = take(L.lm_bytes);
@@ -131,7 +135,9 @@ static int forward_chunk(const lbx_model *m, const int64_t *tokens, int32_t n, i
   float *up = reinterpret_cast<float *>(w + L.up);
   int32_t *posb = reinterpret_cast<int32_t *>(w + L.pos);
   void *lin = w + L.lin;
-  void *attn_ws = w + L.attn;
+  void *attn_part = w + L.attn;
+  unsigned *attn_tk = reinterpret_cast<unsigned *>(w + L.tk);
+  float *rope = reinterpret_cast<float *>(w + L.rope);
   void *lm_ws = w + L.lm;
   const int pdl = m->use_pdl;
 
@@ -143,6 +149,9 @@ static int forward_chunk(const lbx_model *m, const int64_t *tokens, int32_t n, i
     if (rc) return rc;
     pos = posb;
   }
+  // RoPE (cos, sin) of this step's positions, once for all layers
+  rc = lbx_rope_table(pos, n, m->head_dim, m->rope_theta, rope, stream);
+  if (rc) return rc;
   for (int l = 0; l < m->n_layers; ++l) {
     const lbx_layer &ly = m->layers[l];
     // q, k, v from RMSNorm(x)
@@ -179,10 +188,11 @@ static int forward_chunk(const lbx_model *m, const int64_t *tokens, int32_t n, i
     aa.v_new = vv;
     aa.pos = pos;
     aa.tree_mask = tree_mask;
+    aa.rope_cs = rope;
     aa.k_cache = ly.k_cache;
     aa.v_cache = ly.v_cache;
     aa.out = att;
-    rc = lbx_attn_decode(&aa, attn_ws, L.attn_bytes, stream);
+    rc = attn_launch(&aa, attn_part, attn_tk, stream);
     if (rc) return rc;
     // x += o(att)
     lbx_linear_args o = {};
@@ -227,6 +237,221 @@ static int forward_chunk(const lbx_model *m, const int64_t *tokens, int32_t n, i
 }
 }  // namespace lbx
 
+namespace lbx {
+// the whole step as one persistent program (n <= LBX_MAX_TOKENS)
+static int forward_program(const lbx_model *m, const int64_t *tokens, int32_t n, int32_t start,
+                           const int32_t *start_dev, const int32_t *pos, const uint64_t *tree_mask,
+                           float *hidden_out, float *logits, int64_t *argmax_out, void *ws,
+                           size_t ws_bytes, cudaStream_t stream) {
+  LBX_CHECK_SUP(n <= LBX_MAX_TOKENS, "a program step takes at most %d tokens", LBX_MAX_TOKENS);
+  const FwdLayout L = fwd_layout(m, n);
+  LBX_CHECK_ARG(ws && ws_bytes >= L.total, "workspace too small (%zu < %zu)", ws_bytes, L.total);
+  uint8_t *w = reinterpret_cast<uint8_t *>(ws);
+  const int nchunk = (start + n + 63) / 64;
+  const int flags = (tree_mask ? 1 : 0) | (pos ? 2 : 0) | (hidden_out ? 4 : 0) | (logits ? 8 : 0) |
+                    (argmax_out ? 16 : 0) | (m->use_pdl ? 32 : 0);
+  uint64_t key = 0xF0A3Dull;
+  key = mix(key, (uintptr_t)m);
+  key = mix(key, (uintptr_t)m->layers);
+  key = mix(key, (uint64_t)n);
+  key = mix(key, (uint64_t)nchunk);
+  key = mix(key, (uint64_t)flags);
+  key = mix(key, (uintptr_t)ws);
+  key = mix(key, (uintptr_t)m->embed);
+  key = mix(key, (uintptr_t)m->lm_head);
+  key = mix(key, (uintptr_t)m->final_norm);
+  for (int l = 0; l < m->n_layers; ++l) {
+    const lbx_layer &ly = m->layers[l];
+    key = mix(key, (uintptr_t)ly.ln1);
+    key = mix(key, (uintptr_t)ly.ln2);
+    key = mix(key, (uintptr_t)ly.k_cache);
+    key = mix(key, (uintptr_t)ly.v_cache);
+    for (int p = 0; p < 7; ++p)
+      for (int b = 0; b < ly.proj[p].n_branches; ++b) {
+        key = mix(key, (uintptr_t)ly.proj[p].br[b].v_sign);
+        key = mix(key, (uintptr_t)ly.proj[p].br[b].u_sign);
+        key = mix(key, (uintptr_t)ly.proj[p].br[b].mid);
+      }
+  }
+  float *x = reinterpret_cast<float *>(w + L.x);
+  float *q = reinterpret_cast<float *>(w + L.q);
+  float *kk = reinterpret_cast<float *>(w + L.kk);
+  float *vv = reinterpret_cast<float *>(w + L.vv);
+  float *att = reinterpret_cast<float *>(w + L.att);
+  float *gate = reinterpret_cast<float *>(w + L.gate);
+  float *up = reinterpret_cast<float *>(w + L.up);
+  int32_t *posb = reinterpret_cast<int32_t *>(w + L.pos);
+  int32_t *sw = reinterpret_cast<int32_t *>(w + L.sw);
+  float *rope = reinterpret_cast<float *>(w + L.rope);
+  void *lin = w + L.lin;
+  void *attn_part = w + L.attn;
+  unsigned *attn_tk = reinterpret_cast<unsigned *>(w + L.tk);
+  void *lm_ws = w + L.lm;
+
+  std::lock_guard<std::mutex> lk(g_prog_mu);
+  Program *P = nullptr;
+  auto it = g_progs.find(key);
+  if (it != g_progs.end()) {
+    P = it->second;
+  } else {
+    size_t budget = 0;
+    int nsm = 0;
+    int rc = program_budget(budget, nsm);
+    if (rc) return rc;
+    ProgBuilder B;
+    Phase st = {};
+    st.kind = PH_START;
+    st.units = n;
+    st.io = IO_TOKENS;
+    st.st.table = m->embed;
+    st.st.hidden = m->hidden;
+    st.st.vocab = m->vocab;
+    st.st.n = n;
+    st.st.d = m->head_dim;
+    st.st.theta = m->rope_theta;
+    st.st.x = x;
+    st.st.pos = posb;
+    st.st.start_word = sw;
+    st.st.rope = reinterpret_cast<float2 *>(rope);
+    B.push(st, 0, 0);
+    for (int l = 0; l < m->n_layers; ++l) {
+      const lbx_layer &ly = m->layers[l];
+      lbx_linear_args a = {};
+      a.n_proj = 3;
+      a.n_tokens = n;
+      a.x_dtype = a.y_dtype = LBX_F32;
+      a.prologue = LBX_PRO_RMSNORM;
+      a.epilogue = LBX_EPI_STORE;
+      a.eps = m->rms_eps;
+      a.x = x;
+      a.norm_w = ly.ln1;
+      a.y[0] = q;
+      a.y[1] = kk;
+      a.y[2] = vv;
+      rc = build_linear(B, ly.proj + 0, a, lin, budget);
+      if (rc) return rc;
+      lbx_attn_args aa = {};
+      aa.n = n;
+      aa.heads = m->heads;
+      aa.kv_heads = m->kv_heads;
+      aa.head_dim = m->head_dim;
+      aa.max_seq = m->max_seq;
+      aa.prefix_len = start;
+      aa.prefix_dev = sw;
+      aa.scale = m->attn_scale;
+      aa.theta = m->rope_theta;
+      aa.q = q;
+      aa.k_new = kk;
+      aa.v_new = vv;
+      aa.pos = posb;
+      aa.tree_mask = tree_mask;
+      aa.k_cache = ly.k_cache;
+      aa.v_cache = ly.v_cache;
+      aa.out = att;
+      aa.rope_cs = rope;
+      Phase ap = {};
+      size_t asmem = 0;
+      rc = attn_prep(&aa, attn_part, attn_tk, ap.a, asmem);
+      if (rc) return rc;
+      ap.kind = PH_ATTN;
+      ap.units = ap.a.nchunk * ap.a.kvh * ap.a.ngroups;
+      ap.io = tree_mask ? IO_TREE : IO_NONE;
+      ap.a.tree = nullptr;  // the kernel argument, attached at run time
+      B.push(ap, 0, asmem);
+      lbx_linear_args o = {};
+      o.n_proj = 1;
+      o.n_tokens = n;
+      o.x_dtype = o.y_dtype = LBX_F32;
+      o.prologue = LBX_PRO_NONE;
+      o.epilogue = LBX_EPI_ADD;
+      o.x = att;
+      o.y[0] = x;
+      rc = build_linear(B, ly.proj + 3, o, lin, budget);
+      if (rc) return rc;
+      lbx_linear_args gu = a;
+      gu.n_proj = 2;
+      gu.norm_w = ly.ln2;
+      gu.y[0] = gate;
+      gu.y[1] = up;
+      gu.y[2] = nullptr;
+      rc = build_linear(B, ly.proj + 4, gu, lin, budget);
+      if (rc) return rc;
+      lbx_linear_args dn = o;
+      dn.prologue = LBX_PRO_SILU_MUL;
+      dn.x = gate;
+      dn.x2 = up;
+      rc = build_linear(B, ly.proj + 6, dn, lin, budget);
+      if (rc) return rc;
+    }
+    if (hidden_out) {
+      Phase nm = {};
+      nm.kind = PH_NORM;
+      nm.units = n;
+      nm.io = IO_HIDDEN;
+      nm.nm.x = x;
+      nm.nm.w = m->final_norm;
+      nm.nm.hidden = m->hidden;
+      nm.nm.eps = m->rms_eps;
+      B.push(nm, 0, 0);
+    }
+    if (logits || argmax_out) {
+      LBX_CHECK_SUP(m->hidden % 256 == 0, "hidden must be a multiple of 256");
+      // one pass width for the whole program (rows past a pass's tokens are
+      // zero and every token's sum is computed the same way at any width)
+      const int NT = n <= 1 ? 1 : n <= 2 ? 2 : n <= 4 ? 4 : 8;
+      LBX_CHECK_SUP((size_t)NT * m->hidden * 4 <= 128 * 1024, "hidden too wide for a program lm_head pass");
+      B.lmnt = NT;
+      const int per = NT;
+      for (int t0 = 0; t0 < n; t0 += per) {
+        const int nt = std::min(per, n - t0);
+        Phase lp = {};
+        lp.kind = PH_LM;
+        lp.units = nsm;
+        lp.ncb = NT;
+        lp.io = IO_LOGITS;
+        lp.io_off = (int64_t)t0 * m->vocab;
+        lp.l.x = x + (int64_t)t0 * m->hidden;
+        lp.l.norm_w = m->final_norm;
+        lp.l.eps = m->rms_eps;
+        lp.l.n = nt;
+        lp.l.hidden = m->hidden;
+        lp.l.vocab = m->vocab;
+        lp.l.nblocks = nsm;
+        lp.l.w = m->lm_head;
+        lp.l.best = reinterpret_cast<unsigned long long *>(lm_ws);
+        B.push(lp, 0, (size_t)NT * m->hidden * 4);
+        if (argmax_out) {
+          Phase am = {};
+          am.kind = PH_ARGMAX;
+          am.units = 1;
+          am.io = IO_ARGMAX;
+          am.io_off = t0;
+          am.am.best = reinterpret_cast<const unsigned long long *>(lm_ws);
+          am.am.nblocks = nsm;
+          am.am.n = nt;
+          B.push(am, 0, 0);
+        }
+      }
+    }
+    LBX_CHECK_SUP(((B.wmax + 255) & ~(size_t)255) + B.smax <= budget,
+                  "the step program needs %zu bytes of shared memory (max %zu)",
+                  ((B.wmax + 255) & ~(size_t)255) + B.smax, budget);
+    rc = finish_program(key, B, stream, P);
+    if (rc) return rc;
+  }
+  ProgIo io = {};
+  io.tokens = tokens;
+  io.start = start;
+  io.start_dev = start_dev;
+  io.pos = pos;
+  io.tree = tree_mask;
+  io.hidden = hidden_out;
+  io.logits = logits;
+  io.argmax = argmax_out;
+  return launch_program(P, gridbar_of(lin), io, stream);
+}
+}  // namespace lbx
+
 extern "C" int lbx_forward(const lbx_model *m, const int64_t *tokens, int32_t n, int32_t start,
                            const int32_t *start_dev, const int32_t *pos, const uint64_t *tree_mask,
                            float *hidden_out, float *logits, int64_t *argmax_out, void *ws,
@@ -242,6 +467,21 @@ extern "C" int lbx_forward(const lbx_model *m, const int64_t *tokens, int32_t n,
                 "more than %d tokens only as a causal run at a host-given start", FWD_MAX_TOKENS);
   const size_t need = fwd_layout(m, n < FWD_MAX_TOKENS ? n : FWD_MAX_TOKENS).total;
   LBX_CHECK_ARG(ws && ws_bytes >= need, "workspace too small (%zu < %zu)", ws_bytes, need);
+  LBX_CHECK_ARG(m->exec_mode >= LBX_EXEC_AUTO && m->exec_mode <= LBX_EXEC_PROGRAM, "bad exec_mode");
+  if (m->exec_mode == LBX_EXEC_PROGRAM) {
+    // programs of up to LBX_MAX_TOKENS tokens; a longer causal run is a sequence of them
+    LBX_CHECK_SUP(n <= LBX_MAX_TOKENS || (!tree_mask && !start_dev),
+                  "a program step with a tree mask or a device start takes at most %d tokens", LBX_MAX_TOKENS);
+    for (int a = 0; a < n; a += LBX_MAX_TOKENS) {
+      const int c = n - a < LBX_MAX_TOKENS ? n - a : LBX_MAX_TOKENS;
+      const int rc = forward_program(m, tokens + a, c, start + a, start_dev, pos ? pos + a : nullptr, tree_mask,
+                                     hidden_out ? hidden_out + (int64_t)a * m->hidden : nullptr,
+                                     logits ? logits + (int64_t)a * m->vocab : nullptr,
+                                     argmax_out ? argmax_out + a : nullptr, ws, ws_bytes, stream);
+      if (rc) return rc;
+    }
+    return LBX_OK;
+  }
   // a long causal run is a sequence of steps of FWD_MAX_TOKENS tokens
   for (int a = 0; a < n; a += FWD_MAX_TOKENS) {
     const int c = n - a < FWD_MAX_TOKENS ? n - a : FWD_MAX_TOKENS;

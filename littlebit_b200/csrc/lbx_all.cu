@@ -9,4 +9,5 @@
 #include "misc.cu"
 #include "attention.cu"
 #include "lmhead.cu"
+#include "program.cu"
 #include "forward.cu"

@@ -4,7 +4,9 @@
 // Reference: quantization/modules/littlebit.py:95-121 (fp32 semantics) and
 // patches/littlebit_cpu_optimized.cpp:598-701 (packed-word CPU kernel).
 //
-// One call = two kernels chained with programmatic dependent launch (PDL):
+// One call = two stages, each a grid of independent units; standalone they are
+// two kernels chained with programmatic dependent launch (PDL), and a
+// persistent program (program.cu) runs the same unit bodies as phases:
 //   V-stage  CTA = 16 rank rows x all of K, warp = 256-column blocks:
 //            z_b = mid_b ⊙ (V_sign · a) [⊙ rsqrt(mean x^2 + eps) for a fused
 //            RMSNorm],  a = v2 ⊙ prologue(x);  blocks summed in fixed order
@@ -21,9 +23,10 @@
 // depend on how many tokens share the launch (verify batch == batch 1, bit for
 // bit) and repeated calls are deterministic.
 //
-// All weights of a CTA (sign words and scale vectors) are prefetched with
-// cp.async.bulk into shared memory BEFORE griddepcontrol.wait, so their HBM
-// latency overlaps the preceding kernel.
+// All weights of a unit (sign words and scale vectors) are requested with
+// cp.async.bulk into a shared-memory weight region before the unit's inputs
+// exist (before griddepcontrol.wait, or before the preceding grid barrier), so
+// their HBM latency overlaps the preceding work.
 
 #include <algorithm>
 
@@ -55,8 +58,8 @@ struct VSeg {
   const float *mid1;     // [rank] (shared-V residual) or nullptr
   float *z0;             // [k][rank]
   float *z1;             // [k][rank] or nullptr
-  int *zmax0;            // [k] running max |z0| (float bits), zero before the call
-  int *zmax1;            // [k] or nullptr
+  int *zpart0;           // [tiles of this segment][LBX_MAX_TOKENS] max |z0| of each tile (float bits)
+  int *zpart1;           // same for the shared-V residual, or nullptr
   int rank;
   int tile0;             // first CTA (16-row tile) of this segment
 };
@@ -72,13 +75,15 @@ struct VParams {
   const void *x;
   const void *x2;
   const float *norm_w;
+  int w_bytes;           // shared-memory weight region of a standalone launch
 };
 
 struct USeg {
   const int32_t *u_sign[2];
   const float *u1[2];
   const float *z[2];     // [k][rank] from the V-stage
-  const int *zmax[2];    // [k] max |z| per token (float bits) from the V-stage
+  const int *zpart[2];   // per-V-tile maxima of |z| (float bits), [ntile][LBX_MAX_TOKENS]
+  int ntile[2];          // V tiles of each branch's latent
   int rank[2];
   int words[2];   // ceil(rank/32)
   int pitch[2];   // smem row pitch (words)
@@ -98,9 +103,7 @@ struct UParams {
   int ut;             // row tiles per CTA (warps split the ranks 16/ut ways)
   int act_words[2];   // max over projections of 4*ceil(words/4)
   int wtile_words;    // per-tile weight region (words)
-  int *zmax_all;      // all zmax words of this call (reset by the last CTA)
-  int nzmax;
-  unsigned *ticket;   // CTA completion counter (zero before and after the call)
+  int w_bytes;        // shared-memory weight region of a standalone launch
 };
 
 // ---------------------------------------------------------------------------
@@ -196,66 +199,115 @@ LBX_DEV void load8cg(const float *p, float (&v)[8]) {
 }
 
 // ---------------------------------------------------------------------------
-// V-stage
+// per-CTA state shared by the stage bodies (static shared memory of the
+// launching kernel): scale scratch and the mbarriers of the weight copies.
+// bar[0..UT_MAX) serve the U-stage tiles, bar[UT_MAX] the V-stage; par[] is
+// the phase parity each barrier will complete next, so one barrier serves any
+// number of units of a persistent CTA.
 // ---------------------------------------------------------------------------
-template <int NCB>
-__global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_constant__ VParams p) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  __shared__ float s_inv[VWARPS][LBX_MAX_TOKENS];
-  __shared__ int s_sq[VWARPS][LBX_MAX_TOKENS];
-  __shared__ float s_ssq[VWARPS][LBX_MAX_TOKENS];
-  __shared__ __align__(16) float s_mid[2][16];
-  __shared__ int s_zmax[2][LBX_MAX_TOKENS];
-  __shared__ __align__(8) uint64_t bar;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, q = lane & 3;
+struct LinShm {
+  float v_inv[VWARPS][LBX_MAX_TOKENS];
+  int v_sq[VWARPS][LBX_MAX_TOKENS];
+  float v_ssq[VWARPS][LBX_MAX_TOKENS];
+  int v_zmax[2][LBX_MAX_TOKENS];
+  float u_inv[2][LBX_MAX_TOKENS];
+  float u_scale[2][LBX_MAX_TOKENS];
+  int u_sq[2][LBX_MAX_TOKENS];
+  __align__(8) uint64_t bar[UT_MAX + 1];
+  uint32_t par[UT_MAX + 1];
+};
 
-  int s = 0;
-  while (s + 1 < p.nseg && (int)blockIdx.x >= p.seg[s + 1].tile0) ++s;
-  const VSeg &sg = p.seg[s];
-  const int row0 = ((int)blockIdx.x - sg.tile0) * 16;
-  const int rows = min(16, sg.rank - row0);  // 8 or 16 (ranks are multiples of 8)
-  const bool rms = p.prologue == LBX_PRO_RMSNORM;
-
-  const int ws = act_ws(p.ncols);
-  uint32_t *wbuf = reinterpret_cast<uint32_t *>(smem_raw);           // 16 x vpitch
-  float *sv2 = reinterpret_cast<float *>(wbuf + 16 * p.vpitch);       // vcap
-  float *snw = sv2 + p.vcap;                                          // vcap (RMSNorm)
-  uint32_t *act = reinterpret_cast<uint32_t *>(snw + (rms ? p.vcap : 0)); // PASS_WORDS x ws
-  float *red = reinterpret_cast<float *>(act + PASS_WORDS * ws);      // [16][16 rows][k]
-
-  // weights of this CTA (sign rows, v2, norm_w, mid) do not depend on the
-  // preceding kernel: start their copies before waiting for it
-  const int vcap = p.vcap;  // leading columns of v2 / norm_w held in shared memory
-  LBX_PROBE(0);
-  if (tid == 0) {
-    mbar_init(&bar, 1);
-    fence_mbar_init();
-    uint32_t bytes = (uint32_t)rows * p.Wv * 4u + (uint32_t)vcap * 4u * (rms ? 2u : 1u) +
-                     (uint32_t)rows * 4u * (sg.mid1 ? 2u : 1u);
-    mbar_arrive_expect_tx(&bar, bytes);
+LBX_DEV void linshm_init(LinShm &sh) {
+  if (threadIdx.x <= UT_MAX) {
+    mbar_init(&sh.bar[threadIdx.x], 1);
+    sh.par[threadIdx.x] = 0;
   }
-  if (tid < VWARPS * LBX_MAX_TOKENS) (&s_ssq[0][0])[tid] = 0.f;
-  if (tid < 2 * LBX_MAX_TOKENS) (&s_zmax[0][0])[tid] = 0;
+  fence_mbar_init();
+  __syncthreads();
+}
+
+// shared-memory regions of a V-stage unit: W (weights, filled by bulk copies
+// that may be issued long before the unit runs) and S (scratch of the run)
+struct VLayout {
+  uint32_t *wbuf;  // 16 x vpitch sign words
+  float *sv2;      // vcap
+  float *snw;      // vcap (RMSNorm prologue)
+  float *smid;     // 2 x 16
+  uint32_t *act;   // PASS_WORDS x ws
+  float *red;      // VWARPS x 16 x k
+};
+
+LBX_DEV VLayout vlayout(const VParams &p, uint8_t *W, uint8_t *S) {
+  VLayout L;
+  const bool rms = p.prologue == LBX_PRO_RMSNORM;
+  L.wbuf = reinterpret_cast<uint32_t *>(W);
+  L.sv2 = reinterpret_cast<float *>(L.wbuf + 16 * p.vpitch);
+  L.snw = L.sv2 + p.vcap;
+  L.smid = L.snw + (rms ? p.vcap : 0);
+  L.act = reinterpret_cast<uint32_t *>(S);
+  L.red = reinterpret_cast<float *>(L.act + PASS_WORDS * act_ws(p.ncols));
+  return L;
+}
+
+LBX_DEV int vseg_of(const VParams &p, int unit) {
+  int s = 0;
+  while (s + 1 < p.nseg && unit >= p.seg[s + 1].tile0) ++s;
+  return s;
+}
+
+// the weights of V-stage unit `unit` (sign rows, v2, norm_w, mid): independent
+// of every activation, so they may be requested before the inputs exist
+LBX_DEV void vstage_issue(const VParams &p, int unit, uint8_t *W, LinShm &sh) {
+  const int tid = threadIdx.x;
+  const VSeg &sg = p.seg[vseg_of(p, unit)];
+  const int row0 = (unit - sg.tile0) * 16;
+  const int rows = min(16, sg.rank - row0);
+  const bool rms = p.prologue == LBX_PRO_RMSNORM;
+  const VLayout L = vlayout(p, W, nullptr);
+  const int vcap = p.vcap;
+  uint64_t *bar = &sh.bar[UT_MAX];
+  if (tid == 0) {
+    const uint32_t bytes = (uint32_t)rows * p.Wv * 4u + (uint32_t)vcap * 4u * (rms ? 2u : 1u) +
+                           (uint32_t)rows * 4u * (sg.mid1 ? 2u : 1u);
+    mbar_arrive_expect_tx(bar, bytes);
+  }
   __syncthreads();
   if (tid < rows)
-    bulk_g2s(wbuf + tid * p.vpitch, sg.v_sign + (int64_t)(row0 + tid) * p.Wv, (uint32_t)p.Wv * 4u,
-             &bar);
+    bulk_g2s(L.wbuf + tid * p.vpitch, sg.v_sign + (int64_t)(row0 + tid) * p.Wv, (uint32_t)p.Wv * 4u, bar);
   else if (tid == 16)
-    bulk_g2s(sv2, sg.v2, (uint32_t)vcap * 4u, &bar);
+    bulk_g2s(L.sv2, sg.v2, (uint32_t)vcap * 4u, bar);
   else if (tid == 17 && rms)
-    bulk_g2s(snw, p.norm_w, (uint32_t)vcap * 4u, &bar);
+    bulk_g2s(L.snw, p.norm_w, (uint32_t)vcap * 4u, bar);
   else if (tid == 18)
-    bulk_g2s(s_mid[0], sg.mid0 + row0, (uint32_t)rows * 4u, &bar);
+    bulk_g2s(L.smid, sg.mid0 + row0, (uint32_t)rows * 4u, bar);
   else if (tid == 19 && sg.mid1)
-    bulk_g2s(s_mid[1], sg.mid1 + row0, (uint32_t)rows * 4u, &bar);
-  pdl_trigger();
-  pdl_wait();
+    bulk_g2s(L.smid + 16, sg.mid1 + row0, (uint32_t)rows * 4u, bar);
+}
+
+// z = mid ⊙ (V_sign · a) for the 16 rows of unit `unit`; returns false (on
+// every thread) if the weight copies did not arrive in time
+template <int NCB>
+LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinShm &sh) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const VSeg &sg = p.seg[vseg_of(p, unit)];
+  const int row0 = (unit - sg.tile0) * 16;
+  const int rows = min(16, sg.rank - row0);
+  const bool rms = p.prologue == LBX_PRO_RMSNORM;
+  const int ws = act_ws(p.ncols);
+  const VLayout L = vlayout(p, W, S);
+  uint32_t *wbuf = L.wbuf, *act = L.act;
+  float *sv2 = L.sv2, *snw = L.snw, *red = L.red;
+  const int vcap = p.vcap;
+  const uint32_t par = sh.par[UT_MAX];
+  if (tid < VWARPS * LBX_MAX_TOKENS) (&sh.v_ssq[0][0])[tid] = 0.f;
+  if (tid < 2 * LBX_MAX_TOKENS) (&sh.v_zmax[0][0])[tid] = 0;
+  __syncthreads();
   LBX_PROBE(1);
 
   // thread t stages columns 8*(t%4)..+8 of word t/4 of each 128-word pass;
   // warp w = one 256-column scale block
-  const int W = tid >> 2, qq = tid & 3;
+  const int Wd = tid >> 2, qq = tid & 3;
   const int hh = qq >> 1;
   const bool low = (qq & 1) == 0;  // my digits are bytes 0,1 (else 2,3) of the slot words
   float tacc[NCB][2];
@@ -266,8 +318,8 @@ __global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_consta
   for (int pass = 0; pass < npass; ++pass) {
     const int pw0 = pass * PASS_WORDS;
     const int pwords = min(PASS_WORDS, p.Wv - pw0);
-    const bool wvalid = W < pwords;
-    const int64_t col = (int64_t)(pw0 + W) * 32 + 8 * qq;
+    const bool wvalid = Wd < pwords;
+    const int64_t col = (int64_t)(pw0 + Wd) * 32 + 8 * qq;
     const bool silu = p.prologue == LBX_PRO_SILU_MUL;
     float hw[8];
     for (int t0 = 0; t0 < p.k; t0 += TBATCH) {
@@ -285,7 +337,7 @@ __global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_consta
       }
       if (t0 == 0) {
         if (pass == 0) {
-          ok = mbar_wait_bounded(&bar, 0, 0x101);
+          ok = __syncthreads_and(mbar_wait_bounded(&sh.bar[UT_MAX], par, 0x101));
           LBX_PROBE(2);
         }
         if (!wvalid) {
@@ -341,37 +393,37 @@ __global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_consta
           split_digits(qv, hi[i], lo[i]);
         }
         // 16-bit halves of the 4 slot words (h, j): bytes = columns j and j+4
-        uint32_t H[2], L[2];
+        uint32_t H[2], Lw[2];
 #pragma unroll
         for (int jp = 0; jp < 2; ++jp) {
           const int j0 = 2 * jp, j1 = 2 * jp + 1;
           H[jp] = ((hi[j0] & 255) | ((hi[j0 + 4] & 255) << 8)) |
                   (((hi[j1] & 255) | ((hi[j1 + 4] & 255) << 8)) << 16);
-          L[jp] = ((lo[j0] & 255) | ((lo[j0 + 4] & 255) << 8)) |
-                  (((lo[j1] & 255) | ((lo[j1 + 4] & 255) << 8)) << 16);
+          Lw[jp] = ((lo[j0] & 255) | ((lo[j0 + 4] & 255) << 8)) |
+                   (((lo[j1] & 255) | ((lo[j1 + 4] & 255) << 8)) << 16);
         }
         const uint32_t PH0 = __shfl_xor_sync(0xffffffffu, H[0], 1);
         const uint32_t PH1 = __shfl_xor_sync(0xffffffffu, H[1], 1);
-        const uint32_t PL0 = __shfl_xor_sync(0xffffffffu, L[0], 1);
-        const uint32_t PL1 = __shfl_xor_sync(0xffffffffu, L[1], 1);
-        uint32_t *aw = act + W * ws + 2 * t;
+        const uint32_t PL0 = __shfl_xor_sync(0xffffffffu, Lw[0], 1);
+        const uint32_t PL1 = __shfl_xor_sync(0xffffffffu, Lw[1], 1);
+        uint32_t *aw = act + Wd * ws + 2 * t;
         if (low) {  // slots j = 0, 1: my half low, partner's high
           aw[(4 * hh + 0) * p.ncols] = (H[0] & 0xFFFFu) | (PH0 << 16);
-          aw[(4 * hh + 0) * p.ncols + 1] = (L[0] & 0xFFFFu) | (PL0 << 16);
+          aw[(4 * hh + 0) * p.ncols + 1] = (Lw[0] & 0xFFFFu) | (PL0 << 16);
           aw[(4 * hh + 1) * p.ncols] = (H[0] >> 16) | (PH0 & 0xFFFF0000u);
-          aw[(4 * hh + 1) * p.ncols + 1] = (L[0] >> 16) | (PL0 & 0xFFFF0000u);
+          aw[(4 * hh + 1) * p.ncols + 1] = (Lw[0] >> 16) | (PL0 & 0xFFFF0000u);
         } else {    // slots j = 2, 3: partner's half low, mine high
           aw[(4 * hh + 2) * p.ncols] = (PH1 & 0xFFFFu) | (H[1] << 16);
-          aw[(4 * hh + 2) * p.ncols + 1] = (PL1 & 0xFFFFu) | (L[1] << 16);
+          aw[(4 * hh + 2) * p.ncols + 1] = (PL1 & 0xFFFFu) | (Lw[1] << 16);
           aw[(4 * hh + 3) * p.ncols] = (PH1 >> 16) | (H[1] & 0xFFFF0000u);
-          aw[(4 * hh + 3) * p.ncols + 1] = (PL1 >> 16) | (L[1] & 0xFFFF0000u);
+          aw[(4 * hh + 3) * p.ncols + 1] = (PL1 >> 16) | (Lw[1] & 0xFFFF0000u);
         }
         sqi = __reduce_add_sync(0xffffffffu, sqi);
         if (rms) sq2 = warp_sum(sq2);
         if (lane == 0) {
-          s_inv[warp][t] = m / QMAX;
-          s_sq[warp][t] = sqi;
-          s_ssq[warp][t] += sq2;
+          sh.v_inv[warp][t] = m / QMAX;
+          sh.v_sq[warp][t] = sqi;
+          sh.v_ssq[warp][t] += sq2;
         }
       }
     }
@@ -390,8 +442,8 @@ __global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_consta
       for (int cb = 0; cb < NCB; ++cb) {
         const int t = cb * 4 + q;
         if (t < p.k) {
-          const int sq = s_sq[warp][t];
-          const float inv = s_inv[warp][t];
+          const int sq = sh.v_sq[warp][t];
+          const float inv = sh.v_inv[warp][t];
           tacc[cb][0] += __int2float_rn(sq + 2 * (256 * acc[cb][0] + acc[cb][1])) * inv;
           tacc[cb][1] += __int2float_rn(sq + 2 * (256 * acc[cb][2] + acc[cb][3])) * inv;
         }
@@ -399,6 +451,9 @@ __global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_consta
     }
     __syncthreads();
   }
+  // the weight barrier completed its phase (or timed out on every thread)
+  if (tid == 0) sh.par[UT_MAX] = par ^ 1u;
+  if (!ok) return false;
   // ---- fixed-order reduction over the 16 warps, then scales
   float *rw = red + warp * 16 * p.k;
 #pragma unroll
@@ -411,7 +466,7 @@ __global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_consta
   }
   __syncthreads();
   LBX_PROBE(4);
-  if (!ok) return;
+  const float *smid = L.smid;
   for (int i = tid; i < rows * p.k; i += VTHREADS) {
     const int rr = i / p.k, t = i - rr * p.k;
     float v = 0.f;
@@ -420,73 +475,88 @@ __global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_consta
     if (rms) {
       float s2 = 0.f;
 #pragma unroll
-      for (int w = 0; w < VWARPS; ++w) s2 += s_ssq[w][t];
+      for (int w = 0; w < VWARPS; ++w) s2 += sh.v_ssq[w][t];
       v *= rsqrtf(s2 / (float)p.K + p.eps);
     }
-    const float z0 = s_mid[0][rr] * v;
+    const float z0 = smid[rr] * v;
     sg.z0[(int64_t)t * sg.rank + row0 + rr] = z0;
-    atomicMax(&s_zmax[0][t], __float_as_int(fabsf(z0)));
+    atomicMax(&sh.v_zmax[0][t], __float_as_int(fabsf(z0)));
     if (sg.z1) {
-      const float z1 = s_mid[1][rr] * v;
+      const float z1 = smid[16 + rr] * v;
       sg.z1[(int64_t)t * sg.rank + row0 + rr] = z1;
-      atomicMax(&s_zmax[1][t], __float_as_int(fabsf(z1)));
+      atomicMax(&sh.v_zmax[1][t], __float_as_int(fabsf(z1)));
     }
   }
   __syncthreads();
+  // this tile's per-token maxima: a slot of its own, no cross-CTA atomics
   if (tid < p.k) {
-    atomicMax(sg.zmax0 + tid, s_zmax[0][tid]);
-    if (sg.z1) atomicMax(sg.zmax1 + tid, s_zmax[1][tid]);
+    const int slot = (unit - sg.tile0) * LBX_MAX_TOKENS + tid;
+    sg.zpart0[slot] = sh.v_zmax[0][tid];
+    if (sg.z1) sg.zpart1[slot] = sh.v_zmax[1][tid];
   }
   LBX_PROBE(5);
+  return true;
+}
+
+template <int NCB>
+__global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_constant__ VParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ LinShm sh;
+  LBX_PROBE(0);
+  linshm_init(sh);
+  uint8_t *W = smem_raw;
+  uint8_t *S = smem_raw + p.w_bytes;
+  vstage_issue(p, blockIdx.x, W, sh);
+  pdl_trigger();
+  pdl_wait();
+  vstage_run<NCB>(p, blockIdx.x, W, S, sh);
 }
 
 // ---------------------------------------------------------------------------
 // U-stage
 // ---------------------------------------------------------------------------
-template <int NCB>
-__global__ void __launch_bounds__(UTHREADS, 2) ustage_kernel(const __grid_constant__ UParams p) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  __shared__ float s_inv[2][LBX_MAX_TOKENS];
-  __shared__ float s_scale[2][LBX_MAX_TOKENS];
-  __shared__ int s_sq[2][LBX_MAX_TOKENS];
-  __shared__ __align__(8) uint64_t bars[UT_MAX];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, q = lane & 3;
-  const int ut = p.ut, nsplit = UWARPS / ut;
-  const int tile = warp % ut, split = warp / ut;
+struct ULayout {
+  uint32_t *wt;   // ut x wtile_words
+  float *su1;     // ut x 48 (u1_0, u1_1, bias)
+  uint32_t *act0, *act1;
+  int *xch;       // [warps][32][2*NCB*4]
+};
 
-  int s = 0;
-  while (s + 1 < p.nseg && (int)blockIdx.x >= p.seg[s + 1].cta0) ++s;
-  const USeg &sg = p.seg[s];
-  const int n0 = ((int)blockIdx.x - sg.cta0) * (16 * ut) + 16 * tile;
-  const bool active = n0 < sg.out;
-
+LBX_DEV ULayout ulayout(const UParams &p, uint8_t *W, uint8_t *S) {
+  ULayout L;
+  L.wt = reinterpret_cast<uint32_t *>(W);
+  L.su1 = reinterpret_cast<float *>(L.wt + p.ut * p.wtile_words);
   const int ws = act_ws(p.ncols);
-  uint32_t *act0 = reinterpret_cast<uint32_t *>(smem_raw);
-  uint32_t *act1 = act0 + p.act_words[0] * ws;
-  int *xch = reinterpret_cast<int *>(act1 + p.act_words[1] * ws);     // [warps][32][2*NCB*4]
-  uint32_t *wt = reinterpret_cast<uint32_t *>(xch + UWARPS * 32 * 8 * NCB);  // ut x wtile_words
-  float *su1 = reinterpret_cast<float *>(wt + ut * p.wtile_words);    // ut x 48 (u1_0, u1_1, bias)
+  L.act0 = reinterpret_cast<uint32_t *>(S);
+  L.act1 = L.act0 + p.act_words[0] * ws;
+  L.xch = reinterpret_cast<int *>(L.act1 + p.act_words[1] * ws);
+  return L;
+}
 
-  uint32_t *mywt0 = wt + tile * p.wtile_words;
+LBX_DEV int useg_of(const UParams &p, int unit) {
+  int s = 0;
+  while (s + 1 < p.nseg && unit >= p.seg[s + 1].cta0) ++s;
+  return s;
+}
+
+LBX_DEV void ustage_issue(const UParams &p, int unit, uint8_t *W, LinShm &sh) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ut = p.ut;
+  const int tile = warp % ut, split = warp / ut;
+  const USeg &sg = p.seg[useg_of(p, unit)];
+  const int n0 = (unit - sg.cta0) * (16 * ut) + 16 * tile;
+  const bool active = n0 < sg.out;
+  const ULayout L = ulayout(p, W, nullptr);
+  uint32_t *mywt0 = L.wt + tile * p.wtile_words;
   uint32_t *mywt1 = mywt0 + 16 * sg.pitch[0] + 4;
-  float *myu1 = su1 + tile * 48;
-  const int r0 = sg.rank[0], r1 = sg.nbr > 1 ? sg.rank[1] : 0;
-
-  LBX_PROBE(10);
-  if (tid < ut) {
-    mbar_init(bars + tid, 1);
-    fence_mbar_init();
-  }
-  if (tid < 2 * LBX_MAX_TOKENS) (&s_sq[0][0])[tid] = 0;
-  __syncthreads();
-  // weights (signs, u1, bias of each tile) do not depend on the preceding
-  // kernel: start their copies before waiting for it
+  float *myu1 = L.su1 + tile * 48;
+  uint64_t *bar = &sh.bar[tile];
+  LBX_PROBE(20);
   if (active && split == 0) {
     uint32_t bytes = 0;
     for (int b = 0; b < sg.nbr; ++b) bytes += 16u * sg.words[b] * 4u + 64u;
     if (sg.bias) bytes += 64u;
-    if (lane == 0) mbar_arrive_expect_tx(bars + tile, bytes);
+    if (lane == 0) mbar_arrive_expect_tx(bar, bytes);
     __syncwarp();
     for (int b = 0; b < sg.nbr; ++b) {
       uint32_t *dst = b == 0 ? mywt0 : mywt1;
@@ -494,69 +564,122 @@ __global__ void __launch_bounds__(UTHREADS, 2) ustage_kernel(const __grid_consta
       if (sg.perrow[b]) {
         if (lane < 16)
           bulk_g2s(dst + lane * sg.pitch[b], src + (int64_t)lane * sg.words[b],
-                   (uint32_t)sg.words[b] * 4u, bars + tile);
+                   (uint32_t)sg.words[b] * 4u, bar);
       } else if (lane == 0) {
-        bulk_g2s(dst, src, 16u * sg.words[b] * 4u, bars + tile);
+        bulk_g2s(dst, src, 16u * sg.words[b] * 4u, bar);
       }
-      if (lane == 16 + b) bulk_g2s(myu1 + 16 * b, sg.u1[b] + n0, 64u, bars + tile);
+      if (lane == 16 + b) bulk_g2s(myu1 + 16 * b, sg.u1[b] + n0, 64u, bar);
     }
-    if (lane == 18 && sg.bias) bulk_g2s(myu1 + 32, sg.bias + n0, 64u, bars + tile);
+    if (lane == 18 && sg.bias) bulk_g2s(myu1 + 32, sg.bias + n0, 64u, bar);
   }
-  pdl_trigger();
-  pdl_wait();
+  LBX_PROBE(21);
+}
+
+template <int NCB>
+LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint8_t *S, LinShm &sh) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int ut = p.ut, nsplit = UWARPS / ut;
+  const int tile = warp % ut, split = warp / ut;
+  const USeg &sg = p.seg[useg_of(p, unit)];
+  const int n0 = (unit - sg.cta0) * (16 * ut) + 16 * tile;
+  const bool active = n0 < sg.out;
+  const int ws = act_ws(p.ncols);
+  const ULayout L = ulayout(p, W, S);
+  uint32_t *act0 = L.act0, *act1 = L.act1;
+  int *xch = L.xch;
+  uint32_t *mywt0 = L.wt + tile * p.wtile_words;
+  uint32_t *mywt1 = mywt0 + 16 * sg.pitch[0] + 4;
+  float *myu1 = L.su1 + tile * 48;
+  const int r0 = sg.rank[0], r1 = sg.nbr > 1 ? sg.rank[1] : 0;
+  const uint32_t par = sh.par[tile];
+  if (tid < 2 * LBX_MAX_TOKENS) (&sh.u_sq[0][0])[tid] = 0;
   LBX_PROBE(11);
 
-  // ---- per-(branch, token) scale from the V-stage maxima, 16-bit digits of z
-  if (tid < 2 * p.k) {
-    const int b = tid / p.k, t = tid - b * p.k;
-    const float m = (b < sg.nbr) ? __int_as_float(__ldcg(sg.zmax[b] + t)) : 0.f;
-    s_inv[b][t] = m / QMAX;
-    s_scale[b][t] = m > 0.f ? QMAX / m : 0.f;
+  // items (t, b, W, slot): each (t, b) segment is a multiple of 32 items, so a
+  // warp's 32 items always share (t, b) and reduce with one redux
+  const int nw0 = 4 * ((sg.words[0] + 3) / 4);
+  const int nw1 = sg.nbr > 1 ? 4 * ((sg.words[1] + 3) / 4) : 0;
+  const int per = (nw0 + nw1) * 8;
+  const int total = p.k * per;
+  constexpr int UB = 2;  // items per thread whose z loads are in flight together
+  float zv[UB][4];
+  auto load_batch = [&](int base0) {
+#pragma unroll
+    for (int ib = 0; ib < UB; ++ib) {
+      const int i = base0 + ib * UTHREADS + lane;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) zv[ib][e] = 0.f;
+      if (base0 + ib * UTHREADS < total) {  // uniform across the warp
+        const int t = i / per, rem = i - t * per;
+        const int b = rem < nw0 * 8 ? 0 : 1;
+        const int rr = b ? rem - nw0 * 8 : rem;
+        const int Wd = rr >> 3, slot = rr & 7;
+        const int hh = slot >> 2, jj = slot & 3;
+        const int r = b ? r1 : r0;
+        const float *zrow = sg.z[b] + (int64_t)t * r;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int pos = 32 * Wd + 16 * hh + jj + 4 * e;
+          if (pos < r) zv[ib][e] = __ldcg(zrow + pos);
+        }
+      }
+    }
+  };
+  // the first batch of z is requested before the scales: both reads share
+  // one L2 round trip
+  load_batch(warp * 32);
+
+  // ---- per-(branch, token) scale from the V tiles' maxima (one warp per
+  // (branch, token); max is exact in any order), 16-bit digits of z
+  for (int bt = warp; bt < 2 * p.k; bt += UWARPS) {
+    const int b = bt / p.k, t = bt - b * p.k;
+    int m = 0;
+    if (b < sg.nbr)
+      for (int j = lane; j < sg.ntile[b]; j += 32) m = max(m, __ldcg(sg.zpart[b] + j * LBX_MAX_TOKENS + t));
+    m = __reduce_max_sync(0xffffffffu, m);
+    if (lane == 0) {
+      const float mf = __int_as_float(m);
+      sh.u_inv[b][t] = mf / QMAX;
+      sh.u_scale[b][t] = mf > 0.f ? QMAX / mf : 0.f;
+    }
   }
   __syncthreads();
   LBX_PROBE(12);
-  {
-    // items (t, b, W, slot): each (t, b) segment is a multiple of 32 items, so a
-    // warp's 32 items always share (t, b) and reduce with one redux
-    const int nw0 = 4 * ((sg.words[0] + 3) / 4);
-    const int nw1 = sg.nbr > 1 ? 4 * ((sg.words[1] + 3) / 4) : 0;
-    const int per = (nw0 + nw1) * 8;
-    const int total = p.k * per;
-    for (int base = warp * 32; base < total; base += UTHREADS) {
+  for (int base0 = warp * 32; base0 < total; base0 += UB * UTHREADS) {
+    if (base0 != warp * 32) load_batch(base0);
+#pragma unroll
+    for (int ib = 0; ib < UB; ++ib) {
+      const int base = base0 + ib * UTHREADS;
+      if (base >= total) break;  // uniform across the warp
       const int i = base + lane;
       const int t = i / per, rem = i - t * per;
       const int b = rem < nw0 * 8 ? 0 : 1;
       const int rr = b ? rem - nw0 * 8 : rem;
-      const int W = rr >> 3, slot = rr & 7;
-      const int hh = slot >> 2, jj = slot & 3;
-      const int r = b ? r1 : r0;
-      const float *zrow = sg.z[b] + (int64_t)t * r;
-      const float sc = s_scale[b][t];
-      float zv[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int pos = 32 * W + 16 * hh + jj + 4 * e;
-        zv[e] = pos < r ? __ldcg(zrow + pos) : 0.f;
-      }
+      const int Wd = rr >> 3, slot = rr & 7;
+      const float sc = sh.u_scale[b][t];
       int hi[4], lo[4], sq = 0;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int qv = __float2int_rn(zv[e] * sc);
+        const int qv = __float2int_rn(zv[ib][e] * sc);
         sq += qv;
         split_digits(qv, hi[e], lo[e]);
       }
-      uint32_t *aw = (b ? act1 : act0) + W * ws + 2 * t;
+      uint32_t *aw = (b ? act1 : act0) + Wd * ws + 2 * t;
       aw[slot * p.ncols] = pack4(hi[0], hi[1], hi[2], hi[3]);
       aw[slot * p.ncols + 1] = pack4(lo[0], lo[1], lo[2], lo[3]);
       sq = __reduce_add_sync(0xffffffffu, sq);
-      if (lane == 0) atomicAdd(&s_sq[b][t], sq);
+      if (lane == 0) atomicAdd(&sh.u_sq[b][t], sq);
     }
   }
   __syncthreads();
 
   LBX_PROBE(13);
   bool ok = true;
-  if (active) ok = mbar_wait_bounded(bars + tile, 0, 0x201);
+  if (active) ok = mbar_wait_bounded(&sh.bar[tile], par, 0x201);
+  ok = __syncthreads_and(ok);
+  // every armed barrier (one per active tile) completed this phase
+  if (tid < ut && (unit - sg.cta0) * (16 * ut) + 16 * tid < sg.out) sh.par[tid] ^= 1u;
   LBX_PROBE(14);
 
   int acc0[NCB][4], acc1[NCB][4];
@@ -602,45 +725,51 @@ __global__ void __launch_bounds__(UTHREADS, 2) ustage_kernel(const __grid_consta
     }
   }
   LBX_PROBE(15);
-  // the last CTA to get here clears the call's bookkeeping words for the next call
-  // (every CTA has read its scales before this point)
-  if (tid == 0) {
-    __threadfence();
-    const unsigned done = atomicAdd(p.ticket, 1u);
-    if (done == gridDim.x - 1) {
-      for (int i = 0; i < p.nzmax; ++i) p.zmax_all[i] = 0;
-      *p.ticket = 0u;
-      __threadfence();
-    }
-  }
-  if (!active || !ok || split != 0) return;
-
+  (void)nunits;
+  if (!ok) return false;
+  if (active && split == 0) {
 #pragma unroll
-  for (int cb = 0; cb < NCB; ++cb) {
-    const int t = cb * 4 + q;
-    if (t >= p.k) continue;
+    for (int cb = 0; cb < NCB; ++cb) {
+      const int t = cb * 4 + q;
+      if (t >= p.k) continue;
 #pragma unroll
-    for (int hrow = 0; hrow < 2; ++hrow) {
-      const int nl = g + 8 * hrow;
-      const int n = n0 + nl;
-      float v = myu1[nl] *
-                (__int2float_rn(s_sq[0][t] + 2 * (256 * acc0[cb][2 * hrow] + acc0[cb][2 * hrow + 1])) *
-                 s_inv[0][t]);
-      if (sg.nbr > 1)
-        v += myu1[16 + nl] *
-             (__int2float_rn(s_sq[1][t] + 2 * (256 * acc1[cb][2 * hrow] + acc1[cb][2 * hrow + 1])) *
-              s_inv[1][t]);
-      if (sg.bias) v += myu1[32 + nl];
-      const int64_t off = (int64_t)t * sg.y_ld + n;
-      if (p.ydt == LBX_F32) {
-        float *y = reinterpret_cast<float *>(sg.y) + off;
-        if (p.epi == LBX_EPI_ADD) v += *y;
-        *y = v;
-      } else {
-        reinterpret_cast<uint16_t *>(sg.y)[off] = f32_to_bf16(v);
+      for (int hrow = 0; hrow < 2; ++hrow) {
+        const int nl = g + 8 * hrow;
+        const int n = n0 + nl;
+        float v = myu1[nl] *
+                  (__int2float_rn(sh.u_sq[0][t] + 2 * (256 * acc0[cb][2 * hrow] + acc0[cb][2 * hrow + 1])) *
+                   sh.u_inv[0][t]);
+        if (sg.nbr > 1)
+          v += myu1[16 + nl] *
+               (__int2float_rn(sh.u_sq[1][t] + 2 * (256 * acc1[cb][2 * hrow] + acc1[cb][2 * hrow + 1])) *
+                sh.u_inv[1][t]);
+        if (sg.bias) v += myu1[32 + nl];
+        const int64_t off = (int64_t)t * sg.y_ld + n;
+        if (p.ydt == LBX_F32) {
+          float *y = reinterpret_cast<float *>(sg.y) + off;
+          if (p.epi == LBX_EPI_ADD) v += *y;
+          *y = v;
+        } else {
+          reinterpret_cast<uint16_t *>(sg.y)[off] = f32_to_bf16(v);
+        }
       }
     }
   }
+  return true;
+}
+
+template <int NCB>
+__global__ void __launch_bounds__(UTHREADS, 2) ustage_kernel(const __grid_constant__ UParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ LinShm sh;
+  LBX_PROBE(10);
+  linshm_init(sh);
+  uint8_t *W = smem_raw;
+  uint8_t *S = smem_raw + p.w_bytes;
+  ustage_issue(p, blockIdx.x, W, sh);
+  pdl_trigger();
+  pdl_wait();
+  ustage_run<NCB>(p, blockIdx.x, gridDim.x, W, S, sh);
 }
 
 // ---------------------------------------------------------------------------
@@ -648,13 +777,19 @@ __global__ void __launch_bounds__(UTHREADS, 2) ustage_kernel(const __grid_consta
 // ---------------------------------------------------------------------------
 constexpr size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
 
-// scratch: [bookkeeping: zmax words + CTA ticket] then z of every (projection, branch)
-constexpr size_t WS_HDR = al256((2 * LBX_MAX_PROJ * LBX_MAX_TOKENS + 1) * sizeof(int));
+// scratch: [header: the grid barrier of a persistent program] then, for every
+// (projection, branch), z [k][rank] and the per-V-tile maxima
+// [ceil(rank/16)][LBX_MAX_TOKENS].  Only the header must be zero when a
+// program first uses the workspace; the rest is written before it is read.
+constexpr size_t WS_GRIDBAR = 0;  // byte offset of the grid barrier words
+constexpr size_t WS_HDR = 256;
 
 static size_t ws_bytes_for(const lbx_proj *projs, int n_proj, int k) {
   size_t tot = WS_HDR;
   for (int i = 0; i < n_proj; ++i)
-    for (int b = 0; b < projs[i].n_branches; ++b) tot += al256((size_t)k * projs[i].br[b].rank * 4);
+    for (int b = 0; b < projs[i].n_branches; ++b)
+      tot += al256((size_t)k * projs[i].br[b].rank * 4) +
+             al256((size_t)((projs[i].br[b].rank + 15) / 16) * LBX_MAX_TOKENS * 4);
   return tot;
 }
 
@@ -688,12 +823,64 @@ static int validate(const lbx_proj *projs, int n_proj) {
   return LBX_OK;
 }
 
-static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, int k, void *ws,
-                     cudaStream_t stream) {
+static int check_args(const lbx_proj *projs, const lbx_linear_args *a) {
+  LBX_CHECK_ARG(a, "args is NULL");
+  int rc = validate(projs, a->n_proj);
+  if (rc) return rc;
+  LBX_CHECK_ARG(a->n_tokens >= 1, "n_tokens must be >= 1");
+  LBX_CHECK_ARG(a->x, "x is NULL");
+  LBX_CHECK_ARG(a->x_dtype == LBX_F32 || a->x_dtype == LBX_BF16, "bad x_dtype");
+  LBX_CHECK_ARG(a->y_dtype == LBX_F32 || a->y_dtype == LBX_BF16, "bad y_dtype");
+  LBX_CHECK_ARG(aligned16(a->x) && (!a->x2 || aligned16(a->x2)), "x/x2 must be 16-byte aligned");
+  LBX_CHECK_ARG(a->prologue >= LBX_PRO_NONE && a->prologue <= LBX_PRO_SILU_MUL, "bad prologue");
+  LBX_CHECK_ARG(a->prologue != LBX_PRO_RMSNORM || (a->norm_w && aligned16(a->norm_w)),
+                "RMSNorm prologue needs a 16-byte aligned norm_w");
+  LBX_CHECK_ARG(a->prologue != LBX_PRO_SILU_MUL || a->x2, "SiLU-mul prologue needs x2");
+  LBX_CHECK_ARG(a->epilogue == LBX_EPI_STORE || (a->epilogue == LBX_EPI_ADD && a->y_dtype == LBX_F32),
+                "bad epilogue (ADD needs fp32 y)");
+  for (int i = 0; i < a->n_proj; ++i) LBX_CHECK_ARG(a->y[i], "y[%d] is NULL", i);
+  return LBX_OK;
+}
+
+// dynamic shared memory the stage kernels may use (after their static
+// shared memory); established once per process, before any graph capture
+static int stage_smem_limits(size_t &vmax, size_t &umax) {
+  static size_t v_ = 0, u_ = 0;
+  if (!v_) {
+    size_t m = 0, vv = (size_t)-1, uu = (size_t)-1;
+    for (auto kk : {vstage_kernel<1>, vstage_kernel<2>, vstage_kernel<4>}) {
+      cudaError_t e = allow_max_smem(kk, &m);
+      if (e != cudaSuccess) return cuda_status(e, "vstage smem attribute");
+      vv = std::min(vv, m);
+    }
+    for (auto kk : {ustage_kernel<1>, ustage_kernel<2>, ustage_kernel<4>}) {
+      cudaError_t e = allow_max_smem(kk, &m);
+      if (e != cudaSuccess) return cuda_status(e, "ustage smem attribute");
+      uu = std::min(uu, m);
+    }
+    v_ = vv;
+    u_ = uu;
+  }
+  vmax = v_;
+  umax = u_;
+  return LBX_OK;
+}
+
+// one batch of k <= LBX_MAX_TOKENS tokens of a linear call, as the parameters
+// of its two stages
+struct LinPrep {
+  VParams vp;
+  UParams up;
+  int ncb, vunits, uunits;
+  size_t v_w, v_s, u_w, u_s;  // weight (W) and scratch (S) shared-memory bytes of each stage
+};
+
+static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0, int k, void *ws,
+                       size_t vmax, size_t umax, LinPrep &P) {
   const int n_proj = a->n_proj;
   const int K = projs[0].in_features;
   const int ncols = 2 * k;
-  // MMA column blocks the launched kernel is instantiated for (1, 2 or 4); every
+  // MMA column blocks the stage code is instantiated for (1, 2 or 4); every
   // size below must use this, not the bare ceil(ncols/8)
   const int ncb_need = (ncols + 7) / 8;
   const int ncb = ncb_need <= 1 ? 1 : ncb_need <= 2 ? 2 : 4;
@@ -702,9 +889,7 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
   const int Wv = K / 32;
   const bool rms = a->prologue == LBX_PRO_RMSNORM;
 
-  // scratch: bookkeeping, then z of every (projection, branch), [k][rank]
-  int *zmax_all = reinterpret_cast<int *>(ws);
-  unsigned *ticket = reinterpret_cast<unsigned *>(zmax_all + 2 * LBX_MAX_PROJ * LBX_MAX_TOKENS);
+  // scratch: header, then z and the per-tile maxima of every (projection, branch)
   float *zp[LBX_MAX_PROJ][2] = {};
   int *zm[LBX_MAX_PROJ][2] = {};
   {
@@ -712,13 +897,15 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
     for (int i = 0; i < n_proj; ++i)
       for (int b = 0; b < projs[i].n_branches; ++b) {
         zp[i][b] = reinterpret_cast<float *>(w);
-        zm[i][b] = zmax_all + (2 * i + b) * LBX_MAX_TOKENS;
         w += al256((size_t)k * projs[i].br[b].rank * 4);
+        zm[i][b] = reinterpret_cast<int *>(w);
+        w += al256((size_t)((projs[i].br[b].rank + 15) / 16) * LBX_MAX_TOKENS * 4);
       }
   }
 
   // ---------------- V-stage
-  VParams vp = {};
+  VParams &vp = P.vp;
+  vp = VParams{};
   vp.K = K;
   vp.Wv = Wv;
   vp.vpitch = row_pitch(Wv);
@@ -741,22 +928,26 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
       sg.v2 = pr.br[b].v2;
       sg.mid0 = pr.br[b].mid;
       sg.z0 = zp[i][b];
-      sg.zmax0 = zm[i][b];
+      sg.zpart0 = zm[i][b];
       sg.rank = pr.br[b].rank;
       if (b == 0 && pr.n_branches == 2 && !pr.br[1].v_sign) {
         sg.mid1 = pr.br[1].mid;
         sg.z1 = zp[i][1];
-        sg.zmax1 = zm[i][1];
+        sg.zpart1 = zm[i][1];
       }
       sg.tile0 = vtiles;
       vtiles += (sg.rank + 15) / 16;
     }
   }
-  const size_t vsmem = (size_t)16 * vp.vpitch * 4 + (size_t)vp.vcap * 4 * (rms ? 2 : 1) +
-                       (size_t)PASS_WORDS * act_ws(ncols) * 4 + (size_t)VWARPS * 16 * k * 4;
+  P.v_w = al256((size_t)16 * vp.vpitch * 4 + (size_t)vp.vcap * 4 * (rms ? 2 : 1) + 32 * 4);
+  P.v_s = (size_t)PASS_WORDS * act_ws(ncols) * 4 + (size_t)VWARPS * 16 * k * 4;
+  vp.w_bytes = (int)P.v_w;
+  LBX_CHECK_SUP(P.v_w + P.v_s <= vmax, "V-stage needs %zu bytes of shared memory (max %zu)",
+                P.v_w + P.v_s, vmax);
 
   // ---------------- U-stage
-  UParams up = {};
+  UParams &up = P.up;
+  up = UParams{};
   up.k = k;
   up.ncols = ncols;
   up.ydt = a->y_dtype;
@@ -776,7 +967,8 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
       sg.u_sign[b] = pr.br[b].u_sign;
       sg.u1[b] = pr.br[b].u1;
       sg.z[b] = zp[i][b];
-      sg.zmax[b] = zm[i][b];
+      sg.zpart[b] = zm[i][b];
+      sg.ntile[b] = (pr.br[b].rank + 15) / 16;
       sg.rank[b] = pr.br[b].rank;
       sg.words[b] = (pr.br[b].rank + 31) / 32;
       sg.perrow[b] = (sg.words[b] % 4) == 0;
@@ -790,55 +982,46 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
   up.act_words[0] = maxw[0];
   up.act_words[1] = maxw[1];
   up.wtile_words = (maxtile + 3) & ~3;
-  up.zmax_all = zmax_all;
-  up.nzmax = 2 * LBX_MAX_PROJ * LBX_MAX_TOKENS;
-  up.ticket = ticket;
-
-  cudaError_t e;
-  // once per process, before any graph capture
-  static size_t vmax = 0, umax = 0;
-  if (!vmax) {
-    size_t m = 0;
-    size_t v_ = (size_t)-1, u_ = (size_t)-1;
-    for (auto kk : {vstage_kernel<1>, vstage_kernel<2>, vstage_kernel<4>}) {
-      e = allow_max_smem(kk, &m);
-      if (e != cudaSuccess) return cuda_status(e, "vstage smem attribute");
-      v_ = std::min(v_, m);
-    }
-    for (auto kk : {ustage_kernel<1>, ustage_kernel<2>, ustage_kernel<4>}) {
-      e = allow_max_smem(kk, &m);
-      if (e != cudaSuccess) return cuda_status(e, "ustage smem attribute");
-      u_ = std::min(u_, m);
-    }
-    umax = u_;
-    vmax = v_;
-  }
-  LBX_CHECK_SUP(vsmem <= vmax, "V-stage needs %zu bytes of shared memory (max %zu)", vsmem, vmax);
   // row tiles per CTA: enough CTAs to cover the SMs, within shared memory; the
   // remaining warps of a CTA split the ranks of its tiles
   int ut = UT_MAX;
   while (ut > 1 && tiles / ut < 120) ut >>= 1;
-  size_t usmem = 0;
+  const size_t u_s = (size_t)(maxw[0] + maxw[1]) * act_ws(ncols) * 4 + (size_t)UWARPS * 32 * 8 * ncb * 4;
   for (; ut >= 1; ut >>= 1) {
-    usmem = (size_t)(maxw[0] + maxw[1]) * act_ws(ncols) * 4 + (size_t)UWARPS * 32 * 8 * ncb * 4 +
-            (size_t)ut * up.wtile_words * 4 + (size_t)ut * 48 * 4;
-    if (usmem <= umax) break;
+    const size_t u_w = al256((size_t)ut * up.wtile_words * 4 + (size_t)ut * 48 * 4);
+    if (u_w + u_s <= umax) break;
   }
   LBX_CHECK_SUP(ut >= 1, "U-stage needs too much shared memory (rank too large for k=%d)", k);
   up.ut = ut;
+  P.u_w = al256((size_t)ut * up.wtile_words * 4 + (size_t)ut * 48 * 4);
+  P.u_s = u_s;
+  up.w_bytes = (int)P.u_w;
   int ctas = 0;
   for (int i = 0; i < n_proj; ++i) {
     up.seg[i].cta0 = ctas;
     ctas += (projs[i].out_features + 16 * ut - 1) / (16 * ut);
   }
   up.nseg = n_proj;
+  P.ncb = ncb;
+  P.vunits = vtiles;
+  P.uunits = ctas;
+  return LBX_OK;
+}
 
+static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, int k, void *ws,
+                     cudaStream_t stream) {
+  size_t vmax = 0, umax = 0;
+  int rc = stage_smem_limits(vmax, umax);
+  if (rc) return rc;
+  LinPrep P;
+  rc = prep_linear(projs, a, tok0, k, ws, vmax, umax, P);
+  if (rc) return rc;
   const bool pdl = a->use_pdl != 0;
-  auto vk = ncb == 1 ? vstage_kernel<1> : ncb == 2 ? vstage_kernel<2> : vstage_kernel<4>;
-  auto uk = ncb == 1 ? ustage_kernel<1> : ncb == 2 ? ustage_kernel<2> : ustage_kernel<4>;
-  e = launch(vk, dim3(vtiles), dim3(VTHREADS), vsmem, stream, pdl, vp);
+  auto vk = P.ncb == 1 ? vstage_kernel<1> : P.ncb == 2 ? vstage_kernel<2> : vstage_kernel<4>;
+  auto uk = P.ncb == 1 ? ustage_kernel<1> : P.ncb == 2 ? ustage_kernel<2> : ustage_kernel<4>;
+  cudaError_t e = launch(vk, dim3(P.vunits), dim3(VTHREADS), P.v_w + P.v_s, stream, pdl, P.vp);
   if (e != cudaSuccess) return cuda_status(e, "vstage launch");
-  e = launch(uk, dim3(ctas), dim3(UTHREADS), usmem, stream, pdl, up);
+  e = launch(uk, dim3(P.uunits), dim3(UTHREADS), P.u_w + P.u_s, stream, pdl, P.up);
   if (e != cudaSuccess) return cuda_status(e, "ustage launch");
   return LBX_OK;
 }
@@ -855,21 +1038,8 @@ extern "C" size_t lbx_linear_workspace_size(const lbx_proj *projs, int32_t n_pro
 extern "C" int lbx_linear_verify(const lbx_proj *projs, const lbx_linear_args *a, void *ws,
                                  size_t ws_bytes, cudaStream_t stream) {
   using namespace lbx;
-  LBX_CHECK_ARG(a, "args is NULL");
-  int rc = validate(projs, a->n_proj);
+  int rc = check_args(projs, a);
   if (rc) return rc;
-  LBX_CHECK_ARG(a->n_tokens >= 1, "n_tokens must be >= 1");
-  LBX_CHECK_ARG(a->x, "x is NULL");
-  LBX_CHECK_ARG(a->x_dtype == LBX_F32 || a->x_dtype == LBX_BF16, "bad x_dtype");
-  LBX_CHECK_ARG(a->y_dtype == LBX_F32 || a->y_dtype == LBX_BF16, "bad y_dtype");
-  LBX_CHECK_ARG(aligned16(a->x) && (!a->x2 || aligned16(a->x2)), "x/x2 must be 16-byte aligned");
-  LBX_CHECK_ARG(a->prologue >= LBX_PRO_NONE && a->prologue <= LBX_PRO_SILU_MUL, "bad prologue");
-  LBX_CHECK_ARG(a->prologue != LBX_PRO_RMSNORM || (a->norm_w && aligned16(a->norm_w)),
-                "RMSNorm prologue needs a 16-byte aligned norm_w");
-  LBX_CHECK_ARG(a->prologue != LBX_PRO_SILU_MUL || a->x2, "SiLU-mul prologue needs x2");
-  LBX_CHECK_ARG(a->epilogue == LBX_EPI_STORE || (a->epilogue == LBX_EPI_ADD && a->y_dtype == LBX_F32),
-                "bad epilogue (ADD needs fp32 y)");
-  for (int i = 0; i < a->n_proj; ++i) LBX_CHECK_ARG(a->y[i], "y[%d] is NULL", i);
   const size_t need = lbx_linear_workspace_size(projs, a->n_proj, a->n_tokens);
   LBX_CHECK_ARG(ws && ws_bytes >= need, "workspace too small (%zu < %zu)", ws_bytes, need);
   for (int t0 = 0; t0 < a->n_tokens; t0 += LBX_MAX_TOKENS) {

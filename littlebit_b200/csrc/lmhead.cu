@@ -33,32 +33,30 @@ LBX_DEV unsigned long long argmax_key(float v, int idx) {
   return ((unsigned long long)u << 32) | (0xFFFFFFFFu - (uint32_t)idx);
 }
 
+// one unit of the vocabulary stream (units interleave rows warp by warp);
+// S holds the NT normalised hidden states
 template <int NT>
-__global__ void __launch_bounds__(LM_WARPS * 32) lmhead_kernel(const __grid_constant__ LmParams p) {
-  extern __shared__ __align__(16) float xs[];  // NT x hidden
+LBX_DEV void lmhead_unit(const LmParams &p, int unit, int nunits, float *xs) {
   __shared__ float s_rs[LM_TOK];
   __shared__ unsigned long long s_best[LM_WARPS][LM_TOK];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int H = p.hidden;
 
-  pdl_trigger();
-  pdl_wait();
-
-  // normalised hidden states (RMSNorm recomputed per CTA: n*hidden L2 reads)
+  // normalised hidden states (RMSNorm recomputed per unit: n*hidden L2 reads)
   for (int t = warp; t < NT; t += LM_WARPS) {
     float ss = 0.f;
     if (p.norm_w && t < p.n)
       for (int h = lane; h < H; h += 32) {
-        const float v = p.x[(int64_t)t * H + h];
+        const float v = __ldcg(p.x + (int64_t)t * H + h);
         ss += v * v;
       }
     ss = warp_sum(ss);
     if (lane == 0) s_rs[t] = p.norm_w ? 1.0f / sqrtf(ss / (float)H + p.eps) : 1.0f;
   }
   __syncthreads();
-  for (int e = tid; e < NT * H; e += blockDim.x) {
+  for (int e = tid; e < NT * H; e += LM_WARPS * 32) {
     const int t = e / H, h = e - t * H;
-    float v = t < p.n ? p.x[(int64_t)t * H + h] * s_rs[t] : 0.f;
+    float v = t < p.n ? __ldcg(p.x + (int64_t)t * H + h) * s_rs[t] : 0.f;
     if (p.norm_w) v *= p.norm_w[h];
     xs[e] = v;
   }
@@ -69,8 +67,8 @@ __global__ void __launch_bounds__(LM_WARPS * 32) lmhead_kernel(const __grid_cons
   for (int t = 0; t < NT; ++t) best[t] = 0ull;
 
   const int nvec = H / 256;  // 16-byte vectors per lane per row
-  const int gw = blockIdx.x * LM_WARPS + warp;
-  const int tw = gridDim.x * LM_WARPS;
+  const int gw = unit * LM_WARPS + warp;
+  const int tw = nunits * LM_WARPS;
   for (int row = gw; row < p.vocab; row += tw) {
     const uint4 *wr = reinterpret_cast<const uint4 *>(p.w + (int64_t)row * H);
     float acc[NT];
@@ -123,7 +121,29 @@ __global__ void __launch_bounds__(LM_WARPS * 32) lmhead_kernel(const __grid_cons
   if (tid < NT && p.best) {
     unsigned long long b = 0ull;
     for (int w = 0; w < LM_WARPS; ++w) b = s_best[w][tid] > b ? s_best[w][tid] : b;
-    p.best[(int64_t)blockIdx.x * LM_TOK + tid] = b;
+    p.best[(int64_t)unit * LM_TOK + tid] = b;
+  }
+  __syncthreads();
+}
+
+template <int NT>
+__global__ void __launch_bounds__(LM_WARPS * 32) lmhead_kernel(const __grid_constant__ LmParams p) {
+  extern __shared__ __align__(16) float xs[];  // NT x hidden
+  pdl_trigger();
+  pdl_wait();
+  lmhead_unit<NT>(p, blockIdx.x, gridDim.x, xs);
+}
+
+// per-unit winners -> token ids (lowest index among equal maxima)
+LBX_DEV void argmax_unit(const unsigned long long *best, int nblocks, int n, int64_t *out) {
+  const int t = threadIdx.x;
+  if (t < n) {
+    unsigned long long b = 0ull;
+    for (int i = 0; i < nblocks; ++i) {
+      const unsigned long long v = __ldcg(best + (int64_t)i * LM_TOK + t);
+      b = v > b ? v : b;
+    }
+    out[t] = (int64_t)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull));
   }
 }
 
@@ -131,11 +151,7 @@ __global__ void argmax_final_kernel(const unsigned long long *best, int nblocks,
                                     int64_t *out) {
   pdl_trigger();
   pdl_wait();
-  const int t = threadIdx.x;
-  if (t >= n) return;
-  unsigned long long b = 0ull;
-  for (int i = 0; i < nblocks; ++i) b = best[(int64_t)i * LM_TOK + t] > b ? best[(int64_t)i * LM_TOK + t] : b;
-  out[t] = (int64_t)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull));
+  argmax_unit(best, nblocks, n, out);
 }
 
 static int lm_blocks() {

@@ -65,6 +65,7 @@ def _branch0_view(dec: LittleBitDecoder, max_seq: int) -> LittleBitDecoder:
     its own KV cache and workspace)."""
     v = LittleBitDecoder.__new__(LittleBitDecoder)
     v.shape, v.device, v.max_seq, v.use_pdl = dec.shape, dec.device, max_seq, dec.use_pdl
+    v.exec_mode = getattr(dec, "exec_mode", L.LBX_EXEC_AUTO)
     v.embed, v.lm_head, v.final_norm = dec.embed, dec.lm_head, dec.final_norm
     v.layers = []
     for ly in dec.layers:

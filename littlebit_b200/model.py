@@ -104,11 +104,16 @@ class LittleBitDecoder:
 
     def __init__(self, shape: DecoderShape, state: Dict[str, torch.Tensor], device="cuda",
                  max_seq: int = 4096, include_residual: bool = True, use_pdl: bool = True,
-                 lm_head: Optional[torch.Tensor] = None, embed: Optional[torch.Tensor] = None):
+                 lm_head: Optional[torch.Tensor] = None, embed: Optional[torch.Tensor] = None,
+                 exec_mode: int = L.LBX_EXEC_AUTO):
+        """``exec_mode``: LBX_EXEC_AUTO / LBX_EXEC_KERNELS launch one grid per
+        op; LBX_EXEC_PROGRAM runs a step of up to 16 tokens as one persistent
+        cooperative program (same numerics)."""
         self.shape = shape
         self.device = torch.device(device)
         self.max_seq = int(max_seq)
         self.use_pdl = use_pdl
+        self.exec_mode = exec_mode
         dev = self.device
         H = shape.hidden_size
         emb = embed if embed is not None else state["model.embed_tokens.weight"]
@@ -168,6 +173,7 @@ class LittleBitDecoder:
         m.rope_theta = s.rope_theta
         m.attn_scale = 1.0 / math.sqrt(s.head_dim)
         m.use_pdl = 1 if self.use_pdl else 0
+        m.exec_mode = int(getattr(self, "exec_mode", L.LBX_EXEC_AUTO))
         m.embed = _p(self.embed)
         m.final_norm = _p(self.final_norm)
         m.lm_head = _p(self.lm_head)

@@ -215,6 +215,27 @@ def projs_array(projs: Sequence[PackedLinear]):
     return arr
 
 
+def linear_chain(layers: Sequence[PackedLinear], acts: Sequence[torch.Tensor],
+                 ws: Optional[torch.Tensor] = None, arr=None, ptrs=None) -> None:
+    """acts[i+1] = layers[i](acts[i]) for every layer, as one persistent program
+    (lbx_linear_chain).  All activations [k, features] share one dtype."""
+    n = len(layers)
+    if len(acts) != n + 1:
+        raise ValueError("need len(layers) + 1 activation buffers")
+    for i, t in enumerate(acts):
+        _cuda(f"acts[{i}]", t)
+    k = acts[0].shape[0]
+    if arr is None:
+        arr = projs_array(layers)
+    if ptrs is None:
+        ptrs = (ctypes.c_void_p * (n + 1))(*[t.data_ptr() for t in acts])
+    need = int(lib().lbx_linear_chain_workspace_size(arr, n, k))
+    if ws is None:
+        ws = workspace(acts[0].device, "chain").get(need)
+    L.check(lib().lbx_linear_chain(arr, n, k, _dt(acts[0]), ptrs, _p(ws), ws.numel(),
+                                   _stream(acts[0].device)), "linear_chain")
+
+
 def linear_workspace_bytes(projs: Sequence[PackedLinear], n_tokens: int) -> int:
     return int(lib().lbx_linear_workspace_size(projs_array(projs), len(projs), n_tokens))
 

@@ -119,3 +119,38 @@ def test_tree_mask_matches_path_decode(tiny, tree):
         m2.forward_tokens(prompt, 0)
         ref = m2.forward_tokens(nodes[path], P)["logits"][-1].cpu()
         assert torch.equal(lt[i], ref), (i, float((lt[i] - ref).abs().max()))
+
+
+@pytest.mark.parametrize("shared", [False, True])
+def test_program_matches_kernel_path_bitwise(tiny, shared):
+    """The persistent program (one cooperative launch per step) computes the same
+    bits as one grid per op: prefill chunks, single-token steps, a tree step."""
+    from littlebit_b200 import _lib as L
+    from littlebit_b200.model import LittleBitDecoder, synthetic_runtime_state
+    from littlebit_b200.tree_utils import generate_tree_buffers
+
+    shape, st = tiny
+    if shared:
+        st = synthetic_runtime_state(shape, {k: [v[0], v[0]] for k, v in TINY_RANKS.items()}, seed=6,
+                                     shared_residual=True, unit_gain=True)
+    mk = LittleBitDecoder(shape, st, max_seq=256, exec_mode=L.LBX_EXEC_KERNELS)
+    mp = LittleBitDecoder(shape, st, max_seq=256, exec_mode=L.LBX_EXEC_PROGRAM)
+    ids = torch.randint(0, shape.vocab_size, (80,), generator=torch.Generator().manual_seed(8))
+    for a, b in [(0, 16), (16, 25), (25, 26), (26, 27), (27, 35), (35, 36)] + [(t, t + 1) for t in range(60, 66)]:
+        if a == 60:  # jump over slots 36..59 (a prefix past one 64-key chunk)
+            for m in (mk, mp):
+                m.forward_tokens(ids[36:60], 36, want_logits=False, want_argmax=False, want_hidden=True)
+        ok = mk.forward_tokens(ids[a:b], a, want_hidden=True)
+        op = mp.forward_tokens(ids[a:b], a, want_hidden=True)
+        assert torch.equal(ok["logits"], op["logits"]), (a, b)
+        assert torch.equal(ok["argmax"], op["argmax"]), (a, b)
+        assert torch.equal(ok["hidden"], op["hidden"]), (a, b)
+    for lk, lp in zip(mk.k_cache + mk.v_cache, mp.k_cache + mp.v_cache):
+        assert torch.equal(lk[:, :66], lp[:, :66])
+    tb = generate_tree_buffers([[0], [1], [0, 0], [0, 1], [1, 0], [0, 0, 0]], device="cpu")
+    T = tb["tree_len"]
+    mask = tb["tree_attn_mask"][0, 0]
+    tmask = [int(sum(1 << j for j in range(T) if mask[i, j])) for i in range(T)]
+    pos = 66 + tb["tree_position_ids"]
+    outs = [m.forward_tokens(ids[:T], 66, pos=pos, tree_mask=tmask) for m in (mk, mp)]
+    assert torch.equal(outs[0]["logits"], outs[1]["logits"])

@@ -193,3 +193,27 @@ def test_c2_k16(ops):
     assert_linear_close(y.numpy(), _ref(x.float(), brs, 4096, 4096))
     y1 = ops.lb_linear(lay, x[5:6].to(DEV)).cpu()
     assert torch.equal(y1[0], y[5])
+
+
+def test_linear_chain_program_matches_layer_calls():
+    """lbx_linear_chain (all layers in one persistent program) equals calling
+    lbx_linear layer by layer, bit for bit, for k = 1, 5 and 12 bf16 tokens."""
+    from littlebit_b200 import ops, synthetic
+
+    g = torch.Generator().manual_seed(77)
+    layers = []
+    for i in range(6):
+        ranks = [208, 1840] if i % 2 == 0 else [96]
+        layers.append(synthetic.to_packed_linear(4096, 4096, synthetic.layer(4096, 4096, ranks, g), "cuda"))
+    for k in (1, 5, 12):
+        x = torch.randn(k, 4096, generator=g).bfloat16().cuda()
+        acts = [x] + [torch.empty(k, 4096, dtype=torch.bfloat16, device="cuda") for _ in layers]
+        ops.linear_chain(layers, acts)
+        ref = x
+        for lay in layers:
+            y = torch.empty(k, 4096, dtype=torch.bfloat16, device="cuda")
+            ops.linear_group([lay], ref, [y])
+            ref = y
+        torch.cuda.synchronize()
+        assert torch.equal(acts[-1], ref), k
+        assert ops.device_error() == 0
