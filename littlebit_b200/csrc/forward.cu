@@ -433,9 +433,9 @@ static int forward_program(const lbx_model *m, const int64_t *tokens, int32_t n,
         }
       }
     }
-    LBX_CHECK_SUP(((B.wmax + 255) & ~(size_t)255) + B.smax <= budget,
+    LBX_CHECK_SUP(((B.smax + 255) & ~(size_t)255) + B.wmax <= budget,
                   "the step program needs %zu bytes of shared memory (max %zu)",
-                  ((B.wmax + 255) & ~(size_t)255) + B.smax, budget);
+                  ((B.smax + 255) & ~(size_t)255) + B.wmax, budget);
     rc = finish_program(key, B, stream, P);
     if (rc) return rc;
   }

@@ -58,8 +58,8 @@ struct VSeg {
   const float *mid1;     // [rank] (shared-V residual) or nullptr
   float *z0;             // [k][rank]
   float *z1;             // [k][rank] or nullptr
-  int *zpart0;           // [tiles of this segment][LBX_MAX_TOKENS] max |z0| of each tile (float bits)
-  int *zpart1;           // same for the shared-V residual, or nullptr
+  int *zmax0;            // [k] running max |z0| (float bits), zero before the call
+  int *zmax1;            // [k] or nullptr
   int rank;
   int tile0;             // first CTA (16-row tile) of this segment
 };
@@ -75,15 +75,14 @@ struct VParams {
   const void *x;
   const void *x2;
   const float *norm_w;
-  int w_bytes;           // shared-memory weight region of a standalone launch
+  int s_bytes;           // shared-memory scratch region of a standalone launch (weights follow)
 };
 
 struct USeg {
   const int32_t *u_sign[2];
   const float *u1[2];
   const float *z[2];     // [k][rank] from the V-stage
-  const int *zpart[2];   // per-V-tile maxima of |z| (float bits), [ntile][LBX_MAX_TOKENS]
-  int ntile[2];          // V tiles of each branch's latent
+  const int *zmax[2];    // [k] max |z| per token (float bits) from the V-stage
   int rank[2];
   int words[2];   // ceil(rank/32)
   int pitch[2];   // smem row pitch (words)
@@ -103,7 +102,10 @@ struct UParams {
   int ut;             // row tiles per CTA (warps split the ranks 16/ut ways)
   int act_words[2];   // max over projections of 4*ceil(words/4)
   int wtile_words;    // per-tile weight region (words)
-  int w_bytes;        // shared-memory weight region of a standalone launch
+  int *zmax_all;      // all zmax words of this call (reset by the last unit)
+  int nzmax;
+  unsigned *ticket;   // unit completion counter (zero before and after the call)
+  int s_bytes;        // shared-memory scratch region of a standalone launch (weights follow)
 };
 
 // ---------------------------------------------------------------------------
@@ -221,8 +223,8 @@ LBX_DEV void linshm_init(LinShm &sh) {
   if (threadIdx.x <= UT_MAX) {
     mbar_init(&sh.bar[threadIdx.x], 1);
     sh.par[threadIdx.x] = 0;
+    fence_mbar_init();
   }
-  fence_mbar_init();
   __syncthreads();
 }
 
@@ -287,7 +289,7 @@ LBX_DEV void vstage_issue(const VParams &p, int unit, uint8_t *W, LinShm &sh) {
 // z = mid ⊙ (V_sign · a) for the 16 rows of unit `unit`; returns false (on
 // every thread) if the weight copies did not arrive in time
 template <int NCB>
-LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinShm &sh) {
+LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinShm &sh, bool zero = true) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, q = lane & 3;
   const VSeg &sg = p.seg[vseg_of(p, unit)];
@@ -300,9 +302,11 @@ LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinS
   float *sv2 = L.sv2, *snw = L.snw, *red = L.red;
   const int vcap = p.vcap;
   const uint32_t par = sh.par[UT_MAX];
-  if (tid < VWARPS * LBX_MAX_TOKENS) (&sh.v_ssq[0][0])[tid] = 0.f;
-  if (tid < 2 * LBX_MAX_TOKENS) (&sh.v_zmax[0][0])[tid] = 0;
-  __syncthreads();
+  if (zero) {  // per-unit scratch (standalone kernels clear it before their wait)
+    if (tid < VWARPS * LBX_MAX_TOKENS) (&sh.v_ssq[0][0])[tid] = 0.f;
+    if (tid < 2 * LBX_MAX_TOKENS) (&sh.v_zmax[0][0])[tid] = 0;
+    __syncthreads();
+  }
   LBX_PROBE(1);
 
   // thread t stages columns 8*(t%4)..+8 of word t/4 of each 128-word pass;
@@ -335,6 +339,7 @@ LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinS
           for (int i = 0; i < 8; ++i) xv[j][i] = uv[j][i] = 0.f;
         }
       }
+
       if (t0 == 0) {
         if (pass == 0) {
           ok = __syncthreads_and(mbar_wait_bounded(&sh.bar[UT_MAX], par, 0x101));
@@ -488,11 +493,9 @@ LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinS
     }
   }
   __syncthreads();
-  // this tile's per-token maxima: a slot of its own, no cross-CTA atomics
-  if (tid < p.k) {
-    const int slot = (unit - sg.tile0) * LBX_MAX_TOKENS + tid;
-    sg.zpart0[slot] = sh.v_zmax[0][tid];
-    if (sg.z1) sg.zpart1[slot] = sh.v_zmax[1][tid];
+  if (tid < p.k) {  // reductions without a returned value: no round trip
+    atomicMax(sg.zmax0 + tid, sh.v_zmax[0][tid]);
+    if (sg.z1) atomicMax(sg.zmax1 + tid, sh.v_zmax[1][tid]);
   }
   LBX_PROBE(5);
   return true;
@@ -503,13 +506,16 @@ __global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_consta
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ LinShm sh;
   LBX_PROBE(0);
-  linshm_init(sh);
-  uint8_t *W = smem_raw;
-  uint8_t *S = smem_raw + p.w_bytes;
+  if (threadIdx.x < VWARPS * LBX_MAX_TOKENS) (&sh.v_ssq[0][0])[threadIdx.x] = 0.f;
+  if (threadIdx.x < 2 * LBX_MAX_TOKENS) (&sh.v_zmax[0][0])[threadIdx.x] = 0;
+  linshm_init(sh);  // (ends with a CTA barrier)
+  // scratch first, weights after: measured faster than the reverse order
+  uint8_t *S = smem_raw;
+  uint8_t *W = smem_raw + p.s_bytes;
   vstage_issue(p, blockIdx.x, W, sh);
   pdl_trigger();
   pdl_wait();
-  vstage_run<NCB>(p, blockIdx.x, W, S, sh);
+  vstage_run<NCB>(p, blockIdx.x, W, S, sh, false);
 }
 
 // ---------------------------------------------------------------------------
@@ -551,7 +557,6 @@ LBX_DEV void ustage_issue(const UParams &p, int unit, uint8_t *W, LinShm &sh) {
   uint32_t *mywt1 = mywt0 + 16 * sg.pitch[0] + 4;
   float *myu1 = L.su1 + tile * 48;
   uint64_t *bar = &sh.bar[tile];
-  LBX_PROBE(20);
   if (active && split == 0) {
     uint32_t bytes = 0;
     for (int b = 0; b < sg.nbr; ++b) bytes += 16u * sg.words[b] * 4u + 64u;
@@ -572,11 +577,11 @@ LBX_DEV void ustage_issue(const UParams &p, int unit, uint8_t *W, LinShm &sh) {
     }
     if (lane == 18 && sg.bias) bulk_g2s(myu1 + 32, sg.bias + n0, 64u, bar);
   }
-  LBX_PROBE(21);
 }
 
 template <int NCB>
-LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint8_t *S, LinShm &sh) {
+LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint8_t *S, LinShm &sh,
+                        bool zero = true) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, q = lane & 3;
   const int ut = p.ut, nsplit = UWARPS / ut;
@@ -593,7 +598,7 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
   float *myu1 = L.su1 + tile * 48;
   const int r0 = sg.rank[0], r1 = sg.nbr > 1 ? sg.rank[1] : 0;
   const uint32_t par = sh.par[tile];
-  if (tid < 2 * LBX_MAX_TOKENS) (&sh.u_sq[0][0])[tid] = 0;
+  if (zero && tid < 2 * LBX_MAX_TOKENS) (&sh.u_sq[0][0])[tid] = 0;  // ordered by the CTA barrier below
   LBX_PROBE(11);
 
   // items (t, b, W, slot): each (t, b) segment is a multiple of 32 items, so a
@@ -603,13 +608,13 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
   const int per = (nw0 + nw1) * 8;
   const int total = p.k * per;
   constexpr int UB = 2;  // items per thread whose z loads are in flight together
-  float zv[UB][4];
-  auto load_batch = [&](int base0) {
+  float zv[UB][4], zn[UB][4];
+  auto load_batch = [&](int base0, float (&zd)[UB][4]) {
 #pragma unroll
     for (int ib = 0; ib < UB; ++ib) {
       const int i = base0 + ib * UTHREADS + lane;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) zv[ib][e] = 0.f;
+      for (int e = 0; e < 4; ++e) zd[ib][e] = 0.f;
       if (base0 + ib * UTHREADS < total) {  // uniform across the warp
         const int t = i / per, rem = i - t * per;
         const int b = rem < nw0 * 8 ? 0 : 1;
@@ -621,33 +626,28 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int pos = 32 * Wd + 16 * hh + jj + 4 * e;
-          if (pos < r) zv[ib][e] = __ldcg(zrow + pos);
+          if (pos < r) zd[ib][e] = __ldcg(zrow + pos);
         }
       }
     }
   };
   // the first batch of z is requested before the scales: both reads share
   // one L2 round trip
-  load_batch(warp * 32);
+  load_batch(warp * 32, zv);
 
-  // ---- per-(branch, token) scale from the V tiles' maxima (one warp per
-  // (branch, token); max is exact in any order), 16-bit digits of z
-  for (int bt = warp; bt < 2 * p.k; bt += UWARPS) {
-    const int b = bt / p.k, t = bt - b * p.k;
-    int m = 0;
-    if (b < sg.nbr)
-      for (int j = lane; j < sg.ntile[b]; j += 32) m = max(m, __ldcg(sg.zpart[b] + j * LBX_MAX_TOKENS + t));
-    m = __reduce_max_sync(0xffffffffu, m);
-    if (lane == 0) {
-      const float mf = __int_as_float(m);
-      sh.u_inv[b][t] = mf / QMAX;
-      sh.u_scale[b][t] = mf > 0.f ? QMAX / mf : 0.f;
-    }
+  // ---- per-(branch, token) scale from the V-stage maxima, 16-bit digits of z
+  if (tid < 2 * p.k) {
+    const int b = tid / p.k, t = tid - b * p.k;
+    const float m = (b < sg.nbr) ? __int_as_float(__ldcg(sg.zmax[b] + t)) : 0.f;
+    sh.u_inv[b][t] = m / QMAX;
+    sh.u_scale[b][t] = m > 0.f ? QMAX / m : 0.f;
   }
   __syncthreads();
   LBX_PROBE(12);
   for (int base0 = warp * 32; base0 < total; base0 += UB * UTHREADS) {
-    if (base0 != warp * 32) load_batch(base0);
+    // the next batch's z loads are in flight while this batch is quantised
+    const bool more = base0 + UB * UTHREADS < total;
+    if (more) load_batch(base0 + UB * UTHREADS, zn);
 #pragma unroll
     for (int ib = 0; ib < UB; ++ib) {
       const int base = base0 + ib * UTHREADS;
@@ -670,6 +670,12 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
       aw[slot * p.ncols + 1] = pack4(lo[0], lo[1], lo[2], lo[3]);
       sq = __reduce_add_sync(0xffffffffu, sq);
       if (lane == 0) atomicAdd(&sh.u_sq[b][t], sq);
+    }
+    if (more) {
+#pragma unroll
+      for (int ib = 0; ib < UB; ++ib)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) zv[ib][e] = zn[ib][e];
     }
   }
   __syncthreads();
@@ -725,7 +731,17 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
     }
   }
   LBX_PROBE(15);
-  (void)nunits;
+  // the last unit to get here clears the call's bookkeeping words for the next
+  // call (every unit has read its scales before this point)
+  if (tid == 0) {
+    __threadfence();
+    const unsigned done = atomicAdd(p.ticket, 1u);
+    if (done == (unsigned)nunits - 1) {
+      for (int i = 0; i < p.nzmax; ++i) p.zmax_all[i] = 0;
+      *p.ticket = 0u;
+      __threadfence();
+    }
+  }
   if (!ok) return false;
   if (active && split == 0) {
 #pragma unroll
@@ -763,13 +779,15 @@ __global__ void __launch_bounds__(UTHREADS, 2) ustage_kernel(const __grid_consta
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ LinShm sh;
   LBX_PROBE(10);
-  linshm_init(sh);
-  uint8_t *W = smem_raw;
-  uint8_t *S = smem_raw + p.w_bytes;
+  if (threadIdx.x < 2 * LBX_MAX_TOKENS) (&sh.u_sq[0][0])[threadIdx.x] = 0;
+  linshm_init(sh);  // (ends with a CTA barrier)
+  // scratch first, weights after: measured faster than the reverse order
+  uint8_t *S = smem_raw;
+  uint8_t *W = smem_raw + p.s_bytes;
   ustage_issue(p, blockIdx.x, W, sh);
   pdl_trigger();
   pdl_wait();
-  ustage_run<NCB>(p, blockIdx.x, gridDim.x, W, S, sh);
+  ustage_run<NCB>(p, blockIdx.x, gridDim.x, W, S, sh, false);
 }
 
 // ---------------------------------------------------------------------------
@@ -777,19 +795,17 @@ __global__ void __launch_bounds__(UTHREADS, 2) ustage_kernel(const __grid_consta
 // ---------------------------------------------------------------------------
 constexpr size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
 
-// scratch: [header: the grid barrier of a persistent program] then, for every
-// (projection, branch), z [k][rank] and the per-V-tile maxima
-// [ceil(rank/16)][LBX_MAX_TOKENS].  Only the header must be zero when a
-// program first uses the workspace; the rest is written before it is read.
-constexpr size_t WS_GRIDBAR = 0;  // byte offset of the grid barrier words
-constexpr size_t WS_HDR = 256;
+// scratch: [header: zmax words and the unit ticket of a call (zero between
+// calls), the grid barrier of a persistent program] then z [k][rank] of every
+// (projection, branch)
+constexpr size_t WS_GRIDBAR = 400;  // byte offset of the grid barrier words in the header
+constexpr size_t WS_HDR = al256(WS_GRIDBAR + 16);
+static_assert((2 * LBX_MAX_PROJ * LBX_MAX_TOKENS + 1) * sizeof(int) <= WS_GRIDBAR, "header layout");
 
 static size_t ws_bytes_for(const lbx_proj *projs, int n_proj, int k) {
   size_t tot = WS_HDR;
   for (int i = 0; i < n_proj; ++i)
-    for (int b = 0; b < projs[i].n_branches; ++b)
-      tot += al256((size_t)k * projs[i].br[b].rank * 4) +
-             al256((size_t)((projs[i].br[b].rank + 15) / 16) * LBX_MAX_TOKENS * 4);
+    for (int b = 0; b < projs[i].n_branches; ++b) tot += al256((size_t)k * projs[i].br[b].rank * 4);
   return tot;
 }
 
@@ -889,7 +905,9 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
   const int Wv = K / 32;
   const bool rms = a->prologue == LBX_PRO_RMSNORM;
 
-  // scratch: header, then z and the per-tile maxima of every (projection, branch)
+  // scratch: bookkeeping, then z of every (projection, branch), [k][rank]
+  int *zmax_all = reinterpret_cast<int *>(ws);
+  unsigned *ticket = reinterpret_cast<unsigned *>(zmax_all + 2 * LBX_MAX_PROJ * LBX_MAX_TOKENS);
   float *zp[LBX_MAX_PROJ][2] = {};
   int *zm[LBX_MAX_PROJ][2] = {};
   {
@@ -897,9 +915,8 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
     for (int i = 0; i < n_proj; ++i)
       for (int b = 0; b < projs[i].n_branches; ++b) {
         zp[i][b] = reinterpret_cast<float *>(w);
+        zm[i][b] = zmax_all + (2 * i + b) * LBX_MAX_TOKENS;
         w += al256((size_t)k * projs[i].br[b].rank * 4);
-        zm[i][b] = reinterpret_cast<int *>(w);
-        w += al256((size_t)((projs[i].br[b].rank + 15) / 16) * LBX_MAX_TOKENS * 4);
       }
   }
 
@@ -928,12 +945,12 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
       sg.v2 = pr.br[b].v2;
       sg.mid0 = pr.br[b].mid;
       sg.z0 = zp[i][b];
-      sg.zpart0 = zm[i][b];
+      sg.zmax0 = zm[i][b];
       sg.rank = pr.br[b].rank;
       if (b == 0 && pr.n_branches == 2 && !pr.br[1].v_sign) {
         sg.mid1 = pr.br[1].mid;
         sg.z1 = zp[i][1];
-        sg.zpart1 = zm[i][1];
+        sg.zmax1 = zm[i][1];
       }
       sg.tile0 = vtiles;
       vtiles += (sg.rank + 15) / 16;
@@ -941,7 +958,8 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
   }
   P.v_w = al256((size_t)16 * vp.vpitch * 4 + (size_t)vp.vcap * 4 * (rms ? 2 : 1) + 32 * 4);
   P.v_s = (size_t)PASS_WORDS * act_ws(ncols) * 4 + (size_t)VWARPS * 16 * k * 4;
-  vp.w_bytes = (int)P.v_w;
+  P.v_s = (P.v_s + 255) & ~(size_t)255;
+  vp.s_bytes = (int)P.v_s;
   LBX_CHECK_SUP(P.v_w + P.v_s <= vmax, "V-stage needs %zu bytes of shared memory (max %zu)",
                 P.v_w + P.v_s, vmax);
 
@@ -967,8 +985,7 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
       sg.u_sign[b] = pr.br[b].u_sign;
       sg.u1[b] = pr.br[b].u1;
       sg.z[b] = zp[i][b];
-      sg.zpart[b] = zm[i][b];
-      sg.ntile[b] = (pr.br[b].rank + 15) / 16;
+      sg.zmax[b] = zm[i][b];
       sg.rank[b] = pr.br[b].rank;
       sg.words[b] = (pr.br[b].rank + 31) / 32;
       sg.perrow[b] = (sg.words[b] % 4) == 0;
@@ -986,16 +1003,19 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
   // remaining warps of a CTA split the ranks of its tiles
   int ut = UT_MAX;
   while (ut > 1 && tiles / ut < 120) ut >>= 1;
-  const size_t u_s = (size_t)(maxw[0] + maxw[1]) * act_ws(ncols) * 4 + (size_t)UWARPS * 32 * 8 * ncb * 4;
+  const size_t u_s = al256((size_t)(maxw[0] + maxw[1]) * act_ws(ncols) * 4 + (size_t)UWARPS * 32 * 8 * ncb * 4);
   for (; ut >= 1; ut >>= 1) {
     const size_t u_w = al256((size_t)ut * up.wtile_words * 4 + (size_t)ut * 48 * 4);
     if (u_w + u_s <= umax) break;
   }
   LBX_CHECK_SUP(ut >= 1, "U-stage needs too much shared memory (rank too large for k=%d)", k);
   up.ut = ut;
+  up.zmax_all = zmax_all;
+  up.nzmax = 2 * LBX_MAX_PROJ * LBX_MAX_TOKENS;
+  up.ticket = ticket;
   P.u_w = al256((size_t)ut * up.wtile_words * 4 + (size_t)ut * 48 * 4);
   P.u_s = u_s;
-  up.w_bytes = (int)P.u_w;
+  up.s_bytes = (int)P.u_s;
   int ctas = 0;
   for (int i = 0; i < n_proj; ++i) {
     up.seg[i].cta0 = ctas;

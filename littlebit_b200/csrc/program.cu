@@ -215,9 +215,7 @@ struct ArmState {
 
 LBX_DEV void issue_unit(const Phase &P, int u, uint8_t *W, LinShm &sh, ArmState &as) {
   if (P.kind != PH_V && P.kind != PH_U) return;
-  LBX_PROBE(22);
   __syncthreads();  // the previous unit's reads of the weight region are complete
-  LBX_PROBE(23);
   if (P.kind == PH_V) {
     vstage_issue(P.v, u, W, sh);
     if (threadIdx.x == 0) as.armed |= 1u << UT_MAX;
@@ -230,7 +228,6 @@ LBX_DEV void issue_unit(const Phase &P, int u, uint8_t *W, LinShm &sh, ArmState 
         if ((u - sg.cta0) * (16 * ut) + 16 * t < sg.out) as.armed |= 1u << t;
     }
   }
-  LBX_PROBE(24);
 }
 
 // the executor is specialised per program: every linear of a program has the
@@ -305,15 +302,15 @@ LBX_DEV void drain(LinShm &sh, const ArmState &as) {
 
 template <int NCB, int LMNT>
 __global__ void __launch_bounds__(PTHREADS, 1)
-    program_kernel(const Phase *__restrict__ prog, int nph, GridBar *gb, ProgIo io, int w_bytes) {
+    program_kernel(const Phase *__restrict__ prog, int nph, GridBar *gb, ProgIo io, int s_bytes) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ LinShm sh;
   __shared__ Phase sph[2];
   __shared__ ArmState as;
   __shared__ __align__(8) uint64_t pbar;
   __shared__ unsigned long long s_base;
-  uint8_t *W = smem;
-  uint8_t *S = smem + w_bytes;
+  uint8_t *S = smem;            // scratch of the running unit
+  uint8_t *W = smem + s_bytes;  // weights of the running / next unit
   linshm_init(sh);
   if (threadIdx.x == 0) {
     as.armed = 0;
@@ -476,8 +473,8 @@ static int finish_program(uint64_t key, ProgBuilder &B, cudaStream_t stream, Pro
   Program *P = new Program();
   P->host = std::move(B.ph);
   P->nph = (int)P->host.size();
-  P->w_bytes = (B.wmax + 255) & ~(size_t)255;
-  P->s_bytes = B.smax;
+  P->w_bytes = B.wmax;
+  P->s_bytes = (B.smax + 255) & ~(size_t)255;
   P->ncb = B.ncb ? B.ncb : 1;
   P->lmnt = B.lmnt ? B.lmnt : 1;
   e = cudaMalloc(&P->dev, P->host.size() * sizeof(Phase));
@@ -511,7 +508,7 @@ static int launch_program(const Program *P, GridBar *gb, const ProgIo &io, cudaS
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, program_instance(P->ncb, P->lmnt), (const Phase *)P->dev,
-                                           P->nph, gb, io, (int)P->w_bytes);
+                                           P->nph, gb, io, (int)P->s_bytes);
   return cuda_status(e, "program launch");
 }
 
