@@ -626,7 +626,10 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int pos = 32 * Wd + 16 * hh + jj + 4 * e;
-          if (pos < r) zd[ib][e] = __ldcg(zrow + pos);
+          // standalone: z is read-only in this grid and written by the previous
+          // one, so the L1 path absorbs the 4x sector reuse of this pattern;
+          // inside a persistent program z is produced in the same launch: L2 only
+          if (pos < r) zd[ib][e] = zero ? __ldcg(zrow + pos) : __ldg(zrow + pos);
         }
       }
     }
