@@ -344,12 +344,15 @@ def run_decode(args, dev, rank, ws):
 # row-sharded 8192 -> 28672 LittleBitLinear (N > 1)
 # ---------------------------------------------------------------------------
 def run_row_shard(args, dev, rank, ws, reps: int = 200):
-    """BASELINE config 5's GEMV sweep point at this world size: U rows split over
-    the ranks, V replicated, one NCCL all-gather of the y slices per call.
+    """The 70B-MLP-shaped LittleBitLinear at this world size: U rows split over
+    the ranks, V replicated, the y slices all-gathered, timed two ways — the
+    local layer followed by an NCCL all-gather, and the all-gather fused into
+    the U-stage (tagged NVLink stores + an unpack kernel; ``us_per_call``).
     GB/s counts the whole layer's algorithmic bytes once per call."""
     import torch.distributed as dist
     from littlebit_b200 import synthetic
-    from littlebit_b200.sharded import RowShardedLinear
+    from littlebit_b200 import ops
+    from littlebit_b200.sharded import FusedRowShardedLinear, RowShardedLinear
 
     K, N, r = 8192, 28672, 616
     g = torch.Generator().manual_seed(4242)
@@ -360,29 +363,54 @@ def run_row_shard(args, dev, rank, ws, reps: int = 200):
     gat = torch.empty(ws, 1, N // ws, device=dev)
     stream = torch.cuda.current_stream(dev)
 
+    per = 20  # calls per CUDA graph
+
     def timed(fn):
-        for _ in range(5):
+        """Device time per call: ``per`` calls captured in one CUDA graph (the
+        Python launch cost of a call exceeds its GPU time), replayed."""
+        for _ in range(4):
             fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(per):
+                fn()
+        for _ in range(3):
+            graph.replay()
         barrier(ws)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(reps):
-            fn()
+        for _ in range(reps // per):
+            graph.replay()
         e1.record(stream)
         torch.cuda.synchronize()
-        return max_over_ranks(e0.elapsed_time(e1) / reps * 1e3, ws)
+        t = max_over_ranks(e0.elapsed_time(e1) / (reps // per * per) * 1e3, ws)
+        del graph  # a graph holding NCCL calls goes before the process group
+        return t
 
     t_local = timed(lambda: sh.local_forward(x, part))
     t_ag = timed(lambda: dist.all_gather_into_tensor(gat, part))
     t_all = timed(lambda: (sh.local_forward(x, part), dist.all_gather_into_tensor(gat, part)))
+    # the all-gather fused into the U-stage; must agree with the NCCL path bitwise
+    fsh = FusedRowShardedLinear(full, ws, rank, max_tokens=1)
+    yf = torch.empty(1, N, device=dev)
+    t_fused = timed(lambda: fsh.forward(x, yf))
+    ref = gat.permute(1, 0, 2).reshape(1, N)
+    same = bool(torch.equal(fsh.forward(x, yf), ref))
+    dev_err = ops.device_error(dev)
+    fsh.close()
+    if not same or dev_err:
+        raise RuntimeError(f"fused all-gather disagrees with NCCL (equal={same}, device error {dev_err:#x})")
     alg = (r * K + 7) // 8 + (N * r + 7) // 8 + 4 * (K + r + N) + 4 * K + 4 * N
     return {"workload": f"LittleBitLinear {K}->{N} r={r}, k=1 fp32, U rows split over {ws} GPUs, "
-                        f"V replicated, NCCL all-gather of y",
-            "us_per_call": round(t_all, 3), "local_kernel_us": round(t_local, 3),
-            "allgather_us": round(t_ag, 3), "allgather_bytes_per_rank": 4 * N // ws,
-            "gbs_whole_layer": round(alg / (t_all * 1e-6) / 1e9, 2), "algorithmic_bytes": alg,
-            "timing": f"CUDA events over {reps} calls, max over ranks"}
+                        f"V replicated, y all-gathered",
+            "us_per_call": round(t_fused, 3), "local_kernel_us": round(t_local, 3),
+            "nccl_us_per_call": round(t_all, 3), "nccl_allgather_us": round(t_ag, 3),
+            "fused_us_per_call": round(t_fused, 3), "fused_equals_nccl": same,
+            "allgather_bytes_per_rank": 4 * N // ws,
+            "gbs_whole_layer": round(alg / (t_fused * 1e-6) / 1e9, 2), "algorithmic_bytes": alg,
+            "timing": f"CUDA events over {reps} calls ({per} per CUDA graph), max over ranks"}
 
 
 def run_ours(args):

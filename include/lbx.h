@@ -235,6 +235,35 @@ size_t lbx_linear_chain_workspace_size(const lbx_proj *projs, int32_t n_layers, 
 int lbx_linear_chain(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens, int32_t dtype,
                      void *const *acts, void *ws, size_t ws_bytes, cudaStream_t stream);
 
+/* ---- row-sharded LittleBitLinear over NVLink ----------------------------
+ * No reference counterpart (the reference decodes on one CPU host): the
+ * tensor-parallel split of one wide layer, with its all-gather fused into the
+ * U-stage.  `proj` holds this rank's rows of U and u1 (out_features = its
+ * share) and the full V, h, l.  Every result (token t, column y_col0 + i) is
+ * stored into every rank's exchange buffer xbuf_peers[j] as one 8-byte word
+ * (call number << 32 | fp32 bits) at word t * ld + y_col0 + i of the half
+ * given by the call number's parity (halves half_words apart).  The buffers
+ * must be addressable from this GPU (symmetric memory or IPC mappings, this
+ * rank's own included), zero-filled before the first call.  state (device,
+ * two zeroed uint32: completed calls, ticket) is this rank's call counter;
+ * lbx_allgather_unpack advances it.  One projection, fp32, store epilogue,
+ * n_tokens <= LBX_MAX_TOKENS; workspace as for lbx_linear.  Every rank makes
+ * the same sequence of calls. */
+int lbx_linear_allgather(const lbx_proj *proj, const lbx_linear_args *a, int32_t n_peer,
+                         uint64_t *const *xbuf_peers /* host array */, int64_t half_words,
+                         int32_t y_col0, int64_t ld, const uint32_t *state, void *ws,
+                         size_t ws_bytes, cudaStream_t stream);
+
+/* This rank's exchange buffer -> y [n_tokens, n] fp32 (row stride y_ld):
+ * waits for every word of the current call (bounded: after 1 s it records
+ * device error 0x601, writes NaN for what is missing and returns), then
+ * advances state.  Launch it on the stream of the lbx_linear_allgather call,
+ * before that stream's next lbx_linear_allgather: a rank overwrites a buffer
+ * half only after every rank has unpacked it. */
+int lbx_allgather_unpack(const uint64_t *xbuf, int64_t half_words, int32_t n_tokens, int32_t n,
+                         int64_t ld, float *y, int64_t y_ld, uint32_t *state, int32_t use_pdl,
+                         cudaStream_t stream);
+
 /* ---- whole decoder step (cpp:1522-1840 full_forward, 1846-2079
  *      full_forward_batch, 2256-2317 generate_token) ----------------------- */
 typedef struct lbx_layer {

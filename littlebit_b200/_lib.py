@@ -102,6 +102,10 @@ _SIGNATURES = {
     "lbx_linear_chain_workspace_size": (c_size_t, [POINTER(Proj), c_int32, c_int32]),
     "lbx_linear_chain": (c_int, [POINTER(Proj), c_int32, c_int32, c_int32, POINTER(c_void_p), c_void_p,
                                  c_size_t, c_void_p]),
+    "lbx_linear_allgather": (c_int, [POINTER(Proj), POINTER(LinearArgs), c_int32, POINTER(c_void_p),
+                                     c_int64, c_int32, c_int64, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "lbx_allgather_unpack": (c_int, [c_void_p, c_int64, c_int32, c_int32, c_int64, c_void_p, c_int64,
+                                     c_void_p, c_int32, c_void_p]),
     "lbx_forward_workspace_size": (c_size_t, [POINTER(Model), c_int32]),
     "lbx_forward": (c_int, [POINTER(Model), c_void_p, c_int32, c_int32, c_void_p, c_void_p,
                             c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),

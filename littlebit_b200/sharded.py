@@ -130,3 +130,95 @@ class RowShardedLinear:
                                        device=part.device)
         dist.all_gather_into_tensor(self._gather, part, group=self.group)
         return self._gather.permute(1, 0, 2).reshape(k, self.out_features)
+
+
+class FusedRowShardedLinear(RowShardedLinear):
+    """Row-sharded LittleBitLinear with the all-gather fused into the U-stage
+    (lbx_linear_allgather + lbx_allgather_unpack).
+
+    Each rank's U-stage stores every result straight into every rank's
+    exchange buffer over NVLink, as an 8-byte word tagged with the call
+    number; the unpack kernel polls its own buffer until every word of the
+    call has arrived and writes the plain fp32 y.  No fence, signal or
+    collective launch sits between the layer and its consumer.
+
+    The exchange buffers are torch symmetric memory (CUDA backend): two
+    halves of [max_tokens, N] words per rank, used by alternate calls.  A
+    rank rewrites half h two calls later, after its own unpack of the call in
+    between, which needs every peer's U-stage of that call, which each peer's
+    stream runs after its unpack of the call that used h — so the ordering is
+    automatic as long as every rank makes the same sequence of calls on one
+    stream."""
+
+    def __init__(self, full: PackedLinear, world_size: int, rank: int, group=None,
+                 max_tokens: int = 16):
+        super().__init__(full, world_size, rank, group)
+        import ctypes
+
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        from . import _lib as L
+        from .ops import lib, projs_array
+
+        if not 1 <= max_tokens <= L.LBX_MAX_TOKENS:
+            raise ValueError(f"max_tokens must be in [1, {L.LBX_MAX_TOKENS}]")
+        if world_size > 8:
+            raise ValueError("at most 8 ranks")
+        self._L, self._lib, self._ct = L, lib(), ctypes
+        dev = self.local.device
+        pg = group if group is not None else dist.group.WORLD
+        self.max_tokens = max_tokens
+        self.half = max_tokens * self.out_features  # words per half
+        if symm.get_backend(dev) is None:
+            symm.set_backend("CUDA")
+        self.xbuf = symm.empty(2 * self.half, dtype=torch.int64, device=dev)
+        self.xbuf.zero_()
+        self.state = torch.zeros(2, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        self.hdl = symm.rendezvous(self.xbuf, pg)
+        self._peers = (ctypes.c_void_p * world_size)(*[int(p) for p in self.hdl.buffer_ptrs])
+        self._arr = projs_array([self.local])
+        self._ws = torch.zeros(int(self._lib.lbx_linear_workspace_size(self._arr, 1, max_tokens)),
+                               dtype=torch.uint8, device=dev)
+        # every rank's buffer is zero before any peer writes into it
+        dist.barrier(group=pg)
+        torch.cuda.synchronize(dev)
+
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """y [k, N] fp32 on every rank (``out`` if given)."""
+        from .ops import _cuda, _dt, _stream
+
+        L, ct = self._L, self._ct
+        _cuda("x", x)
+        k = x.shape[0]
+        if k > self.max_tokens or x.shape[1] != self.in_features:
+            raise RuntimeError(f"x {tuple(x.shape)}: at most {self.max_tokens} rows of {self.in_features}")
+        N = self.out_features
+        if out is None:
+            out = torch.empty(k, N, dtype=torch.float32, device=x.device)
+        elif out.dtype != torch.float32 or out.shape != (k, N) or out.stride(1) != 1:
+            raise RuntimeError(f"out must be float32 [{k}, {N}] with unit column stride")
+        a = L.LinearArgs()
+        a.n_proj = 1
+        a.n_tokens = k
+        a.x_dtype = _dt(x)
+        a.y_dtype = L.LBX_F32
+        a.prologue = L.LBX_PRO_NONE
+        a.epilogue = L.LBX_EPI_STORE
+        a.use_pdl = 1
+        a.x = x.data_ptr()
+        st = _stream(x.device)
+        L.check(self._lib.lbx_linear_allgather(
+            self._arr, ct.byref(a), self.world_size, self._peers, self.half, self.lo, N,
+            self.state.data_ptr(), self._ws.data_ptr(), self._ws.numel(), st), "linear_allgather")
+        L.check(self._lib.lbx_allgather_unpack(self.xbuf.data_ptr(), self.half, k, N, N, out.data_ptr(),
+                                               out.stride(0), self.state.data_ptr(), 1, st),
+                "allgather_unpack")
+        return out
+
+    def close(self) -> None:
+        """Release the symmetric-memory handle (call on every rank)."""
+        torch.cuda.synchronize(self.local.device)
+        self.hdl = None
+        self.xbuf = None

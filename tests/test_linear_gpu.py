@@ -217,3 +217,50 @@ def test_linear_chain_program_matches_layer_calls():
         torch.cuda.synchronize()
         assert torch.equal(acts[-1], ref), k
         assert ops.device_error() == 0
+
+
+def test_allgather_exchange_two_shards_one_gpu():
+    """lbx_linear_allgather + lbx_allgather_unpack with two row shards emulated
+    on one GPU: both shards' tagged words go into two exchange buffers, each
+    unpack yields the unsharded layer's y bit for bit, over alternating buffer
+    halves and ragged token counts.  The calls run in stream order (every
+    word is written before the unpack that reads it starts), so no launch
+    waits on a concurrent one."""
+    import ctypes
+
+    from littlebit_b200 import _lib as L
+    from littlebit_b200 import ops, synthetic
+    from littlebit_b200.sharded import RowShardedLinear
+
+    K, N, r, G, kmax = 4096, 2048, 208, 2, 8
+    g = torch.Generator().manual_seed(91)
+    full = synthetic.to_packed_linear(K, N, synthetic.layer(K, N, [r, 96], g), DEV)
+    shards = [RowShardedLinear(full, G, rank) for rank in range(G)]
+    half = kmax * N
+    xbufs = [torch.zeros(2 * half, dtype=torch.int64, device=DEV) for _ in range(G)]
+    states = [torch.zeros(2, dtype=torch.int32, device=DEV) for _ in range(G)]
+    peers = (ctypes.c_void_p * G)(*[b.data_ptr() for b in xbufs])
+    arrs = [ops.projs_array([s.local]) for s in shards]
+    wss = [torch.zeros(ops.linear_workspace_bytes([s.local], kmax), dtype=torch.uint8, device=DEV)
+           for s in shards]
+    lib = ops.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    for k in (1, 3, 8, 1, 2):
+        x = torch.randn(k, K, generator=g).cuda()
+        for rank, s in enumerate(shards):
+            a = L.LinearArgs()
+            a.n_proj, a.n_tokens, a.x_dtype, a.y_dtype = 1, k, L.LBX_F32, L.LBX_F32
+            a.epilogue, a.use_pdl, a.x = L.LBX_EPI_STORE, 1, x.data_ptr()
+            L.check(lib.lbx_linear_allgather(arrs[rank], ctypes.byref(a), G, peers, half, s.lo, N,
+                                             states[rank].data_ptr(), wss[rank].data_ptr(),
+                                             wss[rank].numel(), st), "allgather")
+        ys = [torch.empty(k, N, device=DEV) for _ in range(G)]
+        for rank in range(G):
+            L.check(lib.lbx_allgather_unpack(xbufs[rank].data_ptr(), half, k, N, N, ys[rank].data_ptr(),
+                                             N, states[rank].data_ptr(), 1, st), "unpack")
+        ref = ops.lb_linear(full, x)
+        torch.cuda.synchronize()
+        assert ops.device_error() == 0
+        for rank in range(G):
+            assert torch.equal(ys[rank], ref), (k, rank)
+    assert [int(s[0]) for s in states] == [5, 5] and [int(s[1]) for s in states] == [0, 0]
