@@ -90,6 +90,11 @@ typedef struct lbx_linear_args {
   const float *norm_w; /* [in] RMSNorm weight of LBX_PRO_RMSNORM               */
   void *y[LBX_MAX_PROJ];   /* per projection [k, out] row-major                */
   int64_t y_ld[LBX_MAX_PROJ]; /* row stride (elements) of each y; 0 => out    */
+  int32_t exec;        /* LBX_EXEC_AUTO: one cluster launch when the call fits
+                        * it, else the two stage grids; LBX_EXEC_KERNELS: the
+                        * two stage grids; LBX_EXEC_CLUSTER: the cluster launch
+                        * or LBX_EUNSUPPORTED.  All give the same bits.       */
+  int32_t _pad;
 } lbx_linear_args;
 
 /* Bytes of device scratch one lbx_linear / lbx_linear_verify call needs.
@@ -296,6 +301,7 @@ typedef struct lbx_model {
 #define LBX_EXEC_AUTO 0
 #define LBX_EXEC_KERNELS 1
 #define LBX_EXEC_PROGRAM 2
+#define LBX_EXEC_CLUSTER 3 /* lbx_linear_args.exec only */
 
 /* Workspace of lbx_forward: zero-filled once at allocation, like lbx_linear's. */
 size_t lbx_forward_workspace_size(const lbx_model *m /* host */, int32_t n_tokens);

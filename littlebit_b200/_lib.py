@@ -17,7 +17,7 @@ LBX_MAX_TOKENS = 16
 LBX_MAX_PROJ = 3
 LBX_PRO_NONE, LBX_PRO_RMSNORM, LBX_PRO_SILU_MUL = 0, 1, 2
 LBX_EPI_STORE, LBX_EPI_ADD = 0, 1
-LBX_EXEC_AUTO, LBX_EXEC_KERNELS, LBX_EXEC_PROGRAM = 0, 1, 2
+LBX_EXEC_AUTO, LBX_EXEC_KERNELS, LBX_EXEC_PROGRAM, LBX_EXEC_CLUSTER = 0, 1, 2, 3
 
 
 class Branch(ctypes.Structure):
@@ -40,6 +40,7 @@ class LinearArgs(ctypes.Structure):
         ("prologue", c_int32), ("epilogue", c_int32), ("eps", c_float), ("use_pdl", c_int32),
         ("x", c_void_p), ("x2", c_void_p), ("norm_w", c_void_p),
         ("y", c_void_p * LBX_MAX_PROJ), ("y_ld", c_int64 * LBX_MAX_PROJ),
+        ("exec", c_int32), ("_pad", c_int32),
     ]
 
 

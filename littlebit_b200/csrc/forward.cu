@@ -156,6 +156,7 @@ static int forward_chunk(const lbx_model *m, const int64_t *tokens, int32_t n, i
     const lbx_layer &ly = m->layers[l];
     // q, k, v from RMSNorm(x)
     lbx_linear_args a = {};
+    a.exec = m->exec_mode == LBX_EXEC_KERNELS ? LBX_EXEC_KERNELS : LBX_EXEC_AUTO;
     a.n_proj = 3;
     a.n_tokens = n;
     a.x_dtype = LBX_F32;
@@ -196,6 +197,7 @@ static int forward_chunk(const lbx_model *m, const int64_t *tokens, int32_t n, i
     if (rc) return rc;
     // x += o(att)
     lbx_linear_args o = {};
+    o.exec = a.exec;
     o.n_proj = 1;
     o.n_tokens = n;
     o.x_dtype = LBX_F32;

@@ -43,6 +43,8 @@ constexpr int VCAP_MAX = 12288; // leading v2/norm_w columns prefetched into sha
 constexpr int UWARPS = 16;      // warp (tile, split): ut row tiles x (16/ut) rank splits
 constexpr int UTHREADS = UWARPS * 32;
 constexpr int UT_MAX = 8;
+constexpr int UGRP = 128;       // U-stage quantisation group: 128 ranks (4 sign words) of one branch
+constexpr int ZGMAX = 64;       // quantisation groups per branch (rank <= 8192)
 constexpr int LBX_MAX_PEERS = 8;
 
 // activation buffer: act[W][slot][col] uint32, word stride 8*ncols+8
@@ -59,8 +61,8 @@ struct VSeg {
   const float *mid1;     // [rank] (shared-V residual) or nullptr
   float *z0;             // [k][rank]
   float *z1;             // [k][rank] or nullptr
-  int *zmax0;            // [k] running max |z0| (float bits), zero before the call
-  int *zmax1;            // [k] or nullptr
+  int *zmax0;            // [group][LBX_MAX_TOKENS] running max |z0| per 128-rank group (float bits), zero before the call
+  int *zmax1;            // [group][LBX_MAX_TOKENS] or nullptr
   int rank;
   int tile0;             // first CTA (16-row tile) of this segment
 };
@@ -83,7 +85,7 @@ struct USeg {
   const int32_t *u_sign[2];
   const float *u1[2];
   const float *z[2];     // [k][rank] from the V-stage
-  const int *zmax[2];    // [k] max |z| per token (float bits) from the V-stage
+  const int *zmax[2];    // [group][LBX_MAX_TOKENS] max |z| per 128-rank group and token (float bits), from the V-stage
   int rank[2];
   int words[2];   // ceil(rank/32)
   int pitch[2];   // smem row pitch (words)
@@ -103,8 +105,8 @@ struct UParams {
   int ut;             // row tiles per CTA (warps split the ranks 16/ut ways)
   int act_words[2];   // max over projections of 4*ceil(words/4)
   int wtile_words;    // per-tile weight region (words)
-  int *zmax_all;      // all zmax words of this call (reset by the last unit)
-  int nzmax;
+  int ugm;            // max quantisation groups of a branch (scratch arrays [2][ugm][k])
+  int *zmax_all;      // maxima slots [proj][branch][ZGMAX][LBX_MAX_TOKENS] (the used ones reset by the last unit)
   unsigned *ticket;   // unit completion counter (zero before and after the call)
   int s_bytes;        // shared-memory scratch region of a standalone launch (weights follow)
   // fused all-gather of a row-sharded layer (one projection): every result
@@ -220,9 +222,7 @@ struct LinShm {
   int v_sq[VWARPS][LBX_MAX_TOKENS];
   float v_ssq[VWARPS][LBX_MAX_TOKENS];
   int v_zmax[2][LBX_MAX_TOKENS];
-  float u_inv[2][LBX_MAX_TOKENS];
-  float u_scale[2][LBX_MAX_TOKENS];
-  int u_sq[2][LBX_MAX_TOKENS];
+  int u_ec[2][LBX_MAX_TOKENS];  // per (branch, token): the coarsest group exponent
   __align__(8) uint64_t bar[UT_MAX + 1];
   uint32_t par[UT_MAX + 1];
 };
@@ -294,6 +294,135 @@ LBX_DEV void vstage_issue(const VParams &p, int unit, uint8_t *W, LinShm &sh) {
     bulk_g2s(L.smid + 16, sg.mid1 + row0, (uint32_t)rows * 4u, bar);
 }
 
+// One staging pass of the V-stage: every token's a = v2 ⊙ prologue(x) over
+// the (up to) 4096 columns of pass `pass`, as int8 digit pairs in act, with
+// the per-(warp, token) scale, digit sum and RMSNorm sum of squares in sh.
+// Thread t stages columns 8*(t%4)..+8 of word t/4; warp w = one 256-column
+// scale block.  on_first() runs once, after the first tokens' x loads are
+// issued and before v2 is used (the V-stage waits for its weight copies
+// there).  Columns below p.vcap take v2 / norm_w from the shared-memory
+// copies sv2 / snw, the rest from global memory (same arithmetic).
+template <class OnFirst>
+LBX_DEV void vstage_stage(const VParams &p, const float *v2, const float *sv2, const float *snw,
+                          int pass, uint32_t *act, LinShm &sh, OnFirst &&on_first) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool rms = p.prologue == LBX_PRO_RMSNORM;
+  const int ws = act_ws(p.ncols);
+  const int vcap = p.vcap;
+  const int Wd = tid >> 2, qq = tid & 3;
+  const int hh = qq >> 1;
+  const bool low = (qq & 1) == 0;  // my digits are bytes 0,1 (else 2,3) of the slot words
+  const int pw0 = pass * PASS_WORDS;
+  const int pwords = min(PASS_WORDS, p.Wv - pw0);
+  const bool wvalid = Wd < pwords;
+  const int64_t col = (int64_t)(pw0 + Wd) * 32 + 8 * qq;
+  const bool silu = p.prologue == LBX_PRO_SILU_MUL;
+  float hw[8];
+  for (int t0 = 0; t0 < p.k; t0 += TBATCH) {
+    // issue the loads of a batch of tokens before using any of them
+    float xv[TBATCH][8], uv[TBATCH][8];
+#pragma unroll
+    for (int j = 0; j < TBATCH; ++j) {
+      if (wvalid && t0 + j < p.k) {
+        load8(p.x, p.xdt, (int64_t)(t0 + j) * p.K + col, xv[j]);
+        if (silu) load8(p.x2, p.xdt, (int64_t)(t0 + j) * p.K + col, uv[j]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) xv[j][i] = uv[j][i] = 0.f;
+      }
+    }
+
+    if (t0 == 0) {
+      on_first();
+      if (!wvalid) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) hw[i] = 0.f;
+      } else if (col < vcap) {
+        const float4 *v4 = reinterpret_cast<const float4 *>(sv2 + col);
+        const float4 a0 = v4[0], a1 = v4[1];
+        hw[0] = a0.x; hw[1] = a0.y; hw[2] = a0.z; hw[3] = a0.w;
+        hw[4] = a1.x; hw[5] = a1.y; hw[6] = a1.z; hw[7] = a1.w;
+        if (rms) {
+          const float4 *n4 = reinterpret_cast<const float4 *>(snw + col);
+          const float4 b0 = n4[0], b1 = n4[1];
+          hw[0] *= b0.x; hw[1] *= b0.y; hw[2] *= b0.z; hw[3] *= b0.w;
+          hw[4] *= b1.x; hw[5] *= b1.y; hw[6] *= b1.z; hw[7] *= b1.w;
+        }
+      } else {  // columns beyond the shared-memory copy (very wide inputs)
+        load8f(v2 + col, hw);
+        if (rms) {
+          float nw[8];
+          load8f(p.norm_w + col, nw);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) hw[i] *= nw[i];
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < TBATCH; ++j) {
+      const int t = t0 + j;
+      if (t >= p.k) break;  // uniform across the CTA
+      float a[8];
+      float sq2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float xx = xv[j][i];
+        if (silu) {
+          a[i] = (xx / (1.0f + expf(-xx))) * uv[j][i] * hw[i];
+        } else {
+          sq2 = fmaf(xx, xx, sq2);
+          a[i] = xx * hw[i];
+        }
+      }
+      float m = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(a[i]));
+      m = __int_as_float(__reduce_max_sync(0xffffffffu, __float_as_int(m)));
+      const float sc = m > 0.f ? QMAX / m : 0.f;
+      int hi[8], lo[8], sqi = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int qv = __float2int_rn(a[i] * sc);
+        sqi += qv;
+        split_digits(qv, hi[i], lo[i]);
+      }
+      // 16-bit halves of the 4 slot words (h, j): bytes = columns j and j+4
+      uint32_t H[2], Lw[2];
+#pragma unroll
+      for (int jp = 0; jp < 2; ++jp) {
+        const int j0 = 2 * jp, j1 = 2 * jp + 1;
+        H[jp] = ((hi[j0] & 255) | ((hi[j0 + 4] & 255) << 8)) |
+                (((hi[j1] & 255) | ((hi[j1 + 4] & 255) << 8)) << 16);
+        Lw[jp] = ((lo[j0] & 255) | ((lo[j0 + 4] & 255) << 8)) |
+                 (((lo[j1] & 255) | ((lo[j1 + 4] & 255) << 8)) << 16);
+      }
+      const uint32_t PH0 = __shfl_xor_sync(0xffffffffu, H[0], 1);
+      const uint32_t PH1 = __shfl_xor_sync(0xffffffffu, H[1], 1);
+      const uint32_t PL0 = __shfl_xor_sync(0xffffffffu, Lw[0], 1);
+      const uint32_t PL1 = __shfl_xor_sync(0xffffffffu, Lw[1], 1);
+      uint32_t *aw = act + Wd * ws + 2 * t;
+      if (low) {  // slots j = 0, 1: my half low, partner's high
+        aw[(4 * hh + 0) * p.ncols] = (H[0] & 0xFFFFu) | (PH0 << 16);
+        aw[(4 * hh + 0) * p.ncols + 1] = (Lw[0] & 0xFFFFu) | (PL0 << 16);
+        aw[(4 * hh + 1) * p.ncols] = (H[0] >> 16) | (PH0 & 0xFFFF0000u);
+        aw[(4 * hh + 1) * p.ncols + 1] = (Lw[0] >> 16) | (PL0 & 0xFFFF0000u);
+      } else {    // slots j = 2, 3: partner's half low, mine high
+        aw[(4 * hh + 2) * p.ncols] = (PH1 & 0xFFFFu) | (H[1] << 16);
+        aw[(4 * hh + 2) * p.ncols + 1] = (PL1 & 0xFFFFu) | (Lw[1] << 16);
+        aw[(4 * hh + 3) * p.ncols] = (PH1 >> 16) | (H[1] & 0xFFFF0000u);
+        aw[(4 * hh + 3) * p.ncols + 1] = (PL1 >> 16) | (Lw[1] & 0xFFFF0000u);
+      }
+      sqi = __reduce_add_sync(0xffffffffu, sqi);
+      if (rms) sq2 = warp_sum(sq2);
+      if (lane == 0) {
+        sh.v_inv[warp][t] = m / QMAX;
+        sh.v_sq[warp][t] = sqi;
+        sh.v_ssq[warp][t] += sq2;
+      }
+    }
+  }
+}
+
 // z = mid ⊙ (V_sign · a) for the 16 rows of unit `unit`; returns false (on
 // every thread) if the weight copies did not arrive in time
 template <int NCB>
@@ -308,7 +437,6 @@ LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinS
   const VLayout L = vlayout(p, W, S);
   uint32_t *wbuf = L.wbuf, *act = L.act;
   float *sv2 = L.sv2, *snw = L.snw, *red = L.red;
-  const int vcap = p.vcap;
   const uint32_t par = sh.par[UT_MAX];
   if (zero) {  // per-unit scratch (standalone kernels clear it before their wait)
     if (tid < VWARPS * LBX_MAX_TOKENS) (&sh.v_ssq[0][0])[tid] = 0.f;
@@ -317,11 +445,6 @@ LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinS
   }
   LBX_PROBE(1);
 
-  // thread t stages columns 8*(t%4)..+8 of word t/4 of each 128-word pass;
-  // warp w = one 256-column scale block
-  const int Wd = tid >> 2, qq = tid & 3;
-  const int hh = qq >> 1;
-  const bool low = (qq & 1) == 0;  // my digits are bytes 0,1 (else 2,3) of the slot words
   float tacc[NCB][2];
 #pragma unroll
   for (int cb = 0; cb < NCB; ++cb) tacc[cb][0] = tacc[cb][1] = 0.f;
@@ -330,116 +453,12 @@ LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinS
   for (int pass = 0; pass < npass; ++pass) {
     const int pw0 = pass * PASS_WORDS;
     const int pwords = min(PASS_WORDS, p.Wv - pw0);
-    const bool wvalid = Wd < pwords;
-    const int64_t col = (int64_t)(pw0 + Wd) * 32 + 8 * qq;
-    const bool silu = p.prologue == LBX_PRO_SILU_MUL;
-    float hw[8];
-    for (int t0 = 0; t0 < p.k; t0 += TBATCH) {
-      // issue the loads of a batch of tokens before using any of them
-      float xv[TBATCH][8], uv[TBATCH][8];
-#pragma unroll
-      for (int j = 0; j < TBATCH; ++j) {
-        if (wvalid && t0 + j < p.k) {
-          load8(p.x, p.xdt, (int64_t)(t0 + j) * p.K + col, xv[j]);
-          if (silu) load8(p.x2, p.xdt, (int64_t)(t0 + j) * p.K + col, uv[j]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) xv[j][i] = uv[j][i] = 0.f;
-        }
+    vstage_stage(p, sg.v2, sv2, snw, pass, act, sh, [&] {
+      if (pass == 0) {
+        ok = __syncthreads_and(mbar_wait_bounded(&sh.bar[UT_MAX], par, 0x101));
+        LBX_PROBE(2);
       }
-
-      if (t0 == 0) {
-        if (pass == 0) {
-          ok = __syncthreads_and(mbar_wait_bounded(&sh.bar[UT_MAX], par, 0x101));
-          LBX_PROBE(2);
-        }
-        if (!wvalid) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) hw[i] = 0.f;
-        } else if (col < vcap) {
-          const float4 *v4 = reinterpret_cast<const float4 *>(sv2 + col);
-          const float4 a0 = v4[0], a1 = v4[1];
-          hw[0] = a0.x; hw[1] = a0.y; hw[2] = a0.z; hw[3] = a0.w;
-          hw[4] = a1.x; hw[5] = a1.y; hw[6] = a1.z; hw[7] = a1.w;
-          if (rms) {
-            const float4 *n4 = reinterpret_cast<const float4 *>(snw + col);
-            const float4 b0 = n4[0], b1 = n4[1];
-            hw[0] *= b0.x; hw[1] *= b0.y; hw[2] *= b0.z; hw[3] *= b0.w;
-            hw[4] *= b1.x; hw[5] *= b1.y; hw[6] *= b1.z; hw[7] *= b1.w;
-          }
-        } else {  // columns beyond the shared-memory copy (very wide inputs)
-          load8f(sg.v2 + col, hw);
-          if (rms) {
-            float nw[8];
-            load8f(p.norm_w + col, nw);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) hw[i] *= nw[i];
-          }
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < TBATCH; ++j) {
-        const int t = t0 + j;
-        if (t >= p.k) break;  // uniform across the CTA
-        float a[8];
-        float sq2 = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float xx = xv[j][i];
-          if (silu) {
-            a[i] = (xx / (1.0f + expf(-xx))) * uv[j][i] * hw[i];
-          } else {
-            sq2 = fmaf(xx, xx, sq2);
-            a[i] = xx * hw[i];
-          }
-        }
-        float m = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(a[i]));
-        m = __int_as_float(__reduce_max_sync(0xffffffffu, __float_as_int(m)));
-        const float sc = m > 0.f ? QMAX / m : 0.f;
-        int hi[8], lo[8], sqi = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int qv = __float2int_rn(a[i] * sc);
-          sqi += qv;
-          split_digits(qv, hi[i], lo[i]);
-        }
-        // 16-bit halves of the 4 slot words (h, j): bytes = columns j and j+4
-        uint32_t H[2], Lw[2];
-#pragma unroll
-        for (int jp = 0; jp < 2; ++jp) {
-          const int j0 = 2 * jp, j1 = 2 * jp + 1;
-          H[jp] = ((hi[j0] & 255) | ((hi[j0 + 4] & 255) << 8)) |
-                  (((hi[j1] & 255) | ((hi[j1 + 4] & 255) << 8)) << 16);
-          Lw[jp] = ((lo[j0] & 255) | ((lo[j0 + 4] & 255) << 8)) |
-                   (((lo[j1] & 255) | ((lo[j1 + 4] & 255) << 8)) << 16);
-        }
-        const uint32_t PH0 = __shfl_xor_sync(0xffffffffu, H[0], 1);
-        const uint32_t PH1 = __shfl_xor_sync(0xffffffffu, H[1], 1);
-        const uint32_t PL0 = __shfl_xor_sync(0xffffffffu, Lw[0], 1);
-        const uint32_t PL1 = __shfl_xor_sync(0xffffffffu, Lw[1], 1);
-        uint32_t *aw = act + Wd * ws + 2 * t;
-        if (low) {  // slots j = 0, 1: my half low, partner's high
-          aw[(4 * hh + 0) * p.ncols] = (H[0] & 0xFFFFu) | (PH0 << 16);
-          aw[(4 * hh + 0) * p.ncols + 1] = (Lw[0] & 0xFFFFu) | (PL0 << 16);
-          aw[(4 * hh + 1) * p.ncols] = (H[0] >> 16) | (PH0 & 0xFFFF0000u);
-          aw[(4 * hh + 1) * p.ncols + 1] = (Lw[0] >> 16) | (PL0 & 0xFFFF0000u);
-        } else {    // slots j = 2, 3: partner's half low, mine high
-          aw[(4 * hh + 2) * p.ncols] = (PH1 & 0xFFFFu) | (H[1] << 16);
-          aw[(4 * hh + 2) * p.ncols + 1] = (PL1 & 0xFFFFu) | (Lw[1] << 16);
-          aw[(4 * hh + 3) * p.ncols] = (PH1 >> 16) | (H[1] & 0xFFFF0000u);
-          aw[(4 * hh + 3) * p.ncols + 1] = (PL1 >> 16) | (Lw[1] & 0xFFFF0000u);
-        }
-        sqi = __reduce_add_sync(0xffffffffu, sqi);
-        if (rms) sq2 = warp_sum(sq2);
-        if (lane == 0) {
-          sh.v_inv[warp][t] = m / QMAX;
-          sh.v_sq[warp][t] = sqi;
-          sh.v_ssq[warp][t] += sq2;
-        }
-      }
-    }
+    });
     __syncthreads();
     LBX_PROBE(3);
     // MMA: warp w contracts its own 256-column block of this pass
@@ -502,8 +521,9 @@ LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinS
   }
   __syncthreads();
   if (tid < p.k) {  // reductions without a returned value: no round trip
-    atomicMax(sg.zmax0 + tid, sh.v_zmax[0][tid]);
-    if (sg.z1) atomicMax(sg.zmax1 + tid, sh.v_zmax[1][tid]);
+    const int zo = (row0 / UGRP) * LBX_MAX_TOKENS + tid;  // this unit's 16 rows lie in one U quantisation group
+    atomicMax(sg.zmax0 + zo, sh.v_zmax[0][tid]);
+    if (sg.z1) atomicMax(sg.zmax1 + zo, sh.v_zmax[1][tid]);
   }
   LBX_PROBE(5);
   return true;
@@ -533,6 +553,7 @@ struct ULayout {
   uint32_t *wt;   // ut x wtile_words
   float *su1;     // ut x 48 (u1_0, u1_1, bias)
   uint32_t *act0, *act1;
+  int *ue, *usq;  // [2][ugm][k]: group exponent (UE_NONE: all-zero group), group digit sum
   int *xch;       // [warps][32][2*NCB*4]
 };
 
@@ -543,9 +564,26 @@ LBX_DEV ULayout ulayout(const UParams &p, uint8_t *W, uint8_t *S) {
   const int ws = act_ws(p.ncols);
   L.act0 = reinterpret_cast<uint32_t *>(S);
   L.act1 = L.act0 + p.act_words[0] * ws;
-  L.xch = reinterpret_cast<int *>(L.act1 + p.act_words[1] * ws);
+  L.ue = reinterpret_cast<int *>(L.act1 + p.act_words[1] * ws);
+  L.usq = L.ue + 2 * p.ugm * p.k;
+  L.xch = L.usq + 2 * p.ugm * p.k;
   return L;
 }
+
+constexpr int UE_NONE = 0x7fffffff;  // exponent of an all-zero quantisation group
+
+// largest e with m * 2^e <= QMAX (m > 0), within the normal exponents
+LBX_DEV int u_group_exp(float m) {
+  int em;
+  frexpf(m, &em);  // m = f * 2^em, f in [0.5, 1)
+  int e = 15 - em;
+  if (e > 127) return 127;
+  if (ldexpf(m, e) > QMAX) --e;
+  return max(e, -126);
+}
+LBX_DEV float pow2f(int e) { return __int_as_float((e + 127) << 23); }  // e in [-126, 127]
+// v / 2^s rounded half up, s >= 0 (|v| < 2^24)
+LBX_DEV int rshr(int v, int s) { return s == 0 ? v : s > 30 ? 0 : (v + (1 << (s - 1))) >> s; }
 
 LBX_DEV int useg_of(const UParams &p, int unit) {
   int s = 0;
@@ -608,7 +646,6 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
   const uint32_t par = sh.par[tile];
   unsigned call = 0;  // this call's number (fused all-gather); loaded early, used in the epilogue
   if constexpr (PEER) call = __ldcg(p.seq) + 1u;
-  if (zero && tid < 2 * LBX_MAX_TOKENS) (&sh.u_sq[0][0])[tid] = 0;  // ordered by the CTA barrier below
   LBX_PROBE(11);
 
   // items (t, b, W, slot): each (t, b) segment is a multiple of 32 items, so a
@@ -648,14 +685,27 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
   // one L2 round trip
   load_batch(warp * 32, zv);
 
-  // ---- per-(branch, token) scale from the V-stage maxima, 16-bit digits of z
-  if (tid < 2 * p.k) {
-    const int b = tid / p.k, t = tid - b * p.k;
-    const float m = (b < sg.nbr) ? __int_as_float(__ldcg(sg.zmax[b] + t)) : 0.f;
-    sh.u_inv[b][t] = m / QMAX;
-    sh.u_scale[b][t] = m > 0.f ? QMAX / m : 0.f;
+  // ---- quantisation scales: a power of two per (branch, 128-rank group,
+  // token) from the V-stage maxima, and per (branch, token) the coarsest one
+  const int ng0 = (sg.words[0] + 3) / 4, ng1 = sg.nbr > 1 ? (sg.words[1] + 3) / 4 : 0;
+  int *ue = L.ue, *usq = L.usq;
+  const int gk = p.ugm * p.k;
+  for (int i = tid; i < (ng0 + ng1) * p.k; i += UTHREADS) {
+    const int b = i < ng0 * p.k ? 0 : 1;
+    const int j = b ? i - ng0 * p.k : i;  // group * k + token
+    const int grp = j / p.k, tk = j - grp * p.k;
+    const float m = __int_as_float(__ldcg(sg.zmax[b] + grp * LBX_MAX_TOKENS + tk));
+    ue[b * gk + j] = m > 0.f ? u_group_exp(m) : UE_NONE;
+    usq[b * gk + j] = 0;
   }
   __syncthreads();
+  if (tid < 2 * p.k) {
+    const int b = tid / p.k, t = tid - b * p.k;
+    const int ng = b ? ng1 : ng0;
+    int ec = UE_NONE;
+    for (int G = 0; G < ng; ++G) ec = min(ec, ue[b * gk + G * p.k + t]);
+    sh.u_ec[b][t] = ec == UE_NONE ? 0 : ec;
+  }
   LBX_PROBE(12);
   for (int base0 = warp * 32; base0 < total; base0 += UB * UTHREADS) {
     // the next batch's z loads are in flight while this batch is quantised
@@ -670,7 +720,9 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
       const int b = rem < nw0 * 8 ? 0 : 1;
       const int rr = b ? rem - nw0 * 8 : rem;
       const int Wd = rr >> 3, slot = rr & 7;
-      const float sc = sh.u_scale[b][t];
+      const int gi = b * gk + (Wd >> 2) * p.k + t;  // a warp's 32 items are one group
+      const int ex = ue[gi];
+      const float sc = ex == UE_NONE ? 0.f : pow2f(ex);
       int hi[4], lo[4], sq = 0;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -682,7 +734,7 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
       aw[slot * p.ncols] = pack4(hi[0], hi[1], hi[2], hi[3]);
       aw[slot * p.ncols + 1] = pack4(lo[0], lo[1], lo[2], lo[3]);
       sq = __reduce_add_sync(0xffffffffu, sq);
-      if (lane == 0) atomicAdd(&sh.u_sq[b][t], sq);
+      if (lane == 0) atomicAdd(&usq[gi], sq);
     }
     if (more) {
 #pragma unroll
@@ -701,58 +753,97 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
   if (tid < ut && (unit - sg.cta0) * (16 * ut) + 16 * tid < sg.out) sh.par[tid] ^= 1u;
   LBX_PROBE(14);
 
-  int acc0[NCB][4], acc1[NCB][4];
+  // ---- contraction: every 128-rank group on its own (exact int32), rounded
+  // to its branch's coarsest exponent by an integer shift; the rounded values
+  // add exactly, so any split of the groups over warps, CTAs or clusters gives
+  // the same bits
+  int I0[NCB][2], I1[NCB][2];
 #pragma unroll
-  for (int cb = 0; cb < NCB; ++cb)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc0[cb][e] = acc1[cb][e] = 0;
-  // this warp's share of the flattened (branch, group) list
-  const int ng0 = (sg.words[0] + 3) / 4, ng1 = sg.nbr > 1 ? (sg.words[1] + 3) / 4 : 0;
-  const int ngt = ng0 + ng1;
+  for (int cb = 0; cb < NCB; ++cb) I0[cb][0] = I0[cb][1] = I1[cb][0] = I1[cb][1] = 0;
+  const int ngt = ng0 + ng1;  // this warp's share of the flattened (branch, group) list
   const int ga = (split * ngt) / nsplit, gb = ((split + 1) * ngt) / nsplit;
   if (active && ok) {
-    if (ga < ng0)
-      sign_mma<NCB>(acc0, mywt0 + g * sg.pitch[0], mywt0 + (g + 8) * sg.pitch[0], act0, ws,
-                    p.ncols, ga, min(gb, ng0), lane);
-    if (gb > ng0)
-      sign_mma<NCB>(acc1, mywt1 + g * sg.pitch[1], mywt1 + (g + 8) * sg.pitch[1], act1, ws,
-                    p.ncols, max(ga, ng0) - ng0, gb - ng0, lane);
+    for (int G = ga; G < gb; ++G) {
+      const int b = G < ng0 ? 0 : 1;
+      const int Gl = b ? G - ng0 : G;
+      const uint32_t *wt = b ? mywt1 : mywt0;
+      const int pt = sg.pitch[b];
+      int acc[NCB][4];
+#pragma unroll
+      for (int cb = 0; cb < NCB; ++cb) acc[cb][0] = acc[cb][1] = acc[cb][2] = acc[cb][3] = 0;
+      sign_mma<NCB>(acc, wt + g * pt, wt + (g + 8) * pt, b ? act1 : act0, ws, p.ncols, Gl, Gl + 1, lane);
+#pragma unroll
+      for (int cb = 0; cb < NCB; ++cb) {
+        const int t = cb * 4 + q;
+        if (t < p.k) {
+          const int gi = b * gk + Gl * p.k + t;
+          const int ex = ue[gi];
+          if (ex != UE_NONE) {
+            const int sft = ex - sh.u_ec[b][t];
+            const int sq = usq[gi];
+            const int va = rshr(sq + 2 * (256 * acc[cb][0] + acc[cb][1]), sft);
+            const int vb = rshr(sq + 2 * (256 * acc[cb][2] + acc[cb][3]), sft);
+            if (b) {
+              I1[cb][0] += va;
+              I1[cb][1] += vb;
+            } else {
+              I0[cb][0] += va;
+              I0[cb][1] += vb;
+            }
+          }
+        }
+      }
+    }
   }
   if (nsplit > 1) {
     int *xw = xch + (warp * 32 + lane) * (8 * NCB);
     if (split > 0) {
 #pragma unroll
-      for (int cb = 0; cb < NCB; ++cb)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          xw[cb * 4 + e] = acc0[cb][e];
-          xw[4 * NCB + cb * 4 + e] = acc1[cb][e];
-        }
+      for (int cb = 0; cb < NCB; ++cb) {
+        xw[cb * 4 + 0] = I0[cb][0];
+        xw[cb * 4 + 1] = I0[cb][1];
+        xw[cb * 4 + 2] = I1[cb][0];
+        xw[cb * 4 + 3] = I1[cb][1];
+      }
     }
     __syncthreads();
     if (split == 0) {
       for (int sp = 1; sp < nsplit; ++sp) {
         const int *xr = xch + ((sp * ut + tile) * 32 + lane) * (8 * NCB);
 #pragma unroll
-        for (int cb = 0; cb < NCB; ++cb)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            acc0[cb][e] += xr[cb * 4 + e];
-            acc1[cb][e] += xr[4 * NCB + cb * 4 + e];
-          }
+        for (int cb = 0; cb < NCB; ++cb) {
+          I0[cb][0] += xr[cb * 4 + 0];
+          I0[cb][1] += xr[cb * 4 + 1];
+          I1[cb][0] += xr[cb * 4 + 2];
+          I1[cb][1] += xr[cb * 4 + 3];
+        }
       }
     }
   }
   LBX_PROBE(15);
   // the last unit to get here clears the call's bookkeeping words for the next
-  // call (every unit has read its scales before this point)
-  if (tid == 0) {
-    __threadfence();
-    const unsigned done = atomicAdd(p.ticket, 1u);
-    if (done == (unsigned)nunits - 1) {
-      for (int i = 0; i < p.nzmax; ++i) p.zmax_all[i] = 0;
-      *p.ticket = 0u;
+  // call (every unit has read its scales before this point).  The last warp
+  // does it: it has no output stores (nsplit >= 2), so the ticket's round trip
+  // stays off the epilogue
+  if (warp == UWARPS - 1) {
+    unsigned done = 0;
+    if (lane == 0) {
       __threadfence();
+      done = atomicAdd(p.ticket, 1u);
+    }
+    done = __shfl_sync(0xffffffffu, done, 0);
+    if (done == (unsigned)nunits - 1) {
+      for (int si = 0; si < p.nseg; ++si)
+        for (int b = 0; b < p.seg[si].nbr; ++b) {
+          int *zs = p.zmax_all + (si * 2 + b) * ZGMAX * LBX_MAX_TOKENS;
+          const int nw = (p.seg[si].rank[b] + UGRP - 1) / UGRP * LBX_MAX_TOKENS;
+          for (int i = lane; i < nw; i += 32) zs[i] = 0;
+        }
+      __syncwarp();
+      if (lane == 0) {
+        *p.ticket = 0u;
+        __threadfence();
+      }
     }
   }
   if (!ok) return false;
@@ -765,13 +856,8 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
       for (int hrow = 0; hrow < 2; ++hrow) {
         const int nl = g + 8 * hrow;
         const int n = n0 + nl;
-        float v = myu1[nl] *
-                  (__int2float_rn(sh.u_sq[0][t] + 2 * (256 * acc0[cb][2 * hrow] + acc0[cb][2 * hrow + 1])) *
-                   sh.u_inv[0][t]);
-        if (sg.nbr > 1)
-          v += myu1[16 + nl] *
-               (__int2float_rn(sh.u_sq[1][t] + 2 * (256 * acc1[cb][2 * hrow] + acc1[cb][2 * hrow + 1])) *
-                sh.u_inv[1][t]);
+        float v = myu1[nl] * ldexpf(__int2float_rn(I0[cb][hrow]), -sh.u_ec[0][t]);
+        if (sg.nbr > 1) v += myu1[16 + nl] * ldexpf(__int2float_rn(I1[cb][hrow]), -sh.u_ec[1][t]);
         if (sg.bias) v += myu1[32 + nl];
         const int64_t off = (int64_t)t * sg.y_ld + n;
         if constexpr (PEER) {  // NVLink stores of (call number, value) words
@@ -797,7 +883,6 @@ __global__ void __launch_bounds__(UTHREADS, 2) ustage_kernel(const __grid_consta
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ LinShm sh;
   LBX_PROBE(10);
-  if (threadIdx.x < 2 * LBX_MAX_TOKENS) (&sh.u_sq[0][0])[threadIdx.x] = 0;
   linshm_init(sh);  // (ends with a CTA barrier)
   // scratch first, weights after: measured faster than the reverse order
   uint8_t *S = smem_raw;
@@ -813,12 +898,15 @@ __global__ void __launch_bounds__(UTHREADS, 2) ustage_kernel(const __grid_consta
 // ---------------------------------------------------------------------------
 constexpr size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
 
-// scratch: [header: zmax words and the unit ticket of a call (zero between
-// calls), the grid barrier of a persistent program] then z [k][rank] of every
-// (projection, branch)
+// scratch: [header: the unit ticket of a call, the grid barrier of a
+// persistent program, the maxima slots of z per (projection, branch, 128-rank
+// group, token); zero between calls, at fixed offsets so that calls of any
+// shape may share a workspace] then z [k][rank] of every (projection, branch)
 constexpr size_t WS_GRIDBAR = 400;  // byte offset of the grid barrier words in the header
-constexpr size_t WS_HDR = al256(WS_GRIDBAR + 16);
-static_assert((2 * LBX_MAX_PROJ * LBX_MAX_TOKENS + 1) * sizeof(int) <= WS_GRIDBAR, "header layout");
+constexpr size_t WS_ZMAX = 512;     // byte offset of the maxima slots
+constexpr size_t WS_HDR = al256(WS_ZMAX + (size_t)LBX_MAX_PROJ * 2 * ZGMAX * LBX_MAX_TOKENS * 4);
+
+static int u_groups(int rank) { return (rank + UGRP - 1) / UGRP; }
 
 static size_t ws_bytes_for(const lbx_proj *projs, int n_proj, int k) {
   size_t tot = WS_HDR;
@@ -843,6 +931,7 @@ static int validate(const lbx_proj *projs, int n_proj) {
       const lbx_branch &br = pr.br[b];
       LBX_CHECK_SUP(br.rank > 0 && br.rank % 8 == 0, "rank must be a positive multiple of 8 (got %d)",
                     br.rank);
+      LBX_CHECK_SUP(br.rank <= UGRP * ZGMAX, "rank must be at most %d (got %d)", UGRP * ZGMAX, br.rank);
       LBX_CHECK_ARG(br.mid && br.u_sign && br.u1, "branch %d: mid/u_sign/u1 required", b);
       LBX_CHECK_ARG(aligned16(br.u_sign) && aligned16(br.mid), "u_sign/mid must be 16-byte aligned");
       if (br.v_sign) {
@@ -873,6 +962,8 @@ static int check_args(const lbx_proj *projs, const lbx_linear_args *a) {
   LBX_CHECK_ARG(a->epilogue == LBX_EPI_STORE || (a->epilogue == LBX_EPI_ADD && a->y_dtype == LBX_F32),
                 "bad epilogue (ADD needs fp32 y)");
   for (int i = 0; i < a->n_proj; ++i) LBX_CHECK_ARG(a->y[i], "y[%d] is NULL", i);
+  LBX_CHECK_ARG(a->exec == LBX_EXEC_AUTO || a->exec == LBX_EXEC_KERNELS || a->exec == LBX_EXEC_CLUSTER,
+                "bad exec (LBX_EXEC_AUTO, _KERNELS or _CLUSTER)");
   return LBX_OK;
 }
 
@@ -923,9 +1014,10 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
   const int Wv = K / 32;
   const bool rms = a->prologue == LBX_PRO_RMSNORM;
 
-  // scratch: bookkeeping, then z of every (projection, branch), [k][rank]
-  int *zmax_all = reinterpret_cast<int *>(ws);
-  unsigned *ticket = reinterpret_cast<unsigned *>(zmax_all + 2 * LBX_MAX_PROJ * LBX_MAX_TOKENS);
+  // scratch: header (ticket, maxima slots), then z of every (projection,
+  // branch), [k][rank]
+  unsigned *ticket = reinterpret_cast<unsigned *>(ws);
+  int *zmax_all = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(ws) + WS_ZMAX);
   float *zp[LBX_MAX_PROJ][2] = {};
   int *zm[LBX_MAX_PROJ][2] = {};
   {
@@ -933,7 +1025,7 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
     for (int i = 0; i < n_proj; ++i)
       for (int b = 0; b < projs[i].n_branches; ++b) {
         zp[i][b] = reinterpret_cast<float *>(w);
-        zm[i][b] = zmax_all + (2 * i + b) * LBX_MAX_TOKENS;
+        zm[i][b] = zmax_all + (i * 2 + b) * ZGMAX * LBX_MAX_TOKENS;
         w += al256((size_t)k * projs[i].br[b].rank * 4);
       }
   }
@@ -988,7 +1080,7 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
   up.ncols = ncols;
   up.ydt = a->y_dtype;
   up.epi = a->epilogue;
-  int maxw[2] = {0, 0}, maxtile = 0, tiles = 0;
+  int maxw[2] = {0, 0}, maxtile = 0, tiles = 0, ugm = 1;
   for (int i = 0; i < n_proj; ++i) {
     const lbx_proj &pr = projs[i];
     USeg &sg = up.seg[i];
@@ -1009,6 +1101,7 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
       sg.perrow[b] = (sg.words[b] % 4) == 0;
       sg.pitch[b] = sg.perrow[b] ? row_pitch(sg.words[b]) : sg.words[b];
       maxw[b] = std::max(maxw[b], 4 * ((sg.words[b] + 3) / 4));
+      ugm = std::max(ugm, u_groups(sg.rank[b]));
       tw += 16 * sg.pitch[b] + 4;
     }
     maxtile = std::max(maxtile, tw);
@@ -1016,12 +1109,14 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
   }
   up.act_words[0] = maxw[0];
   up.act_words[1] = maxw[1];
+  up.ugm = ugm;
   up.wtile_words = (maxtile + 3) & ~3;
   // row tiles per CTA: enough CTAs to cover the SMs, within shared memory; the
   // remaining warps of a CTA split the ranks of its tiles
   int ut = UT_MAX;
   while (ut > 1 && tiles / ut < 120) ut >>= 1;
-  const size_t u_s = al256((size_t)(maxw[0] + maxw[1]) * act_ws(ncols) * 4 + (size_t)UWARPS * 32 * 8 * ncb * 4);
+  const size_t u_s = al256((size_t)(maxw[0] + maxw[1]) * act_ws(ncols) * 4 + (size_t)4 * ugm * k * 4 +
+                           (size_t)UWARPS * 32 * 8 * ncb * 4);
   for (; ut >= 1; ut >>= 1) {
     const size_t u_w = al256((size_t)ut * up.wtile_words * 4 + (size_t)ut * 48 * 4);
     if (u_w + u_s <= umax) break;
@@ -1029,7 +1124,6 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
   LBX_CHECK_SUP(ut >= 1, "U-stage needs too much shared memory (rank too large for k=%d)", k);
   up.ut = ut;
   up.zmax_all = zmax_all;
-  up.nzmax = 2 * LBX_MAX_PROJ * LBX_MAX_TOKENS;
   up.ticket = ticket;
   P.u_w = al256((size_t)ut * up.wtile_words * 4 + (size_t)ut * 48 * 4);
   P.u_s = u_s;
@@ -1054,6 +1148,7 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
   LinPrep P;
   rc = prep_linear(projs, a, tok0, k, ws, vmax, umax, P);
   if (rc) return rc;
+  LBX_CHECK_SUP(a->exec != LBX_EXEC_CLUSTER, "the cluster executor is not available");
   const bool pdl = a->use_pdl != 0;
   auto vk = P.ncb == 1 ? vstage_kernel<1> : P.ncb == 2 ? vstage_kernel<2> : vstage_kernel<4>;
   auto uk = P.ncb == 1 ? ustage_kernel<1> : P.ncb == 2 ? ustage_kernel<2> : ustage_kernel<4>;
@@ -1145,8 +1240,8 @@ extern "C" int lbx_linear_noalloc(const lbx_proj *projs, const lbx_linear_args *
     }
     scratch = g_noalloc_ptr[dev];
   }
-  // the bookkeeping words must start at zero; clear them rather than trusting
-  // whatever an earlier (possibly failed) call left behind
+  // the bookkeeping words (header and z maxima) must start at zero; clear them
+  // rather than trusting whatever an earlier (possibly failed) call left behind
   e = cudaMemsetAsync(scratch, 0, WS_HDR, stream);
   if (e != cudaSuccess) return cuda_status(e, "lbx_linear_noalloc: clear scratch");
   return lbx_linear_verify(projs, a, scratch, NOALLOC_SCRATCH_BYTES, stream);

@@ -244,8 +244,13 @@ def linear_group(projs: Sequence[PackedLinear], x: torch.Tensor, outs: Sequence[
                  prologue: int = L.LBX_PRO_NONE, norm_w: Optional[torch.Tensor] = None,
                  eps: float = 1e-6, x2: Optional[torch.Tensor] = None,
                  epilogue: int = L.LBX_EPI_STORE, use_pdl: bool = True,
-                 ws: Optional[torch.Tensor] = None, arr=None) -> None:
-    """Run 1..3 LittleBit projections that share the input x [k, in]."""
+                 ws: Optional[torch.Tensor] = None, arr=None,
+                 exec_mode: int = L.LBX_EXEC_AUTO) -> None:
+    """Run 1..3 LittleBit projections that share the input x [k, in].
+
+    ``exec_mode``: LBX_EXEC_AUTO (one cluster launch when the call fits it,
+    else the two stage grids), LBX_EXEC_KERNELS or LBX_EXEC_CLUSTER; all give
+    the same bits."""
     _cuda("x", x)
     k = x.shape[0]
     a = L.LinearArgs()
@@ -257,6 +262,7 @@ def linear_group(projs: Sequence[PackedLinear], x: torch.Tensor, outs: Sequence[
     a.epilogue = epilogue
     a.eps = float(eps)
     a.use_pdl = 1 if use_pdl else 0
+    a.exec = exec_mode
     a.x = _p(x)
     a.x2 = _p(x2)
     a.norm_w = _p(norm_w)
