@@ -62,8 +62,13 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def traffic_from_profiles(k: int):
-    f = ROOT / "profiles" / f"linear_c2_k{k}.md"
+def traffic_from_profiles(k: int, exec_name: str):
+    """DRAM bytes per layer of the committed ncu capture of this executor
+    (None when there is none: the persistent program has no per-layer launch)."""
+    name = {"kernels": f"linear_c2_k{k}.md", "cluster": f"linear_cluster_c2_k{k}.md"}.get(exec_name)
+    if name is None:
+        return None
+    f = ROOT / "profiles" / name
     if not f.exists():
         return None
     m = re.search(r"traffic_bytes_per_launch\s*=\s*([0-9]+)", f.read_text())
@@ -414,6 +419,7 @@ def run_row_shard(args, dev, rank, ws, reps: int = 200):
 
 
 def run_ours(args):
+    from littlebit_b200 import _lib as L
     from littlebit_b200 import ops
 
     rank, ws, lrank = dist_init()
@@ -433,7 +439,13 @@ def run_ours(args):
 
     def step_kernels():  # one V-stage + one U-stage grid per layer, chained with PDL
         for i in range(P):
-            ops.linear_group([pool[i]], acts[i], [acts[i + 1]], use_pdl=args.pdl, ws=wsb, arr=arrs[i])
+            ops.linear_group([pool[i]], acts[i], [acts[i + 1]], use_pdl=args.pdl, ws=wsb, arr=arrs[i],
+                             exec_mode=L.LBX_EXEC_KERNELS)
+
+    def step_cluster():  # one split-rank cluster launch per layer, chained with PDL
+        for i in range(P):
+            ops.linear_group([pool[i]], acts[i], [acts[i + 1]], use_pdl=args.pdl, ws=wsb, arr=arrs[i],
+                             exec_mode=L.LBX_EXEC_CLUSTER)
 
     def step_program():  # the whole chain as one persistent program
         ops.linear_chain(pool, acts, ws=wsc, arr=arr_all, ptrs=ptrs)
@@ -464,7 +476,8 @@ def run_ours(args):
         del graph
         return out
 
-    main_fn = step_program if args.exec == "program" else step_kernels
+    execs = {"cluster": step_cluster, "kernels": step_kernels, "program": step_program}
+    main_fn = execs[args.exec]
     sampler = ClockSampler(lrank)
     sampler.start()
     time.sleep(0.3)
@@ -474,14 +487,20 @@ def run_ours(args):
     if not torch.isfinite(acts[-1].float()).all():
         raise RuntimeError("non-finite output in the layer chain")
     y_main = acts[-1].clone()
-    t_other = timed_graph(step_kernels if args.exec == "program" else step_program)
-    if not torch.equal(acts[-1], y_main):
-        raise RuntimeError("program and kernel paths disagree")
+    # the other executors: timed the same way, and they must give the same bits
+    exec_t = {}
+    for name, fn in execs.items():
+        if name == args.exec:
+            continue
+        exec_t[name] = timed_graph(fn)
+        if not torch.equal(acts[-1], y_main):
+            raise RuntimeError(f"{name} and {args.exec} executors disagree")
 
     b_layer, packed = layer_bytes(k)
     total_bytes = b_layer * P * args.steps * ws
     value = total_bytes / (t_ms * 1e-3) / 1e9
-    other_gbs = total_bytes / (t_other * 1e-3) / 1e9
+    exec_gbs = {n: round(total_bytes / (t_o * 1e-3) / 1e9, 2) for n, t_o in exec_t.items()}
+    exec_gbs[args.exec] = round(value, 2)
     per_launch_s = t_ms * 1e-3 / (P * args.steps)
     peak, peak_kind = peaks()
     achieved = b_layer / per_launch_s / 1e9
@@ -512,7 +531,7 @@ def run_ours(args):
     row_shard = run_row_shard(args, dev, rank, ws) if ws > 1 else None
 
     if rank == 0:
-        traffic = traffic_from_profiles(k) if args.exec == "kernels" else None
+        traffic = traffic_from_profiles(k, args.exec)
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 4),
@@ -524,15 +543,17 @@ def run_ours(args):
                        "pool_mb": round(P * (packed + sum(4 * (IN_F + r + OUT_F) for r in RANKS)) / 1e6, 1),
                        "l2": "weight pool > 2x L2 (126 MB): no flush needed",
                        "parallelism": f"dp{ws} (independent replicas)",
-                       "exec": ("one persistent cooperative program per step (lbx_linear_chain)"
-                                if args.exec == "program" else "two kernels per layer, PDL-chained")},
+                       "exec": {"program": "one persistent cooperative program per step (lbx_linear_chain)",
+                                "kernels": "two kernels per layer (V-stage, U-stage grids), PDL-chained",
+                                "cluster": "one split-rank cluster launch per layer (16-CTA clusters), "
+                                           "PDL-chained"}[args.exec]},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": b_layer,
-                         "launch": "one LittleBit layer (V-stage + U-stage units)",
+                         "launch": "one LittleBit layer",
                          "mean_launch_us": round(per_launch_s * 1e6, 3)},
-            "other_exec_gbs": round(other_gbs, 2),
+            "exec_gbs": exec_gbs,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": 2 * k * IN_F, "d2h_bytes_per_step": 2 * k * OUT_F,
                     "ms_per_step": round(t2 / args.steps, 4),
@@ -540,7 +561,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "decode": decode,
             "row_shard": row_shard,
-            "gpu_launches": (1 if args.exec == "program" else 2 * P) * args.steps,
+            "gpu_launches": {"program": 1, "kernels": 2 * P, "cluster": P}[args.exec] * args.steps,
             "clocks": clocks,
         }
         print(json.dumps(out))
@@ -559,8 +580,9 @@ def main():
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--pool", type=int, default=128)
     ap.add_argument("--pdl", type=int, default=1)
-    ap.add_argument("--exec", default="kernels", choices=["program", "kernels"],
-                    help="program: each step is one persistent launch; kernels: one grid per stage")
+    ap.add_argument("--exec", default="kernels", choices=["kernels", "cluster", "program"],
+                    help="cluster: one split-rank cluster launch per layer; kernels: one grid per stage; "
+                         "program: each step is one persistent launch")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--decode", type=int, default=1, help="also run the 7B-shape decode section")

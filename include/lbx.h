@@ -97,11 +97,12 @@ typedef struct lbx_linear_args {
   int32_t _pad;
 } lbx_linear_args;
 
-/* Bytes of device scratch one lbx_linear / lbx_linear_verify call needs.
- * The workspace must be zero-filled once when it is allocated: it holds a few
- * bookkeeping words (per-token maxima, a CTA counter) that every call expects
- * at zero and leaves at zero when it completes.  Calls sharing a workspace must
- * be ordered on one stream. */
+/* Bytes of device scratch one lbx_linear / lbx_linear_verify call needs on
+ * any executor (the two stage grids need less; LBX_EXEC_CLUSTER needs this).
+ * The workspace must be zero-filled once when it is allocated: its header
+ * holds a few bookkeeping words (the cluster executor's tickets) that every
+ * call expects at zero and leaves at zero when it completes.  Calls sharing a
+ * workspace must be ordered on one stream. */
 size_t lbx_linear_workspace_size(const lbx_proj *projs /* host */, int32_t n_proj,
                                  int32_t n_tokens);
 

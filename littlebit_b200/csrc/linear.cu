@@ -61,8 +61,7 @@ struct VSeg {
   const float *mid1;     // [rank] (shared-V residual) or nullptr
   float *z0;             // [k][rank]
   float *z1;             // [k][rank] or nullptr
-  int *zmax0;            // [group][LBX_MAX_TOKENS] running max |z0| per 128-rank group (float bits), zero before the call
-  int *zmax1;            // [group][LBX_MAX_TOKENS] or nullptr
+  int *tmax;             // [tile][2][k] per-unit max |z0|, |z1| per token (float bits)
   int rank;
   int tile0;             // first CTA (16-row tile) of this segment
 };
@@ -85,7 +84,8 @@ struct USeg {
   const int32_t *u_sign[2];
   const float *u1[2];
   const float *z[2];     // [k][rank] from the V-stage
-  const int *zmax[2];    // [group][LBX_MAX_TOKENS] max |z| per 128-rank group and token (float bits), from the V-stage
+  const int *tmax[2];    // per-unit maxima [tile][2][k] of the V segment that produced z[b] (float bits)
+  int tsel[2];           // which of the two per-unit maxima belongs to z[b]
   int rank[2];
   int words[2];   // ceil(rank/32)
   int pitch[2];   // smem row pitch (words)
@@ -106,8 +106,6 @@ struct UParams {
   int act_words[2];   // max over projections of 4*ceil(words/4)
   int wtile_words;    // per-tile weight region (words)
   int ugm;            // max quantisation groups of a branch (scratch arrays [2][ugm][k])
-  int *zmax_all;      // maxima slots [proj][branch][ZGMAX][LBX_MAX_TOKENS] (the used ones reset by the last unit)
-  unsigned *ticket;   // unit completion counter (zero before and after the call)
   int s_bytes;        // shared-memory scratch region of a standalone launch (weights follow)
   // fused all-gather of a row-sharded layer (one projection): every result
   // goes to each rank's exchange buffer as one 8-byte word (call number << 32
@@ -520,10 +518,10 @@ LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinS
     }
   }
   __syncthreads();
-  if (tid < p.k) {  // reductions without a returned value: no round trip
-    const int zo = (row0 / UGRP) * LBX_MAX_TOKENS + tid;  // this unit's 16 rows lie in one U quantisation group
-    atomicMax(sg.zmax0 + zo, sh.v_zmax[0][tid]);
-    if (sg.z1) atomicMax(sg.zmax1 + zo, sh.v_zmax[1][tid]);
+  if (tid < p.k) {  // this unit's maxima: plain stores, overwritten by every call (nothing to reset)
+    int *tm = sg.tmax + (int64_t)(unit - sg.tile0) * 2 * p.k;
+    tm[tid] = sh.v_zmax[0][tid];
+    if (sg.z1) tm[p.k + tid] = sh.v_zmax[1][tid];
   }
   LBX_PROBE(5);
   return true;
@@ -694,7 +692,19 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
     const int b = i < ng0 * p.k ? 0 : 1;
     const int j = b ? i - ng0 * p.k : i;  // group * k + token
     const int grp = j / p.k, tk = j - grp * p.k;
-    const float m = __int_as_float(__ldcg(sg.zmax[b] + grp * LBX_MAX_TOKENS + tk));
+    // max over the group's (up to) 8 V units: all loads in flight together
+    const int nt = (sg.rank[b] + 15) / 16;
+    const int *tm = sg.tmax[b] + sg.tsel[b] * p.k + tk;
+    int v[UGRP / 16];
+#pragma unroll
+    for (int e = 0; e < UGRP / 16; ++e) {
+      const int tile = grp * (UGRP / 16) + e;
+      v[e] = tile < nt ? __ldcg(tm + (int64_t)tile * 2 * p.k) : 0;
+    }
+    int mm = 0;
+#pragma unroll
+    for (int e = 0; e < UGRP / 16; ++e) mm = max(mm, v[e]);
+    const float m = __int_as_float(mm);
     ue[b * gk + j] = m > 0.f ? u_group_exp(m) : UE_NONE;
     usq[b * gk + j] = 0;
   }
@@ -821,31 +831,7 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
     }
   }
   LBX_PROBE(15);
-  // the last unit to get here clears the call's bookkeeping words for the next
-  // call (every unit has read its scales before this point).  The last warp
-  // does it: it has no output stores (nsplit >= 2), so the ticket's round trip
-  // stays off the epilogue
-  if (warp == UWARPS - 1) {
-    unsigned done = 0;
-    if (lane == 0) {
-      __threadfence();
-      done = atomicAdd(p.ticket, 1u);
-    }
-    done = __shfl_sync(0xffffffffu, done, 0);
-    if (done == (unsigned)nunits - 1) {
-      for (int si = 0; si < p.nseg; ++si)
-        for (int b = 0; b < p.seg[si].nbr; ++b) {
-          int *zs = p.zmax_all + (si * 2 + b) * ZGMAX * LBX_MAX_TOKENS;
-          const int nw = (p.seg[si].rank[b] + UGRP - 1) / UGRP * LBX_MAX_TOKENS;
-          for (int i = lane; i < nw; i += 32) zs[i] = 0;
-        }
-      __syncwarp();
-      if (lane == 0) {
-        *p.ticket = 0u;
-        __threadfence();
-      }
-    }
-  }
+  (void)nunits;
   if (!ok) return false;
   if (active && split == 0) {
 #pragma unroll
@@ -893,26 +879,58 @@ __global__ void __launch_bounds__(UTHREADS, 2) ustage_kernel(const __grid_consta
   ustage_run<NCB, PEER>(p, blockIdx.x, gridDim.x, W, S, sh, false);
 }
 
+#include "slice.cuh"
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 constexpr size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
 
-// scratch: [header: the unit ticket of a call, the grid barrier of a
-// persistent program, the maxima slots of z per (projection, branch, 128-rank
-// group, token); zero between calls, at fixed offsets so that calls of any
-// shape may share a workspace] then z [k][rank] of every (projection, branch)
+// scratch: [header: the cluster executor's range tickets and the grid barrier
+// of a persistent program (zero between calls, at fixed offsets)] then z
+// [k][rank] of every (projection, branch) and the per-unit maxima [tile][2][k]
+// of every V segment (both overwritten by every call)
 constexpr size_t WS_GRIDBAR = 400;  // byte offset of the grid barrier words in the header
-constexpr size_t WS_ZMAX = 512;     // byte offset of the maxima slots
-constexpr size_t WS_HDR = al256(WS_ZMAX + (size_t)LBX_MAX_PROJ * 2 * ZGMAX * LBX_MAX_TOKENS * 4);
+constexpr size_t WS_HDR = 512;
 
 static int u_groups(int rank) { return (rank + UGRP - 1) / UGRP; }
 
-static size_t ws_bytes_for(const lbx_proj *projs, int n_proj, int k) {
+constexpr size_t WS_SLTICKET = 16;  // byte offset of the cluster executor's range tickets
+static_assert(WS_SLTICKET + LBX_MAX_PROJ * SL_S * 4 <= WS_GRIDBAR, "header layout");
+
+// cluster executor scratch after the header: per projection the exact group
+// sums [groups][k][out] and the group exponents [2][ZGMAX][LBX_MAX_TOKENS]
+static size_t slice_ws_bytes(const lbx_proj *projs, int n_proj, int k) {
+  size_t tot = WS_HDR;
+  for (int i = 0; i < n_proj; ++i) {
+    size_t ng = 0;
+    for (int b = 0; b < projs[i].n_branches; ++b) ng += (projs[i].br[b].rank + UGRP - 1) / UGRP;
+    tot += al256(ng * k * projs[i].out_features * 4) + al256((size_t)2 * ZGMAX * LBX_MAX_TOKENS * 4);
+  }
+  return tot;
+}
+
+// scratch of the two stage grids
+static size_t stage_ws_bytes(const lbx_proj *projs, int n_proj, int k) {
   size_t tot = WS_HDR;
   for (int i = 0; i < n_proj; ++i)
-    for (int b = 0; b < projs[i].n_branches; ++b) tot += al256((size_t)k * projs[i].br[b].rank * 4);
+    for (int b = 0; b < projs[i].n_branches; ++b) {
+      tot += al256((size_t)k * projs[i].br[b].rank * 4);
+      if (projs[i].br[b].v_sign) tot += al256((size_t)(projs[i].br[b].rank + 15) / 16 * 2 * k * 4);
+    }
   return tot;
+}
+
+// scratch of a call on any executor (the public workspace size)
+static size_t ws_bytes_for(const lbx_proj *projs, int n_proj, int k) {
+  return std::max(stage_ws_bytes(projs, n_proj, k), slice_ws_bytes(projs, n_proj, k));
+}
+
+// scratch of this call on the executor it selects
+static size_t ws_bytes_call(const lbx_proj *projs, const lbx_linear_args *a) {
+  const int k = a->n_tokens < LBX_MAX_TOKENS ? a->n_tokens : LBX_MAX_TOKENS;
+  return a->exec == LBX_EXEC_CLUSTER ? ws_bytes_for(projs, a->n_proj, k)
+                                     : stage_ws_bytes(projs, a->n_proj, k);
 }
 
 static int validate(const lbx_proj *projs, int n_proj) {
@@ -1014,19 +1032,20 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
   const int Wv = K / 32;
   const bool rms = a->prologue == LBX_PRO_RMSNORM;
 
-  // scratch: header (ticket, maxima slots), then z of every (projection,
-  // branch), [k][rank]
-  unsigned *ticket = reinterpret_cast<unsigned *>(ws);
-  int *zmax_all = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(ws) + WS_ZMAX);
+  // scratch: header, then z of every (projection, branch), [k][rank], and the
+  // per-unit maxima of every V segment, [tile][2][k]
   float *zp[LBX_MAX_PROJ][2] = {};
-  int *zm[LBX_MAX_PROJ][2] = {};
+  int *tm[LBX_MAX_PROJ][2] = {};
   {
     uint8_t *w = reinterpret_cast<uint8_t *>(ws) + WS_HDR;
     for (int i = 0; i < n_proj; ++i)
       for (int b = 0; b < projs[i].n_branches; ++b) {
         zp[i][b] = reinterpret_cast<float *>(w);
-        zm[i][b] = zmax_all + (i * 2 + b) * ZGMAX * LBX_MAX_TOKENS;
         w += al256((size_t)k * projs[i].br[b].rank * 4);
+        if (projs[i].br[b].v_sign) {
+          tm[i][b] = reinterpret_cast<int *>(w);
+          w += al256((size_t)(projs[i].br[b].rank + 15) / 16 * 2 * k * 4);
+        }
       }
   }
 
@@ -1055,12 +1074,12 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
       sg.v2 = pr.br[b].v2;
       sg.mid0 = pr.br[b].mid;
       sg.z0 = zp[i][b];
-      sg.zmax0 = zm[i][b];
+      sg.tmax = tm[i][b];
       sg.rank = pr.br[b].rank;
       if (b == 0 && pr.n_branches == 2 && !pr.br[1].v_sign) {
         sg.mid1 = pr.br[1].mid;
         sg.z1 = zp[i][1];
-        sg.zmax1 = zm[i][1];
+
       }
       sg.tile0 = vtiles;
       vtiles += (sg.rank + 15) / 16;
@@ -1095,7 +1114,8 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
       sg.u_sign[b] = pr.br[b].u_sign;
       sg.u1[b] = pr.br[b].u1;
       sg.z[b] = zp[i][b];
-      sg.zmax[b] = zm[i][b];
+      sg.tmax[b] = pr.br[b].v_sign ? tm[i][b] : tm[i][0];  // a shared-V residual: the main segment's units
+      sg.tsel[b] = pr.br[b].v_sign ? 0 : 1;
       sg.rank[b] = pr.br[b].rank;
       sg.words[b] = (pr.br[b].rank + 31) / 32;
       sg.perrow[b] = (sg.words[b] % 4) == 0;
@@ -1123,8 +1143,7 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
   }
   LBX_CHECK_SUP(ut >= 1, "U-stage needs too much shared memory (rank too large for k=%d)", k);
   up.ut = ut;
-  up.zmax_all = zmax_all;
-  up.ticket = ticket;
+
   P.u_w = al256((size_t)ut * up.wtile_words * 4 + (size_t)ut * 48 * 4);
   P.u_s = u_s;
   up.s_bytes = (int)P.u_s;
@@ -1140,6 +1159,213 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
   return LBX_OK;
 }
 
+#ifndef LBX_SL_CLUSTERS
+#define LBX_SL_CLUSTERS 9  // clusters per cluster-executor launch (9 x 16 CTAs on 148 SMs)
+#endif
+
+// dynamic shared memory the cluster kernel may use, and the cluster-size opt-in
+static int slice_smem_limit(size_t &cmax) {
+  static size_t c_ = 0;
+  if (!c_) {
+    size_t m = 0;
+    cudaError_t e = allow_max_smem(slice_kernel<1>, &m);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(slice_kernel<1>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return cuda_status(e, "cluster kernel attributes");
+    c_ = m;
+  }
+  cmax = c_;
+  return LBX_OK;
+}
+
+static cudaLaunchConfig_t slice_cfg(cudaLaunchAttribute (&attr)[2], int nclusters, size_t smem,
+                                    cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nclusters * SL_S);
+  cfg.blockDim = dim3(VTHREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = SL_S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  int na = 1;
+  if (pdl) {
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    na = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cfg;
+}
+
+// clusters of the cluster kernel with `smem` bytes each that can be resident
+// at once (cached per shared-memory size)
+static int slice_active(size_t smem) {
+  static int cache[256] = {};
+  const int kb = (int)((smem + 1023) / 1024);
+  if (kb >= 256) return 0;
+  int &v = cache[kb];
+  if (!v) {
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = slice_cfg(attr, LBX_SL_CLUSTERS, (size_t)kb * 1024, nullptr, false);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (const void *)slice_kernel<1>, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      n = 0;
+    }
+    v = n + 1;
+  }
+  return v - 1;
+}
+
+// cluster-executor parameters; false (with the reason in `why`) when the call
+// does not fit it
+static bool prep_slice(const lbx_proj *projs, const lbx_linear_args *a, int k, const LinPrep &P,
+                       void *ws, size_t cmax, SlParams &sp, size_t &smem, char (&why)[160]) {
+  const VParams &vp = P.vp;
+  const int n_proj = a->n_proj;
+  why[0] = 0;
+  if (P.ncb != 1 || vp.Wv > PASS_WORDS) {
+    snprintf(why, sizeof why, "needs k <= 4 and in_features <= 4096");
+    return false;
+  }
+  const int ncl_max = LBX_SL_CLUSTERS;
+  if (vp.nseg > ncl_max) {
+    snprintf(why, sizeof why, "%d V segments for %d clusters", vp.nseg, ncl_max);
+    return false;
+  }
+  sp = SlParams{};
+  sp.vp = vp;
+  sp.vp.vcap = 0;  // v2 / norm_w straight from global memory (prefetched to L2)
+  // segment -> (projection, branch, shared-V) in prep_linear's order
+  int sproj[2 * LBX_MAX_PROJ], sbr[2 * LBX_MAX_PROJ], NG[2 * LBX_MAX_PROJ], nc[2 * LBX_MAX_PROJ];
+  {
+    int si = 0;
+    for (int i = 0; i < n_proj; ++i)
+      for (int b = 0; b < projs[i].n_branches; ++b)
+        if (projs[i].br[b].v_sign) {
+          sproj[si] = i;
+          sbr[si] = b;
+          NG[si] = (projs[i].br[b].rank + UGRP - 1) / UGRP;
+          nc[si] = 1;
+          ++si;
+        }
+  }
+  // clusters: one per segment, the rest to the segment with the most groups per cluster
+  for (int left = ncl_max - vp.nseg; left > 0; --left) {
+    int best = -1;
+    for (int i = 0; i < vp.nseg; ++i)
+      if (nc[i] < NG[i] && (best < 0 || (NG[i] + nc[i] - 1) / nc[i] > (NG[best] + nc[best] - 1) / nc[best]))
+        best = i;
+    if (best < 0) break;
+    ++nc[best];
+  }
+  int ncl = 0, ugmax = 1, zcap = 4;
+  int pncl[LBX_MAX_PROJ] = {};
+  for (int si = 0; si < vp.nseg; ++si) {
+    const VSeg &vs = vp.seg[si];
+    const int base = NG[si] / nc[si], extra = NG[si] % nc[si];
+    for (int c = 0, g0 = 0; c < nc[si]; ++c) {
+      const int ng = base + (c < extra ? 1 : 0);
+      SlCluster &C = sp.cl[ncl++];
+      C.proj = sproj[si];
+      C.vseg = si;
+      C.row0 = g0 * UGRP;
+      C.rows = std::min(ng * UGRP, vs.rank - C.row0);
+      C.tpc = ((C.rows + 15) / 16 + SL_S - 1) / SL_S;
+      C.nplane = vs.mid1 ? 2 : 1;
+      C.br[0] = sbr[si];
+      C.br[1] = 1;
+      if (C.tpc > SL_VT) {
+        snprintf(why, sizeof why, "%d V tiles per CTA (max %d)", C.tpc, SL_VT);
+        return false;
+      }
+      ugmax = std::max(ugmax, ng);
+      zcap = std::max(zcap, C.rows);
+      ++pncl[C.proj];
+      g0 += ng;
+    }
+  }
+  sp.ncl = ncl;
+  // projections
+  uint8_t *w = reinterpret_cast<uint8_t *>(ws) + WS_HDR;
+  int rmax = 16, gmax = 1;
+  for (int i = 0; i < n_proj; ++i) {
+    const lbx_proj &pr = projs[i];
+    SlProj &Pj = sp.pj[i];
+    Pj.out = pr.out_features;
+    Pj.nbr = pr.n_branches;
+    int ng = 0;
+    for (int b = 0; b < pr.n_branches; ++b) {
+      Pj.u_sign[b] = pr.br[b].u_sign;
+      Pj.words[b] = (pr.br[b].rank + 31) / 32;
+      Pj.ngrp[b] = (pr.br[b].rank + UGRP - 1) / UGRP;
+      Pj.u1[b] = pr.br[b].u1;
+      ng += Pj.ngrp[b];
+    }
+    Pj.bias = pr.bias;
+    Pj.y = P.up.seg[i].y;
+    Pj.y_ld = P.up.seg[i].y_ld;
+    Pj.rtiles = (pr.out_features / 16 + SL_S - 1) / SL_S;
+    Pj.ncl = pncl[i];
+    Pj.part = reinterpret_cast<int *>(w);
+    w += al256((size_t)ng * k * pr.out_features * 4);
+    Pj.gexp = reinterpret_cast<int *>(w);
+    w += al256((size_t)2 * ZGMAX * LBX_MAX_TOKENS * 4);
+    rmax = std::max(rmax, Pj.rtiles * 16);
+    gmax = std::max(gmax, ng);
+  }
+  for (int c = 0; c < ncl; ++c) {
+    const SlCluster &C = sp.cl[c];
+    const int nug = C.nplane * ((C.rows + UGRP - 1) / UGRP);
+    const int pairs = sp.pj[C.proj].rtiles * nug;
+    if ((pairs + VWARPS - 1) / VWARPS > SL_UP) {
+      snprintf(why, sizeof why, "%d output (tile, group) pairs per warp (max %d)",
+               (pairs + VWARPS - 1) / VWARPS, SL_UP);
+      return false;
+    }
+  }
+  sp.ydt = a->y_dtype;
+  sp.epi = a->epilogue;
+  sp.ticket = reinterpret_cast<unsigned *>(reinterpret_cast<uint8_t *>(ws) + WS_SLTICKET);
+  sp.zcap = zcap;
+  sp.rmax = rmax;
+  sp.ugmax = ugmax;
+  // shared memory: V staging / U digits | V partials | gathered z | mid |
+  // exponents, digit sums | U sign words | u1, bias
+  const size_t ws_ = (size_t)act_ws(vp.ncols);
+  sp.o_red = (int)al256((size_t)PASS_WORDS * ws_ * 4);
+  sp.o_zall = (int)al256(sp.o_red + (size_t)SL_VT * VWARPS * 16 * k * 4);
+  sp.o_mid = (int)al256(sp.o_zall + (size_t)2 * k * zcap * 4);
+  sp.o_ue = (int)al256(sp.o_mid + (size_t)2 * SL_ZR * 4);
+  sp.o_uw = (int)al256(sp.o_ue + (size_t)4 * ugmax * k * 4);
+  sp.o_u1 = (int)al256(sp.o_uw + (size_t)SL_UP * VWARPS * 32 * 8);
+  smem = al256(sp.o_u1 + (size_t)3 * rmax * 4);
+  // the finalize staging overlays everything before u1: after the cluster
+  // barrier no other CTA touches this CTA's shared memory, and the U
+  // contraction is done
+  sp.o_fin = 0;
+  const size_t fe = (size_t)2 * ZGMAX * k * 4;
+  const size_t room = (size_t)sp.o_u1 - fe;
+  sp.fin_rows = std::min(rmax, (int)(room / ((size_t)gmax * k * 4)) / 16 * 16);
+  if (sp.fin_rows < 16) {
+    snprintf(why, sizeof why, "no room to combine %d groups", gmax);
+    return false;
+  }
+  if (smem > cmax) {
+    snprintf(why, sizeof why, "%zu bytes of shared memory (max %zu)", smem, cmax);
+    return false;
+  }
+  const int act = slice_active(smem);
+  if (act < ncl) {
+    snprintf(why, sizeof why, "%d clusters resident at once (need %d)", act, ncl);
+    return false;
+  }
+  return true;
+}
+
 static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, int k, void *ws,
                      cudaStream_t stream) {
   size_t vmax = 0, umax = 0;
@@ -1148,8 +1374,21 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
   LinPrep P;
   rc = prep_linear(projs, a, tok0, k, ws, vmax, umax, P);
   if (rc) return rc;
-  LBX_CHECK_SUP(a->exec != LBX_EXEC_CLUSTER, "the cluster executor is not available");
   const bool pdl = a->use_pdl != 0;
+  if (a->exec == LBX_EXEC_CLUSTER) {
+    size_t cmax = 0;
+    rc = slice_smem_limit(cmax);
+    if (rc) return rc;
+    SlParams sp;
+    size_t smem = 0;
+    char why[160];
+    if (prep_slice(projs, a, k, P, ws, cmax, sp, smem, why)) {
+      cudaLaunchAttribute attr[2];
+      const cudaLaunchConfig_t cfg = slice_cfg(attr, sp.ncl, smem, stream, pdl);
+      return cuda_status(cudaLaunchKernelEx(&cfg, slice_kernel<1>, sp), "cluster kernel launch");
+    }
+    LBX_CHECK_SUP(false, "this call does not fit the cluster executor: %s", why);
+  }
   auto vk = P.ncb == 1 ? vstage_kernel<1> : P.ncb == 2 ? vstage_kernel<2> : vstage_kernel<4>;
   auto uk = P.ncb == 1 ? ustage_kernel<1> : P.ncb == 2 ? ustage_kernel<2> : ustage_kernel<4>;
   cudaError_t e = launch(vk, dim3(P.vunits), dim3(VTHREADS), P.v_w + P.v_s, stream, pdl, P.vp);
@@ -1173,7 +1412,7 @@ extern "C" int lbx_linear_verify(const lbx_proj *projs, const lbx_linear_args *a
   using namespace lbx;
   int rc = check_args(projs, a);
   if (rc) return rc;
-  const size_t need = lbx_linear_workspace_size(projs, a->n_proj, a->n_tokens);
+  const size_t need = ws_bytes_call(projs, a);
   LBX_CHECK_ARG(ws && ws_bytes >= need, "workspace too small (%zu < %zu)", ws_bytes, need);
   for (int t0 = 0; t0 < a->n_tokens; t0 += LBX_MAX_TOKENS) {
     const int k = std::min(LBX_MAX_TOKENS, a->n_tokens - t0);
@@ -1219,7 +1458,7 @@ extern "C" int lbx_linear_noalloc(const lbx_proj *projs, const lbx_linear_args *
   int rc = validate(projs, a->n_proj);
   if (rc) return rc;
   LBX_CHECK_ARG(a->n_tokens >= 1, "n_tokens must be >= 1");
-  const size_t need = lbx_linear_workspace_size(projs, a->n_proj, a->n_tokens);
+  const size_t need = ws_bytes_call(projs, a);
   LBX_CHECK_SUP(need <= NOALLOC_SCRATCH_BYTES,
                 "lbx_linear_noalloc: this call needs %zu bytes of scratch but the fixed buffer holds "
                 "%zu; use lbx_linear with a caller-provided workspace",

@@ -264,3 +264,86 @@ def test_allgather_exchange_two_shards_one_gpu():
         for rank in range(G):
             assert torch.equal(ys[rank], ref), (k, rank)
     assert [int(s[0]) for s in states] == [5, 5] and [int(s[1]) for s in states] == [0, 0]
+
+
+def _run_both(ops, projs, x, out_shapes, dt=torch.float32, y_init=None, **kw):
+    """The same call on the cluster executor and on the two stage grids."""
+    from littlebit_b200 import _lib as L
+
+    res = []
+    for mode in (L.LBX_EXEC_CLUSTER, L.LBX_EXEC_KERNELS):
+        outs = [torch.zeros(s, dtype=dt, device=DEV) for s in out_shapes]
+        for o, i0 in zip(outs, y_init or []):
+            o.copy_(i0)
+        ops.linear_group(projs, x, outs, exec_mode=mode, **kw)
+        res.append(outs)
+    torch.cuda.synchronize()
+    return res
+
+
+@pytest.mark.parametrize("case", [
+    ("c2", 4096, 4096, [208, 1840], (1, 2, 3, 4), torch.bfloat16, False, False),
+    ("c1", 4096, 4096, [208], (1, 3), torch.float32, False, False),
+    ("shared_bias", 1024, 512, [96, 96], (1, 3, 4), torch.float32, True, True),
+    ("shared_big", 4096, 4096, [1840, 1840], (1, 2), torch.bfloat16, True, False),
+    ("odd_rank", 256, 128, [40, 8], (1, 4), torch.float32, False, False),
+    ("gate", 4096, 11008, [280], (1, 2), torch.float32, False, False),
+    ("narrow_k", 2048, 1024, [136, 24], (1, 4), torch.bfloat16, False, True),
+    ("tiny", 128, 16, [8], (1,), torch.float32, False, False),
+])
+def test_cluster_executor_matches_two_stage_bitwise(ops, case):
+    """The split-rank cluster executor (one launch: each cluster's share of z in
+    distributed shared memory, exact group sums combined by the last CTA of
+    each output range) computes the same bits as the V-stage + U-stage grids:
+    shared-V and independent residuals, bias, ranks that are not multiples of
+    16 or 128, inputs narrower than 4096, k = 1..4, repeated calls."""
+    name, in_f, out_f, ranks, ks, dt, shared, bias = case
+    _, _, lay = _layer(ops, in_f, out_f, ranks, seed=sum(map(ord, name)) + 5, shared=shared, bias=bias)
+    for rep in range(2):
+        for k in ks:
+            x = torch.randn(k, in_f, generator=_gen(k + 40 + rep)).to(dt).to(DEV)
+            (yc,), (yk,) = _run_both(ops, [lay], x, [(k, out_f)], dt=dt)
+            assert torch.equal(yc, yk), (name, k, float((yc.float() - yk.float()).abs().max()))
+
+
+def test_cluster_executor_prologues_epilogues_groups(ops):
+    """q/k/v-style groups with the RMSNorm prologue, and the SiLU-mul prologue
+    with the residual-add epilogue: cluster executor == two stage grids."""
+    from littlebit_b200 import _lib as L
+
+    g = _gen(61)
+    H, I = 1024, 1536
+    layers = [_layer(ops, H, o, r, seed=70 + i)[2] for i, (o, r) in
+              enumerate(((H, [64, 32]), (256, [48]), (256, [48, 48])))]
+    w = (1 + 0.1 * torch.randn(H, generator=g)).abs().to(DEV)
+    dn = _layer(ops, I, H, [80, 40], seed=80)[2]
+    for k in (1, 3, 4):
+        x = torch.randn(k, H, generator=g).to(DEV)
+        yc, yk = _run_both(ops, layers, x, [(k, l.out_features) for l in layers],
+                           prologue=L.LBX_PRO_RMSNORM, norm_w=w, eps=1e-6)
+        for a, b in zip(yc, yk):
+            assert torch.equal(a, b), k
+        gt, up = torch.randn(k, I, generator=g).to(DEV), torch.randn(k, I, generator=g).to(DEV)
+        res = torch.randn(k, H, generator=g).to(DEV)
+        (ac,), (ak,) = _run_both(ops, [dn], gt, [(k, H)], prologue=L.LBX_PRO_SILU_MUL, x2=up,
+                                 epilogue=L.LBX_EPI_ADD, y_init=[res])
+        assert torch.equal(ac, ak), k
+
+
+def test_cluster_executor_rejects_what_it_cannot_take(ops):
+    """LBX_EXEC_CLUSTER refuses calls outside the executor (k > 4, K > 4096);
+    LBX_EXEC_AUTO runs them."""
+    from littlebit_b200 import _lib as L
+
+    _, _, lay = _layer(ops, 8192, 512, [64], seed=91)
+    x = torch.randn(1, 8192, generator=_gen(92)).to(DEV)
+    y = torch.empty(1, 512, device=DEV)
+    with pytest.raises(RuntimeError, match="unsupported"):
+        ops.linear_group([lay], x, [y], exec_mode=L.LBX_EXEC_CLUSTER)
+    ops.linear_group([lay], x, [y], exec_mode=L.LBX_EXEC_AUTO)
+    _, _, lay2 = _layer(ops, 512, 256, [64], seed=93)
+    x5 = torch.randn(5, 512, generator=_gen(94)).to(DEV)
+    y5 = torch.empty(5, 256, device=DEV)
+    with pytest.raises(RuntimeError, match="unsupported"):
+        ops.linear_group([lay2], x5, [y5], exec_mode=L.LBX_EXEC_CLUSTER)
+    torch.cuda.synchronize()
