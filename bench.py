@@ -492,6 +492,8 @@ def run_ours(args):
     for name, fn in execs.items():
         if name == args.exec:
             continue
+        if name == "cluster" and k > 4:
+            continue  # the cluster executor takes k <= 4
         exec_t[name] = timed_graph(fn)
         if not torch.equal(acts[-1], y_main):
             raise RuntimeError(f"{name} and {args.exec} executors disagree")

@@ -300,7 +300,7 @@ LBX_DEV void vstage_issue(const VParams &p, int unit, uint8_t *W, LinShm &sh) {
 // issued and before v2 is used (the V-stage waits for its weight copies
 // there).  Columns below p.vcap take v2 / norm_w from the shared-memory
 // copies sv2 / snw, the rest from global memory (same arithmetic).
-template <class OnFirst>
+template <bool SILU, class OnFirst>
 LBX_DEV void vstage_stage(const VParams &p, const float *v2, const float *sv2, const float *snw,
                           int pass, uint32_t *act, LinShm &sh, OnFirst &&on_first) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -314,19 +314,21 @@ LBX_DEV void vstage_stage(const VParams &p, const float *v2, const float *sv2, c
   const int pwords = min(PASS_WORDS, p.Wv - pw0);
   const bool wvalid = Wd < pwords;
   const int64_t col = (int64_t)(pw0 + Wd) * 32 + 8 * qq;
-  const bool silu = p.prologue == LBX_PRO_SILU_MUL;
   float hw[8];
   for (int t0 = 0; t0 < p.k; t0 += TBATCH) {
     // issue the loads of a batch of tokens before using any of them
-    float xv[TBATCH][8], uv[TBATCH][8];
+    float xv[TBATCH][8], uv[SILU ? TBATCH : 1][8];
 #pragma unroll
     for (int j = 0; j < TBATCH; ++j) {
       if (wvalid && t0 + j < p.k) {
         load8(p.x, p.xdt, (int64_t)(t0 + j) * p.K + col, xv[j]);
-        if (silu) load8(p.x2, p.xdt, (int64_t)(t0 + j) * p.K + col, uv[j]);
+        if constexpr (SILU) load8(p.x2, p.xdt, (int64_t)(t0 + j) * p.K + col, uv[j]);
       } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) xv[j][i] = uv[j][i] = 0.f;
+        for (int i = 0; i < 8; ++i) {
+          xv[j][i] = 0.f;
+          if constexpr (SILU) uv[j][i] = 0.f;
+        }
       }
     }
 
@@ -365,7 +367,7 @@ LBX_DEV void vstage_stage(const VParams &p, const float *v2, const float *sv2, c
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float xx = xv[j][i];
-        if (silu) {
+        if constexpr (SILU) {
           a[i] = (xx / (1.0f + expf(-xx))) * uv[j][i] * hw[i];
         } else {
           sq2 = fmaf(xx, xx, sq2);
@@ -423,7 +425,9 @@ LBX_DEV void vstage_stage(const VParams &p, const float *v2, const float *sv2, c
 
 // z = mid ⊙ (V_sign · a) for the 16 rows of unit `unit`; returns false (on
 // every thread) if the weight copies did not arrive in time
-template <int NCB>
+// SILU: the SiLU-mul prologue (a compile-time choice: its second input array
+// would otherwise cost registers in every V-stage)
+template <int NCB, bool SILU>
 LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinShm &sh, bool zero = true) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, q = lane & 3;
@@ -451,7 +455,7 @@ LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinS
   for (int pass = 0; pass < npass; ++pass) {
     const int pw0 = pass * PASS_WORDS;
     const int pwords = min(PASS_WORDS, p.Wv - pw0);
-    vstage_stage(p, sg.v2, sv2, snw, pass, act, sh, [&] {
+    vstage_stage<SILU>(p, sg.v2, sv2, snw, pass, act, sh, [&] {
       if (pass == 0) {
         ok = __syncthreads_and(mbar_wait_bounded(&sh.bar[UT_MAX], par, 0x101));
         LBX_PROBE(2);
@@ -527,7 +531,7 @@ LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinS
   return true;
 }
 
-template <int NCB>
+template <int NCB, bool SILU>
 __global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_constant__ VParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ LinShm sh;
@@ -541,7 +545,7 @@ __global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_consta
   vstage_issue(p, blockIdx.x, W, sh);
   pdl_trigger();
   pdl_wait();
-  vstage_run<NCB>(p, blockIdx.x, W, S, sh, false);
+  vstage_run<NCB, SILU>(p, blockIdx.x, W, S, sh, false);
 }
 
 // ---------------------------------------------------------------------------
@@ -985,13 +989,20 @@ static int check_args(const lbx_proj *projs, const lbx_linear_args *a) {
   return LBX_OK;
 }
 
+using VKern = void (*)(VParams);
+static VKern vstage_for(int ncb, bool silu) {
+  if (silu) return ncb == 1 ? vstage_kernel<1, true> : ncb == 2 ? vstage_kernel<2, true> : vstage_kernel<4, true>;
+  return ncb == 1 ? vstage_kernel<1, false> : ncb == 2 ? vstage_kernel<2, false> : vstage_kernel<4, false>;
+}
+
 // dynamic shared memory the stage kernels may use (after their static
 // shared memory); established once per process, before any graph capture
 static int stage_smem_limits(size_t &vmax, size_t &umax) {
   static size_t v_ = 0, u_ = 0;
   if (!v_) {
     size_t m = 0, vv = (size_t)-1, uu = (size_t)-1;
-    for (auto kk : {vstage_kernel<1>, vstage_kernel<2>, vstage_kernel<4>}) {
+    for (auto kk : {vstage_kernel<1, false>, vstage_kernel<2, false>, vstage_kernel<4, false>,
+                    vstage_kernel<1, true>, vstage_kernel<2, true>, vstage_kernel<4, true>}) {
       cudaError_t e = allow_max_smem(kk, &m);
       if (e != cudaSuccess) return cuda_status(e, "vstage smem attribute");
       vv = std::min(vv, m);
@@ -1389,7 +1400,7 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
     }
     LBX_CHECK_SUP(false, "this call does not fit the cluster executor: %s", why);
   }
-  auto vk = P.ncb == 1 ? vstage_kernel<1> : P.ncb == 2 ? vstage_kernel<2> : vstage_kernel<4>;
+  auto vk = vstage_for(P.ncb, a->prologue == LBX_PRO_SILU_MUL);
   auto uk = P.ncb == 1 ? ustage_kernel<1> : P.ncb == 2 ? ustage_kernel<2> : ustage_kernel<4>;
   cudaError_t e = launch(vk, dim3(P.vunits), dim3(VTHREADS), P.v_w + P.v_s, stream, pdl, P.vp);
   if (e != cudaSuccess) return cuda_status(e, "vstage launch");
@@ -1529,7 +1540,7 @@ extern "C" int lbx_linear_allgather(const lbx_proj *proj, const lbx_linear_args 
   for (int j = 0; j < n_peer; ++j)
     P.up.xbuf[j] = reinterpret_cast<unsigned long long *>(xbuf_peers[j]) + y_col0;
   const bool pdl = a->use_pdl != 0;
-  auto vk = P.ncb == 1 ? vstage_kernel<1> : P.ncb == 2 ? vstage_kernel<2> : vstage_kernel<4>;
+  auto vk = vstage_for(P.ncb, a->prologue == LBX_PRO_SILU_MUL);
   auto uk = P.ncb == 1   ? ustage_kernel<1, true>
             : P.ncb == 2 ? ustage_kernel<2, true>
                          : ustage_kernel<4, true>;

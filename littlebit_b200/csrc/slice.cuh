@@ -222,7 +222,10 @@ __global__ void __launch_bounds__(VTHREADS, LBX_SL_MINBLOCKS) slice_kernel(const
 
   // ---- V: this CTA's z rows
   if (ntl > 0) {
-    vstage_stage(vp, sg.v2, nullptr, nullptr, 0, act, sh, [] {});
+    if (vp.prologue == LBX_PRO_SILU_MUL)
+      vstage_stage<true>(vp, sg.v2, nullptr, nullptr, 0, act, sh, [] {});
+    else
+      vstage_stage<false>(vp, sg.v2, nullptr, nullptr, 0, act, sh, [] {});
     __syncthreads();
     LBX_PROBE(33);
 #pragma unroll
