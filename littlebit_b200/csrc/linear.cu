@@ -995,6 +995,10 @@ static VKern vstage_for(int ncb, bool silu) {
   return ncb == 1 ? vstage_kernel<1, false> : ncb == 2 ? vstage_kernel<2, false> : vstage_kernel<4, false>;
 }
 
+#ifndef LBX_U_MIN_CTAS
+#define LBX_U_MIN_CTAS 60  // U-stage CTAs to aim for when choosing tiles per CTA (measured: 4 tiles per CTA beat 2 and 8 at C2)
+#endif
+
 // dynamic shared memory the stage kernels may use (after their static
 // shared memory); established once per process, before any graph capture
 static int stage_smem_limits(size_t &vmax, size_t &umax) {
@@ -1145,7 +1149,7 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
   // row tiles per CTA: enough CTAs to cover the SMs, within shared memory; the
   // remaining warps of a CTA split the ranks of its tiles
   int ut = UT_MAX;
-  while (ut > 1 && tiles / ut < 120) ut >>= 1;
+  while (ut > 1 && tiles / ut < LBX_U_MIN_CTAS) ut >>= 1;
   const size_t u_s = al256((size_t)(maxw[0] + maxw[1]) * act_ws(ncols) * 4 + (size_t)4 * ugm * k * 4 +
                            (size_t)UWARPS * 32 * 8 * ncb * 4);
   for (; ut >= 1; ut >>= 1) {
