@@ -152,68 +152,93 @@ def max_over_ranks(v: float, ws: int) -> float:
 # ---------------------------------------------------------------------------
 # reference arm / CPU baseline: the reference's own C++ op on host cores
 # ---------------------------------------------------------------------------
-def cpu_reference(k: int, budget_s: float, nlayers: int = 4):
-    from oracle import build_ref  # CPU baseline leg only
+def ref_chain(k: int, nlayers: int):
+    """The reference's CPU op (littlebit_cpu_ops.littlebit_linear, compiled from
+    the reference's own sources into oracle/_ref) over a chain of `nlayers`
+    distinct C2 layers, main + residual branch summed per layer
+    (littlebit.py:104-107); returns (one_pass, threads) or None when the op is
+    not built."""
+    from oracle import build_ref  # CPU baseline / reference arm only
 
     if not build_ref.load():
         return None
     from littlebit_b200 import synthetic as syn
 
     torch.set_num_threads(os.cpu_count() or 1)
-    threads = torch.get_num_threads()
     g = torch.Generator().manual_seed(0)
     layers = [syn.layer(IN_F, OUT_F, RANKS, g) for _ in range(nlayers)]
     op = torch.ops.littlebit_cpu_ops.littlebit_linear
-    x = torch.randn(k, IN_F, generator=g).bfloat16().float()
+    x0 = torch.randn(k, IN_F, generator=g).bfloat16().float()
 
-    def run(lay, xin):
-        y = None
-        for b in lay:  # main + residual branch, summed (littlebit.py:104-107)
-            yb = op(xin, b["v2"][None], b["v_sign"], IN_F, b["mid"][None], b["u_sign"], b["rank"],
-                    b["u1"][None])
-            y = yb if y is None else y + yb
-        return y.bfloat16().float()
+    def one_pass():
+        x = x0
+        for lay in layers:
+            y = None
+            for b in lay:
+                yb = op(x, b["v2"][None], b["v_sign"], IN_F, b["mid"][None], b["u_sign"], b["rank"],
+                        b["u1"][None])
+                y = yb if y is None else y + yb
+            x = y.bfloat16().float()
+        return x
 
-    for i in range(5):  # warm-up (benchmark_models_cpu.py:31-77 uses 5)
-        x = run(layers[i % nlayers], x)
+    return one_pass, torch.get_num_threads()
+
+
+def cpu_reference(k: int, budget_s: float, nlayers: int):
+    """CPU baseline of our arm: passes of the reference op over the layer chain
+    for about `budget_s` seconds."""
+    r = ref_chain(k, nlayers)
+    if r is None:
+        return None
+    one_pass, threads = r
+    for _ in range(2):  # warm-up
+        one_pass()
     times = []
     t_end = time.perf_counter() + budget_s
-    i = 0
     while time.perf_counter() < t_end or len(times) < 3:
         t0 = time.perf_counter()
-        x = run(layers[i % nlayers], x)
+        one_pass()
         times.append(time.perf_counter() - t0)
-        i += 1
     b, _ = layer_bytes(k)
     med = statistics.median(times)
-    return {"gbs": b / med / 1e9, "sec_per_layer": med, "threads": threads, "calls": len(times),
-            "sample": f"{len(times)} calls of littlebit_linear x2 branches (r={RANKS}) on {nlayers} "
-                      f"distinct layers, k={k}, median per layer"}
+    return {"gbs": b * nlayers / med / 1e9, "threads": threads,
+            "sample": f"{len(times)} passes (median) of littlebit_linear x2 branches (r={RANKS}) over "
+                      f"{nlayers} distinct layers, k={k}, {threads} threads"}
 
 
 def run_reference(args):
+    """The reference's CPU op on this workload: W warm-up passes, then exactly K
+    timed passes over the chain of --pool distinct layers."""
     rank, ws, _ = dist_init()
     if rank != 0:
         return 0
-    t0 = time.perf_counter()
-    res = cpu_reference(args.tokens, budget_s=max(2.0, 2.0 * args.steps / 10))
-    if res is None:
+    r = ref_chain(args.tokens, args.pool)
+    if r is None:
         print(json.dumps({"impl": "reference", "unavailable":
                           "reference C++ op not built (oracle/_ref missing: run oracle/build_ref.py)"}))
         return 0
+    one_pass, threads = r
+    for _ in range(args.warmup):
+        one_pass()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one_pass()
+    dt = time.perf_counter() - t0
     b, _ = layer_bytes(args.tokens)
-    val = res["gbs"]
+    val = b * args.pool * args.steps / dt / 1e9
+    sample = (f"{args.steps} passes of littlebit_linear x2 branches (r={RANKS}) over {args.pool} distinct "
+              f"layers, k={args.tokens}, {threads} threads")
     out = {
         "metric": METRIC, "impl": "reference", "value": round(val, 4), "unit": "GB/s",
-        "n_gpus": args.gpus, "steps": res["calls"], "warmup": 5,
-        "ms_per_step": round(res["sec_per_layer"] * 1e3, 4), "higher_is_better": True,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8xsign/fp32 (W1A8)", "data": "synthetic",
-        "config": {"workload": f"C2 4096->4096 LittleBitLinear r={RANKS[0]}+{RANKS[1]}, k={args.tokens}, "
-                               "reference CPU op per layer", "tokens": args.tokens},
-        "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": res["threads"],
-                         "kind": "reference", "sample": res["sample"]},
+        "config": {"workload": f"C2 4096->4096 LittleBitLinear r={RANKS[0]}+{RANKS[1]} (independent V_R), "
+                               f"k={args.tokens}, chain of {args.pool} distinct layers per step, reference "
+                               "CPU op", "tokens": args.tokens, "pool_layers": args.pool},
+        "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": threads,
+                         "kind": "reference", "sample": sample},
         "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "wall_s": round(time.perf_counter() - t0, 2),
     }
     print(json.dumps(out))
     return 0
@@ -524,7 +549,7 @@ def run_ours(args):
     # ---- CPU baseline (rank 0, N=1 only)
     cpu = None
     if ws == 1 and not args.no_cpu:
-        r = cpu_reference(k, budget_s=args.cpu_seconds)
+        r = cpu_reference(k, budget_s=args.cpu_seconds, nlayers=P)
         if r is not None:
             cpu = {"value": round(r["gbs"], 4), "unit": "GB/s", "cores": r["threads"],
                    "kind": "reference", "sample": r["sample"]}
