@@ -129,20 +129,25 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
     Qs[r * KP + j] = x1 * cs.x - x2 * cs.y;
     Qs[r * KP + j + half] = x2 * cs.x + x1 * cs.y;
   }
-  // cached keys / values of ranks r0.. (rank == slot below the prefix)
+  // cached keys / values of ranks r0.. (rank == slot below the prefix): four
+  // bf16 per 8-byte load (head_dim % 4 == 0), several loads in flight
   const int64_t cache_base = (int64_t)h * p.max_seq * d;
-  for (int e = tid; e < ACH * half; e += nthr) {
-    const int jj = e / half, j = e - jj * half;
+  const int d4 = d / 4;
+#pragma unroll 4
+  for (int e = tid; e < ACH * d4; e += nthr) {
+    const int jj = e / d4, j4 = e - jj * d4;
     const int slot = r0 + jj;
-    float k1 = 0.f, k2 = 0.f, v1 = 0.f, v2 = 0.f;
+    uint2 kq = make_uint2(0u, 0u), vq = make_uint2(0u, 0u);
     if (slot < prefix) {
-      const uint16_t *kr = p.kc + cache_base + (int64_t)slot * d;
-      const uint16_t *vr = p.vc + cache_base + (int64_t)slot * d;
-      k1 = bf16_to_f32(kr[j]); k2 = bf16_to_f32(kr[j + half]);
-      v1 = bf16_to_f32(vr[j]); v2 = bf16_to_f32(vr[j + half]);
+      kq = *reinterpret_cast<const uint2 *>(p.kc + cache_base + (int64_t)slot * d + 4 * j4);
+      vq = *reinterpret_cast<const uint2 *>(p.vc + cache_base + (int64_t)slot * d + 4 * j4);
     }
-    Ka[jj * KP + j] = k1; Ka[jj * KP + j + half] = k2;
-    Va[jj * d + j] = v1; Va[jj * d + j + half] = v2;
+    *reinterpret_cast<float4 *>(Ka + jj * KP + 4 * j4) =
+        make_float4(__uint_as_float(kq.x << 16), __uint_as_float(kq.x & 0xFFFF0000u),
+                    __uint_as_float(kq.y << 16), __uint_as_float(kq.y & 0xFFFF0000u));
+    *reinterpret_cast<float4 *>(Va + jj * d + 4 * j4) =
+        make_float4(__uint_as_float(vq.x << 16), __uint_as_float(vq.x & 0xFFFF0000u),
+                    __uint_as_float(vq.y << 16), __uint_as_float(vq.y & 0xFFFF0000u));
   }
   // the new tokens: rotate, round to bf16; the unit whose slot range holds
   // cache slot prefix+i writes it
@@ -239,20 +244,41 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
   __syncthreads();
   if (s_last) {
     __threadfence();
+    constexpr int MB = 8;  // chunks whose partials are loaded together
     for (int e = tid; e < Rg * d; e += nthr) {
       const int r = e / d, t = e - r * d;
       const int gr = rlo + r;
       float M = -INFINITY;
-      for (int cc = 0; cc < nlive; ++cc)
-        M = fmaxf(M, __ldcg(p.part_ml + ((int64_t)h * p.nchunk + cc) * p.R + gr).x);
-      float L = 0.f, O = 0.f;
-      for (int cc = 0; cc < nlive; ++cc) {
-        const int64_t b = ((int64_t)h * p.nchunk + cc) * p.R + gr;
-        const float2 ml = __ldcg(p.part_ml + b);
-        if (ml.x == -INFINITY) continue;
-        const float w = expf(ml.x - M);
-        L = fmaf(w, ml.y, L);
-        O = fmaf(w, __ldcg(p.part_o + b * d + t), O);
+      for (int c0 = 0; c0 < nlive; c0 += MB) {
+        float mx[MB];
+#pragma unroll
+        for (int u = 0; u < MB; ++u)
+          mx[u] = c0 + u < nlive ? __ldcg(p.part_ml + ((int64_t)h * p.nchunk + c0 + u) * p.R + gr).x
+                                 : -INFINITY;
+#pragma unroll
+        for (int u = 0; u < MB; ++u) M = fmaxf(M, mx[u]);
+      }
+      float L = 0.f, O = 0.f;  // in chunk order
+      for (int c0 = 0; c0 < nlive; c0 += MB) {
+        float2 ml[MB];
+        float ov[MB];
+#pragma unroll
+        for (int u = 0; u < MB; ++u) {
+          ml[u] = make_float2(-INFINITY, 0.f);
+          ov[u] = 0.f;
+          if (c0 + u < nlive) {
+            const int64_t b = ((int64_t)h * p.nchunk + c0 + u) * p.R + gr;
+            ml[u] = __ldcg(p.part_ml + b);
+            ov[u] = __ldcg(p.part_o + b * d + t);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < MB; ++u) {
+          if (ml[u].x == -INFINITY) continue;
+          const float w = expf(ml[u].x - M);
+          L = fmaf(w, ml[u].y, L);
+          O = fmaf(w, ov[u], O);
+        }
       }
       const int i = gr / p.rep, qh = h * p.rep + (gr - i * p.rep);
       p.out[(int64_t)i * p.heads * d + (int64_t)qh * d + t] = L > 0.f ? O / L : 0.f;

@@ -39,7 +39,8 @@ constexpr int BLK_WORDS = 8;    // V-stage scale block: 256 columns (one warp)
 constexpr int VWARPS = 16;
 constexpr int VTHREADS = VWARPS * 32;
 constexpr int TBATCH = 2;       // tokens whose x loads are issued together in staging
-constexpr int VCAP_MAX = 12288; // leading v2/norm_w columns prefetched into shared memory
+constexpr int VCAP_MAX = 4096;  // leading v2/norm_w columns prefetched into shared memory (the rest
+                                // come from L2 with the x loads: keeps wide inputs at 2 CTAs per SM)
 constexpr int UWARPS = 16;      // warp (tile, split): ut row tiles x (16/ut) rank splits
 constexpr int UTHREADS = UWARPS * 32;
 constexpr int UT_MAX = 8;
@@ -63,13 +64,14 @@ struct VSeg {
   float *z1;             // [k][rank] or nullptr
   int *tmax;             // [tile][2][k] per-unit max |z0|, |z1| per token (float bits)
   int rank;
-  int tile0;             // first CTA (16-row tile) of this segment
+  int unit0;             // first unit (vt 16-row tiles) of this segment
 };
 
 struct VParams {
   VSeg seg[2 * LBX_MAX_PROJ];
   int nseg;
   int K, Wv, vpitch;
+  int vt;                // 16-row tiles per unit (1 or 2)
   int vcap;              // columns of v2 / norm_w staged in shared memory
   int k, ncols;
   int xdt, prologue;
@@ -237,10 +239,10 @@ LBX_DEV void linshm_init(LinShm &sh) {
 // shared-memory regions of a V-stage unit: W (weights, filled by bulk copies
 // that may be issued long before the unit runs) and S (scratch of the run)
 struct VLayout {
-  uint32_t *wbuf;  // 16 x vpitch sign words
+  uint32_t *wbuf;  // 16 vt x vpitch sign words
   float *sv2;      // vcap
   float *snw;      // vcap (RMSNorm prologue)
-  float *smid;     // 2 x 16
+  float *smid;     // 2 x 16 vt (mid0 rows, then mid1 rows)
   uint32_t *act;   // PASS_WORDS x ws
   float *red;      // VWARPS x 16 x k
 };
@@ -249,7 +251,7 @@ LBX_DEV VLayout vlayout(const VParams &p, uint8_t *W, uint8_t *S) {
   VLayout L;
   const bool rms = p.prologue == LBX_PRO_RMSNORM;
   L.wbuf = reinterpret_cast<uint32_t *>(W);
-  L.sv2 = reinterpret_cast<float *>(L.wbuf + 16 * p.vpitch);
+  L.sv2 = reinterpret_cast<float *>(L.wbuf + 16 * p.vt * p.vpitch);
   L.snw = L.sv2 + p.vcap;
   L.smid = L.snw + (rms ? p.vcap : 0);
   L.act = reinterpret_cast<uint32_t *>(S);
@@ -259,7 +261,7 @@ LBX_DEV VLayout vlayout(const VParams &p, uint8_t *W, uint8_t *S) {
 
 LBX_DEV int vseg_of(const VParams &p, int unit) {
   int s = 0;
-  while (s + 1 < p.nseg && unit >= p.seg[s + 1].tile0) ++s;
+  while (s + 1 < p.nseg && unit >= p.seg[s + 1].unit0) ++s;
   return s;
 }
 
@@ -268,8 +270,8 @@ LBX_DEV int vseg_of(const VParams &p, int unit) {
 LBX_DEV void vstage_issue(const VParams &p, int unit, uint8_t *W, LinShm &sh) {
   const int tid = threadIdx.x;
   const VSeg &sg = p.seg[vseg_of(p, unit)];
-  const int row0 = (unit - sg.tile0) * 16;
-  const int rows = min(16, sg.rank - row0);
+  const int row0 = (unit - sg.unit0) * 16 * p.vt;
+  const int rows = min(16 * p.vt, sg.rank - row0);
   const bool rms = p.prologue == LBX_PRO_RMSNORM;
   const VLayout L = vlayout(p, W, nullptr);
   const int vcap = p.vcap;
@@ -282,14 +284,14 @@ LBX_DEV void vstage_issue(const VParams &p, int unit, uint8_t *W, LinShm &sh) {
   __syncthreads();
   if (tid < rows)
     bulk_g2s(L.wbuf + tid * p.vpitch, sg.v_sign + (int64_t)(row0 + tid) * p.Wv, (uint32_t)p.Wv * 4u, bar);
-  else if (tid == 16)
+  else if (tid == VTHREADS - 1)
     bulk_g2s(L.sv2, sg.v2, (uint32_t)vcap * 4u, bar);
-  else if (tid == 17 && rms)
+  else if (tid == VTHREADS - 2 && rms)
     bulk_g2s(L.snw, p.norm_w, (uint32_t)vcap * 4u, bar);
-  else if (tid == 18)
+  else if (tid == VTHREADS - 3)
     bulk_g2s(L.smid, sg.mid0 + row0, (uint32_t)rows * 4u, bar);
-  else if (tid == 19 && sg.mid1)
-    bulk_g2s(L.smid + 16, sg.mid1 + row0, (uint32_t)rows * 4u, bar);
+  else if (tid == VTHREADS - 4 && sg.mid1)
+    bulk_g2s(L.smid + 16 * p.vt, sg.mid1 + row0, (uint32_t)rows * 4u, bar);
 }
 
 // One staging pass of the V-stage: every token's a = v2 ⊙ prologue(x) over
@@ -426,14 +428,15 @@ LBX_DEV void vstage_stage(const VParams &p, const float *v2, const float *sv2, c
 // z = mid ⊙ (V_sign · a) for the 16 rows of unit `unit`; returns false (on
 // every thread) if the weight copies did not arrive in time
 // SILU: the SiLU-mul prologue (a compile-time choice: its second input array
-// would otherwise cost registers in every V-stage)
-template <int NCB, bool SILU>
+// would otherwise cost registers in every V-stage).  VT: 16-row tiles per unit
+// (p.vt); every tile gets exactly the one-tile arithmetic, x is staged once.
+template <int NCB, bool SILU, int VT = 1>
 LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinShm &sh, bool zero = true) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, q = lane & 3;
   const VSeg &sg = p.seg[vseg_of(p, unit)];
-  const int row0 = (unit - sg.tile0) * 16;
-  const int rows = min(16, sg.rank - row0);
+  const int row0 = (unit - sg.unit0) * 16 * VT;
+  const int ntl = min(VT, (sg.rank - row0 + 15) / 16);
   const bool rms = p.prologue == LBX_PRO_RMSNORM;
   const int ws = act_ws(p.ncols);
   const VLayout L = vlayout(p, W, S);
@@ -447,9 +450,11 @@ LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinS
   }
   LBX_PROBE(1);
 
-  float tacc[NCB][2];
+  float tacc[VT][NCB][2];
 #pragma unroll
-  for (int cb = 0; cb < NCB; ++cb) tacc[cb][0] = tacc[cb][1] = 0.f;
+  for (int tl = 0; tl < VT; ++tl)
+#pragma unroll
+    for (int cb = 0; cb < NCB; ++cb) tacc[tl][cb][0] = tacc[tl][cb][1] = 0.f;
   bool ok = true;
   const int npass = (p.Wv + PASS_WORDS - 1) / PASS_WORDS;
   for (int pass = 0; pass < npass; ++pass) {
@@ -463,23 +468,29 @@ LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinS
     });
     __syncthreads();
     LBX_PROBE(3);
-    // MMA: warp w contracts its own 256-column block of this pass
+    // MMA: warp w contracts its own 256-column block of this pass, every tile
     if (ok && BLK_WORDS * warp < pwords) {
-      int acc[NCB][4];
-#pragma unroll
-      for (int cb = 0; cb < NCB; ++cb) acc[cb][0] = acc[cb][1] = acc[cb][2] = acc[cb][3] = 0;
       const int wb = pw0 + BLK_WORDS * warp;
       const int ng = min(BLK_WORDS, pwords - BLK_WORDS * warp) / 4;
-      sign_mma<NCB>(acc, wbuf + g * p.vpitch + wb, wbuf + (g + 8) * p.vpitch + wb,
-                    act + BLK_WORDS * warp * ws, ws, p.ncols, 0, ng, lane);
 #pragma unroll
-      for (int cb = 0; cb < NCB; ++cb) {
-        const int t = cb * 4 + q;
-        if (t < p.k) {
-          const int sq = sh.v_sq[warp][t];
-          const float inv = sh.v_inv[warp][t];
-          tacc[cb][0] += __int2float_rn(sq + 2 * (256 * acc[cb][0] + acc[cb][1])) * inv;
-          tacc[cb][1] += __int2float_rn(sq + 2 * (256 * acc[cb][2] + acc[cb][3])) * inv;
+      for (int tl = 0; tl < VT; ++tl) {
+        if (tl < ntl) {
+          int acc[NCB][4];
+#pragma unroll
+          for (int cb = 0; cb < NCB; ++cb) acc[cb][0] = acc[cb][1] = acc[cb][2] = acc[cb][3] = 0;
+          const uint32_t *wt = wbuf + tl * 16 * p.vpitch + wb;
+          sign_mma<NCB>(acc, wt + g * p.vpitch, wt + (g + 8) * p.vpitch, act + BLK_WORDS * warp * ws, ws,
+                        p.ncols, 0, ng, lane);
+#pragma unroll
+          for (int cb = 0; cb < NCB; ++cb) {
+            const int t = cb * 4 + q;
+            if (t < p.k) {
+              const int sq = sh.v_sq[warp][t];
+              const float inv = sh.v_inv[warp][t];
+              tacc[tl][cb][0] += __int2float_rn(sq + 2 * (256 * acc[cb][0] + acc[cb][1])) * inv;
+              tacc[tl][cb][1] += __int2float_rn(sq + 2 * (256 * acc[cb][2] + acc[cb][3])) * inv;
+            }
+          }
         }
       }
     }
@@ -488,50 +499,57 @@ LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinS
   // the weight barrier completed its phase (or timed out on every thread)
   if (tid == 0) sh.par[UT_MAX] = par ^ 1u;
   if (!ok) return false;
-  // ---- fixed-order reduction over the 16 warps, then scales
-  float *rw = red + warp * 16 * p.k;
-#pragma unroll
-  for (int cb = 0; cb < NCB; ++cb) {
-    const int t = cb * 4 + q;
-    if (t < p.k) {
-      rw[g * p.k + t] = tacc[cb][0];
-      rw[(g + 8) * p.k + t] = tacc[cb][1];
-    }
-  }
-  __syncthreads();
-  LBX_PROBE(4);
+  // ---- per tile: fixed-order reduction over the 16 warps, then scales
   const float *smid = L.smid;
-  for (int i = tid; i < rows * p.k; i += VTHREADS) {
-    const int rr = i / p.k, t = i - rr * p.k;
-    float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < VWARPS; ++w) v += red[(w * 16 + rr) * p.k + t];
-    if (rms) {
-      float s2 = 0.f;
+  for (int tl = 0; tl < VT; ++tl) {
+    if (tl >= ntl) break;  // uniform across the CTA
+    const int trow = row0 + tl * 16;
+    const int rows = min(16, sg.rank - trow);
+    float *rw = red + warp * 16 * p.k;
 #pragma unroll
-      for (int w = 0; w < VWARPS; ++w) s2 += sh.v_ssq[w][t];
-      v *= rsqrtf(s2 / (float)p.K + p.eps);
+    for (int cb = 0; cb < NCB; ++cb) {
+      const int t = cb * 4 + q;
+      if (t < p.k) {
+        rw[g * p.k + t] = tacc[tl][cb][0];
+        rw[(g + 8) * p.k + t] = tacc[tl][cb][1];
+      }
     }
-    const float z0 = smid[rr] * v;
-    sg.z0[(int64_t)t * sg.rank + row0 + rr] = z0;
-    atomicMax(&sh.v_zmax[0][t], __float_as_int(fabsf(z0)));
-    if (sg.z1) {
-      const float z1 = smid[16 + rr] * v;
-      sg.z1[(int64_t)t * sg.rank + row0 + rr] = z1;
-      atomicMax(&sh.v_zmax[1][t], __float_as_int(fabsf(z1)));
+    __syncthreads();
+    LBX_PROBE(4);
+    for (int i = tid; i < rows * p.k; i += VTHREADS) {
+      const int rr = i / p.k, t = i - rr * p.k;
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < VWARPS; ++w) v += red[(w * 16 + rr) * p.k + t];
+      if (rms) {
+        float s2 = 0.f;
+#pragma unroll
+        for (int w = 0; w < VWARPS; ++w) s2 += sh.v_ssq[w][t];
+        v *= rsqrtf(s2 / (float)p.K + p.eps);
+      }
+      const float z0 = smid[tl * 16 + rr] * v;
+      sg.z0[(int64_t)t * sg.rank + trow + rr] = z0;
+      atomicMax(&sh.v_zmax[0][t], __float_as_int(fabsf(z0)));
+      if (sg.z1) {
+        const float z1 = smid[16 * VT + tl * 16 + rr] * v;
+        sg.z1[(int64_t)t * sg.rank + trow + rr] = z1;
+        atomicMax(&sh.v_zmax[1][t], __float_as_int(fabsf(z1)));
+      }
     }
-  }
-  __syncthreads();
-  if (tid < p.k) {  // this unit's maxima: plain stores, overwritten by every call (nothing to reset)
-    int *tm = sg.tmax + (int64_t)(unit - sg.tile0) * 2 * p.k;
-    tm[tid] = sh.v_zmax[0][tid];
-    if (sg.z1) tm[p.k + tid] = sh.v_zmax[1][tid];
+    __syncthreads();
+    if (tid < p.k) {  // this tile's maxima: plain stores, overwritten by every call (nothing to reset)
+      int *tm = sg.tmax + (int64_t)(trow / 16) * 2 * p.k;
+      tm[tid] = sh.v_zmax[0][tid];
+      if (sg.z1) tm[p.k + tid] = sh.v_zmax[1][tid];
+      sh.v_zmax[0][tid] = sh.v_zmax[1][tid] = 0;  // (read and cleared by the same thread)
+    }
   }
   LBX_PROBE(5);
   return true;
 }
 
-template <int NCB, bool SILU>
+template <int NCB, bool SILU, int VT>
 __global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_constant__ VParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ LinShm sh;
@@ -545,7 +563,7 @@ __global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_consta
   vstage_issue(p, blockIdx.x, W, sh);
   pdl_trigger();
   pdl_wait();
-  vstage_run<NCB, SILU>(p, blockIdx.x, W, S, sh, false);
+  vstage_run<NCB, SILU, VT>(p, blockIdx.x, W, S, sh, false);
 }
 
 // ---------------------------------------------------------------------------
@@ -990,9 +1008,24 @@ static int check_args(const lbx_proj *projs, const lbx_linear_args *a) {
 }
 
 using VKern = void (*)(VParams);
-static VKern vstage_for(int ncb, bool silu) {
-  if (silu) return ncb == 1 ? vstage_kernel<1, true> : ncb == 2 ? vstage_kernel<2, true> : vstage_kernel<4, true>;
-  return ncb == 1 ? vstage_kernel<1, false> : ncb == 2 ? vstage_kernel<2, false> : vstage_kernel<4, false>;
+template <int VT>
+static VKern vstage_for_vt(int ncb, bool silu) {
+  if (silu)
+    return ncb == 1 ? vstage_kernel<1, true, VT> : ncb == 2 ? vstage_kernel<2, true, VT> : vstage_kernel<4, true, VT>;
+  return ncb == 1 ? vstage_kernel<1, false, VT> : ncb == 2 ? vstage_kernel<2, false, VT> : vstage_kernel<4, false, VT>;
+}
+static VKern vstage_for(int ncb, bool silu, int vt) {
+  return vt == 2 ? vstage_for_vt<2>(ncb, silu) : vstage_for_vt<1>(ncb, silu);
+}
+
+static int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  }
+  return n;
 }
 
 #ifndef LBX_U_MIN_CTAS
@@ -1005,8 +1038,10 @@ static int stage_smem_limits(size_t &vmax, size_t &umax) {
   static size_t v_ = 0, u_ = 0;
   if (!v_) {
     size_t m = 0, vv = (size_t)-1, uu = (size_t)-1;
-    for (auto kk : {vstage_kernel<1, false>, vstage_kernel<2, false>, vstage_kernel<4, false>,
-                    vstage_kernel<1, true>, vstage_kernel<2, true>, vstage_kernel<4, true>}) {
+    for (auto kk : {vstage_kernel<1, false, 1>, vstage_kernel<2, false, 1>, vstage_kernel<4, false, 1>,
+                    vstage_kernel<1, true, 1>, vstage_kernel<2, true, 1>, vstage_kernel<4, true, 1>,
+                    vstage_kernel<1, false, 2>, vstage_kernel<2, false, 2>, vstage_kernel<4, false, 2>,
+                    vstage_kernel<1, true, 2>, vstage_kernel<2, true, 2>, vstage_kernel<4, true, 2>}) {
       cudaError_t e = allow_max_smem(kk, &m);
       if (e != cudaSuccess) return cuda_status(e, "vstage smem attribute");
       vv = std::min(vv, m);
@@ -1033,8 +1068,10 @@ struct LinPrep {
   size_t v_w, v_s, u_w, u_s;  // weight (W) and scratch (S) shared-memory bytes of each stage
 };
 
+// multi_tile: V units of two tiles when one-tile units would not all be
+// resident at once (the persistent program keeps one tile per unit)
 static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0, int k, void *ws,
-                       size_t vmax, size_t umax, LinPrep &P) {
+                       size_t vmax, size_t umax, LinPrep &P, bool multi_tile = true) {
   const int n_proj = a->n_proj;
   const int K = projs[0].in_features;
   const int ncols = 2 * k;
@@ -1079,7 +1116,12 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
   vp.x = reinterpret_cast<const uint8_t *>(a->x) + (size_t)tok0 * K * esz_x;
   vp.x2 = a->x2 ? reinterpret_cast<const uint8_t *>(a->x2) + (size_t)tok0 * K * esz_x : nullptr;
   vp.norm_w = a->norm_w;
-  int vtiles = 0;
+  int ttiles = 0;
+  for (int i = 0; i < n_proj; ++i)
+    for (int b = 0; b < projs[i].n_branches; ++b)
+      if (projs[i].br[b].v_sign) ttiles += (projs[i].br[b].rank + 15) / 16;
+  vp.vt = multi_tile && ttiles > 2 * sm_count() ? 2 : 1;
+  int vunits = 0;
   for (int i = 0; i < n_proj; ++i) {
     const lbx_proj &pr = projs[i];
     for (int b = 0; b < pr.n_branches; ++b) {
@@ -1096,11 +1138,11 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
         sg.z1 = zp[i][1];
 
       }
-      sg.tile0 = vtiles;
-      vtiles += (sg.rank + 15) / 16;
+      sg.unit0 = vunits;
+      vunits += ((sg.rank + 15) / 16 + vp.vt - 1) / vp.vt;
     }
   }
-  P.v_w = al256((size_t)16 * vp.vpitch * 4 + (size_t)vp.vcap * 4 * (rms ? 2 : 1) + 32 * 4);
+  P.v_w = al256((size_t)16 * vp.vt * vp.vpitch * 4 + (size_t)vp.vcap * 4 * (rms ? 2 : 1) + 32 * vp.vt * 4);
   P.v_s = (size_t)PASS_WORDS * act_ws(ncols) * 4 + (size_t)VWARPS * 16 * k * 4;
   P.v_s = (P.v_s + 255) & ~(size_t)255;
   vp.s_bytes = (int)P.v_s;
@@ -1169,7 +1211,7 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
   }
   up.nseg = n_proj;
   P.ncb = ncb;
-  P.vunits = vtiles;
+  P.vunits = vunits;
   P.uunits = ctas;
   return LBX_OK;
 }
@@ -1404,7 +1446,7 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
     }
     LBX_CHECK_SUP(false, "this call does not fit the cluster executor: %s", why);
   }
-  auto vk = vstage_for(P.ncb, a->prologue == LBX_PRO_SILU_MUL);
+  auto vk = vstage_for(P.ncb, a->prologue == LBX_PRO_SILU_MUL, P.vp.vt);
   auto uk = P.ncb == 1 ? ustage_kernel<1> : P.ncb == 2 ? ustage_kernel<2> : ustage_kernel<4>;
   cudaError_t e = launch(vk, dim3(P.vunits), dim3(VTHREADS), P.v_w + P.v_s, stream, pdl, P.vp);
   if (e != cudaSuccess) return cuda_status(e, "vstage launch");
@@ -1544,7 +1586,7 @@ extern "C" int lbx_linear_allgather(const lbx_proj *proj, const lbx_linear_args 
   for (int j = 0; j < n_peer; ++j)
     P.up.xbuf[j] = reinterpret_cast<unsigned long long *>(xbuf_peers[j]) + y_col0;
   const bool pdl = a->use_pdl != 0;
-  auto vk = vstage_for(P.ncb, a->prologue == LBX_PRO_SILU_MUL);
+  auto vk = vstage_for(P.ncb, a->prologue == LBX_PRO_SILU_MUL, P.vp.vt);
   auto uk = P.ncb == 1   ? ustage_kernel<1, true>
             : P.ncb == 2 ? ustage_kernel<2, true>
                          : ustage_kernel<4, true>;

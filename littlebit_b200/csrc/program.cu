@@ -436,7 +436,7 @@ static int build_linear(ProgBuilder &B, const lbx_proj *projs, const lbx_linear_
   for (int t0 = 0; t0 < a.n_tokens; t0 += LBX_MAX_TOKENS) {
     const int k = std::min(LBX_MAX_TOKENS, a.n_tokens - t0);
     LinPrep P;
-    rc = prep_linear(projs, &a, t0, k, ws, budget, budget, P);
+    rc = prep_linear(projs, &a, t0, k, ws, budget, budget, P, /*multi_tile=*/false);
     if (rc) return rc;
     LBX_CHECK_SUP(!B.ncb || B.ncb == P.ncb, "a program's linears must share the token count");
     B.ncb = P.ncb;

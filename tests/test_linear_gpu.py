@@ -347,3 +347,24 @@ def test_cluster_executor_rejects_what_it_cannot_take(ops):
     with pytest.raises(RuntimeError, match="unsupported"):
         ops.linear_group([lay2], x5, [y5], exec_mode=L.LBX_EXEC_CLUSTER)
     torch.cuda.synchronize()
+
+
+def test_two_tile_v_units_match_one_tile(ops):
+    """A q/k/v call of the 7B shape (375 V tiles, more than two CTAs per SM hold)
+    runs two 16-row tiles per V unit; each projection alone (125 tiles) runs one.
+    Both give the same bits, for k = 1, 3, 5 and with the RMSNorm prologue."""
+    from littlebit_b200 import _lib as L
+
+    layers = [_layer(ops, 4096, 4096, [184, 1816], seed=300 + i)[2] for i in range(3)]
+    w = (1 + 0.1 * torch.randn(4096, generator=_gen(301))).abs().to(DEV)
+    for k in (1, 3, 5):
+        x = torch.randn(k, 4096, generator=_gen(310 + k)).to(DEV)
+        grouped = [torch.empty(k, 4096, device=DEV) for _ in layers]
+        ops.linear_group(layers, x, grouped, prologue=L.LBX_PRO_RMSNORM, norm_w=w,
+                         exec_mode=L.LBX_EXEC_KERNELS)
+        for lay, yg in zip(layers, grouped):
+            y1 = torch.empty(k, 4096, device=DEV)
+            ops.linear_group([lay], x, [y1], prologue=L.LBX_PRO_RMSNORM, norm_w=w,
+                             exec_mode=L.LBX_EXEC_KERNELS)
+            torch.cuda.synchronize()
+            assert torch.equal(yg, y1), k
