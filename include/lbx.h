@@ -71,10 +71,16 @@ typedef struct lbx_proj {
 #define LBX_PRO_NONE 0
 #define LBX_PRO_RMSNORM 1 /* x <- x * rsqrt(mean(x^2)+eps) * norm_w              */
 #define LBX_PRO_SILU_MUL 2 /* x <- silu(x) * x2   (cpp:1117-1170 silu_mul)        */
+#define LBX_PRO_MUL 3      /* x <- x * x2 (x already silu'd by LBX_EPI_SILU0)     */
 
 /* Output mode. */
 #define LBX_EPI_STORE 0 /* y  = linear(x)                                        */
 #define LBX_EPI_ADD 1   /* y += linear(x)   (residual stream update, fp32 only)  */
+#define LBX_EPI_SILU0 2 /* y[0] = silu(linear_0(x)), other projections store:
+                         * a gate/up call whose gate feeds an LBX_PRO_MUL down
+                         * projection computes silu once per element instead of
+                         * in every CTA of the down projection (with fp32 y the
+                         * down projection's bits are those of LBX_PRO_SILU_MUL) */
 
 typedef struct lbx_linear_args {
   int32_t n_proj;      /* 1..LBX_MAX_PROJ projections sharing the input x      */

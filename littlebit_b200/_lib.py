@@ -15,8 +15,8 @@ LBX_OK, LBX_EINVAL, LBX_EUNSUPPORTED, LBX_ECUDA = 0, 1, 2, 3
 LBX_F32, LBX_BF16 = 0, 1
 LBX_MAX_TOKENS = 16
 LBX_MAX_PROJ = 3
-LBX_PRO_NONE, LBX_PRO_RMSNORM, LBX_PRO_SILU_MUL = 0, 1, 2
-LBX_EPI_STORE, LBX_EPI_ADD = 0, 1
+LBX_PRO_NONE, LBX_PRO_RMSNORM, LBX_PRO_SILU_MUL, LBX_PRO_MUL = 0, 1, 2, 3
+LBX_EPI_STORE, LBX_EPI_ADD, LBX_EPI_SILU0 = 0, 1, 2
 LBX_EXEC_AUTO, LBX_EXEC_KERNELS, LBX_EXEC_PROGRAM, LBX_EXEC_CLUSTER = 0, 1, 2, 3
 
 

@@ -213,14 +213,15 @@ static int forward_chunk(const lbx_model *m, const int64_t *tokens, int32_t n, i
     lbx_linear_args gu = a;
     gu.n_proj = 2;
     gu.norm_w = ly.ln2;
-    gu.y[0] = gate;
+    gu.y[0] = gate;  // silu(gate), computed once per element (the down prologue multiplies)
     gu.y[1] = up;
     gu.y[2] = nullptr;
+    gu.epilogue = LBX_EPI_SILU0;
     rc = lbx_linear_verify(ly.proj + 4, &gu, lin, L.lin_bytes, stream);
     if (rc) return rc;
     // x += down(silu(gate) * up)
     lbx_linear_args dn = o;
-    dn.prologue = LBX_PRO_SILU_MUL;
+    dn.prologue = LBX_PRO_MUL;
     dn.x = gate;
     dn.x2 = up;
     rc = lbx_linear_verify(ly.proj + 6, &dn, lin, L.lin_bytes, stream);
@@ -373,13 +374,14 @@ static int forward_program(const lbx_model *m, const int64_t *tokens, int32_t n,
       lbx_linear_args gu = a;
       gu.n_proj = 2;
       gu.norm_w = ly.ln2;
-      gu.y[0] = gate;
+      gu.y[0] = gate;  // silu(gate)
       gu.y[1] = up;
       gu.y[2] = nullptr;
+      gu.epilogue = LBX_EPI_SILU0;
       rc = build_linear(B, ly.proj + 4, gu, lin, budget);
       if (rc) return rc;
       lbx_linear_args dn = o;
-      dn.prologue = LBX_PRO_SILU_MUL;
+      dn.prologue = LBX_PRO_MUL;
       dn.x = gate;
       dn.x2 = up;
       rc = build_linear(B, ly.proj + 6, dn, lin, budget);

@@ -302,7 +302,16 @@ LBX_DEV void vstage_issue(const VParams &p, int unit, uint8_t *W, LinShm &sh) {
 // issued and before v2 is used (the V-stage waits for its weight copies
 // there).  Columns below p.vcap take v2 / norm_w from the shared-memory
 // copies sv2 / snw, the rest from global memory (same arithmetic).
-template <bool SILU, class OnFirst>
+// prologue kinds of the V-stage staging (compile-time: the second input
+// array costs registers)
+constexpr int PM_X = 0;     // x (optionally RMSNorm'd)
+constexpr int PM_SILU = 1;  // silu(x) * x2
+constexpr int PM_MUL = 2;   // x * x2
+__host__ __device__ inline int pm_of(int prologue) {
+  return prologue == LBX_PRO_SILU_MUL ? PM_SILU : prologue == LBX_PRO_MUL ? PM_MUL : PM_X;
+}
+
+template <int PM, class OnFirst>
 LBX_DEV void vstage_stage(const VParams &p, const float *v2, const float *sv2, const float *snw,
                           int pass, uint32_t *act, LinShm &sh, OnFirst &&on_first) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -319,17 +328,17 @@ LBX_DEV void vstage_stage(const VParams &p, const float *v2, const float *sv2, c
   float hw[8];
   for (int t0 = 0; t0 < p.k; t0 += TBATCH) {
     // issue the loads of a batch of tokens before using any of them
-    float xv[TBATCH][8], uv[SILU ? TBATCH : 1][8];
+    float xv[TBATCH][8], uv[PM != PM_X ? TBATCH : 1][8];
 #pragma unroll
     for (int j = 0; j < TBATCH; ++j) {
       if (wvalid && t0 + j < p.k) {
         load8(p.x, p.xdt, (int64_t)(t0 + j) * p.K + col, xv[j]);
-        if constexpr (SILU) load8(p.x2, p.xdt, (int64_t)(t0 + j) * p.K + col, uv[j]);
+        if constexpr (PM != PM_X) load8(p.x2, p.xdt, (int64_t)(t0 + j) * p.K + col, uv[j]);
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           xv[j][i] = 0.f;
-          if constexpr (SILU) uv[j][i] = 0.f;
+          if constexpr (PM != PM_X) uv[j][i] = 0.f;
         }
       }
     }
@@ -369,8 +378,10 @@ LBX_DEV void vstage_stage(const VParams &p, const float *v2, const float *sv2, c
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float xx = xv[j][i];
-        if constexpr (SILU) {
+        if constexpr (PM == PM_SILU) {
           a[i] = (xx / (1.0f + expf(-xx))) * uv[j][i] * hw[i];
+        } else if constexpr (PM == PM_MUL) {
+          a[i] = xx * uv[j][i] * hw[i];
         } else {
           sq2 = fmaf(xx, xx, sq2);
           a[i] = xx * hw[i];
@@ -427,10 +438,9 @@ LBX_DEV void vstage_stage(const VParams &p, const float *v2, const float *sv2, c
 
 // z = mid ⊙ (V_sign · a) for the 16 rows of unit `unit`; returns false (on
 // every thread) if the weight copies did not arrive in time
-// SILU: the SiLU-mul prologue (a compile-time choice: its second input array
-// would otherwise cost registers in every V-stage).  VT: 16-row tiles per unit
+// PM: the prologue kind (PM_X / PM_SILU / PM_MUL).  VT: 16-row tiles per unit
 // (p.vt); every tile gets exactly the one-tile arithmetic, x is staged once.
-template <int NCB, bool SILU, int VT = 1>
+template <int NCB, int PM, int VT = 1>
 LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinShm &sh, bool zero = true) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, q = lane & 3;
@@ -460,7 +470,7 @@ LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinS
   for (int pass = 0; pass < npass; ++pass) {
     const int pw0 = pass * PASS_WORDS;
     const int pwords = min(PASS_WORDS, p.Wv - pw0);
-    vstage_stage<SILU>(p, sg.v2, sv2, snw, pass, act, sh, [&] {
+    vstage_stage<PM>(p, sg.v2, sv2, snw, pass, act, sh, [&] {
       if (pass == 0) {
         ok = __syncthreads_and(mbar_wait_bounded(&sh.bar[UT_MAX], par, 0x101));
         LBX_PROBE(2);
@@ -549,7 +559,7 @@ LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinS
   return true;
 }
 
-template <int NCB, bool SILU, int VT>
+template <int NCB, int PM, int VT>
 __global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_constant__ VParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ LinShm sh;
@@ -563,7 +573,7 @@ __global__ void __launch_bounds__(VTHREADS, 2) vstage_kernel(const __grid_consta
   vstage_issue(p, blockIdx.x, W, sh);
   pdl_trigger();
   pdl_wait();
-  vstage_run<NCB, SILU, VT>(p, blockIdx.x, W, S, sh, false);
+  vstage_run<NCB, PM, VT>(p, blockIdx.x, W, S, sh, false);
 }
 
 // ---------------------------------------------------------------------------
@@ -652,7 +662,8 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
   const int g = lane >> 2, q = lane & 3;
   const int ut = p.ut, nsplit = UWARPS / ut;
   const int tile = warp % ut, split = warp / ut;
-  const USeg &sg = p.seg[useg_of(p, unit)];
+  const int si = useg_of(p, unit);
+  const USeg &sg = p.seg[si];
   const int n0 = (unit - sg.cta0) * (16 * ut) + 16 * tile;
   const bool active = n0 < sg.out;
   const int ws = act_ws(p.ncols);
@@ -867,6 +878,7 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
         float v = myu1[nl] * ldexpf(__int2float_rn(I0[cb][hrow]), -sh.u_ec[0][t]);
         if (sg.nbr > 1) v += myu1[16 + nl] * ldexpf(__int2float_rn(I1[cb][hrow]), -sh.u_ec[1][t]);
         if (sg.bias) v += myu1[32 + nl];
+        if (p.epi == LBX_EPI_SILU0 && si == 0) v = v / (1.0f + expf(-v));
         const int64_t off = (int64_t)t * sg.y_ld + n;
         if constexpr (PEER) {  // NVLink stores of (call number, value) words
           const unsigned long long wv = ((unsigned long long)call << 32) | __float_as_uint(v);
@@ -995,11 +1007,13 @@ static int check_args(const lbx_proj *projs, const lbx_linear_args *a) {
   LBX_CHECK_ARG(a->x_dtype == LBX_F32 || a->x_dtype == LBX_BF16, "bad x_dtype");
   LBX_CHECK_ARG(a->y_dtype == LBX_F32 || a->y_dtype == LBX_BF16, "bad y_dtype");
   LBX_CHECK_ARG(aligned16(a->x) && (!a->x2 || aligned16(a->x2)), "x/x2 must be 16-byte aligned");
-  LBX_CHECK_ARG(a->prologue >= LBX_PRO_NONE && a->prologue <= LBX_PRO_SILU_MUL, "bad prologue");
+  LBX_CHECK_ARG(a->prologue >= LBX_PRO_NONE && a->prologue <= LBX_PRO_MUL, "bad prologue");
   LBX_CHECK_ARG(a->prologue != LBX_PRO_RMSNORM || (a->norm_w && aligned16(a->norm_w)),
                 "RMSNorm prologue needs a 16-byte aligned norm_w");
-  LBX_CHECK_ARG(a->prologue != LBX_PRO_SILU_MUL || a->x2, "SiLU-mul prologue needs x2");
-  LBX_CHECK_ARG(a->epilogue == LBX_EPI_STORE || (a->epilogue == LBX_EPI_ADD && a->y_dtype == LBX_F32),
+  LBX_CHECK_ARG((a->prologue != LBX_PRO_SILU_MUL && a->prologue != LBX_PRO_MUL) || a->x2,
+                "SiLU-mul and mul prologues need x2");
+  LBX_CHECK_ARG(a->epilogue == LBX_EPI_STORE || a->epilogue == LBX_EPI_SILU0 ||
+                    (a->epilogue == LBX_EPI_ADD && a->y_dtype == LBX_F32),
                 "bad epilogue (ADD needs fp32 y)");
   for (int i = 0; i < a->n_proj; ++i) LBX_CHECK_ARG(a->y[i], "y[%d] is NULL", i);
   LBX_CHECK_ARG(a->exec == LBX_EXEC_AUTO || a->exec == LBX_EXEC_KERNELS || a->exec == LBX_EXEC_CLUSTER,
@@ -1008,14 +1022,18 @@ static int check_args(const lbx_proj *projs, const lbx_linear_args *a) {
 }
 
 using VKern = void (*)(VParams);
-template <int VT>
-static VKern vstage_for_vt(int ncb, bool silu) {
-  if (silu)
-    return ncb == 1 ? vstage_kernel<1, true, VT> : ncb == 2 ? vstage_kernel<2, true, VT> : vstage_kernel<4, true, VT>;
-  return ncb == 1 ? vstage_kernel<1, false, VT> : ncb == 2 ? vstage_kernel<2, false, VT> : vstage_kernel<4, false, VT>;
+template <int PM, int VT>
+static VKern vstage_for_pv(int ncb) {
+  return ncb == 1 ? vstage_kernel<1, PM, VT> : ncb == 2 ? vstage_kernel<2, PM, VT> : vstage_kernel<4, PM, VT>;
 }
-static VKern vstage_for(int ncb, bool silu, int vt) {
-  return vt == 2 ? vstage_for_vt<2>(ncb, silu) : vstage_for_vt<1>(ncb, silu);
+template <int VT>
+static VKern vstage_for_vt(int ncb, int pm) {
+  return pm == PM_SILU ? vstage_for_pv<PM_SILU, VT>(ncb)
+         : pm == PM_MUL ? vstage_for_pv<PM_MUL, VT>(ncb)
+                        : vstage_for_pv<PM_X, VT>(ncb);
+}
+static VKern vstage_for(int ncb, int pm, int vt) {
+  return vt == 2 ? vstage_for_vt<2>(ncb, pm) : vstage_for_vt<1>(ncb, pm);
 }
 
 static int sm_count() {
@@ -1038,10 +1056,12 @@ static int stage_smem_limits(size_t &vmax, size_t &umax) {
   static size_t v_ = 0, u_ = 0;
   if (!v_) {
     size_t m = 0, vv = (size_t)-1, uu = (size_t)-1;
-    for (auto kk : {vstage_kernel<1, false, 1>, vstage_kernel<2, false, 1>, vstage_kernel<4, false, 1>,
-                    vstage_kernel<1, true, 1>, vstage_kernel<2, true, 1>, vstage_kernel<4, true, 1>,
-                    vstage_kernel<1, false, 2>, vstage_kernel<2, false, 2>, vstage_kernel<4, false, 2>,
-                    vstage_kernel<1, true, 2>, vstage_kernel<2, true, 2>, vstage_kernel<4, true, 2>}) {
+    VKern all[18];
+    int na = 0;
+    for (int vt = 1; vt <= 2; ++vt)
+      for (int pm = 0; pm < 3; ++pm)
+        for (int ncb : {1, 2, 4}) all[na++] = vstage_for(ncb, pm, vt);
+    for (VKern kk : all) {
       cudaError_t e = allow_max_smem(kk, &m);
       if (e != cudaSuccess) return cuda_status(e, "vstage smem attribute");
       vv = std::min(vv, m);
@@ -1446,7 +1466,7 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
     }
     LBX_CHECK_SUP(false, "this call does not fit the cluster executor: %s", why);
   }
-  auto vk = vstage_for(P.ncb, a->prologue == LBX_PRO_SILU_MUL, P.vp.vt);
+  auto vk = vstage_for(P.ncb, pm_of(a->prologue), P.vp.vt);
   auto uk = P.ncb == 1 ? ustage_kernel<1> : P.ncb == 2 ? ustage_kernel<2> : ustage_kernel<4>;
   cudaError_t e = launch(vk, dim3(P.vunits), dim3(VTHREADS), P.v_w + P.v_s, stream, pdl, P.vp);
   if (e != cudaSuccess) return cuda_status(e, "vstage launch");
@@ -1586,7 +1606,7 @@ extern "C" int lbx_linear_allgather(const lbx_proj *proj, const lbx_linear_args 
   for (int j = 0; j < n_peer; ++j)
     P.up.xbuf[j] = reinterpret_cast<unsigned long long *>(xbuf_peers[j]) + y_col0;
   const bool pdl = a->use_pdl != 0;
-  auto vk = vstage_for(P.ncb, a->prologue == LBX_PRO_SILU_MUL, P.vp.vt);
+  auto vk = vstage_for(P.ncb, pm_of(a->prologue), P.vp.vt);
   auto uk = P.ncb == 1   ? ustage_kernel<1, true>
             : P.ncb == 2 ? ustage_kernel<2, true>
                          : ustage_kernel<4, true>;

@@ -237,8 +237,9 @@ template <int NCB, int LMNT>
 LBX_DEV bool run_unit(const Phase &P, const ProgIo &io, int u, uint8_t *W, uint8_t *S, LinShm &sh) {
   switch (P.kind) {
     case PH_V:
-      return P.v.prologue == LBX_PRO_SILU_MUL ? vstage_run<NCB, true>(P.v, u, W, S, sh)
-                                              : vstage_run<NCB, false>(P.v, u, W, S, sh);
+      return P.v.prologue == LBX_PRO_SILU_MUL ? vstage_run<NCB, PM_SILU>(P.v, u, W, S, sh)
+             : P.v.prologue == LBX_PRO_MUL   ? vstage_run<NCB, PM_MUL>(P.v, u, W, S, sh)
+                                             : vstage_run<NCB, PM_X>(P.v, u, W, S, sh);
     case PH_U:
       return ustage_run<NCB>(P.u, u, P.units, W, S, sh);
     case PH_ATTN:

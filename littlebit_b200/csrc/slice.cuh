@@ -223,9 +223,11 @@ __global__ void __launch_bounds__(VTHREADS, LBX_SL_MINBLOCKS) slice_kernel(const
   // ---- V: this CTA's z rows
   if (ntl > 0) {
     if (vp.prologue == LBX_PRO_SILU_MUL)
-      vstage_stage<true>(vp, sg.v2, nullptr, nullptr, 0, act, sh, [] {});
+      vstage_stage<PM_SILU>(vp, sg.v2, nullptr, nullptr, 0, act, sh, [] {});
+    else if (vp.prologue == LBX_PRO_MUL)
+      vstage_stage<PM_MUL>(vp, sg.v2, nullptr, nullptr, 0, act, sh, [] {});
     else
-      vstage_stage<false>(vp, sg.v2, nullptr, nullptr, 0, act, sh, [] {});
+      vstage_stage<PM_X>(vp, sg.v2, nullptr, nullptr, 0, act, sh, [] {});
     __syncthreads();
     LBX_PROBE(33);
 #pragma unroll
@@ -436,6 +438,7 @@ __global__ void __launch_bounds__(VTHREADS, LBX_SL_MINBLOCKS) slice_kernel(const
         float v = su1[rr] * ldexpf(__int2float_rn(I0), -s_ec[0][t]);
         if (P.nbr > 1) v += su1[p.rmax + rr] * ldexpf(__int2float_rn(I1), -s_ec[1][t]);
         if (P.bias) v += su1[2 * p.rmax + rr];
+        if (p.epi == LBX_EPI_SILU0 && C.proj == 0) v = v / (1.0f + expf(-v));
         const int64_t off = (int64_t)t * P.y_ld + n;
         if (p.ydt == LBX_F32) {
           float *y = reinterpret_cast<float *>(P.y) + off;

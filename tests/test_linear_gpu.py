@@ -368,3 +368,35 @@ def test_two_tile_v_units_match_one_tile(ops):
                              exec_mode=L.LBX_EXEC_KERNELS)
             torch.cuda.synchronize()
             assert torch.equal(yg, y1), k
+
+
+def test_silu_epilogue_then_mul_prologue_equals_silu_mul_prologue(ops):
+    """gate/up with LBX_EPI_SILU0 (gate stored as silu(gate)) followed by down
+    with LBX_PRO_MUL computes the same bits as gate/up stored plainly followed
+    by down with LBX_PRO_SILU_MUL (fp32), on both executors."""
+    from littlebit_b200 import _lib as L
+
+    H, I = 1024, 2816
+    gate, up = (_layer(ops, H, I, [96, 80], seed=400 + i)[2] for i in range(2))
+    down = _layer(ops, I, H, [96, 80], seed=402)[2]
+    w = (1 + 0.1 * torch.randn(H, generator=_gen(403))).abs().to(DEV)
+    for k in (1, 4, 7):
+        x = torch.randn(k, H, generator=_gen(410 + k)).to(DEV)
+        res = torch.randn(k, H, generator=_gen(420 + k)).to(DEV)
+        outs = {}
+        for fused in (False, True):
+            for mode in (L.LBX_EXEC_KERNELS, L.LBX_EXEC_CLUSTER):
+                if mode == L.LBX_EXEC_CLUSTER and k > 4:
+                    continue
+                g_ = torch.empty(k, I, device=DEV)
+                u_ = torch.empty(k, I, device=DEV)
+                ops.linear_group([gate, up], x, [g_, u_], prologue=L.LBX_PRO_RMSNORM, norm_w=w,
+                                 epilogue=L.LBX_EPI_SILU0 if fused else L.LBX_EPI_STORE, exec_mode=mode)
+                y = res.clone()
+                ops.linear_group([down], g_, [y], prologue=L.LBX_PRO_MUL if fused else L.LBX_PRO_SILU_MUL,
+                                 x2=u_, epilogue=L.LBX_EPI_ADD, exec_mode=L.LBX_EXEC_KERNELS)
+                outs[(fused, mode)] = y
+        torch.cuda.synchronize()
+        ref = outs[(False, L.LBX_EXEC_KERNELS)]
+        for key, y in outs.items():
+            assert torch.equal(y, ref), (k, key)
