@@ -350,7 +350,29 @@ def run_decode(args, dev, rank, ws):
     if not (chain_ok and tree_ok):
         raise RuntimeError(f"speculative output differs from target-only greedy (chain {chain_ok}, tree {tree_ok})")
     packed = dec.packed_bytes()
-    return {
+
+    # algorithmic bytes per generated token: packed words and fp32 scales of the
+    # projections a step runs, the bf16 lm_head, and the bf16 KV read at the mean
+    # sequence length of the run
+    def step_bytes(d, branches):
+        b = 0
+        for ly in d.layers:
+            for pr in ly["projs"]:
+                for bi, br in enumerate(pr.branches):
+                    if bi not in branches:
+                        continue
+                    if br.v_sign is not None:
+                        b += (br.rank * pr.in_features + 7) // 8 + 4 * pr.in_features
+                    b += (pr.out_features * br.rank + 7) // 8 + 4 * (br.rank + pr.out_features)
+        kv_tok = 2 * shape.num_hidden_layers * shape.num_key_value_heads * shape.head_dim * 2
+        return b + shape.vocab_size * shape.hidden_size * 2 + kv_tok * (args.prompt + n // 2)
+    bpt_draft, bpt_target = step_bytes(dec, (0,)), step_bytes(dec, (0, 1))
+    peak_gbs, _ = peaks()
+
+    def frac(tps, bpt):
+        return round(bpt * tps / ws / 1e9 / peak_gbs, 4)
+
+    out = {
         "workload": f"Llama-2-7B shape (32 layers, hidden 4096, MLP 11008, vocab 32000), "
                     f"{args.prompt}-token random prompt, {n} greedy tokens, batch 1 per GPU",
         "unit": "tokens/s", "aggregate_over_gpus": ws,
@@ -368,6 +390,11 @@ def run_decode(args, dev, rank, ws):
                            "num_steps": tst["num_steps"], "tokens": n_tr, "token_identical": tree_ok},
         "timing": "wall clock around each whole generate call (host syncs included), max over ranks",
     }
+    out["bytes_per_token"] = {"draft": bpt_draft, "target": bpt_target,
+                              "note": "packed words + fp32 scales + bf16 lm_head + bf16 KV at the mean length"}
+    out["hbm_frac_per_gpu"] = {"draft_greedy": frac(out["draft_greedy"], bpt_draft),
+                               "target_greedy": frac(out["target_greedy"], bpt_target)}
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -441,6 +468,58 @@ def run_row_shard(args, dev, rank, ws, reps: int = 200):
             "allgather_bytes_per_rank": 4 * N // ws,
             "gbs_whole_layer": round(alg / (t_fused * 1e-6) / 1e9, 2), "algorithmic_bytes": alg,
             "timing": f"CUDA events over {reps} calls ({per} per CUDA graph), max over ranks"}
+
+
+def run_dense_ref(args, dev, rank, ws, P: int = 64):
+    """The reference's own GPU path for the same layer, as its module computes it
+    (littlebit.py:114-121 with the residual branch of 104-107): bf16 ±1 U and V
+    unpacked to dense tensors, two cuBLAS GEMMs per branch.  A reported
+    baseline: same chain-of-distinct-layers workload, CUDA-graph timed."""
+    k = args.tokens
+    g = torch.Generator(device=dev).manual_seed(7)
+    sgn = lambda r, c: (torch.randint(0, 2, (r, c), generator=g, device=dev, dtype=torch.int8) * 2 - 1).bfloat16()
+    sc = lambda n: (1 + 0.1 * torch.randn(n, generator=g, device=dev)).abs().bfloat16()
+    layers = [[(sgn(r, IN_F), sc(IN_F), sc(r), sgn(OUT_F, r), sc(OUT_F)) for r in RANKS] for _ in range(P)]
+    acts = [torch.randn(k, IN_F, generator=g, device=dev).bfloat16()] + \
+           [torch.empty(k, OUT_F, device=dev, dtype=torch.bfloat16) for _ in range(P)]
+
+    def step():
+        for i in range(P):
+            x = acts[i]
+            y = None
+            for V, v2, mid, U, u1 in layers[i]:
+                yb = ((x * v2) @ V.t() * mid) @ U.t() * u1
+                y = yb if y is None else y + yb
+            acts[i + 1].copy_(y)
+
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / reps / P * 1e3
+    b, _ = layer_bytes(k)
+    dense_bytes = sum(2 * r * (IN_F + OUT_F) for r in RANKS)
+    del graph
+    return {"workload": f"C2 layer as the reference's module runs it on GPU: bf16 dense ±1 U/V, "
+                        f"two cuBLAS GEMMs per branch, k={k}, chain of {P} distinct layers",
+            "us_per_layer": round(us, 3), "gbs_algorithmic": round(b / (us * 1e-6) / 1e9, 2),
+            "dense_weight_bytes_per_layer": dense_bytes,
+            "speedup_of_packed_kernels": None}
 
 
 def run_ours(args):
@@ -554,6 +633,9 @@ def run_ours(args):
             cpu = {"value": round(r["gbs"], 4), "unit": "GB/s", "cores": r["threads"],
                    "kind": "reference", "sample": r["sample"]}
 
+    dense = run_dense_ref(args, dev, rank, ws) if args.dense_ref and ws == 1 else None
+    if dense:
+        dense["speedup_of_packed_kernels"] = round(dense["us_per_layer"] / (per_launch_s * 1e6), 2)
     decode = run_decode(args, dev, rank, ws) if args.decode else None
     row_shard = run_row_shard(args, dev, rank, ws) if ws > 1 else None
 
@@ -586,6 +668,7 @@ def run_ours(args):
                     "ms_per_step": round(t2 / args.steps, 4),
                     "path": "pinned host x -> chain via the C ABI -> pinned host y, each step"},
             "cpu_baseline": cpu,
+            "dense_bf16_ref": dense,
             "decode": decode,
             "row_shard": row_shard,
             "gpu_launches": {"program": 1, "kernels": 2 * P, "cluster": P}[args.exec] * args.steps,
@@ -613,6 +696,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--decode", type=int, default=1, help="also run the 7B-shape decode section")
+    ap.add_argument("--dense-ref", type=int, default=1,
+                    help="also time the reference's GPU path (bf16 dense GEMMs) on the same layer")
     ap.add_argument("--prompt", type=int, default=128)
     ap.add_argument("--new-tokens", type=int, default=256)
     ap.add_argument("--res-scale", type=float, default=0.08)
