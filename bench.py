@@ -336,6 +336,9 @@ def run_decode(args, dev, rank, ws):
     (dr, _), t_draft = timed(lambda: autoregressive_generate(draft_only, ids, None, max_new_tokens=n,
                                                               eos_token_id=-1))
     (ar, _), t_ar = timed(lambda: autoregressive_generate(tgt, ids, None, max_new_tokens=n, eos_token_id=-1))
+    # prompt prefill + one token: the decode-only rates exclude it
+    _, t_draft1 = timed(lambda: autoregressive_generate(draft_only, ids, None, max_new_tokens=1, eos_token_id=-1))
+    _, t_ar1 = timed(lambda: autoregressive_generate(tgt, ids, None, max_new_tokens=1, eos_token_id=-1))
     (sp, sst), t_sp = timed(lambda: speculative_decode(drf, tgt, ids, None, max_new_tokens=n, draft_length=4,
                                                        eos_token_id=-1))
     (tr, tst), t_tr = timed(lambda: speculative_decode_tree(drf, tgt, ids, None, max_new_tokens=n,
@@ -380,6 +383,10 @@ def run_decode(args, dev, rank, ws):
         "target_packed_mb": round(packed / 1e6, 1),
         "draft_greedy": round(n * ws / t_draft, 2),
         "target_greedy": round(n * ws / t_ar, 2),
+        "decode_only": {"draft_greedy": round((n - 1) * ws / (t_draft - t_draft1), 2),
+                        "target_greedy": round((n - 1) * ws / (t_ar - t_ar1), 2),
+                        "target_prefill_s": round(t_ar1, 4),
+                        "method": "(n - 1) / (t(n tokens) - t(1 token)): prompt prefill excluded"},
         "spec_chain_gamma4": {"tokens_per_s": round(n * ws / t_sp, 2),
                               "acceptance_rate": round(sst["acceptance_rate"], 4),
                               "mean_acceptance_length": round(sst["mean_acceptance_length"], 3),
@@ -388,12 +395,81 @@ def run_decode(args, dev, rank, ws):
                            "acceptance_rate": round(tst["acceptance_rate"], 4),
                            "mean_acceptance_length": round(tst["mean_acceptance_length"], 3),
                            "num_steps": tst["num_steps"], "tokens": n_tr, "token_identical": tree_ok},
-        "timing": "wall clock around each whole generate call (host syncs included), max over ranks",
+        "timing": "wall clock around each whole generate call (prompt prefill and host syncs included), "
+                  "max over ranks",
     }
     out["bytes_per_token"] = {"draft": bpt_draft, "target": bpt_target,
                               "note": "packed words + fp32 scales + bf16 lm_head + bf16 KV at the mean length"}
-    out["hbm_frac_per_gpu"] = {"draft_greedy": frac(out["draft_greedy"], bpt_draft),
-                               "target_greedy": frac(out["target_greedy"], bpt_target)}
+    out["hbm_frac_per_gpu"] = {"draft_greedy": frac(out["decode_only"]["draft_greedy"], bpt_draft),
+                               "target_greedy": frac(out["decode_only"]["target_greedy"], bpt_target)}
+    return out
+
+
+def run_decode70b(args, dev, rank, ws):
+    """Greedy and chain-speculative decode on the Llama-2-70B shape (BASELINE
+    config 5): 0.1-bit draft + 0.9-bit residual target (~8.5 GB packed) on every
+    GPU, one sequence per rank (data parallel), a 512-token random prompt."""
+    from littlebit_b200.cuda_models import CudaDraftModel, CudaTargetModel
+    from littlebit_b200.model import LLAMA2_70B, LittleBitDecoder, synthetic_runtime_state
+    from littlebit_b200.speculative_decoding import autoregressive_generate, speculative_decode
+
+    shape = LLAMA2_70B
+    r_d, r_r = _ranks_at(shape, 0.1), _ranks_at(shape, 0.9)
+    st = synthetic_runtime_state(shape, {k: [r_d[k], r_r[k]] for k in r_d}, seed=91 + rank, device=dev,
+                                 unit_gain=True)
+    for k in list(st):
+        if k.endswith(".u1_r"):
+            st[k] = st[k] * args.res_scale
+    prompt, n = 512, args.new70
+    dec = LittleBitDecoder(shape, st, device=dev, max_seq=prompt + n + 64)
+    del st
+    tgt = CudaTargetModel.from_decoder(dec)
+    drf = CudaDraftModel.from_target(tgt)
+    draft_only = CudaTargetModel.from_decoder(drf.dec)
+    ids = torch.randint(0, shape.vocab_size, (1, prompt),
+                        generator=torch.Generator().manual_seed(2000 + rank)).to(dev)
+
+    def timed(fn):
+        barrier(ws)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        out = fn()
+        torch.cuda.synchronize()
+        return out, max_over_ranks(time.perf_counter() - t0, ws)
+
+    autoregressive_generate(draft_only, ids, None, max_new_tokens=4, eos_token_id=-1)
+    autoregressive_generate(tgt, ids, None, max_new_tokens=4, eos_token_id=-1)
+    speculative_decode(drf, tgt, ids, None, max_new_tokens=8, draft_length=4, eos_token_id=-1)
+    (_, _), t_draft = timed(lambda: autoregressive_generate(draft_only, ids, None, max_new_tokens=n,
+                                                             eos_token_id=-1))
+    (ar, _), t_ar = timed(lambda: autoregressive_generate(tgt, ids, None, max_new_tokens=n, eos_token_id=-1))
+    _, t_draft1 = timed(lambda: autoregressive_generate(draft_only, ids, None, max_new_tokens=1, eos_token_id=-1))
+    _, t_ar1 = timed(lambda: autoregressive_generate(tgt, ids, None, max_new_tokens=1, eos_token_id=-1))
+    (sp, sst), t_sp = timed(lambda: speculative_decode(drf, tgt, ids, None, max_new_tokens=n,
+                                                       draft_length=4, eos_token_id=-1))
+    if sp.tolist() != ar.tolist():
+        raise RuntimeError("70B-shape chain speculation differs from target-only greedy")
+    lm = shape.vocab_size * shape.hidden_size * 2
+    kv = 2 * shape.num_hidden_layers * shape.num_key_value_heads * shape.head_dim * 2 * (prompt + n // 2)
+    peak_gbs, _ = peaks()
+    out = {"workload": f"Llama-2-70B shape (80 layers, hidden 8192, MLP 28672, 64/8 heads), "
+                       f"{prompt}-token random prompt, {n} greedy tokens, one sequence per GPU",
+           "unit": "tokens/s", "aggregate_over_gpus": ws,
+           "target_packed_gb": round(dec.packed_bytes() / 1e9, 2),
+           "draft_greedy": round(n * ws / t_draft, 2), "target_greedy": round(n * ws / t_ar, 2),
+           "decode_only": {"draft_greedy": round((n - 1) * ws / (t_draft - t_draft1), 2),
+                           "target_greedy": round((n - 1) * ws / (t_ar - t_ar1), 2),
+                           "target_prefill_s": round(t_ar1, 4),
+                           "method": "(n - 1) / (t(n tokens) - t(1 token)): prompt prefill excluded"},
+           "timing": "wall clock around each whole generate call (prompt prefill included), max over ranks",
+           "spec_chain_gamma4": {"tokens_per_s": round(n * ws / t_sp, 2),
+                                 "acceptance_rate": round(sst["acceptance_rate"], 4),
+                                 "mean_acceptance_length": round(sst["mean_acceptance_length"], 3),
+                                 "token_identical": True},
+           "lm_head_and_kv_bytes_per_token": lm + kv}
+    out["target_hbm_frac_per_gpu"] = round((dec.packed_bytes() + dec.scale_bytes() + lm + kv)
+                                           * out["decode_only"]["target_greedy"] / ws / 1e9
+                                           / peak_gbs, 4)
     return out
 
 
@@ -637,6 +713,7 @@ def run_ours(args):
     if dense:
         dense["speedup_of_packed_kernels"] = round(dense["us_per_layer"] / (per_launch_s * 1e6), 2)
     decode = run_decode(args, dev, rank, ws) if args.decode else None
+    decode70 = run_decode70b(args, dev, rank, ws) if args.decode70b else None
     row_shard = run_row_shard(args, dev, rank, ws) if ws > 1 else None
 
     if rank == 0:
@@ -670,6 +747,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "dense_bf16_ref": dense,
             "decode": decode,
+            "decode_70b": decode70,
             "row_shard": row_shard,
             "gpu_launches": {"program": 1, "kernels": 2 * P, "cluster": P}[args.exec] * args.steps,
             "clocks": clocks,
@@ -696,6 +774,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--decode", type=int, default=1, help="also run the 7B-shape decode section")
+    ap.add_argument("--decode70b", type=int, default=0,
+                    help="also run the 70B-shape decode section (about a minute more)")
+    ap.add_argument("--new70", type=int, default=32, help="tokens generated in the 70B section")
     ap.add_argument("--dense-ref", type=int, default=1,
                     help="also time the reference's GPU path (bf16 dense GEMMs) on the same layer")
     ap.add_argument("--prompt", type=int, default=128)

@@ -1491,8 +1491,22 @@ extern "C" int lbx_linear_verify(const lbx_proj *projs, const lbx_linear_args *a
   if (rc) return rc;
   const size_t need = ws_bytes_call(projs, a);
   LBX_CHECK_ARG(ws && ws_bytes >= need, "workspace too small (%zu < %zu)", ws_bytes, need);
-  for (int t0 = 0; t0 < a->n_tokens; t0 += LBX_MAX_TOKENS) {
-    const int k = std::min(LBX_MAX_TOKENS, a->n_tokens - t0);
+  // token batches: up to LBX_MAX_TOKENS, fewer when a batch's stages would not
+  // fit in shared memory (large ranks); tokens never interact, so the split
+  // does not change any token's bits
+  int kb = std::min(LBX_MAX_TOKENS, a->n_tokens);
+  {
+    size_t vmax = 0, umax = 0;
+    rc = stage_smem_limits(vmax, umax);
+    if (rc) return rc;
+    while (kb > 1) {
+      LinPrep P;
+      if (prep_linear(projs, a, 0, kb, ws, vmax, umax, P) != LBX_EUNSUPPORTED) break;
+      kb >>= 1;
+    }
+  }
+  for (int t0 = 0; t0 < a->n_tokens; t0 += kb) {
+    const int k = std::min(kb, a->n_tokens - t0);
     rc = run_batch(projs, a, t0, k, ws, stream);
     if (rc) return rc;
   }

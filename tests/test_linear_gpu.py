@@ -400,3 +400,15 @@ def test_silu_epilogue_then_mul_prologue_equals_silu_mul_prologue(ops):
         ref = outs[(False, L.LBX_EXEC_KERNELS)]
         for key, y in outs.items():
             assert torch.equal(y, ref), (k, key)
+
+
+def test_large_rank_splits_token_batches_bitwise(ops):
+    """A rank where 16 tokens' digits do not fit in shared memory (the 70B
+    0.9-bit residual size): the call runs in smaller token batches and every
+    token keeps the bits of a one-token call."""
+    _, _, lay = _layer(ops, 8192, 2048, [5736], seed=500)
+    x = torch.randn(16, 8192, generator=_gen(501)).to(DEV)
+    y = ops.lb_linear(lay, x)
+    for i in (0, 7, 8, 15):
+        assert torch.equal(ops.lb_linear(lay, x[i:i + 1])[0], y[i]), i
+    torch.cuda.synchronize()
