@@ -155,6 +155,37 @@ LBX_DEV uint32_t negbits4(uint32_t sel) {
   return r;
 }
 
+// The same expansion with fewer shifts: a byte table indexed by the selector
+// nibble's bits 2..0 can key on any one of those bits (bit 0:
+// {00,FF,00,FF,..}, bit 1: {00,00,FF,FF,..}, bit 2: {00,00,00,00,FF,FF,FF,FF}),
+// and prmt reads only the selector's low 16 bits, so one sign word needs only
+// the shifted copies w>>1, w>>16 and w>>17.
+LBX_DEV uint32_t prmt_tab(uint32_t lo, uint32_t hi, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(lo), "r"(hi), "r"(sel));
+  return r;
+}
+// k-step R (0..3) of a 4-word group: lo holds the bytes of bits sh+4j, hi those
+// of bits sh+1+4j (sh = 16*(R>>1) + 2*(R&1)), i.e. exactly negbits4(w >> sh)
+// and negbits4(w >> (sh+1))
+template <int R>
+LBX_DEV void sign_frag(uint32_t w, uint32_t &lo, uint32_t &hi) {
+  constexpr uint32_t B0 = 0xFF00FF00u, B1 = 0xFFFF0000u;
+  if constexpr (R == 0) {
+    lo = prmt_tab(B0, B0, w);
+    hi = prmt_tab(B1, B1, w);
+  } else if constexpr (R == 1) {
+    lo = prmt_tab(0u, ~0u, w);
+    hi = prmt_tab(0u, ~0u, w >> 1);
+  } else if constexpr (R == 2) {
+    lo = prmt_tab(B0, B0, w >> 16);
+    hi = prmt_tab(B1, B1, w >> 16);
+  } else {
+    lo = prmt_tab(0u, ~0u, w >> 16);
+    hi = prmt_tab(0u, ~0u, w >> 17);
+  }
+}
+
 // D(16x8,s32) += A(16x32,s8) * B(32x8,s8)
 LBX_DEV void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                     uint32_t b0, uint32_t b1) {

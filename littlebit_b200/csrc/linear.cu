@@ -125,11 +125,69 @@ struct UParams {
 // rows; its 8 prmt expansions feed 4 MMA k-steps.  The activation layout puts,
 // for word w, slot s=(h*4+j), column c, the 4 digits of reduction positions
 // 32w+16h+j+{0,4,8,12} into one uint32, matching the A-fragment bytes.
-// Even and odd groups accumulate into separate registers (two independent
-// MMA dependency chains), summed exactly at the end.
+// Single-column-block form (k <= 4 tokens): NG groups run side by side, their
+// MMAs issued interleaved k-step by k-step so that the NG accumulator chains
+// overlap in the tensor pipe; the A fragments come from the shift-light table
+// expansion.
+template <int R, int NG>
+LBX_DEV void sign_kstep1(int (&acc)[NG][4], const uint32_t (&wa)[NG], const uint32_t (&wb)[NG],
+                         const uint32_t *const (&aw)[NG], int ncols, int n8) {
+  constexpr int slot = 4 * (R >> 1) + 2 * (R & 1);
+#pragma unroll
+  for (int i = 0; i < NG; ++i) {
+    uint32_t a0, a1, a2, a3;
+    sign_frag<R>(wa[i], a0, a2);
+    sign_frag<R>(wb[i], a1, a3);
+    uint32_t b0 = 0, b1 = 0;
+    if (n8 < ncols) {
+      b0 = aw[i][slot * ncols + n8];
+      b1 = aw[i][(slot + 1) * ncols + n8];
+    }
+    mma_s8(acc[i], a0, a1, a2, a3, b0, b1);
+  }
+}
+template <int NG>
+LBX_DEV void sign_mma1(int (&acc)[NG][4], const uint32_t *rowg, const uint32_t *rowg8,
+                       const uint32_t *act, int ws, int ncols, const int (&G)[NG], int lane) {
+  const int q = lane & 3, n8 = lane >> 2;
+  uint32_t wa[NG], wb[NG];
+  const uint32_t *aw[NG];
+#pragma unroll
+  for (int i = 0; i < NG; ++i) {
+    const int w = 4 * G[i] + q;
+    wa[i] = rowg[w];
+    wb[i] = rowg8[w];
+    aw[i] = act + w * ws;
+  }
+  sign_kstep1<0, NG>(acc, wa, wb, aw, ncols, n8);
+  sign_kstep1<1, NG>(acc, wa, wb, aw, ncols, n8);
+  sign_kstep1<2, NG>(acc, wa, wb, aw, ncols, n8);
+  sign_kstep1<3, NG>(acc, wa, wb, aw, ncols, n8);
+}
+
+// Groups [g0, g1) summed into acc.  One column block: pairs of groups as two
+// interleaved chains.  Two or four blocks (already 2 or 4 independent chains
+// per k-step): even and odd groups into separate accumulators with the
+// per-bit-shift expansion, whose fewer live registers keep these widths from
+// spilling.  The int32 sums are exact, so none of this changes a bit.
 template <int NCB>
 LBX_DEV void sign_mma(int (&acc)[NCB][4], const uint32_t *rowg, const uint32_t *rowg8,
                       const uint32_t *act, int ws, int ncols, int g0, int g1, int lane) {
+  if constexpr (NCB == 1) {
+    int G = g0;
+    for (; G + 1 < g1; G += 2) {
+      int a2[2][4] = {};
+      const int gg[2] = {G, G + 1};
+      sign_mma1<2>(a2, rowg, rowg8, act, ws, ncols, gg, lane);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[0][e] += a2[0][e] + a2[1][e];
+    }
+    if (G < g1) {
+      const int gg[1] = {G};
+      sign_mma1<1>(acc, rowg, rowg8, act, ws, ncols, gg, lane);
+    }
+    return;
+  }
   const int q = lane & 3;
   const int n8 = lane >> 2;
   int acc2[NCB][4];
@@ -806,32 +864,76 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
   const int ngt = ng0 + ng1;  // this warp's share of the flattened (branch, group) list
   const int ga = (split * ngt) / nsplit, gb = ((split + 1) * ngt) / nsplit;
   if (active && ok) {
-    for (int G = ga; G < gb; ++G) {
-      const int b = G < ng0 ? 0 : 1;
-      const int Gl = b ? G - ng0 : G;
+    // per branch, this warp's share of the groups; each group is rounded on
+    // its own (with one column block, two groups at a time as two
+    // interleaved MMA chains)
+    auto branch_groups = [&](const int b, int (&Ib)[NCB][2]) {
+      const int lo = b ? max(ga, ng0) - ng0 : ga;
+      const int hi = b ? gb - ng0 : min(gb, ng0);
       const uint32_t *wt = b ? mywt1 : mywt0;
       const int pt = sg.pitch[b];
-      int acc[NCB][4];
+      const uint32_t *actb = b ? act1 : act0;
+      auto round_add = [&](const int (&acc)[NCB][4], int Gl) {
 #pragma unroll
-      for (int cb = 0; cb < NCB; ++cb) acc[cb][0] = acc[cb][1] = acc[cb][2] = acc[cb][3] = 0;
-      sign_mma<NCB>(acc, wt + g * pt, wt + (g + 8) * pt, b ? act1 : act0, ws, p.ncols, Gl, Gl + 1, lane);
+        for (int cb = 0; cb < NCB; ++cb) {
+          const int t = cb * 4 + q;
+          if (t < p.k) {
+            const int gi = b * gk + Gl * p.k + t;
+            const int ex = ue[gi];
+            if (ex != UE_NONE) {
+              const int sft = ex - sh.u_ec[b][t];
+              const int sq = usq[gi];
+              Ib[cb][0] += rshr(sq + 2 * (256 * acc[cb][0] + acc[cb][1]), sft);
+              Ib[cb][1] += rshr(sq + 2 * (256 * acc[cb][2] + acc[cb][3]), sft);
+            }
+          }
+        }
+      };
+      int G = lo;
+      if constexpr (NCB == 1) {
+        for (; G + 1 < hi; G += 2) {
+          int acc[2][4] = {};
+          const int gg[2] = {G, G + 1};
+          sign_mma1<2>(acc, wt + g * pt, wt + (g + 8) * pt, actb, ws, p.ncols, gg, lane);
+          round_add(reinterpret_cast<const int(&)[NCB][4]>(acc[0]), G);
+          round_add(reinterpret_cast<const int(&)[NCB][4]>(acc[1]), G + 1);
+        }
+      }
+      for (; G < hi; ++G) {
+        int acc[NCB][4] = {};
+        sign_mma<NCB>(acc, wt + g * pt, wt + (g + 8) * pt, actb, ws, p.ncols, G, G + 1, lane);
+        round_add(acc, G);
+      }
+    };
+    if constexpr (NCB == 1) {
+      branch_groups(0, I0);
+      if (ng1) branch_groups(1, I1);
+    } else {  // one loop over the flattened (branch, group) list: fewer live registers
+      for (int G = ga; G < gb; ++G) {
+        const int b = G < ng0 ? 0 : 1;
+        const int Gl = b ? G - ng0 : G;
+        const uint32_t *wt = b ? mywt1 : mywt0;
+        const int pt = sg.pitch[b];
+        int acc[NCB][4] = {};
+        sign_mma<NCB>(acc, wt + g * pt, wt + (g + 8) * pt, b ? act1 : act0, ws, p.ncols, Gl, Gl + 1, lane);
 #pragma unroll
-      for (int cb = 0; cb < NCB; ++cb) {
-        const int t = cb * 4 + q;
-        if (t < p.k) {
-          const int gi = b * gk + Gl * p.k + t;
-          const int ex = ue[gi];
-          if (ex != UE_NONE) {
-            const int sft = ex - sh.u_ec[b][t];
-            const int sq = usq[gi];
-            const int va = rshr(sq + 2 * (256 * acc[cb][0] + acc[cb][1]), sft);
-            const int vb = rshr(sq + 2 * (256 * acc[cb][2] + acc[cb][3]), sft);
-            if (b) {
-              I1[cb][0] += va;
-              I1[cb][1] += vb;
-            } else {
-              I0[cb][0] += va;
-              I0[cb][1] += vb;
+        for (int cb = 0; cb < NCB; ++cb) {
+          const int t = cb * 4 + q;
+          if (t < p.k) {
+            const int gi = b * gk + Gl * p.k + t;
+            const int ex = ue[gi];
+            if (ex != UE_NONE) {
+              const int sft = ex - sh.u_ec[b][t];
+              const int sq = usq[gi];
+              const int va = rshr(sq + 2 * (256 * acc[cb][0] + acc[cb][1]), sft);
+              const int vb = rshr(sq + 2 * (256 * acc[cb][2] + acc[cb][3]), sft);
+              if (b) {
+                I1[cb][0] += va;
+                I1[cb][1] += vb;
+              } else {
+                I0[cb][0] += va;
+                I0[cb][1] += vb;
+              }
             }
           }
         }
@@ -1046,6 +1148,9 @@ static int sm_count() {
   return n;
 }
 
+#ifndef LBX_U_GROUPS
+#define LBX_U_GROUPS 136  // quantisation groups per U-stage CTA at most (measured on 7B- and 70B-shaped calls)
+#endif
 #ifndef LBX_U_MIN_CTAS
 #define LBX_U_MIN_CTAS 60  // U-stage CTAs to aim for when choosing tiles per CTA (measured: 4 tiles per CTA beat 2 and 8 at C2)
 #endif
@@ -1176,7 +1281,7 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
   up.ncols = ncols;
   up.ydt = a->y_dtype;
   up.epi = a->epilogue;
-  int maxw[2] = {0, 0}, maxtile = 0, tiles = 0, ugm = 1;
+  int maxw[2] = {0, 0}, maxtile = 0, tiles = 0, ugm = 1, ngt_max = 1;
   for (int i = 0; i < n_proj; ++i) {
     const lbx_proj &pr = projs[i];
     USeg &sg = up.seg[i];
@@ -1203,6 +1308,9 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
     }
     maxtile = std::max(maxtile, tw);
     tiles += pr.out_features / 16;
+    int ng = 0;  // quantisation groups of one output tile (both branches)
+    for (int b = 0; b < pr.n_branches; ++b) ng += (sg.words[b] + 3) / 4;
+    ngt_max = std::max(ngt_max, ng);
   }
   up.act_words[0] = maxw[0];
   up.act_words[1] = maxw[1];
@@ -1210,8 +1318,12 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
   up.wtile_words = (maxtile + 3) & ~3;
   // row tiles per CTA: enough CTAs to cover the SMs, within shared memory; the
   // remaining warps of a CTA split the ranks of its tiles
+  // row tiles per CTA: at least LBX_U_MIN_CTAS CTAs, and no more than
+  // LBX_U_GROUPS quantisation groups per CTA (heavy tiles spread over more
+  // SMs), but not beyond two CTAs per SM
   int ut = UT_MAX;
-  while (ut > 1 && tiles / ut < LBX_U_MIN_CTAS) ut >>= 1;
+  while (ut > 1 && (tiles / ut < LBX_U_MIN_CTAS || ut * ngt_max > LBX_U_GROUPS)) ut >>= 1;
+  while (ut < UT_MAX && tiles / ut > 2 * sm_count()) ut <<= 1;
   const size_t u_s = al256((size_t)(maxw[0] + maxw[1]) * act_ws(ncols) * 4 + (size_t)4 * ugm * k * 4 +
                            (size_t)UWARPS * 32 * 8 * ncb * 4);
   for (; ut >= 1; ut >>= 1) {
