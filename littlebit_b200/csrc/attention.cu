@@ -30,11 +30,12 @@ namespace lbx {
 
 constexpr int ACH = 64;        // keys per chunk
 constexpr int ATHREADS = 128;
-constexpr int AMAX_ROWS = 64;  // query rows (tokens x GQA group) per CTA; more rows -> more CTAs
+constexpr int AMAX_ROWS = 64;  // query rows (tokens x GQA group) per CTA at most; more rows -> more CTAs
 constexpr int ATK_GROUPS = 64; // ticket slots per kv head (row groups of one launch)
 
 struct AttnParams {
   int n, heads, kvh, d, max_seq, prefix, rep, R, nchunk, ngroups;
+  int rows;  // query rows per unit (row group), <= AMAX_ROWS
   const int32_t *prefix_dev;  // actual cached-slot count (prefix is then a bound)
   float scale, theta;
   const float *q; int64_t q_ld;
@@ -79,9 +80,9 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
   const int c = unit % p.nchunk;
   const int h = (unit / p.nchunk) % p.kvh;
   const int g = unit / (p.nchunk * p.kvh);
-  const int rlo = g * AMAX_ROWS;                // this unit's query rows: rlo .. rlo+Rg-1
-  const int Rg = min(AMAX_ROWS, p.R - rlo);
-  const int Rcap = min(AMAX_ROWS, p.R);
+  const int rlo = g * p.rows;                   // this unit's query rows: rlo .. rlo+Rg-1
+  const int Rg = min(p.rows, p.R - rlo);
+  const int Rcap = p.rows;
   const int tid = threadIdx.x, nthr = blockDim.x;
   float *Ka = sm;                               // (ACH + n) x KP: cached rows 0..63, new tokens 64..
   float *Va = Ka + (ACH + p.n) * KP;            // (ACH + n) x d
@@ -130,24 +131,37 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
     Qs[r * KP + j + half] = x2 * cs.x + x1 * cs.y;
   }
   // cached keys / values of ranks r0.. (rank == slot below the prefix): four
-  // bf16 per 8-byte load (head_dim % 4 == 0), several loads in flight
+  // bf16 per 8-byte load (head_dim % 4 == 0); a batch of KB loads of each is
+  // issued before any is stored (one memory round trip for the whole chunk
+  // at head_dim 128 and 128 threads)
   const int64_t cache_base = (int64_t)h * p.max_seq * d;
   const int d4 = d / 4;
-#pragma unroll 4
-  for (int e = tid; e < ACH * d4; e += nthr) {
-    const int jj = e / d4, j4 = e - jj * d4;
-    const int slot = r0 + jj;
-    uint2 kq = make_uint2(0u, 0u), vq = make_uint2(0u, 0u);
-    if (slot < prefix) {
-      kq = *reinterpret_cast<const uint2 *>(p.kc + cache_base + (int64_t)slot * d + 4 * j4);
-      vq = *reinterpret_cast<const uint2 *>(p.vc + cache_base + (int64_t)slot * d + 4 * j4);
+  constexpr int KB = 16;
+  for (int e0 = tid; e0 < ACH * d4; e0 += KB * nthr) {
+    uint2 kq[KB], vq[KB];
+#pragma unroll
+    for (int u = 0; u < KB; ++u) {
+      const int e = e0 + u * nthr;
+      const int jj = e / d4, j4 = e - jj * d4;
+      const int slot = r0 + jj;
+      kq[u] = vq[u] = make_uint2(0u, 0u);
+      if (e < ACH * d4 && slot < prefix) {
+        kq[u] = __ldg(reinterpret_cast<const uint2 *>(p.kc + cache_base + (int64_t)slot * d + 4 * j4));
+        vq[u] = __ldg(reinterpret_cast<const uint2 *>(p.vc + cache_base + (int64_t)slot * d + 4 * j4));
+      }
     }
-    *reinterpret_cast<float4 *>(Ka + jj * KP + 4 * j4) =
-        make_float4(__uint_as_float(kq.x << 16), __uint_as_float(kq.x & 0xFFFF0000u),
-                    __uint_as_float(kq.y << 16), __uint_as_float(kq.y & 0xFFFF0000u));
-    *reinterpret_cast<float4 *>(Va + jj * d + 4 * j4) =
-        make_float4(__uint_as_float(vq.x << 16), __uint_as_float(vq.x & 0xFFFF0000u),
-                    __uint_as_float(vq.y << 16), __uint_as_float(vq.y & 0xFFFF0000u));
+#pragma unroll
+    for (int u = 0; u < KB; ++u) {
+      const int e = e0 + u * nthr;
+      if (e >= ACH * d4) break;
+      const int jj = e / d4, j4 = e - jj * d4;
+      *reinterpret_cast<float4 *>(Ka + jj * KP + 4 * j4) =
+          make_float4(__uint_as_float(kq[u].x << 16), __uint_as_float(kq[u].x & 0xFFFF0000u),
+                      __uint_as_float(kq[u].y << 16), __uint_as_float(kq[u].y & 0xFFFF0000u));
+      *reinterpret_cast<float4 *>(Va + jj * d + 4 * j4) =
+          make_float4(__uint_as_float(vq[u].x << 16), __uint_as_float(vq[u].x & 0xFFFF0000u),
+                      __uint_as_float(vq[u].y << 16), __uint_as_float(vq[u].y & 0xFFFF0000u));
+    }
   }
   // the new tokens: rotate, round to bf16; the unit whose slot range holds
   // cache slot prefix+i writes it
@@ -242,7 +256,69 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
   unsigned *tk = p.ticket + h * ATK_GROUPS + g;
   if (tid == 0) s_last = atomicAdd(tk, 1u) == (unsigned)(nlive - 1);
   __syncthreads();
-  if (s_last) {
+  // (identical arithmetic in both forms: M = max of the chunk maxima, then
+  // in chunk order over the chunks with keys w = exp(m - M), L += w*l,
+  // O += w*o, out = O / L)
+  // staged merge for long sequences (more than 16 chunks: the per-output
+  // form below then needs 6 or more L2 round trips per output), when its
+  // tables fit in Ka/Va
+  const bool staged = nlive > 16 && 2 * Rg * nlive + Rg <= (ACH + p.n) * (KP + d);
+  if (s_last && staged) {
+    __threadfence();
+    // per (row, chunk) (m, l) into shared memory, all loads in flight; per
+    // row M, the weights (-1: a chunk without keys) and L; then each output
+    // loads its chunks' partial sums a batch at a time
+    float *wsm = Ka;                     // [Rg][nlive]: m, then w
+    float *lsm = Ka + Rg * nlive;        // [Rg][nlive]: l
+    float *Lsm = lsm + Rg * nlive;       // [Rg]
+#pragma unroll 4
+    for (int i = tid; i < Rg * nlive; i += nthr) {
+      const int r = i / nlive, c = i - r * nlive;
+      const float2 ml = __ldcg(p.part_ml + ((int64_t)h * p.nchunk + c) * p.R + rlo + r);
+      wsm[i] = ml.x;
+      lsm[i] = ml.y;
+    }
+    __syncthreads();
+    for (int r = tid; r < Rg; r += nthr) {
+      float M = -INFINITY;
+      for (int c = 0; c < nlive; ++c) M = fmaxf(M, wsm[r * nlive + c]);
+      float L = 0.f;
+      for (int c = 0; c < nlive; ++c) {
+        const float m = wsm[r * nlive + c];
+        float w = -1.f;
+        if (m != -INFINITY) {
+          w = expf(m - M);
+          L = fmaf(w, lsm[r * nlive + c], L);
+        }
+        wsm[r * nlive + c] = w;
+      }
+      Lsm[r] = L;
+    }
+    __syncthreads();
+    constexpr int CB = 16;  // chunks whose partial sums one thread loads together
+    for (int e = tid; e < Rg * d; e += nthr) {
+      const int r = e / d, t = e - r * d;
+      const float *wr = wsm + r * nlive;
+      float O = 0.f;
+      for (int c0 = 0; c0 < nlive; c0 += CB) {
+        float ov[CB];
+#pragma unroll
+        for (int u = 0; u < CB; ++u) {
+          ov[u] = 0.f;
+          if (c0 + u < nlive && wr[c0 + u] >= 0.f)
+            ov[u] = __ldcg(p.part_o + (((int64_t)h * p.nchunk + c0 + u) * p.R + rlo + r) * d + t);
+        }
+#pragma unroll
+        for (int u = 0; u < CB; ++u)
+          if (c0 + u < nlive && wr[c0 + u] >= 0.f) O = fmaf(wr[c0 + u], ov[u], O);
+      }
+      const float L = Lsm[r];
+      const int gr = rlo + r;
+      const int i = gr / p.rep, qh = h * p.rep + (gr - i * p.rep);
+      p.out[(int64_t)i * p.heads * d + (int64_t)qh * d + t] = L > 0.f ? O / L : 0.f;
+    }
+    if (tid == 0) *tk = 0u;  // ready for the next launch
+  } else if (s_last) {  // per output, the partials straight from L2
     __threadfence();
     constexpr int MB = 8;  // chunks whose partials are loaded together
     for (int e = tid; e < Rg * d; e += nthr) {
@@ -295,6 +371,16 @@ __global__ void __launch_bounds__(ATHREADS) attn_kernel(const __grid_constant__ 
   attn_unit(p, blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z), sm);
 }
 
+static int attn_sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  }
+  return n;
+}
+
 static void attn_fill(const lbx_attn_args *a, AttnParams &p) {
   p.n = a->n;
   p.heads = a->heads;
@@ -305,7 +391,16 @@ static void attn_fill(const lbx_attn_args *a, AttnParams &p) {
   p.rep = a->heads / a->kv_heads;
   p.R = a->n * p.rep;
   p.nchunk = (a->prefix_len + a->n + ACH - 1) / ACH;
-  p.ngroups = (p.R + AMAX_ROWS - 1) / AMAX_ROWS;
+  // query rows per unit: a kv head's whole GQA group (and tokens) up to
+  // AMAX_ROWS, halved while the units would not cover the SMs twice (the
+  // rows of one unit are scored one after another; each row's arithmetic is
+  // the same whichever unit holds it)
+  int rows = p.R < AMAX_ROWS ? p.R : AMAX_ROWS;
+  while (rows > 1 && (int64_t)p.nchunk * p.kvh * ((p.R + rows - 1) / rows) < 2 * attn_sm_count() &&
+         (p.R + (rows + 1) / 2 - 1) / ((rows + 1) / 2) <= ATK_GROUPS)
+    rows = (rows + 1) / 2;
+  p.rows = rows;
+  p.ngroups = (p.R + rows - 1) / rows;
   p.scale = a->scale;
   p.theta = a->theta;
   p.q = a->q;
@@ -374,7 +469,7 @@ static int attn_prep(const lbx_attn_args *a, void *partials, unsigned *tickets, 
   p.part_o = reinterpret_cast<float *>(partials);
   p.part_ml = reinterpret_cast<float2 *>(reinterpret_cast<uint8_t *>(partials) + ml);
   p.ticket = tickets;
-  const int Rcap = p.R < AMAX_ROWS ? p.R : AMAX_ROWS;
+  const int Rcap = p.rows;
   const int KP = p.d + 4;
   smem = ((size_t)(ACH + p.n) * KP + (size_t)(ACH + p.n) * p.d + (size_t)Rcap * KP + (size_t)Rcap * ACH) * 4 +
          (size_t)Rcap * ACH * 2 + (size_t)p.n * 64;

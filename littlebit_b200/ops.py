@@ -415,8 +415,11 @@ def lmhead_argmax(x: torch.Tensor, weight: torch.Tensor, norm_w: Optional[torch.
 def attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, pos: torch.Tensor,
               k_cache: torch.Tensor, v_cache: torch.Tensor, prefix_len: int, heads: int,
               kv_heads: int, head_dim: int, scale: float, theta: float,
-              tree_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Attention for n new tokens (RoPE + bf16 KV write + causal/tree mask)."""
+              tree_mask: Optional[torch.Tensor] = None,
+              rope_cs: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Attention for n new tokens (RoPE + bf16 KV write + causal/tree mask).
+    ``rope_cs``: the (cos, sin) table of ``pos`` from :func:`rope_table` (the
+    kernel evaluates the same values itself when it is None)."""
     for nm, t in (("q", q), ("k_new", k_new), ("v_new", v_new), ("k_cache", k_cache),
                   ("v_cache", v_cache)):
         _cuda(nm, t)
@@ -437,11 +440,28 @@ def attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, pos: to
         tm = tree_mask.to(device=q.device, dtype=torch.int64).contiguous()
     a.tree_mask = _p(tm)
     a.k_cache, a.v_cache = _p(k_cache), _p(v_cache)
+    if rope_cs is not None:
+        _cuda("rope_cs", rope_cs)
+        if rope_cs.dtype != torch.float32 or rope_cs.numel() != n * head_dim or not rope_cs.is_contiguous():
+            raise RuntimeError("rope_cs must be a contiguous float32 [n, head_dim] table from rope_table")
+        a.rope_cs = _p(rope_cs)
     out = torch.empty(n, heads * head_dim, dtype=torch.float32, device=q.device)
     a.out = _p(out)
     ws = workspace(q.device, "attn").get(int(lib().lbx_attn_workspace_size(ctypes.byref(a))))
     L.check(lib().lbx_attn_decode(ctypes.byref(a), _p(ws), ws.numel(), _stream(q.device)),
             "attention")
+    return out
+
+
+def rope_table(pos: torch.Tensor, head_dim: int, theta: float) -> torch.Tensor:
+    """(cos, sin) of pos[i] * theta^(-2j/head_dim) for j < head_dim/2 as a float32
+    [n, head_dim] table (pairs), for :func:`attention`'s ``rope_cs``."""
+    _cuda("pos", pos)
+    p32 = pos.to(dtype=torch.int32).contiguous()
+    n = p32.numel()
+    out = torch.empty(n, head_dim, dtype=torch.float32, device=pos.device)
+    L.check(lib().lbx_rope_table(_p(p32), n, head_dim, float(theta), _p(out), _stream(pos.device)),
+            "rope_table")
     return out
 
 
