@@ -781,7 +781,7 @@ def main():
                     help="also time the reference's GPU path (bf16 dense GEMMs) on the same layer")
     ap.add_argument("--prompt", type=int, default=128)
     ap.add_argument("--new-tokens", type=int, default=256)
-    ap.add_argument("--res-scale", type=float, default=0.08)
+    ap.add_argument("--res-scale", type=float, default=0.02)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
