@@ -80,6 +80,7 @@ struct VParams {
   const void *x2;
   const float *norm_w;
   int s_bytes;           // shared-memory scratch region of a standalone launch (weights follow)
+  int split;             // pass-split launch: one staging pass per CTA, a cluster per unit
 };
 
 struct USeg {
@@ -370,12 +371,14 @@ __host__ __device__ inline int pm_of(int prologue) {
 }
 
 template <int PM, class OnFirst>
+// vcap_arg >= 0: columns below it read v2 / norm_w from sv2 / snw (the
+// pass-split kernel passes shared-memory copies of its own pass)
 LBX_DEV void vstage_stage(const VParams &p, const float *v2, const float *sv2, const float *snw,
-                          int pass, uint32_t *act, LinShm &sh, OnFirst &&on_first) {
+                          int pass, uint32_t *act, LinShm &sh, OnFirst &&on_first, int vcap_arg = -1) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool rms = p.prologue == LBX_PRO_RMSNORM;
   const int ws = act_ws(p.ncols);
-  const int vcap = p.vcap;
+  const int vcap = vcap_arg >= 0 ? vcap_arg : p.vcap;
   const int Wd = tid >> 2, qq = tid & 3;
   const int hh = qq >> 1;
   const bool low = (qq & 1) == 0;  // my digits are bytes 0,1 (else 2,3) of the slot words
@@ -553,10 +556,13 @@ LBX_DEV bool vstage_run(const VParams &p, int unit, uint8_t *W, uint8_t *S, LinS
           for (int cb = 0; cb < NCB; ++cb) {
             const int t = cb * 4 + q;
             if (t < p.k) {
+              // each pass's product is rounded on its own before it joins the
+              // running sum (no fused multiply-add), so a sum of the per-pass
+              // partials in pass order (the pass-split kernel) gives these bits
               const int sq = sh.v_sq[warp][t];
               const float inv = sh.v_inv[warp][t];
-              tacc[tl][cb][0] += __int2float_rn(sq + 2 * (256 * acc[cb][0] + acc[cb][1])) * inv;
-              tacc[tl][cb][1] += __int2float_rn(sq + 2 * (256 * acc[cb][2] + acc[cb][3])) * inv;
+              tacc[tl][cb][0] += __fmul_rn(__int2float_rn(sq + 2 * (256 * acc[cb][0] + acc[cb][1])), inv);
+              tacc[tl][cb][1] += __fmul_rn(__int2float_rn(sq + 2 * (256 * acc[cb][2] + acc[cb][3])), inv);
             }
           }
         }
@@ -1018,6 +1024,226 @@ __global__ void __launch_bounds__(UTHREADS, 2) ustage_kernel(const __grid_consta
 #include "slice.cuh"
 
 // ---------------------------------------------------------------------------
+// Pass-split V-stage for inputs wider than one staging pass (K > 4096): the
+// passes of a unit run side by side in the CTAs of one thread-block cluster,
+// CTA rank r staging and contracting pass r with its own slice of the sign
+// rows, v2 and norm_w.  Rank 0 then adds the per-warp partial sums of every
+// rank over distributed shared memory, in the one-CTA order (for each warp
+// the passes in order from 0, then the warps in order), so z and the tile
+// maxima are the bits vstage_run computes with all passes in one CTA.  The
+// unit's latency becomes one pass instead of ceil(K / 4096).
+// ---------------------------------------------------------------------------
+constexpr int VSP_PITCH = PASS_WORDS + 4;  // row pitch (words) of a pass's sign rows
+constexpr int VSP_COLS = PASS_WORDS * 32;  // columns of one pass
+
+struct VSplitLayout {
+  uint32_t *wbuf;  // 16 vt x VSP_PITCH sign words of this pass
+  float *sv2;      // v2 of this pass's columns
+  float *snw;      // norm_w of this pass's columns (RMSNorm prologue)
+  float *smid;     // 2 x 16 vt
+  uint32_t *act;   // PASS_WORDS x ws
+  float *red;      // VWARPS x 16 x k: this rank's per-warp partial sums of one tile
+  float *twa;      // VWARPS x 16 x k: rank 0, per-warp sums over the ranks
+  float *ssqa;     // VWARPS x LBX_MAX_TOKENS: rank 0, per-warp sums of squares over the ranks
+};
+
+LBX_DEV VSplitLayout vsplit_layout(const VParams &p, uint8_t *W, uint8_t *S) {
+  VSplitLayout L;
+  const bool rms = p.prologue == LBX_PRO_RMSNORM;
+  L.wbuf = reinterpret_cast<uint32_t *>(W);
+  L.sv2 = reinterpret_cast<float *>(L.wbuf + 16 * p.vt * VSP_PITCH);
+  L.snw = L.sv2 + VSP_COLS;
+  L.smid = L.snw + (rms ? VSP_COLS : 0);
+  L.act = reinterpret_cast<uint32_t *>(S);
+  L.red = reinterpret_cast<float *>(L.act + PASS_WORDS * act_ws(p.ncols));
+  L.twa = L.red + VWARPS * 16 * p.k;
+  L.ssqa = L.twa + VWARPS * 16 * p.k;
+  return L;
+}
+
+// the weights of pass `pass` of unit `unit` (independent of the activations)
+LBX_DEV void vsplit_issue(const VParams &p, int unit, int pass, uint8_t *W, LinShm &sh) {
+  const int tid = threadIdx.x;
+  const VSeg &sg = p.seg[vseg_of(p, unit)];
+  const int row0 = (unit - sg.unit0) * 16 * p.vt;
+  const int rows = min(16 * p.vt, sg.rank - row0);
+  const bool rms = p.prologue == LBX_PRO_RMSNORM;
+  const int pw0 = pass * PASS_WORDS;
+  const int pwords = min(PASS_WORDS, p.Wv - pw0);
+  const int c0 = pw0 * 32, ncols = pwords * 32;
+  const VSplitLayout L = vsplit_layout(p, W, nullptr);
+  uint64_t *bar = &sh.bar[UT_MAX];
+  if (tid == 0) {
+    const uint32_t bytes = (uint32_t)rows * pwords * 4u + (uint32_t)ncols * 4u * (rms ? 2u : 1u) +
+                           (uint32_t)rows * 4u * (sg.mid1 ? 2u : 1u);
+    mbar_arrive_expect_tx(bar, bytes);
+  }
+  __syncthreads();
+  if (tid < rows)
+    bulk_g2s(L.wbuf + tid * VSP_PITCH, sg.v_sign + (int64_t)(row0 + tid) * p.Wv + pw0, (uint32_t)pwords * 4u, bar);
+  else if (tid == VTHREADS - 1)
+    bulk_g2s(L.sv2, sg.v2 + c0, (uint32_t)ncols * 4u, bar);
+  else if (tid == VTHREADS - 2 && rms)
+    bulk_g2s(L.snw, p.norm_w + c0, (uint32_t)ncols * 4u, bar);
+  else if (tid == VTHREADS - 3)
+    bulk_g2s(L.smid, sg.mid0 + row0, (uint32_t)rows * 4u, bar);
+  else if (tid == VTHREADS - 4 && sg.mid1)
+    bulk_g2s(L.smid + 16 * p.vt, sg.mid1 + row0, (uint32_t)rows * 4u, bar);
+}
+
+template <int NCB, int PM, int VT>
+LBX_DEV void vsplit_run(const VParams &p, int unit, int pass, int npass, uint8_t *W, uint8_t *S, LinShm &sh) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const VSeg &sg = p.seg[vseg_of(p, unit)];
+  const int row0 = (unit - sg.unit0) * 16 * VT;
+  const int ntl = min(VT, (sg.rank - row0 + 15) / 16);
+  const bool rms = p.prologue == LBX_PRO_RMSNORM;
+  const int ws = act_ws(p.ncols);
+  const VSplitLayout L = vsplit_layout(p, W, S);
+  const int pw0 = pass * PASS_WORDS;
+  const int pwords = min(PASS_WORDS, p.Wv - pw0);
+  const int c0 = pw0 * 32;
+  const uint32_t par = sh.par[UT_MAX];
+
+  float tacc[VT][NCB][2];
+#pragma unroll
+  for (int tl = 0; tl < VT; ++tl)
+#pragma unroll
+    for (int cb = 0; cb < NCB; ++cb) tacc[tl][cb][0] = tacc[tl][cb][1] = 0.f;
+  bool ok = true;
+  // v2 / norm_w of this pass are in shared memory: index them by column
+  vstage_stage<PM>(p, sg.v2, L.sv2 - c0, L.snw - c0, pass, L.act, sh, [&] {
+    ok = __syncthreads_and(mbar_wait_bounded(&sh.bar[UT_MAX], par, 0x111));
+  }, c0 + VSP_COLS);
+  __syncthreads();
+  if (tid == 0) sh.par[UT_MAX] = par ^ 1u;
+  if (ok && BLK_WORDS * warp < pwords) {
+    const int wb = BLK_WORDS * warp;
+    const int ng = min(BLK_WORDS, pwords - wb) / 4;
+#pragma unroll
+    for (int tl = 0; tl < VT; ++tl) {
+      if (tl < ntl) {
+        int acc[NCB][4];
+#pragma unroll
+        for (int cb = 0; cb < NCB; ++cb) acc[cb][0] = acc[cb][1] = acc[cb][2] = acc[cb][3] = 0;
+        const uint32_t *wt = L.wbuf + tl * 16 * VSP_PITCH + wb;
+        sign_mma<NCB>(acc, wt + g * VSP_PITCH, wt + (g + 8) * VSP_PITCH, L.act + wb * ws, ws, p.ncols, 0, ng,
+                      lane);
+#pragma unroll
+        for (int cb = 0; cb < NCB; ++cb) {
+          const int t = cb * 4 + q;
+          if (t < p.k) {
+            const int sq = sh.v_sq[warp][t];
+            const float inv = sh.v_inv[warp][t];
+            tacc[tl][cb][0] += __fmul_rn(__int2float_rn(sq + 2 * (256 * acc[cb][0] + acc[cb][1])), inv);
+            tacc[tl][cb][1] += __fmul_rn(__int2float_rn(sq + 2 * (256 * acc[cb][2] + acc[cb][3])), inv);
+          }
+        }
+      }
+    }
+  }
+  // ---- per tile: rank 0 adds the ranks' partials in the one-CTA order.  Every
+  // rank takes both cluster barriers of every tile, whatever its status.
+  const float *smid = L.smid;
+#pragma unroll
+  for (int tl = 0; tl < VT; ++tl) {
+    if (tl >= ntl) break;  // uniform across the cluster
+    const int trow = row0 + tl * 16;
+    const int rows = min(16, sg.rank - trow);
+    float *rw = L.red + warp * 16 * p.k;
+#pragma unroll
+    for (int cb = 0; cb < NCB; ++cb) {
+      const int t = cb * 4 + q;
+      if (t < p.k) {
+        rw[g * p.k + t] = tacc[tl][cb][0];
+        rw[(g + 8) * p.k + t] = tacc[tl][cb][1];
+      }
+    }
+    cl_arrive();
+    cl_wait();  // every rank's partials (and sums of squares) are written
+    if (pass == 0) {
+      const int nk = rows * p.k;
+      for (int i = tid; i < VWARPS * nk; i += VTHREADS) {
+        const int w = i / nk, rem = i - w * nk;
+        const int rr = rem / p.k, t = rem - rr * p.k;
+        const float *src = L.red + (w * 16 + rr) * p.k + t;
+        float v[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) v[r] = r < npass ? *cl_map(src, r) : 0.f;
+        float tw = 0.f;
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+          if (r < npass) tw += v[r];
+        L.twa[(w * 16 + rr) * p.k + t] = tw;
+      }
+      if (rms && tl == 0) {
+        for (int i = tid; i < VWARPS * p.k; i += VTHREADS) {
+          const int w = i / p.k, t = i - w * p.k;
+          const float *src = &sh.v_ssq[w][t];
+          float v[8];
+#pragma unroll
+          for (int r = 0; r < 8; ++r) v[r] = r < npass ? *cl_map(src, r) : 0.f;
+          float sw = 0.f;
+#pragma unroll
+          for (int r = 0; r < 8; ++r)
+            if (r < npass) sw += v[r];
+          L.ssqa[w * LBX_MAX_TOKENS + t] = sw;
+        }
+      }
+      __syncthreads();
+      for (int i = tid; i < nk; i += VTHREADS) {
+        const int rr = i / p.k, t = i - rr * p.k;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < VWARPS; ++w) v += L.twa[(w * 16 + rr) * p.k + t];
+        if (rms) {
+          float s2 = 0.f;
+#pragma unroll
+          for (int w = 0; w < VWARPS; ++w) s2 += L.ssqa[w * LBX_MAX_TOKENS + t];
+          v *= rsqrtf(s2 / (float)p.K + p.eps);
+        }
+        const float z0 = smid[tl * 16 + rr] * v;
+        sg.z0[(int64_t)t * sg.rank + trow + rr] = z0;
+        atomicMax(&sh.v_zmax[0][t], __float_as_int(fabsf(z0)));
+        if (sg.z1) {
+          const float z1 = smid[16 * VT + tl * 16 + rr] * v;
+          sg.z1[(int64_t)t * sg.rank + trow + rr] = z1;
+          atomicMax(&sh.v_zmax[1][t], __float_as_int(fabsf(z1)));
+        }
+      }
+      __syncthreads();
+      if (tid < p.k) {
+        int *tm = sg.tmax + (int64_t)(trow / 16) * 2 * p.k;
+        tm[tid] = sh.v_zmax[0][tid];
+        if (sg.z1) tm[p.k + tid] = sh.v_zmax[1][tid];
+        sh.v_zmax[0][tid] = sh.v_zmax[1][tid] = 0;
+      }
+    }
+    cl_arrive();
+    cl_wait();  // rank 0 has read every rank's partials: they may be overwritten, or the CTAs leave
+  }
+}
+
+template <int NCB, int PM, int VT>
+__global__ void __launch_bounds__(VTHREADS, 2) vsplit_kernel(const __grid_constant__ VParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ LinShm sh;
+  const int npass = (p.Wv + PASS_WORDS - 1) / PASS_WORDS;
+  const int pass = cl_rank();  // clusters of npass CTAs along x
+  const int unit = blockIdx.x / npass;
+  if (threadIdx.x < VWARPS * LBX_MAX_TOKENS) (&sh.v_ssq[0][0])[threadIdx.x] = 0.f;
+  if (threadIdx.x < 2 * LBX_MAX_TOKENS) (&sh.v_zmax[0][0])[threadIdx.x] = 0;
+  linshm_init(sh);  // (ends with a CTA barrier)
+  uint8_t *S = smem_raw;
+  uint8_t *W = smem_raw + p.s_bytes;
+  vsplit_issue(p, unit, pass, W, sh);
+  pdl_trigger();
+  pdl_wait();
+  vsplit_run<NCB, PM, VT>(p, unit, pass, npass, W, S, sh);
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 constexpr size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -1137,6 +1363,19 @@ static VKern vstage_for_vt(int ncb, int pm) {
 static VKern vstage_for(int ncb, int pm, int vt) {
   return vt == 2 ? vstage_for_vt<2>(ncb, pm) : vstage_for_vt<1>(ncb, pm);
 }
+template <int PM, int VT>
+static VKern vsplit_for_pv(int ncb) {
+  return ncb == 1 ? vsplit_kernel<1, PM, VT> : ncb == 2 ? vsplit_kernel<2, PM, VT> : vsplit_kernel<4, PM, VT>;
+}
+template <int VT>
+static VKern vsplit_for_vt(int ncb, int pm) {
+  return pm == PM_SILU ? vsplit_for_pv<PM_SILU, VT>(ncb)
+         : pm == PM_MUL ? vsplit_for_pv<PM_MUL, VT>(ncb)
+                        : vsplit_for_pv<PM_X, VT>(ncb);
+}
+static VKern vsplit_for(int ncb, int pm, int vt) {
+  return vt == 2 ? vsplit_for_vt<2>(ncb, pm) : vsplit_for_vt<1>(ncb, pm);
+}
 
 static int sm_count() {
   static int n = 0;
@@ -1161,11 +1400,14 @@ static int stage_smem_limits(size_t &vmax, size_t &umax) {
   static size_t v_ = 0, u_ = 0;
   if (!v_) {
     size_t m = 0, vv = (size_t)-1, uu = (size_t)-1;
-    VKern all[18];
+    VKern all[36];
     int na = 0;
     for (int vt = 1; vt <= 2; ++vt)
       for (int pm = 0; pm < 3; ++pm)
-        for (int ncb : {1, 2, 4}) all[na++] = vstage_for(ncb, pm, vt);
+        for (int ncb : {1, 2, 4}) {
+          all[na++] = vstage_for(ncb, pm, vt);
+          all[na++] = vsplit_for(ncb, pm, vt);
+        }
     for (VKern kk : all) {
       cudaError_t e = allow_max_smem(kk, &m);
       if (e != cudaSuccess) return cuda_status(e, "vstage smem attribute");
@@ -1555,6 +1797,10 @@ static bool prep_slice(const lbx_proj *projs, const lbx_linear_args *a, int k, c
   return true;
 }
 
+#ifndef LBX_V_SPLIT
+#define LBX_V_SPLIT 1  // 0: every V unit runs all of its staging passes in one CTA
+#endif
+
 static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, int k, void *ws,
                      cudaStream_t stream) {
   size_t vmax = 0, umax = 0;
@@ -1578,10 +1824,53 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
     }
     LBX_CHECK_SUP(false, "this call does not fit the cluster executor: %s", why);
   }
-  auto vk = vstage_for(P.ncb, pm_of(a->prologue), P.vp.vt);
   auto uk = P.ncb == 1 ? ustage_kernel<1> : P.ncb == 2 ? ustage_kernel<2> : ustage_kernel<4>;
-  cudaError_t e = launch(vk, dim3(P.vunits), dim3(VTHREADS), P.v_w + P.v_s, stream, pdl, P.vp);
-  if (e != cudaSuccess) return cuda_status(e, "vstage launch");
+  cudaError_t e;
+  // inputs wider than one staging pass on a small V grid: the pass-split
+  // V-stage (a cluster of one CTA per pass for each unit), when all of its
+  // CTAs fit at two per SM.  Measured: 7B draft down projection 12.5 -> 9.3 us,
+  // 70B draft down 22.7 -> 16.0 us; on grids that already fill the GPU (the 7B
+  // and 70B targets) it was slower, 19.5 -> 24.5 us for the 7B down call.
+  const int npass = (P.vp.Wv + PASS_WORDS - 1) / PASS_WORDS;
+  bool split = false;
+  if (LBX_V_SPLIT && npass > 1 && npass <= 8 && P.vunits * npass <= 2 * sm_count()) {
+    const bool rms = a->prologue == LBX_PRO_RMSNORM;
+    const size_t sw = al256((size_t)16 * P.vp.vt * VSP_PITCH * 4 + (size_t)VSP_COLS * 4 * (rms ? 2 : 1) +
+                            (size_t)32 * P.vp.vt * 4);
+    const size_t ss = al256((size_t)PASS_WORDS * act_ws(P.vp.ncols) * 4 + (size_t)2 * VWARPS * 16 * k * 4 +
+                            (size_t)VWARPS * LBX_MAX_TOKENS * 4);
+    if (sw + ss <= vmax) {
+      VParams vp = P.vp;
+      vp.split = 1;
+      vp.s_bytes = (int)ss;
+      cudaLaunchAttribute attr[2];
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(P.vunits * npass);
+      cfg.blockDim = dim3(VTHREADS);
+      cfg.dynamicSmemBytes = sw + ss;
+      cfg.stream = stream;
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = npass;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      int na = 1;
+      if (pdl) {
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        na = 2;
+      }
+      cfg.attrs = attr;
+      cfg.numAttrs = na;
+      e = cudaLaunchKernelEx(&cfg, vsplit_for(P.ncb, pm_of(a->prologue), P.vp.vt), vp);
+      if (e != cudaSuccess) return cuda_status(e, "pass-split vstage launch");
+      split = true;
+    }
+  }
+  if (!split) {
+    auto vk = vstage_for(P.ncb, pm_of(a->prologue), P.vp.vt);
+    e = launch(vk, dim3(P.vunits), dim3(VTHREADS), P.v_w + P.v_s, stream, pdl, P.vp);
+    if (e != cudaSuccess) return cuda_status(e, "vstage launch");
+  }
   e = launch(uk, dim3(P.uunits), dim3(UTHREADS), P.u_w + P.u_s, stream, pdl, P.up);
   if (e != cudaSuccess) return cuda_status(e, "ustage launch");
   return LBX_OK;

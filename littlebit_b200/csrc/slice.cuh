@@ -251,8 +251,8 @@ __global__ void __launch_bounds__(VTHREADS, LBX_SL_MINBLOCKS) slice_kernel(const
             if (vblk) {  // (a single pass: the V-stage's running sum starts from this value)
               const int sq = sh.v_sq[warp][t];
               const float inv = sh.v_inv[warp][t];
-              v0 += __int2float_rn(sq + 2 * (256 * acc[cb][0] + acc[cb][1])) * inv;
-              v1 += __int2float_rn(sq + 2 * (256 * acc[cb][2] + acc[cb][3])) * inv;
+              v0 += __fmul_rn(__int2float_rn(sq + 2 * (256 * acc[cb][0] + acc[cb][1])), inv);
+              v1 += __fmul_rn(__int2float_rn(sq + 2 * (256 * acc[cb][2] + acc[cb][3])), inv);
             }
             rw[g * k + t] = v0;
             rw[(g + 8) * k + t] = v1;

@@ -412,3 +412,22 @@ def test_large_rank_splits_token_batches_bitwise(ops):
     for i in (0, 7, 8, 15):
         assert torch.equal(ops.lb_linear(lay, x[i:i + 1])[0], y[i]), i
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("k", [1, 5])
+def test_pass_split_v_stage_matches_one_cta_passes(ops, k):
+    """Inputs wider than one 4096-column staging pass (8192 and 11008 columns) run
+    the pass-split V-stage: a cluster of one CTA per pass, rank 0 adding the
+    partial sums in the one-CTA order.  The persistent program runs every unit's
+    passes in one CTA; both give the same bits."""
+    from littlebit_b200 import synthetic
+
+    g = _gen(800 + k)
+    for K, N, ranks in ((8192, 1024, [392, 3664]), (11008, 4096, [280, 2664])):
+        lay = synthetic.to_packed_linear(K, N, synthetic.layer(K, N, ranks, g), DEV)
+        x = torch.randn(k, K, generator=g).to(DEV)
+        y = torch.empty(k, N, device=DEV)
+        ops.linear_group([lay], x, [y], exec_mode=ops.L.LBX_EXEC_KERNELS)
+        acts = [x.clone(), torch.empty(k, N, device=DEV)]
+        ops.linear_chain([lay], acts)
+        assert torch.equal(y.view(torch.int32), acts[1].view(torch.int32)), (K, N)
