@@ -10,12 +10,15 @@
 //   V-stage  CTA = 16 rank rows x all of K, warp = 256-column blocks:
 //            z_b = mid_b ⊙ (V_sign · a) [⊙ rsqrt(mean x^2 + eps) for a fused
 //            RMSNorm],  a = v2 ⊙ prologue(x);  blocks summed in fixed order
+//            (K > 4096 on a small grid: a cluster per unit, one CTA per
+//            4096-column pass, vsplit_kernel; same sums, same order)
 //   U-stage  CTA = ut 16-row output tiles, its 16 warps split tiles x ranks:
 //            y = Σ_b u1_b ⊙ U_b · z_b (+ bias)
 // Both contractions run on the int8 tensor cores:
 //   * activations are quantised to 16-bit integers (two int8 digits); the
-//     V-stage uses one scale per token per 256 columns, the U-stage one per
-//     token per branch, so every Σ_j s_j·q_j inside a scale block is EXACT;
+//     V-stage uses one scale per token per 256 columns, the U-stage a power
+//     of two per token per 128-rank group, so every Σ_j s_j·q_j inside a
+//     scale block is EXACT (U groups are then combined by exact integer shifts);
 //   * a sign word is expanded in registers by one prmt per 4 signs into int8
 //     0/−1 (= −bit), and mma.m16n8k32.s8 gives D = Σ_j (−b_j)·digit_j;
 //   * Σ_j s_j q_j = Σ_j q_j + 2·(256·D_hi + D_lo).
