@@ -128,9 +128,9 @@ int lbx_linear_verify(const lbx_proj *projs, const lbx_linear_args *a, void *ws,
 /* lbx_linear_verify for callers that cannot allocate device memory.  No
  * counterpart in the reference (its CPU op allocated its own scratch): this
  * entry point is for code that must not call cudaMalloc or hand the library a
- * buffer — e.g. work recorded while a CUDA graph is captured in a mode that
- * forbids allocation, or a host application that owns every device
- * allocation.  The scratch is a fixed module-level device array of
+ * buffer — e.g. a host application whose own allocator owns every device
+ * allocation and cannot lend one, or a service that sets up all device
+ * memory at start-up and may not allocate while serving.  The scratch is a fixed module-level device array of
  * lbx_linear_noalloc_max_bytes() bytes (1 MiB) that every GPU loading the
  * library holds until exit; calls needing more scratch than that are rejected
  * with LBX_EUNSUPPORTED.  No cudaMalloc, cudaFree or allocating library

@@ -1932,10 +1932,10 @@ extern "C" int lbx_linear(const lbx_proj *projs, const lbx_linear_args *a, void 
 // ---------------------------------------------------------------------------
 // Allocation-free variant: the scratch lives in a fixed device array
 // ---------------------------------------------------------------------------
-// Some callers cannot hand the library device memory: code that runs while a
-// CUDA graph is being captured in a mode that forbids allocation, a host
-// application that owns every device allocation through its own pool, or a
-// plugin without access to any allocator.  lbx_linear_noalloc runs the same two
+// Some callers cannot hand the library device memory: a host application that
+// owns every device allocation through its own pool, a service that sets up all
+// device memory at start-up and may not allocate while serving, or a plugin
+// without access to any allocator.  lbx_linear_noalloc runs the same two
 // kernels as lbx_linear_verify with its scratch in this module-level array.
 // Device code could name the array directly; host code cannot (there the name
 // is only a host-side stand-in), so its device address is fetched once per

@@ -1,8 +1,8 @@
 """The allocation-free linear entry point (lbx_linear_noalloc).
 
-It exists for callers that cannot give the library device memory (work
-recorded during a CUDA graph capture that forbids allocation, or a host
-application that owns every device allocation).  It keeps its scratch in a
+It exists for callers that cannot give the library device memory (a host
+application whose own allocator owns every device allocation, or a service
+that sets up all device memory at start-up and may not allocate later).  It keeps its scratch in a
 fixed 1 MiB device array instead of a caller workspace.  Its results must
 match the allocating entry point (lbx_linear_verify with a caller workspace)
 within the per-layer tolerance, on consecutive calls that reuse the shared
