@@ -11,9 +11,18 @@ with programmatic dependent launch).
 
 value   = algorithmic bytes of all layers of all ranks / max-over-ranks time
           (packed bits without word padding + fp32 scales + activations in/out)
-e2e     = the same metric through the C-ABI call per layer with pinned HOST
-          x/y: every layer copies its input host->device and its output
-          device->host inside the timed region
+e2e     = the same metric through the C-ABI call itself: every step copies
+          x from pinned host memory to the device, the host calls
+          lbx_linear_verify (ctypes) once per layer of the chain, and the
+          last layer's y is copied back to pinned host memory (8 KB each
+          way per step at k=1); no CUDA graph.  e2e_graph is the same step
+          captured in a CUDA graph.
+configs = the other BASELINE layer configs, each as its own chain: C1 (fp32,
+          r=208), C2 verify at k=5 and k=8, the shared-factor target layer of
+          config 4 (draft r=208 + residual U_R of the same rank on the draft's
+          V-stage) at k=1 and k=5.
+floor   = the same grids with the same PDL chaining and no arithmetic
+          (lbx_linear_floor), without and with the weight copies.
 roofline: the linear (V+U kernel pair) is the dominant kernel; achieved =
           bytes per layer call / mean layer time; peak = MEASURED_PEAKS.json
 cpu_baseline: the reference's own C++ op (oracle/_ref, littlebit_linear from
@@ -46,11 +55,16 @@ IN_F = OUT_F = 4096
 RANKS = [208, 1840]
 
 
-def layer_bytes(k: int) -> tuple[int, int]:
-    """(algorithmic bytes per layer call, packed-weight bytes) for k bf16 tokens."""
-    packed = sum((r * IN_F + 7) // 8 + (OUT_F * r + 7) // 8 for r in RANKS)
-    scales = sum(4 * (IN_F + r + OUT_F) for r in RANKS)
-    act = 2 * k * IN_F + 2 * k * OUT_F
+def layer_bytes(k: int, ranks=RANKS, shared: bool = False, esz: int = 2) -> tuple[int, int]:
+    """(algorithmic bytes per layer call, packed-weight bytes) for k tokens of
+    esz-byte activations: packed bits without word padding, fp32 scales, x read
+    and y written.  A shared-factor residual (config 4) has no V or v2 of its own."""
+    packed, scales = 0, 0
+    for i, r in enumerate(ranks):
+        own_v = not (shared and i > 0)
+        packed += (OUT_F * r + 7) // 8 + ((r * IN_F + 7) // 8 if own_v else 0)
+        scales += 4 * (r + OUT_F) + (4 * IN_F if own_v else 0)
+    act = esz * k * IN_F + esz * k * OUT_F
     return packed + scales + act, packed
 
 
@@ -206,6 +220,121 @@ def cpu_reference(k: int, budget_s: float, nlayers: int):
                       f"{nlayers} distinct layers, k={k}, {threads} threads"}
 
 
+def cpu_decode_reference(r_d: dict, r_r: dict, prompt: int, quick: bool = False):
+    """C3/C4 CPU baselines: the reference's own full_forward, generate_token and
+    full_forward_batch ops (oracle/_ref, compiled from
+    patches/littlebit_cpu_optimized.cpp:1522-2317) on the Llama-2-7B shape with
+    random packed signs in the layout CPUDraftModel builds
+    (cpu_draft_model.py:229-264: 37 tensors and 28 dims per layer, signs
+    repacked by the reference's repack_signs_to_i2), timed the way
+    benchmark_models_cpu.py:31-135 does: warm-up tokens, per-token
+    perf_counter, tokens/s = measured tokens / summed time.
+
+      draft_full_forward   per token dense_gemv_f32 lm_head + argmax +
+                           full_forward (benchmark_draft's loop)
+      draft_generate_token generate_token (Q4_0 lm_head, fused argmax)
+      target_two_model     CPUTargetModel's step: full_forward_batch of the new
+                           token on the draft and the residual model, hidden
+                           sum, fp32 lm_head (benchmark_target's loop)
+      verify_gamma4        the same step over 5 tokens (chain verify, gamma 4)
+
+    The KV caches hold ``prompt`` zero-filled positions standing in for the
+    prompt's prefill: the ops' work per token depends on the position only."""
+    from oracle import build_ref  # CPU baseline only
+
+    if not build_ref.load():
+        return None
+    import torch.nn.functional as F
+
+    from littlebit_b200.model import LLAMA2_7B, PROJ_NAMES
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    threads = torch.get_num_threads()
+    ro = torch.ops.littlebit_cpu_ops
+    sh = LLAMA2_7B
+    H, I, nl, V = sh.hidden_size, sh.intermediate_size, sh.num_hidden_layers, sh.vocab_size
+    kvh, hd = sh.num_key_value_heads, sh.head_dim
+    dims = {"q_proj": (H, H), "k_proj": (H, kvh * hd), "v_proj": (H, kvh * hd), "o_proj": (H, H),
+            "gate_proj": (H, I), "up_proj": (H, I), "down_proj": (I, H)}
+    g = torch.Generator().manual_seed(3)
+
+    def words(rows, cols):
+        w = torch.randint(-(2 ** 31), 2 ** 31, (rows, (cols + 31) // 32), generator=g, dtype=torch.int64)
+        if cols % 32:
+            w[:, -1] &= (1 << (cols % 32)) - 1
+        return w.to(torch.int32)
+
+    sc = lambda n: (1 + 0.1 * torch.randn(n, generator=g)).abs()
+    max_seq = prompt + 32
+    t_build = time.perf_counter()
+
+    def unit(ranks):
+        tens, ld = [], []
+        for _ in range(nl):
+            tens += [sc(H), sc(H)]
+            for nm in PROJ_NAMES:
+                in_f, out_f = dims[nm]
+                r = ranks[nm]
+                tens += [sc(in_f), ro.repack_signs_to_i2(words(r, in_f), in_f), sc(r) / in_f ** 0.5,
+                         ro.repack_signs_to_i2(words(out_f, r), r), sc(out_f) / r ** 0.5]
+                ld += [in_f, r, r, out_f]
+        kv = [torch.zeros(kvh, max_seq, hd) for _ in range(2 * nl)]
+        return tens, ld, kv
+
+    embed = 0.02 * torch.randn(V, H, generator=g)
+    head = 0.02 * torch.randn(V, H, generator=g)
+    fnorm = sc(H)
+    d_t, d_l, d_kv = unit(r_d)
+    q4 = ro.quantize_lm_head_q4(head)
+    common = (nl, H, kvh, sh.num_attention_heads // kvh, hd, max_seq)
+    scale, eps = hd ** -0.5, sh.rms_norm_eps
+
+    def per_token(fn, warm, meas):
+        ts = []
+        for i in range(warm + meas):
+            t0 = time.perf_counter()
+            fn(prompt + i)
+            if i >= warm:
+                ts.append(time.perf_counter() - t0)
+        return {"tokens_per_s": round(len(ts) / sum(ts), 3), "ms_per_token": round(sum(ts) / len(ts) * 1e3, 2),
+                "measured_tokens": len(ts), "warmup_tokens": warm}
+
+    state = {"tok": 1, "h": torch.zeros(1, H)}
+
+    def draft_ff(pos):
+        lg = ro.dense_gemv_f32(state["h"].reshape(1, -1).contiguous(), head)
+        state["tok"] = int(torch.argmax(lg, dim=-1).item())
+        state["h"] = ro.full_forward(state["tok"], embed, fnorm, d_t, d_kv, d_l, *common[:5], max_seq, pos,
+                                     scale, eps)
+
+    def draft_gt(pos):
+        state["tok"] = int(ro.generate_token(state["tok"] % V, embed, fnorm, d_t, d_kv, d_l, q4, V, *common[:5],
+                                             max_seq, pos, scale, eps))
+
+    out = {"threads": threads, "model": "Llama-2-7B shape, 0.1-bit draft ranks " + json.dumps(r_d),
+           "start_position": prompt}
+    out["draft_full_forward"] = per_token(draft_ff, 5, 8 if quick else 20)
+    out["draft_generate_token"] = per_token(draft_gt, 5, 8 if quick else 20)
+    r_t, r_l, r_kv = unit(r_r)
+    out["build_s"] = round(time.perf_counter() - t_build, 1)
+
+    def target_n(n):
+        def fn(pos):
+            ids = torch.full((n,), 1, dtype=torch.int64)
+            hdd = ro.full_forward_batch(ids, embed, fnorm, d_t, d_kv, d_l, *common[:5], max_seq, pos, scale, eps)
+            hr = ro.full_forward_batch(ids, embed, fnorm, r_t, r_kv, r_l, *common[:5], max_seq, pos, scale, eps)
+            lg = F.linear((hdd + hr).to(torch.float32), head)
+            state["tok"] = int(lg[-1].argmax().item())
+        return fn
+
+    out["target_two_model"] = per_token(target_n(1), 2, 3 if quick else 6)
+    out["target_two_model"]["residual_ranks"] = r_r
+    out["verify_gamma4"] = per_token(target_n(5), 1, 2 if quick else 3)
+    out["verify_gamma4"]["note"] = "tokens_per_s counts verify calls of 5 tokens"
+    out["timing"] = "benchmark_models_cpu.py:31-135 method (warm-up, per-token perf_counter); reference ops"
+    return out
+
+
 def run_reference(args):
     """The reference's CPU op on this workload: W warm-up passes, then exactly K
     timed passes over the chain of --pool distinct layers."""
@@ -247,15 +376,17 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
-def build_pool(P: int, device, seed: int):
-    """P distinct C2 layers generated on the device (random words == Bernoulli(0.5) signs)."""
+def build_pool(P: int, device, seed: int, ranks=RANKS, shared: bool = False):
+    """P distinct layers generated on the device (random words == Bernoulli(0.5)
+    signs, |N(1,0.1)| scales); ``shared``: the second branch reuses the first
+    branch's V-stage (littlespec_ref/littlebit_itq_spec.py:298-309)."""
     from littlebit_b200.ops import Branch, PackedLinear
 
     g = torch.Generator(device=device).manual_seed(seed)
     pool = []
     for _ in range(P):
         brs = []
-        for r in RANKS:
+        for i, r in enumerate(ranks):
             def words(rows, cols):
                 w = torch.randint(-(2 ** 31), 2 ** 31, (rows, (cols + 31) // 32), generator=g,
                                   device=device, dtype=torch.int64)
@@ -263,7 +394,10 @@ def build_pool(P: int, device, seed: int):
                     w[:, -1] &= (1 << (cols % 32)) - 1
                 return w.to(torch.int32)
             sc = lambda n: (1 + 0.1 * torch.randn(n, generator=g, device=device)).abs()
-            brs.append(Branch(words(r, IN_F), sc(IN_F), sc(r), words(OUT_F, r), sc(OUT_F), r))
+            if shared and i > 0:
+                brs.append(Branch(None, None, sc(r), words(OUT_F, r), sc(OUT_F), r))
+            else:
+                brs.append(Branch(words(r, IN_F), sc(IN_F), sc(r), words(OUT_F, r), sc(OUT_F), r))
         pool.append(PackedLinear(IN_F, OUT_F, brs))
     return pool
 
@@ -402,6 +536,62 @@ def run_decode(args, dev, rank, ws):
                               "note": "packed words + fp32 scales + bf16 lm_head + bf16 KV at the mean length"}
     out["hbm_frac_per_gpu"] = {"draft_greedy": frac(out["decode_only"]["draft_greedy"], bpt_draft),
                                "target_greedy": frac(out["decode_only"]["target_greedy"], bpt_target)}
+    out["weights"] = ("signs Bernoulli(0.5), scales |N(1,0.1)| times unit-gain constants (mid / sqrt(in), "
+                      f"u1 / sqrt(rank)); residual u1 further x{args.res_scale}")
+    del tgt, drf, draft_only, dec
+    torch.cuda.empty_cache()
+
+    # ---- BASELINE config 4 as stated: the target shares the packed draft
+    # factors (littlespec_ref/littlebit_itq_spec.py:298-309): the residual of
+    # every projection is a rank-matched U_R (own mid_R, u1_R) on the draft's
+    # V-stage, so one V-stage feeds both U and U_R
+    st = synthetic_runtime_state(shape, {k: [r_d[k], r_d[k]] for k in r_d}, seed=177 + rank,
+                                 shared_residual=True, device=dev, unit_gain=True)
+    for kk in list(st):
+        if kk.endswith(".u1_r"):
+            st[kk] = st[kk] * args.res_scale
+    dec_s = LittleBitDecoder(shape, st, device=dev, max_seq=max_seq)
+    del st
+    tgt_s = CudaTargetModel.from_decoder(dec_s)
+    drf_s = CudaDraftModel.from_target(tgt_s)
+    autoregressive_generate(tgt_s, ids, None, max_new_tokens=8, eos_token_id=-1)
+    speculative_decode(drf_s, tgt_s, ids, None, max_new_tokens=8, draft_length=4, eos_token_id=-1)
+    speculative_decode_tree(drf_s, tgt_s, ids, None, max_new_tokens=8, tree_buffers=tb, top_k=2, eos_token_id=-1)
+    (ar_s, _), t_ar_s = timed(lambda: autoregressive_generate(tgt_s, ids, None, max_new_tokens=n, eos_token_id=-1))
+    _, t_ar1_s = timed(lambda: autoregressive_generate(tgt_s, ids, None, max_new_tokens=1, eos_token_id=-1))
+    (sp_s, sst_s), t_sp_s = timed(lambda: speculative_decode(drf_s, tgt_s, ids, None, max_new_tokens=n,
+                                                             draft_length=4, eos_token_id=-1))
+    (tr_s, tst_s), t_tr_s = timed(lambda: speculative_decode_tree(drf_s, tgt_s, ids, None, max_new_tokens=n,
+                                                                  tree_buffers=tb, top_k=2, eos_token_id=-1))
+    n_tr_s = tr_s.shape[1] - ids.shape[1]
+    ar_s_long = ar_s
+    if n_tr_s > n:
+        ar_s_long, _ = autoregressive_generate(tgt_s, ids, None, max_new_tokens=n_tr_s, eos_token_id=-1)
+    ok_c = sp_s.tolist() == ar_s.tolist()
+    ok_t = tr_s.tolist() == ar_s_long[:, :tr_s.shape[1]].tolist()
+    if not (ok_c and ok_t):
+        raise RuntimeError(f"shared-factor speculation differs from target-only greedy (chain {ok_c}, tree {ok_t})")
+    out["c4_shared_target"] = {
+        "workload": "config 4: 0.1-bit draft + rank-matched residual U_R sharing the draft's packed V "
+                    "(one V-stage per projection feeds U and U_R), 7B shape, same prompt and length",
+        "residual_ranks": r_d, "target_packed_mb": round(dec_s.packed_bytes() / 1e6, 1),
+        "target_greedy": round(n * ws / t_ar_s, 2),
+        "target_decode_only": round((n - 1) * ws / (t_ar_s - t_ar1_s), 2),
+        "spec_chain_gamma4": {"tokens_per_s": round(n * ws / t_sp_s, 2),
+                              "acceptance_rate": round(sst_s["acceptance_rate"], 4),
+                              "mean_acceptance_length": round(sst_s["mean_acceptance_length"], 3),
+                              "num_steps": sst_s["num_steps"], "token_identical": ok_c},
+        "spec_tree_d4b2": {"tokens_per_s": round(n_tr_s * ws / t_tr_s, 2),
+                           "acceptance_rate": round(tst_s["acceptance_rate"], 4),
+                           "mean_acceptance_length": round(tst_s["mean_acceptance_length"], 3),
+                           "num_steps": tst_s["num_steps"], "tokens": n_tr_s, "token_identical": ok_t},
+    }
+    del tgt_s, drf_s, dec_s
+    torch.cuda.empty_cache()
+
+    # ---- the reference's CPU decode ops on this box's host cores (rank 0, N=1)
+    if ws == 1 and not args.no_cpu:
+        out["cpu_reference"] = cpu_decode_reference(r_d, r_r, args.prompt)
     return out
 
 
@@ -598,6 +788,120 @@ def run_dense_ref(args, dev, rank, ws, P: int = 64):
             "speedup_of_packed_kernels": None}
 
 
+class Chain:
+    """A chain of distinct layers, x_{i+1} = y_i, with its activation buffers and
+    the prebuilt C-ABI arguments of every layer call."""
+
+    def __init__(self, pool, k: int, dtype, dev, seed: int = 5):
+        from littlebit_b200 import ops
+
+        self.pool, self.k, self.dev = pool, k, dev
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.acts = [torch.randn(k, IN_F, device=dev, generator=g).to(dtype)] + \
+                    [torch.empty(k, OUT_F, device=dev, dtype=dtype) for _ in pool]
+        self.arrs = [ops.projs_array([p]) for p in pool]
+        self.args = [ops.linear_args([pool[i]], self.acts[i], [self.acts[i + 1]]) for i in range(len(pool))]
+        self.ws = torch.zeros(ops.linear_workspace_bytes([pool[0]], k), dtype=torch.uint8, device=dev)
+        self.lib = ops.lib()
+
+    def run(self, exec_mode: int, stream, use_pdl: int = 1):
+        """Every layer through lbx_linear_verify (the C-ABI call), on ``stream``."""
+        from littlebit_b200 import _lib as L
+
+        fn, ws, n, st = self.lib.lbx_linear_verify, self.ws.data_ptr(), self.ws.numel(), stream.cuda_stream
+        for arr, a in zip(self.arrs, self.args):
+            a.exec = exec_mode
+            a.use_pdl = use_pdl
+            rc = fn(arr, ctypes.byref(a), ws, n, st)
+            if rc:
+                L.check(rc, "lbx_linear_verify")
+
+    def floor(self, mode: int, stream):
+        from littlebit_b200 import _lib as L
+
+        for arr, a in zip(self.arrs, self.args):
+            a.use_pdl = 1
+            L.check(self.lib.lbx_linear_floor(arr, ctypes.byref(a), mode, self.ws.data_ptr(), self.ws.numel(),
+                                              stream.cuda_stream), "lbx_linear_floor")
+
+
+def timed_graph(fn, stream, warmup: int, steps: int, ws: int):
+    """Device ms of ``steps`` replays of fn captured in one CUDA graph, after
+    ``warmup`` replays, bracketed by barrier + synchronize; max over ranks."""
+    from littlebit_b200 import ops
+
+    with torch.cuda.stream(stream):
+        fn()  # eager warm-up (kernel attributes, programs)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        fn()
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    ops.clear_device_error()
+    barrier(ws)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(ws)
+    out = max_over_ranks(e0.elapsed_time(e1), ws)
+    del graph
+    return out
+
+
+def roofline_entry(b_layer: int, us: float, peak: float, peak_kind: str, traffic=None) -> dict:
+    gbs = b_layer / (us * 1e-6) / 1e9
+    return {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "unit": "GB/s",
+            "frac": round(gbs / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+            "algorithmic_bytes_per_launch": b_layer, "launch": "one LittleBit layer",
+            "mean_launch_us": round(us, 3)}
+
+
+def run_configs(args, dev, stream, ws, main_pool, peak, peak_kind):
+    """The other BASELINE layer configs, each a chain of distinct layers timed
+    like the headline (CUDA graph of the C-ABI calls, weights streamed from HBM)."""
+    from littlebit_b200 import _lib as L
+
+    out = {}
+    steps, warm = max(5, args.steps // 2), args.warmup
+
+    def one(name, pool, k, dtype, ranks, shared, desc):
+        ch = Chain(pool, k, dtype, dev)
+        t = timed_graph(lambda: ch.run(L.LBX_EXEC_KERNELS, stream), stream, warm, steps, ws)
+        us = t * 1e3 / (steps * len(pool))
+        b, packed = layer_bytes(k, ranks, shared, 4 if dtype == torch.float32 else 2)
+        e = roofline_entry(b, us, peak, peak_kind)
+        e.update({"workload": desc, "tokens": k, "pool_layers": len(pool),
+                  "pool_mb": round(len(pool) * (b - (4 if dtype == torch.float32 else 2) * k * (IN_F + OUT_F)) / 1e6, 1),
+                  "gbs_aggregate": round(b * len(pool) * steps * ws / (t * 1e-3) / 1e9, 2),
+                  "finite": bool(torch.isfinite(ch.acts[-1].float()).all())})
+        out[name] = e
+        del ch
+
+    c1 = build_pool(1024, dev, seed=4321, ranks=[208])
+    one("c1_k1", c1, 1, torch.float32, [208], False,
+        "C1 4096->4096 r=208 (~0.1 BPW), fp32 x/y, k=1, chain of 1024 distinct layers (> 2x L2)")
+    del c1
+    for k in (5, 8):
+        one(f"c2_k{k}", main_pool, k, torch.bfloat16, RANKS, False,
+            f"C2 verify batch k={k}: r=208+1840 (independent V_R), bf16, chain of {len(main_pool)} layers")
+    c4 = build_pool(768, dev, seed=8765, ranks=[208, 208], shared=True)
+    for k in (1, 5):
+        one(f"c4_shared_k{k}", c4, k, torch.bfloat16, [208, 208], True,
+            f"config-4 shared-factor target layer: draft r=208 + rank-matched residual U_R on the draft's "
+            f"V-stage (one V-stage feeds U and U_R), bf16, k={k}, chain of 768 layers")
+    del c4
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args):
     from littlebit_b200 import _lib as L
     from littlebit_b200 import ops
@@ -607,61 +911,29 @@ def run_ours(args):
     dev = torch.device("cuda", lrank)
     k, P = args.tokens, args.pool
     pool = build_pool(P, dev, seed=1234 + rank)
-    arrs = [ops.projs_array([p]) for p in pool]
+    ch = Chain(pool, k, torch.bfloat16, dev)
+    acts = ch.acts
     arr_all = ops.projs_array(pool)
-    acts = [torch.randn(k, IN_F, device=dev).bfloat16()] + \
-           [torch.empty(k, OUT_F, device=dev, dtype=torch.bfloat16) for _ in range(P)]
     ptrs = (ctypes.c_void_p * (P + 1))(*[t.data_ptr() for t in acts])
-    wsb = torch.zeros(ops.linear_workspace_bytes([pool[0]], k), dtype=torch.uint8, device=dev)
     wsc = torch.zeros(int(ops.lib().lbx_linear_chain_workspace_size(arr_all, P, k)), dtype=torch.uint8,
                       device=dev)
     stream = torch.cuda.Stream(dev)
 
     def step_kernels():  # one V-stage + one U-stage grid per layer, chained with PDL
-        for i in range(P):
-            ops.linear_group([pool[i]], acts[i], [acts[i + 1]], use_pdl=args.pdl, ws=wsb, arr=arrs[i],
-                             exec_mode=L.LBX_EXEC_KERNELS)
+        ch.run(L.LBX_EXEC_KERNELS, stream, args.pdl)
 
     def step_cluster():  # one split-rank cluster launch per layer, chained with PDL
-        for i in range(P):
-            ops.linear_group([pool[i]], acts[i], [acts[i + 1]], use_pdl=args.pdl, ws=wsb, arr=arrs[i],
-                             exec_mode=L.LBX_EXEC_CLUSTER)
+        ch.run(L.LBX_EXEC_CLUSTER, stream, args.pdl)
 
     def step_program():  # the whole chain as one persistent program
         ops.linear_chain(pool, acts, ws=wsc, arr=arr_all, ptrs=ptrs)
-
-    def timed_graph(fn):
-        with torch.cuda.stream(stream):
-            fn()  # eager warm-up (builds the program, sets kernel attributes)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            fn()
-        with torch.cuda.stream(stream):
-            for _ in range(args.warmup):
-                graph.replay()
-        torch.cuda.synchronize()
-        ops.clear_device_error()
-        barrier(ws)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            for _ in range(args.steps):
-                graph.replay()
-            e1.record(stream)
-        torch.cuda.synchronize()
-        barrier(ws)
-        out = max_over_ranks(e0.elapsed_time(e1), ws)
-        del graph
-        return out
 
     execs = {"cluster": step_cluster, "kernels": step_kernels, "program": step_program}
     main_fn = execs[args.exec]
     sampler = ClockSampler(lrank)
     sampler.start()
     time.sleep(0.3)
-    t_ms = timed_graph(main_fn)
+    t_ms = timed_graph(main_fn, stream, args.warmup, args.steps, ws)
     clocks = sampler.stop()
     assert ops.device_error() == 0, "device error word set during the bench"
     if not torch.isfinite(acts[-1].float()).all():
@@ -674,7 +946,7 @@ def run_ours(args):
             continue
         if name == "cluster" and k > 4:
             continue  # the cluster executor takes k <= 4
-        exec_t[name] = timed_graph(fn)
+        exec_t[name] = timed_graph(fn, stream, args.warmup, args.steps, ws)
         if not torch.equal(acts[-1], y_main):
             raise RuntimeError(f"{name} and {args.exec} executors disagree")
 
@@ -685,21 +957,56 @@ def run_ours(args):
     exec_gbs[args.exec] = round(value, 2)
     per_launch_s = t_ms * 1e-3 / (P * args.steps)
     peak, peak_kind = peaks()
-    achieved = b_layer / per_launch_s / 1e9
 
-    # ---- e2e: the chain through the C-ABI call with pinned HOST input/output:
-    # every step copies x host->device, runs the chain, copies y device->host
+    # ---- launch floor: the same grids and PDL chaining without arithmetic
+    floor = {}
+    for mode, nm in ((0, "launch_only_us"), (1, "with_weight_copies_us")):
+        tf = timed_graph(lambda: ch.floor(mode, stream), stream, args.warmup, args.steps, ws)
+        floor[nm] = round(tf * 1e3 / (P * args.steps), 3)
+    floor["kernel_us"] = round(per_launch_s * 1e6, 3)
+    floor["what"] = ("per-layer time of the same V/U grids (launch shapes, shared memory, PDL chaining) "
+                     "doing no arithmetic (lbx_linear_floor): launches only, and with each unit's weight "
+                     "bulk copies and their wait")
+
+    # ---- e2e through the C-ABI call: pinned host x -> device, the host calls
+    # lbx_linear_verify for every layer (ctypes), device y -> pinned host
     hx = torch.empty(k, IN_F, dtype=torch.bfloat16).pin_memory()
     hx.copy_(acts[0].cpu())
     hy = torch.empty(k, OUT_F, dtype=torch.bfloat16).pin_memory()
 
     def e2e_step():
+        with torch.cuda.stream(stream):
+            acts[0].copy_(hx, non_blocking=True)
+            ch.run(L.LBX_EXEC_KERNELS, stream, args.pdl)
+            hy.copy_(acts[-1], non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t_wall = time.perf_counter() - t_wall0
+    t2 = max_over_ranks(e0.elapsed_time(e1), ws)
+    barrier(ws)
+    e2e_val = b_layer * P * args.steps * ws / (t2 * 1e-3) / 1e9
+
+    def e2e_graph_step():
         acts[0].copy_(hx, non_blocking=True)
         main_fn()
         hy.copy_(acts[-1], non_blocking=True)
 
-    t2 = timed_graph(e2e_step)
-    e2e_val = b_layer * P * args.steps * ws / (t2 * 1e-3) / 1e9
+    tg = timed_graph(e2e_graph_step, stream, args.warmup, args.steps, ws)
+    e2e_graph_val = b_layer * P * args.steps * ws / (tg * 1e-3) / 1e9
+
+    # ---- the other layer configs
+    configs = run_configs(args, dev, stream, ws, pool, peak, peak_kind) if args.configs else None
 
     # ---- CPU baseline (rank 0, N=1 only)
     cpu = None
@@ -718,6 +1025,7 @@ def run_ours(args):
 
     if rank == 0:
         traffic = traffic_from_profiles(k, args.exec)
+        roof = roofline_entry(b_layer, per_launch_s * 1e6, peak, peak_kind, traffic)
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 4),
@@ -733,17 +1041,19 @@ def run_ours(args):
                                 "kernels": "two kernels per layer (V-stage, U-stage grids), PDL-chained",
                                 "cluster": "one split-rank cluster launch per layer (16-CTA clusters), "
                                            "PDL-chained"}[args.exec]},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "peak_kind": peak_kind,
-                         "algorithmic_bytes_per_launch": b_layer,
-                         "launch": "one LittleBit layer",
-                         "mean_launch_us": round(per_launch_s * 1e6, 3)},
+            "roofline": roof,
             "exec_gbs": exec_gbs,
+            "floor": floor,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": 2 * k * IN_F, "d2h_bytes_per_step": 2 * k * OUT_F,
                     "ms_per_step": round(t2 / args.steps, 4),
-                    "path": "pinned host x -> chain via the C ABI -> pinned host y, each step"},
+                    "host_wall_ms_per_step": round(t_wall * 1e3 / args.steps, 4),
+                    "path": f"pinned host x -> device; the host calls lbx_linear_verify (C ABI, ctypes) for "
+                            f"each of the {P} layers, no CUDA graph; last y -> pinned host; every step"},
+            "e2e_graph": {"value": round(e2e_graph_val, 2), "unit": "GB/s",
+                          "ms_per_step": round(tg / args.steps, 4),
+                          "path": "the same step (copies + chain) captured in one CUDA graph"},
+            "configs": configs,
             "cpu_baseline": cpu,
             "dense_bf16_ref": dense,
             "decode": decode,
@@ -772,6 +1082,7 @@ def main():
                     help="cluster: one split-rank cluster launch per layer; kernels: one grid per stage; "
                          "program: each step is one persistent launch")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--configs", type=int, default=1, help="also time C1, C2 k=5/8 and the config-4 layer")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--decode", type=int, default=1, help="also run the 7B-shape decode section")
     ap.add_argument("--decode70b", type=int, default=0,

@@ -99,7 +99,8 @@ typedef struct lbx_linear_args {
   int32_t exec;        /* LBX_EXEC_AUTO: one cluster launch when the call fits
                         * it, else the two stage grids; LBX_EXEC_KERNELS: the
                         * two stage grids; LBX_EXEC_CLUSTER: the cluster launch
-                        * or LBX_EUNSUPPORTED.  All give the same bits.       */
+                        * or LBX_EUNSUPPORTED; LBX_EXEC_KERNELS_ONE_CTA_V (see
+                        * below).  All give the same bits.                    */
   int32_t _pad;
 } lbx_linear_args;
 
@@ -309,6 +310,10 @@ typedef struct lbx_model {
 #define LBX_EXEC_KERNELS 1
 #define LBX_EXEC_PROGRAM 2
 #define LBX_EXEC_CLUSTER 3 /* lbx_linear_args.exec only */
+/* lbx_linear_args.exec only: the two stage grids with every V unit's staging
+ * passes in one CTA (inputs wider than 4096 columns otherwise run a cluster of
+ * one CTA per pass on small grids).  Same bits; for validation. */
+#define LBX_EXEC_KERNELS_ONE_CTA_V 4
 
 /* Workspace of lbx_forward: zero-filled once at allocation, like lbx_linear's. */
 size_t lbx_forward_workspace_size(const lbx_model *m /* host */, int32_t n_tokens);
@@ -336,6 +341,17 @@ int lbx_kv_move(uint16_t *const *k_caches, uint16_t *const *v_caches, int32_t n_
                 const int32_t *dst, int32_t n, cudaStream_t stream);
 
 /* ---- diagnostics --------------------------------------------------------- */
+/* Launch floor of a linear call, for benchmarks (no reference counterpart):
+ * the call's two stage grids with the same launch shapes, shared memory and
+ * PDL chaining as lbx_linear_verify (the one-CTA V-stage form), each CTA doing
+ * no arithmetic.  mode 0: each CTA waits for the preceding grid and makes one
+ * dependent load and store; mode 1: it also streams its unit's weights into
+ * shared memory and waits for them.  Writes one word per CTA of the call's
+ * scratch and of each y; the results are meaningless.  Arguments and
+ * workspace as for lbx_linear_verify. */
+int lbx_linear_floor(const lbx_proj *projs, const lbx_linear_args *a, int32_t mode, void *ws,
+                     size_t ws_bytes, cudaStream_t stream);
+
 /* Copies the last host-side error text of the calling thread. */
 int lbx_last_error(char *buf, size_t n);
 /* Device error word written by bounded waits that ran out (0 = none). */

@@ -18,6 +18,7 @@ LBX_MAX_PROJ = 3
 LBX_PRO_NONE, LBX_PRO_RMSNORM, LBX_PRO_SILU_MUL, LBX_PRO_MUL = 0, 1, 2, 3
 LBX_EPI_STORE, LBX_EPI_ADD, LBX_EPI_SILU0 = 0, 1, 2
 LBX_EXEC_AUTO, LBX_EXEC_KERNELS, LBX_EXEC_PROGRAM, LBX_EXEC_CLUSTER = 0, 1, 2, 3
+LBX_EXEC_KERNELS_ONE_CTA_V = 4
 
 
 class Branch(ctypes.Structure):
@@ -82,6 +83,7 @@ _SIGNATURES = {
     "lbx_linear": (c_int, [POINTER(Proj), POINTER(LinearArgs), c_void_p, c_size_t, c_void_p]),
     "lbx_linear_verify": (c_int, [POINTER(Proj), POINTER(LinearArgs), c_void_p, c_size_t, c_void_p]),
     "lbx_linear_noalloc": (c_int, [POINTER(Proj), POINTER(LinearArgs), c_void_p]),
+    "lbx_linear_floor": (c_int, [POINTER(Proj), POINTER(LinearArgs), c_int32, c_void_p, c_size_t, c_void_p]),
     "lbx_linear_noalloc_max_bytes": (c_size_t, []),
     "lbx_pack_signs": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "lbx_unpack_signs": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p]),

@@ -371,15 +371,7 @@ __global__ void __launch_bounds__(ATHREADS) attn_kernel(const __grid_constant__ 
   attn_unit(p, blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z), sm);
 }
 
-static int attn_sm_count() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-  }
-  return n;
-}
+static int attn_sm_count() { return device_sm_count(); }
 
 static void attn_fill(const lbx_attn_args *a, AttnParams &p) {
   p.n = a->n;
@@ -481,11 +473,13 @@ static int attn_launch(const lbx_attn_args *a, void *partials, unsigned *tickets
   size_t smem = 0;
   int rc = attn_prep(a, partials, tickets, p, smem);
   if (rc) return rc;
-  static size_t smax = 0;
-  if (!smax) {
-    cudaError_t e = allow_max_smem(attn_kernel, &smax);
-    if (e != cudaSuccess) return cuda_status(e, "attn smem attribute");
-  }
+  static DevCache<size_t> smax_cache;
+  size_t smax = 0;
+  rc = smax_cache.get(smax, [](size_t &out) {
+    cudaError_t e = allow_max_smem(attn_kernel, &out);
+    return e != cudaSuccess ? cuda_status(e, "attn smem attribute") : (int)LBX_OK;
+  });
+  if (rc) return rc;
   LBX_CHECK_SUP(smem <= smax, "attention needs %zu bytes of shared memory (max %zu)", smem, smax);
   const bool pdl = a->use_pdl != 0;
   const cudaError_t e =

@@ -5,6 +5,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <mutex>
 #include <string>
 
 #include "../../include/lbx.h"
@@ -36,6 +37,63 @@ int cuda_status(cudaError_t e, const char *what);
   } while (0)
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------------------
+// per-device set-up values
+// ---------------------------------------------------------------------------
+// Kernel attributes (cudaFuncSetAttribute) and device properties belong to one
+// device.  Values established on the first call are therefore cached per
+// device, so a process that drives several GPUs sets each of them up on its
+// first call there.  One recursive mutex guards every cache (an initialiser
+// may read another cache).  Devices beyond the table are set up on every call.
+constexpr int LBX_MAX_DEVICES = 64;
+inline std::recursive_mutex &dev_cache_mu() {
+  static std::recursive_mutex m;
+  return m;
+}
+inline int cur_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) d = -1;
+  return d;
+}
+template <typename T>
+struct DevCache {
+  T v[LBX_MAX_DEVICES] = {};
+  bool ok[LBX_MAX_DEVICES] = {};
+  // init(T &) returns an LBX status; its value is kept only when it succeeds
+  template <typename F>
+  int get(T &out, F &&init) {
+    const int d = cur_device();
+    const bool slot = d >= 0 && d < LBX_MAX_DEVICES;
+    std::lock_guard<std::recursive_mutex> lk(dev_cache_mu());
+    if (slot && ok[d]) {
+      out = v[d];
+      return LBX_OK;
+    }
+    T t{};
+    const int rc = init(t);
+    if (rc) return rc;
+    if (slot) {
+      v[d] = t;
+      ok[d] = true;
+    }
+    out = t;
+    return LBX_OK;
+  }
+};
+
+// multiprocessors of the current device (148 if the query fails)
+inline int device_sm_count() {
+  static DevCache<int> c;
+  int n = 148;
+  c.get(n, [](int &v) {
+    int dev = cur_device();
+    if (dev < 0 || cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+      v = 148;
+    return LBX_OK;
+  });
+  return n;
+}
 
 // Device error word: bounded waits that run out record a code here and the
 // kernel returns instead of spinning forever.  The library is one translation

@@ -1347,8 +1347,9 @@ static int check_args(const lbx_proj *projs, const lbx_linear_args *a) {
                     (a->epilogue == LBX_EPI_ADD && a->y_dtype == LBX_F32),
                 "bad epilogue (ADD needs fp32 y)");
   for (int i = 0; i < a->n_proj; ++i) LBX_CHECK_ARG(a->y[i], "y[%d] is NULL", i);
-  LBX_CHECK_ARG(a->exec == LBX_EXEC_AUTO || a->exec == LBX_EXEC_KERNELS || a->exec == LBX_EXEC_CLUSTER,
-                "bad exec (LBX_EXEC_AUTO, _KERNELS or _CLUSTER)");
+  LBX_CHECK_ARG(a->exec == LBX_EXEC_AUTO || a->exec == LBX_EXEC_KERNELS || a->exec == LBX_EXEC_CLUSTER ||
+                    a->exec == LBX_EXEC_KERNELS_ONE_CTA_V,
+                "bad exec (LBX_EXEC_AUTO, _KERNELS, _CLUSTER or _KERNELS_ONE_CTA_V)");
   return LBX_OK;
 }
 
@@ -1380,15 +1381,7 @@ static VKern vsplit_for(int ncb, int pm, int vt) {
   return vt == 2 ? vsplit_for_vt<2>(ncb, pm) : vsplit_for_vt<1>(ncb, pm);
 }
 
-static int sm_count() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-  }
-  return n;
-}
+static int sm_count() { return device_sm_count(); }
 
 #ifndef LBX_U_GROUPS
 #define LBX_U_GROUPS 136  // quantisation groups per U-stage CTA at most (measured on 7B- and 70B-shaped calls)
@@ -1398,10 +1391,14 @@ static int sm_count() {
 #endif
 
 // dynamic shared memory the stage kernels may use (after their static
-// shared memory); established once per process, before any graph capture
+// shared memory); established once per device, before any graph capture
+struct StageSmem {
+  size_t v, u;
+};
 static int stage_smem_limits(size_t &vmax, size_t &umax) {
-  static size_t v_ = 0, u_ = 0;
-  if (!v_) {
+  static DevCache<StageSmem> cache;
+  StageSmem lim{};
+  const int rc = cache.get(lim, [](StageSmem &out) {
     size_t m = 0, vv = (size_t)-1, uu = (size_t)-1;
     VKern all[36];
     int na = 0;
@@ -1421,12 +1418,13 @@ static int stage_smem_limits(size_t &vmax, size_t &umax) {
       if (e != cudaSuccess) return cuda_status(e, "ustage smem attribute");
       uu = std::min(uu, m);
     }
-    v_ = vv;
-    u_ = uu;
-  }
-  vmax = v_;
-  umax = u_;
-  return LBX_OK;
+    out.v = vv;
+    out.u = uu;
+    return (int)LBX_OK;
+  });
+  vmax = lim.v;
+  umax = lim.u;
+  return rc;
 }
 
 // one batch of k <= LBX_MAX_TOKENS tokens of a linear call, as the parameters
@@ -1599,17 +1597,16 @@ static int prep_linear(const lbx_proj *projs, const lbx_linear_args *a, int tok0
 
 // dynamic shared memory the cluster kernel may use, and the cluster-size opt-in
 static int slice_smem_limit(size_t &cmax) {
-  static size_t c_ = 0;
-  if (!c_) {
+  static DevCache<size_t> cache;
+  return cache.get(cmax, [](size_t &out) {
     size_t m = 0;
     cudaError_t e = allow_max_smem(slice_kernel<1>, &m);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(slice_kernel<1>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return cuda_status(e, "cluster kernel attributes");
-    c_ = m;
-  }
-  cmax = c_;
-  return LBX_OK;
+    out = m;
+    return (int)LBX_OK;
+  });
 }
 
 static cudaLaunchConfig_t slice_cfg(cudaLaunchAttribute (&attr)[2], int nclusters, size_t smem,
@@ -1635,12 +1632,15 @@ static cudaLaunchConfig_t slice_cfg(cudaLaunchAttribute (&attr)[2], int ncluster
 }
 
 // clusters of the cluster kernel with `smem` bytes each that can be resident
-// at once (cached per shared-memory size)
+// at once (cached per device and shared-memory size)
 static int slice_active(size_t smem) {
-  static int cache[256] = {};
+  static int cache[LBX_MAX_DEVICES][256] = {};
   const int kb = (int)((smem + 1023) / 1024);
+  const int dev = cur_device();
   if (kb >= 256) return 0;
-  int &v = cache[kb];
+  int scratch = 0;
+  std::lock_guard<std::recursive_mutex> lk(dev_cache_mu());
+  int &v = dev >= 0 && dev < LBX_MAX_DEVICES ? cache[dev][kb] : scratch;
   if (!v) {
     cudaLaunchAttribute attr[2];
     cudaLaunchConfig_t cfg = slice_cfg(attr, LBX_SL_CLUSTERS, (size_t)kb * 1024, nullptr, false);
@@ -1804,6 +1804,49 @@ static bool prep_slice(const lbx_proj *projs, const lbx_linear_args *a, int k, c
 #define LBX_V_SPLIT 1  // 0: every V unit runs all of its staging passes in one CTA
 #endif
 
+// Whether one cluster of `npass` pass-split CTAs with `smem` bytes each can be
+// resident on this device (a partitioned or heavily shared GPU may not offer a
+// whole cluster); when it cannot, the call runs the one-CTA V-stage, which
+// gives the same bits.  Cached per device, kernel, cluster size and size.
+static bool vsplit_schedulable(VKern kern, int npass, size_t smem) {
+  struct Key {
+    int dev;
+    VKern k;
+    int npass;
+    size_t smem;
+  };
+  static Key seen[256];
+  static bool fits[256];
+  static int nseen = 0;
+  const int dev = cur_device();
+  std::lock_guard<std::recursive_mutex> lk(dev_cache_mu());
+  for (int i = 0; i < nseen; ++i)
+    if (seen[i].dev == dev && seen[i].k == kern && seen[i].npass == npass && seen[i].smem == smem)
+      return fits[i];
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(npass);
+  cfg.blockDim = dim3(VTHREADS);
+  cfg.dynamicSmemBytes = smem;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = npass;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, (const void *)kern, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    n = 0;
+  }
+  const bool ok = n >= 1;
+  if (nseen < 256) {
+    seen[nseen] = Key{dev, kern, npass, smem};
+    fits[nseen++] = ok;
+  }
+  return ok;
+}
+
 static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, int k, void *ws,
                      cudaStream_t stream) {
   size_t vmax = 0, umax = 0;
@@ -1836,13 +1879,14 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
   // and 70B targets) it was slower, 19.5 -> 24.5 us for the 7B down call.
   const int npass = (P.vp.Wv + PASS_WORDS - 1) / PASS_WORDS;
   bool split = false;
-  if (LBX_V_SPLIT && npass > 1 && npass <= 8 && P.vunits * npass <= 2 * sm_count()) {
+  if (LBX_V_SPLIT && a->exec != LBX_EXEC_KERNELS_ONE_CTA_V && npass > 1 && npass <= 8 &&
+      P.vunits * npass <= 2 * sm_count()) {
     const bool rms = a->prologue == LBX_PRO_RMSNORM;
     const size_t sw = al256((size_t)16 * P.vp.vt * VSP_PITCH * 4 + (size_t)VSP_COLS * 4 * (rms ? 2 : 1) +
                             (size_t)32 * P.vp.vt * 4);
     const size_t ss = al256((size_t)PASS_WORDS * act_ws(P.vp.ncols) * 4 + (size_t)2 * VWARPS * 16 * k * 4 +
                             (size_t)VWARPS * LBX_MAX_TOKENS * 4);
-    if (sw + ss <= vmax) {
+    if (sw + ss <= vmax && vsplit_schedulable(vsplit_for(P.ncb, pm_of(a->prologue), P.vp.vt), npass, sw + ss)) {
       VParams vp = P.vp;
       vp.split = 1;
       vp.s_bytes = (int)ss;
@@ -1930,6 +1974,98 @@ extern "C" int lbx_linear(const lbx_proj *projs, const lbx_linear_args *a, void 
 }
 
 // ---------------------------------------------------------------------------
+// Launch floor of a linear call (a benchmarking aid): the call's two stage
+// grids with their launch shapes, shared memory and PDL chaining, each CTA
+// doing no arithmetic.  MODE 0: trigger, wait for the preceding grid, one
+// dependent load and one store per CTA.  MODE 1: also every unit's weight
+// bulk copies and the wait for them (the HBM latency a stage has to cover).
+// The time of a chain of these against a chain of real calls separates the
+// cost of the grid boundaries from the cost of the stage bodies.
+// ---------------------------------------------------------------------------
+namespace lbx {
+template <int MODE>
+__global__ void __launch_bounds__(VTHREADS, 2) vfloor_kernel(const __grid_constant__ VParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ LinShm sh;
+  linshm_init(sh);
+  uint8_t *W = smem_raw + p.s_bytes;
+  if (MODE) vstage_issue(p, blockIdx.x, W, sh);
+  pdl_trigger();
+  pdl_wait();
+  bool ok = true;
+  if (MODE) ok = __syncthreads_and(mbar_wait_bounded(&sh.bar[UT_MAX], 0, 0x121));
+  if (threadIdx.x == 0) {
+    const VSeg &sg = p.seg[vseg_of(p, blockIdx.x)];
+    const int row0 = (blockIdx.x - sg.unit0) * 16 * p.vt;
+    sg.z0[row0] = load_act(p.x, p.xdt, 0) + (ok ? 0.f : 1.f);
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(UTHREADS, 2) ufloor_kernel(const __grid_constant__ UParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ LinShm sh;
+  linshm_init(sh);
+  uint8_t *W = smem_raw + p.s_bytes;
+  if (MODE) ustage_issue(p, blockIdx.x, W, sh);
+  pdl_trigger();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, tile = warp % p.ut;
+  const USeg &sg = p.seg[useg_of(p, blockIdx.x)];
+  const int n0 = (blockIdx.x - sg.cta0) * (16 * p.ut) + 16 * tile;
+  bool ok = true;
+  if (MODE && n0 < sg.out) ok = mbar_wait_bounded(&sh.bar[tile], 0, 0x221);
+  ok = __syncthreads_and(ok);
+  if (threadIdx.x == 0) {
+    const float v = __ldcg(sg.z[0]) + (ok ? 0.f : 1.f);
+    const int64_t off = (int64_t)(blockIdx.x - sg.cta0) * 16 * p.ut;
+    if (p.ydt == LBX_F32)
+      reinterpret_cast<float *>(sg.y)[off] = v;
+    else
+      reinterpret_cast<uint16_t *>(sg.y)[off] = f32_to_bf16(v);
+  }
+}
+}  // namespace lbx
+
+extern "C" int lbx_linear_floor(const lbx_proj *projs, const lbx_linear_args *a, int32_t mode, void *ws,
+                                size_t ws_bytes, cudaStream_t stream) {
+  using namespace lbx;
+  int rc = check_args(projs, a);
+  if (rc) return rc;
+  LBX_CHECK_ARG(mode == 0 || mode == 1, "mode must be 0 (launches only) or 1 (with weight copies)");
+  const size_t need = stage_ws_bytes(projs, a->n_proj, std::min(a->n_tokens, (int32_t)LBX_MAX_TOKENS));
+  LBX_CHECK_ARG(ws && ws_bytes >= need, "workspace too small (%zu < %zu)", ws_bytes, need);
+  size_t vmax = 0, umax = 0;
+  rc = stage_smem_limits(vmax, umax);
+  if (rc) return rc;
+  static DevCache<int> attr;
+  int done = 0;
+  rc = attr.get(done, [](int &out) {
+    cudaError_t e = allow_max_smem(vfloor_kernel<0>);
+    if (e == cudaSuccess) e = allow_max_smem(vfloor_kernel<1>);
+    if (e == cudaSuccess) e = allow_max_smem(ufloor_kernel<0>);
+    if (e == cudaSuccess) e = allow_max_smem(ufloor_kernel<1>);
+    out = 1;
+    return e != cudaSuccess ? cuda_status(e, "floor kernel attributes") : (int)LBX_OK;
+  });
+  if (rc) return rc;
+  const bool pdl = a->use_pdl != 0;
+  for (int t0 = 0; t0 < a->n_tokens; t0 += LBX_MAX_TOKENS) {
+    const int k = std::min((int)LBX_MAX_TOKENS, a->n_tokens - t0);
+    LinPrep P;
+    rc = prep_linear(projs, a, t0, k, ws, vmax, umax, P);
+    if (rc) return rc;
+    cudaError_t e = launch(mode ? vfloor_kernel<1> : vfloor_kernel<0>, dim3(P.vunits), dim3(VTHREADS),
+                           P.v_w + P.v_s, stream, pdl, P.vp);
+    if (e == cudaSuccess)
+      e = launch(mode ? ufloor_kernel<1> : ufloor_kernel<0>, dim3(P.uunits), dim3(UTHREADS), P.u_w + P.u_s,
+                 stream, pdl, P.up);
+    if (e != cudaSuccess) return cuda_status(e, "floor launch");
+  }
+  return LBX_OK;
+}
+
+// ---------------------------------------------------------------------------
 // Allocation-free variant: the scratch lives in a fixed device array
 // ---------------------------------------------------------------------------
 // Some callers cannot hand the library device memory: a host application that
@@ -1981,8 +2117,10 @@ extern "C" int lbx_linear_noalloc(const lbx_proj *projs, const lbx_linear_args *
     }
     scratch = g_noalloc_ptr[dev];
   }
-  // the bookkeeping words (header and z maxima) must start at zero; clear them
-  // rather than trusting whatever an earlier (possibly failed) call left behind
+  // only the 512-byte header (the cluster executor's range tickets and the
+  // grid barrier words) must start at zero: clear it rather than trusting
+  // whatever an earlier (possibly failed) call left behind.  z and the per-unit
+  // maxima after it are overwritten by every call.
   e = cudaMemsetAsync(scratch, 0, WS_HDR, stream);
   if (e != cudaSuccess) return cuda_status(e, "lbx_linear_noalloc: clear scratch");
   return lbx_linear_verify(projs, a, scratch, NOALLOC_SCRATCH_BYTES, stream);
@@ -2035,14 +2173,17 @@ extern "C" int lbx_linear_allgather(const lbx_proj *proj, const lbx_linear_args 
   auto uk = P.ncb == 1   ? ustage_kernel<1, true>
             : P.ncb == 2 ? ustage_kernel<2, true>
                          : ustage_kernel<4, true>;
-  static bool attr = false;
-  if (!attr) {
+  static DevCache<int> attr;
+  int done = 0;
+  rc = attr.get(done, [](int &out) {
     for (auto kk : {ustage_kernel<1, true>, ustage_kernel<2, true>, ustage_kernel<4, true>}) {
       const cudaError_t e0 = allow_max_smem(kk);
       if (e0 != cudaSuccess) return cuda_status(e0, "ustage smem attribute");
     }
-    attr = true;
-  }
+    out = 1;
+    return (int)LBX_OK;
+  });
+  if (rc) return rc;
   cudaError_t e = launch(vk, dim3(P.vunits), dim3(VTHREADS), P.v_w + P.v_s, stream, pdl, P.vp);
   if (e != cudaSuccess) return cuda_status(e, "vstage launch");
   e = launch(uk, dim3(P.uunits), dim3(UTHREADS), P.u_w + P.u_s, stream, pdl, P.up);

@@ -154,16 +154,7 @@ __global__ void argmax_final_kernel(const unsigned long long *best, int nblocks,
   argmax_unit(best, nblocks, n, out);
 }
 
-static int lm_blocks() {
-  static int nb = 0;
-  if (!nb) {
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    nb = sms;
-  }
-  return nb;
-}
+static int lm_blocks() { return device_sm_count(); }
 
 }  // namespace lbx
 
@@ -186,14 +177,17 @@ extern "C" int lbx_lmhead_argmax(const float *x, const float *norm_w, float eps,
   LBX_CHECK_ARG(logits || argmax_out, "nothing to compute");
   const size_t need = lbx_lmhead_workspace_size(n, vocab);
   LBX_CHECK_ARG(!argmax_out || (ws && ws_bytes >= need), "workspace too small");
-  static bool attr_done = false;
-  if (!attr_done) {
+  static DevCache<int> attr;
+  int attr_done = 0;
+  const int arc = attr.get(attr_done, [](int &out) {
     for (auto k : {lmhead_kernel<1>, lmhead_kernel<2>, lmhead_kernel<4>, lmhead_kernel<8>}) {
       cudaError_t e = allow_max_smem(k);
       if (e != cudaSuccess) return cuda_status(e, "lmhead smem attribute");
     }
-    attr_done = true;
-  }
+    out = 1;
+    return (int)LBX_OK;
+  });
+  if (arc) return arc;
   const bool pdl = use_pdl != 0;
   const int nb = lm_blocks();
   // tokens per pass: the normalised hidden states of a pass live in shared memory

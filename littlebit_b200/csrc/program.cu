@@ -405,9 +405,9 @@ static ProgKern program_instance(int ncb, int lmnt) {
 
 // dynamic shared memory every executor instance may use; SM count
 static int program_budget(size_t &dyn_max, int &nsm) {
-  static size_t m = 0;
-  static int sms = 0;
-  if (!m) {
+  static DevCache<size_t> cache;
+  nsm = device_sm_count();
+  return cache.get(dyn_max, [](size_t &out) {
     size_t mn = (size_t)-1, g = 0;
     for (ProgKern k : {program_kernel<1, 1>, program_kernel<1, 2>, program_kernel<1, 4>, program_kernel<2, 8>,
                        program_kernel<4, 8>}) {
@@ -419,14 +419,9 @@ static int program_budget(size_t &dyn_max, int &nsm) {
       if (e != cudaSuccess) return cuda_status(e, "program smem attribute");
       mn = std::min(mn, g);
     }
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    m = mn;
-  }
-  dyn_max = m;
-  nsm = sms;
-  return LBX_OK;
+    out = mn;
+    return (int)LBX_OK;
+  });
 }
 
 // the two phases of each token batch of one linear call

@@ -240,17 +240,13 @@ def linear_workspace_bytes(projs: Sequence[PackedLinear], n_tokens: int) -> int:
     return int(lib().lbx_linear_workspace_size(projs_array(projs), len(projs), n_tokens))
 
 
-def linear_group(projs: Sequence[PackedLinear], x: torch.Tensor, outs: Sequence[torch.Tensor], *,
-                 prologue: int = L.LBX_PRO_NONE, norm_w: Optional[torch.Tensor] = None,
-                 eps: float = 1e-6, x2: Optional[torch.Tensor] = None,
-                 epilogue: int = L.LBX_EPI_STORE, use_pdl: bool = True,
-                 ws: Optional[torch.Tensor] = None, arr=None,
-                 exec_mode: int = L.LBX_EXEC_AUTO) -> None:
-    """Run 1..3 LittleBit projections that share the input x [k, in].
-
-    ``exec_mode``: LBX_EXEC_AUTO (one cluster launch when the call fits it,
-    else the two stage grids), LBX_EXEC_KERNELS or LBX_EXEC_CLUSTER; all give
-    the same bits."""
+def linear_args(projs: Sequence[PackedLinear], x: torch.Tensor, outs: Sequence[torch.Tensor], *,
+                prologue: int = L.LBX_PRO_NONE, norm_w: Optional[torch.Tensor] = None,
+                eps: float = 1e-6, x2: Optional[torch.Tensor] = None,
+                epilogue: int = L.LBX_EPI_STORE, use_pdl: bool = True,
+                exec_mode: int = L.LBX_EXEC_AUTO) -> L.LinearArgs:
+    """The lbx_linear_args of a call (checked shapes), for callers that issue the
+    C-ABI call themselves, e.g. many times over fixed buffers."""
     _cuda("x", x)
     k = x.shape[0]
     a = L.LinearArgs()
@@ -272,6 +268,23 @@ def linear_group(projs: Sequence[PackedLinear], x: torch.Tensor, outs: Sequence[
             raise RuntimeError(f"out{i} has shape {tuple(o.shape)}, expected ({k}, {projs[i].out_features})")
         a.y[i] = _p(o)
         a.y_ld[i] = o.stride(0)
+    return a
+
+
+def linear_group(projs: Sequence[PackedLinear], x: torch.Tensor, outs: Sequence[torch.Tensor], *,
+                 prologue: int = L.LBX_PRO_NONE, norm_w: Optional[torch.Tensor] = None,
+                 eps: float = 1e-6, x2: Optional[torch.Tensor] = None,
+                 epilogue: int = L.LBX_EPI_STORE, use_pdl: bool = True,
+                 ws: Optional[torch.Tensor] = None, arr=None,
+                 exec_mode: int = L.LBX_EXEC_AUTO) -> None:
+    """Run 1..3 LittleBit projections that share the input x [k, in].
+
+    ``exec_mode``: LBX_EXEC_AUTO (one cluster launch when the call fits it,
+    else the two stage grids), LBX_EXEC_KERNELS or LBX_EXEC_CLUSTER; all give
+    the same bits."""
+    a = linear_args(projs, x, outs, prologue=prologue, norm_w=norm_w, eps=eps, x2=x2, epilogue=epilogue,
+                    use_pdl=use_pdl, exec_mode=exec_mode)
+    k = x.shape[0]
     if arr is None:
         arr = projs_array(projs)
     need = int(lib().lbx_linear_workspace_size(arr, len(projs), k))

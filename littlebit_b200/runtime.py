@@ -86,8 +86,18 @@ def load_hf_state_dict(model_path) -> Dict[str, torch.Tensor]:
     raise FileNotFoundError(f"No safetensors files found in {p}")
 
 
-def build_dummy_config(hf_config: dict, lb_config: dict) -> dict:
-    """dummy_llama3_config.json (convert_hf_to_runtime.py:193-213)."""
+def _json_or_dict(v) -> dict:
+    """A config given as a JSON file path (the reference's argument) or as a dict."""
+    if isinstance(v, dict):
+        return v
+    return json.loads(Path(v).read_text())
+
+
+def build_dummy_config(hf_config, lb_config) -> dict:
+    """dummy_llama3_config.json (convert_hf_to_runtime.py:193-213).  Takes the
+    paths of config.json and littlebit_config.json, as the reference does, or
+    the two configs as dicts."""
+    hf_config, lb_config = _json_or_dict(hf_config), _json_or_dict(lb_config)
     return {
         "name": hf_config.get("_name_or_path", "llama"),
         "hidden_size": hf_config["hidden_size"],
@@ -103,8 +113,10 @@ def build_dummy_config(hf_config: dict, lb_config: dict) -> dict:
     }
 
 
-def build_runtime_config(hf_config: dict, lb_config: dict) -> dict:
-    """littlebit_runtime_config.json (convert_hf_to_runtime.py:216-235)."""
+def build_runtime_config(hf_config, lb_config) -> dict:
+    """littlebit_runtime_config.json (convert_hf_to_runtime.py:216-235); arguments
+    as for :func:`build_dummy_config`."""
+    hf_config, lb_config = _json_or_dict(hf_config), _json_or_dict(lb_config)
     return {
         "format_version": 1,
         "checkpoint_format": "runtime",

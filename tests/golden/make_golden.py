@@ -18,6 +18,10 @@ Records, from the reference's own Python code:
                 with deterministic table-driven models (speculative_decoding.py)
   hf_llama.npz  HF LlamaForCausalLM + apply_littlebit_patch logits of a tiny
                 model (the reference's GPU/HF model path)
+  runtime_tiny/ + runtime.npz  runtime checkpoint directories written by the
+                reference's convert_hf_to_runtime from two tiny HF LittleBit
+                checkpoints (inputs kept beside them), with the HF logits of
+                the draft and of the hidden-sum target
   ref_schemas.json  the reference's littlebit_cpu_ops op schemas (cpp:2321-2377)
 """
 from __future__ import annotations
@@ -134,10 +138,6 @@ def gen_convert():
     for k, v in rt.items():
         out["rt/" + k] = v.numpy()
     np.savez_compressed(HERE / "convert.npz", **out)
-    cfgs = {
-        "dummy": convert_hf_to_runtime.build_dummy_config.__doc__,
-    }
-    _ = cfgs
 
 
 def gen_tree():
@@ -241,6 +241,109 @@ def gen_hf_llama():
     np.savez_compressed(HERE / "hf_llama.npz", **out)
 
 
+def _tiny_lb_llama(name, eff_bit, residual, g, embed=None, head=None):
+    """A tiny HF LlamaForCausalLM patched with the reference's apply_littlebit_patch,
+    seeded +-1 factors and near-unit-gain |N(1,0.1)| scales (v1 / sqrt(in),
+    u1 / sqrt(rank): activations stay in the range of a trained checkpoint),
+    bf16-representable embedding and lm_head.  Returns (config, model, lb_args)."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from quantization.utils.quant_util import apply_littlebit_patch
+    import argparse as ap
+    torch.manual_seed(0)
+    cfg = LlamaConfig(hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, vocab_size=128,
+                      max_position_embeddings=256, rms_norm_eps=1e-6, rope_theta=10000.0,
+                      tie_word_embeddings=False, attn_implementation="eager")
+    cfg._name_or_path = name
+    model = LlamaForCausalLM(cfg)
+    args = ap.Namespace(quant_func="STEBinary", quant_mod="LittleBitLinear", eff_bit=eff_bit,
+                        split_dim=1024, residual=residual, kv_factor=1.0, min_split_dim=8, model_id=name)
+    apply_littlebit_patch(model, args, do_train=False)
+    for _, mod in model.named_modules():
+        if isinstance(mod, LittleBitLinear):
+            r = mod.split_dim
+            for suf in ("", "_R") if residual else ("",):
+                U = (torch.randint(0, 2, (mod.out_features, r), generator=g) * 2 - 1).float()
+                V = (torch.randint(0, 2, (r, mod.in_features), generator=g) * 2 - 1).float()
+                s = lambda *sh: (1 + 0.1 * torch.randn(*sh, generator=g)).abs()
+                setattr(mod, "U" + suf, torch.nn.Parameter(U, requires_grad=False))
+                setattr(mod, "V" + suf, torch.nn.Parameter(V, requires_grad=False))
+                gain = {"u1": r ** -0.5, "v1": mod.in_features ** -0.5, "u2": 1.0, "v2": 1.0}
+                for nm, sh in (("u1", (1, mod.out_features)), ("u2", (1, r)), ("v1", (1, r)),
+                               ("v2", (1, mod.in_features))):
+                    setattr(mod, nm + suf, torch.nn.Parameter(s(*sh) * gain[nm], requires_grad=False))
+            mod._binarized = True
+    with torch.no_grad():
+        if embed is None:
+            embed = (0.02 * torch.randn(cfg.vocab_size, cfg.hidden_size, generator=g)).bfloat16().float()
+            head = (0.02 * torch.randn(cfg.vocab_size, cfg.hidden_size, generator=g)).bfloat16().float()
+        model.model.embed_tokens.weight.copy_(embed)
+        model.lm_head.weight.copy_(head)
+        for ly in model.model.layers:
+            ly.input_layernorm.weight.copy_((1 + 0.1 * torch.randn(cfg.hidden_size, generator=g)).abs())
+            ly.post_attention_layernorm.weight.copy_((1 + 0.1 * torch.randn(cfg.hidden_size, generator=g)).abs())
+        model.model.norm.weight.copy_((1 + 0.1 * torch.randn(cfg.hidden_size, generator=g)).abs())
+    return cfg, model.float().eval(), args
+
+
+def gen_runtime():
+    """Runtime checkpoint directories written by the reference's own converter.
+
+    Two tiny HF LittleBit Llamas sharing one embedding/lm_head (a 0.5-bit
+    "draft" and a 1.0-bit residual-branch "residual" model) are saved as the
+    reference's training scripts save a checkpoint (the packed state_dict of
+    littlebit.py:322-345 as model.safetensors, config.json, and the
+    littlebit_config.json of main.py:282-294).  convert_hf_to_runtime
+    (convert_hf_to_runtime.py:238-290) then writes each runtime directory:
+    littlebit_runtime.safetensors, littlebit_runtime_config.json and
+    dummy_llama3_config.json.  Both the HF inputs and the converter's outputs
+    are kept under runtime_tiny/, with the HF logits of the draft and of the
+    hidden-sum target lm_head(norm(h_draft) + norm(h_res)) of
+    cpu_target_model.py:516-527 in runtime.npz."""
+    import shutil
+    import tempfile
+    from safetensors.torch import save_file
+
+    base = HERE / "runtime_tiny"
+    if base.exists():
+        shutil.rmtree(base)
+    g = torch.Generator().manual_seed(77)
+    cd, md, ad = _tiny_lb_llama("tiny-littlebit-draft", 0.5, False, g)
+    cr, mr, ar = _tiny_lb_llama("tiny-littlebit-residual", 1.0, True, g,
+                                embed=md.model.embed_tokens.weight.detach().clone(),
+                                head=md.lm_head.weight.detach().clone())
+    out = {}
+    ids = torch.randint(0, cd.vocab_size, (1, 12), generator=g)
+    with torch.no_grad():
+        out["draft_logits"] = md(input_ids=ids).logits[0].numpy()
+        hd = md.model(input_ids=ids).last_hidden_state[0]
+        hr = mr.model(input_ids=ids).last_hidden_state[0]
+        out["target_logits"] = ((hd + hr) @ md.lm_head.weight.T).numpy()
+    out["ids"] = ids.numpy()[0]
+    for tag, cfg, model, args in (("draft", cd, md, ad), ("residual", cr, mr, ar)):
+        hf_dir = base / f"{tag}_hf"
+        hf_dir.mkdir(parents=True)
+        sd = {}
+        for k, v in model.state_dict().items():
+            if k in ("model.embed_tokens.weight", "lm_head.weight"):
+                v = v.to(torch.bfloat16)  # as saved in torch_dtype bfloat16 (exact: bf16 values)
+            sd[k] = v.contiguous()
+        save_file(sd, str(hf_dir / "model.safetensors"))
+        (hf_dir / "config.json").write_text(json.dumps(cfg.to_dict(), indent=2, default=str))
+        lb = {"quant_func": args.quant_func, "eff_bit": args.eff_bit, "split_dim": args.split_dim,
+              "residual": args.residual, "kv_factor": args.kv_factor, "min_split_dim": args.min_split_dim,
+              "quant_mod": args.quant_mod}
+        (hf_dir / "littlebit_config.json").write_text(json.dumps(lb, indent=2))
+        with tempfile.TemporaryDirectory() as td:
+            convert_hf_to_runtime.convert_hf_to_runtime(str(hf_dir), td)
+            rt_dir = base / tag
+            rt_dir.mkdir()
+            for f in ("littlebit_runtime.safetensors", "littlebit_runtime_config.json",
+                      "dummy_llama3_config.json"):
+                shutil.copy2(Path(td) / f, rt_dir / f)
+    np.savez_compressed(HERE / "runtime.npz", **out)
+
+
 def gen_schemas():
     """The op schemas of the reference's TORCH_LIBRARY block
     (patches/littlebit_cpu_optimized.cpp:2321-2377), read as text."""
@@ -258,7 +361,8 @@ if __name__ == "__main__":
     ap_ = argparse.ArgumentParser()
     ap_.add_argument("--only", default="")
     a = ap_.parse_args()
-    for fn in (gen_packing, gen_linear, gen_convert, gen_tree, gen_spec, gen_hf_llama, gen_schemas):
+    for fn in (gen_packing, gen_linear, gen_convert, gen_tree, gen_spec, gen_hf_llama, gen_runtime,
+               gen_schemas):
         if a.only and a.only not in fn.__name__:
             continue
         fn()

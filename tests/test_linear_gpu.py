@@ -266,6 +266,78 @@ def test_allgather_exchange_two_shards_one_gpu():
     assert [int(s[0]) for s in states] == [5, 5] and [int(s[1]) for s in states] == [0, 0]
 
 
+def test_allgather_unpack_bounded_wait_reports_missing_shard():
+    """The unpack kernel's wait is bounded: when one (emulated) shard never
+    delivers its words, each unpack gives up after 1 s, records device error
+    0x601, writes NaN for the missing columns and returns with the GPU context
+    intact.  After the error word is cleared, the next call of both shards
+    exchanges normally and matches the unsharded layer bit for bit.  Only the
+    waiting kernel is launched; nothing the wait depends on is in flight."""
+    import ctypes
+
+    from littlebit_b200 import _lib as L
+    from littlebit_b200 import ops, synthetic
+    from littlebit_b200.sharded import RowShardedLinear
+
+    K, N, r, G, k = 4096, 1024, 208, 2, 2
+    g = torch.Generator().manual_seed(93)
+    full = synthetic.to_packed_linear(K, N, synthetic.layer(K, N, [r], g), DEV)
+    shards = [RowShardedLinear(full, G, rank) for rank in range(G)]
+    half = k * N
+    xbufs = [torch.zeros(2 * half, dtype=torch.int64, device=DEV) for _ in range(G)]
+    states = [torch.zeros(2, dtype=torch.int32, device=DEV) for _ in range(G)]
+    peers = (ctypes.c_void_p * G)(*[b.data_ptr() for b in xbufs])
+    arrs = [ops.projs_array([s.local]) for s in shards]
+    wss = [torch.zeros(ops.linear_workspace_bytes([s.local], k), dtype=torch.uint8, device=DEV) for s in shards]
+    lib = ops.lib()
+    st = torch.cuda.current_stream().cuda_stream
+
+    def send(rank, x):
+        a = L.LinearArgs()
+        a.n_proj, a.n_tokens, a.x_dtype, a.y_dtype = 1, k, L.LBX_F32, L.LBX_F32
+        a.epilogue, a.use_pdl, a.x = L.LBX_EPI_STORE, 0, x.data_ptr()
+        L.check(lib.lbx_linear_allgather(arrs[rank], ctypes.byref(a), G, peers, half, shards[rank].lo, N,
+                                         states[rank].data_ptr(), wss[rank].data_ptr(), wss[rank].numel(), st),
+                "allgather")
+
+    def unpack_all():
+        ys = [torch.empty(k, N, device=DEV) for _ in range(G)]
+        for rank in range(G):
+            L.check(lib.lbx_allgather_unpack(xbufs[rank].data_ptr(), half, k, N, N, ys[rank].data_ptr(), N,
+                                             states[rank].data_ptr(), 0, st), "unpack")
+        return ys
+
+    ops.clear_device_error()
+    x = torch.randn(k, K, generator=g).cuda()
+    ref = ops.lb_linear(full, x)
+    send(0, x)  # shard 1 never delivers call 1
+    torch.cuda.synchronize()
+    import time
+
+    t0 = time.perf_counter()
+    ys = unpack_all()
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert ops.device_error() == 0x601
+    assert 1.5 < waited < 30.0, waited  # two unpacks, each bounded at 1 s
+    lo1 = shards[1].lo
+    for y in ys:
+        assert torch.equal(y[:, :lo1], ref[:, :lo1])  # shard 0's columns arrived
+        assert torch.isnan(y[:, lo1:]).all()          # shard 1's are reported missing
+    assert [int(s[0]) for s in states] == [1, 1] and [int(s[1]) for s in states] == [0, 0]
+    # recovery: clear the error word; the next call of both shards is exact
+    ops.clear_device_error()
+    x = torch.randn(k, K, generator=g).cuda()
+    for rank in range(G):
+        send(rank, x)
+    ys = unpack_all()
+    ref = ops.lb_linear(full, x)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    for y in ys:
+        assert torch.equal(y, ref)
+
+
 def _run_both(ops, projs, x, out_shapes, dt=torch.float32, y_init=None, **kw):
     """The same call on the cluster executor and on the two stage grids."""
     from littlebit_b200 import _lib as L
@@ -423,7 +495,10 @@ def test_pass_split_v_stage_matches_one_cta_passes(ops, k):
     from littlebit_b200 import synthetic
 
     g = _gen(800 + k)
-    for K, N, ranks in ((8192, 1024, [392, 3664]), (11008, 4096, [280, 2664])):
+    # draft-sized single branches take the pass-split form (at most two CTAs per
+    # SM for the whole split grid); the two-branch targets keep one CTA per unit
+    for K, N, ranks in ((8192, 1024, [392]), (11008, 4096, [280]), (8192, 1024, [392, 3664]),
+                        (11008, 4096, [280, 2664])):
         lay = synthetic.to_packed_linear(K, N, synthetic.layer(K, N, ranks, g), DEV)
         x = torch.randn(k, K, generator=g).to(DEV)
         y = torch.empty(k, N, device=DEV)
@@ -431,3 +506,35 @@ def test_pass_split_v_stage_matches_one_cta_passes(ops, k):
         acts = [x.clone(), torch.empty(k, N, device=DEV)]
         ops.linear_chain([lay], acts)
         assert torch.equal(y.view(torch.int32), acts[1].view(torch.int32)), (K, N)
+
+
+@pytest.mark.parametrize("k", [1, 5])
+@pytest.mark.parametrize("prologue", ["rmsnorm", "silu_mul", "mul"])
+def test_pass_split_v_stage_prologues_bitwise(ops, k, prologue):
+    """The pass-split V-stage with each fused prologue: RMSNorm (rank 0 adds the
+    other ranks' sums of squares over distributed shared memory), SiLU-mul and
+    mul (the draft down projection).  Bit-identical to the same call with every
+    V unit's passes in one CTA."""
+    from littlebit_b200 import synthetic
+
+    L_ = ops.L
+    pro = {"rmsnorm": L_.LBX_PRO_RMSNORM, "silu_mul": L_.LBX_PRO_SILU_MUL, "mul": L_.LBX_PRO_MUL}[prologue]
+    g = _gen(830 + k)
+    for K, N, ranks in ((8192, 1024, [392]), (11008, 4096, [280]), (11008, 4096, [280, 280])):
+        lay = synthetic.to_packed_linear(K, N, synthetic.layer(K, N, ranks, g), DEV)
+        x = torch.randn(k, K, generator=g).to(DEV)
+        x2 = torch.randn(k, K, generator=g).to(DEV)
+        w = (1 + 0.1 * torch.randn(K, generator=g)).abs().to(DEV)
+        kw = dict(prologue=pro)
+        if pro == L_.LBX_PRO_RMSNORM:
+            kw["norm_w"] = w
+        else:
+            kw["x2"] = x2
+        ys = []
+        for mode in (L_.LBX_EXEC_KERNELS, L_.LBX_EXEC_KERNELS_ONE_CTA_V):
+            y = torch.empty(k, N, device=DEV)
+            ops.linear_group([lay], x, [y], exec_mode=mode, **kw)
+            ys.append(y)
+        torch.cuda.synchronize()
+        assert torch.isfinite(ys[0]).all()
+        assert torch.equal(ys[0].view(torch.int32), ys[1].view(torch.int32)), (K, N, prologue)
