@@ -378,8 +378,10 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 def build_pool(P: int, device, seed: int, ranks=RANKS, shared: bool = False):
     """P distinct layers generated on the device (random words == Bernoulli(0.5)
-    signs, |N(1,0.1)| scales); ``shared``: the second branch reuses the first
-    branch's V-stage (littlespec_ref/littlebit_itq_spec.py:298-309)."""
+    signs, |N(1,0.1)| scales, mid / sqrt(in) and u1 / sqrt(rank) so that a
+    layer has unit gain and a deep chain's activations stay finite);
+    ``shared``: the second branch reuses the first branch's V-stage
+    (littlespec_ref/littlebit_itq_spec.py:298-309)."""
     from littlebit_b200.ops import Branch, PackedLinear
 
     g = torch.Generator(device=device).manual_seed(seed)
@@ -394,10 +396,11 @@ def build_pool(P: int, device, seed: int, ranks=RANKS, shared: bool = False):
                     w[:, -1] &= (1 << (cols % 32)) - 1
                 return w.to(torch.int32)
             sc = lambda n: (1 + 0.1 * torch.randn(n, generator=g, device=device)).abs()
+            mid, u1 = sc(r) / IN_F ** 0.5, sc(OUT_F) / (r * len(ranks)) ** 0.5
             if shared and i > 0:
-                brs.append(Branch(None, None, sc(r), words(OUT_F, r), sc(OUT_F), r))
+                brs.append(Branch(None, None, mid, words(OUT_F, r), u1, r))
             else:
-                brs.append(Branch(words(r, IN_F), sc(IN_F), sc(r), words(OUT_F, r), sc(OUT_F), r))
+                brs.append(Branch(words(r, IN_F), sc(IN_F), mid, words(OUT_F, r), u1, r))
         pool.append(PackedLinear(IN_F, OUT_F, brs))
     return pool
 
@@ -928,7 +931,14 @@ def run_ours(args):
     def step_program():  # the whole chain as one persistent program
         ops.linear_chain(pool, acts, ws=wsc, arr=arr_all, ptrs=ptrs)
 
+    fchain = ops.FusedChain(pool) if k <= 4 else None  # sign words copied once into its layout
+
+    def step_fused():  # n + 1 launches: layer i's U-stage with layer i+1's V partials
+        fchain.run(acts, ptrs=ptrs, stream=stream)
+
     execs = {"cluster": step_cluster, "kernels": step_kernels, "program": step_program}
+    if fchain is not None:
+        execs["fused"] = step_fused
     main_fn = execs[args.exec]
     sampler = ClockSampler(lrank)
     sampler.start()
@@ -944,8 +954,8 @@ def run_ours(args):
     for name, fn in execs.items():
         if name == args.exec:
             continue
-        if name == "cluster" and k > 4:
-            continue  # the cluster executor takes k <= 4
+        if name in ("cluster", "fused") and k > 4:
+            continue  # the cluster and fused executors take k <= 4
         exec_t[name] = timed_graph(fn, stream, args.warmup, args.steps, ws)
         if not torch.equal(acts[-1], y_main):
             raise RuntimeError(f"{name} and {args.exec} executors disagree")
@@ -1036,11 +1046,17 @@ def run_ours(args):
                        "tokens": k, "pool_layers": P,
                        "pool_mb": round(P * (packed + sum(4 * (IN_F + r + OUT_F) for r in RANKS)) / 1e6, 1),
                        "l2": "weight pool > 2x L2 (126 MB): no flush needed",
+                       "scales": "|N(1,0.1)|; mid / sqrt(in), u1 / sqrt(rank x branches) (unit gain: the "
+                                 "128-layer chain's activations stay finite, so the executors' outputs are "
+                                 "compared bit for bit)",
                        "parallelism": f"dp{ws} (independent replicas)",
                        "exec": {"program": "one persistent cooperative program per step (lbx_linear_chain)",
                                 "kernels": "two kernels per layer (V-stage, U-stage grids), PDL-chained",
                                 "cluster": "one split-rank cluster launch per layer (16-CTA clusters), "
-                                           "PDL-chained"}[args.exec]},
+                                           "PDL-chained",
+                                "fused": "one launch per layer (8-CTA clusters per 256 rows): layer i's "
+                                         "U-stage with layer i+1's V-stage partials, PDL-chained "
+                                         "(lbx_chain_fused)"}[args.exec]},
             "roofline": roof,
             "exec_gbs": exec_gbs,
             "floor": floor,
@@ -1059,7 +1075,7 @@ def run_ours(args):
             "decode": decode,
             "decode_70b": decode70,
             "row_shard": row_shard,
-            "gpu_launches": {"program": 1, "kernels": 2 * P, "cluster": P}[args.exec] * args.steps,
+            "gpu_launches": {"program": 1, "kernels": 2 * P, "cluster": P, "fused": P + 1}[args.exec] * args.steps,
             "clocks": clocks,
         }
         print(json.dumps(out))
@@ -1078,7 +1094,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--pool", type=int, default=128)
     ap.add_argument("--pdl", type=int, default=1)
-    ap.add_argument("--exec", default="kernels", choices=["kernels", "cluster", "program"],
+    ap.add_argument("--exec", default="kernels", choices=["kernels", "cluster", "program", "fused"],
                     help="cluster: one split-rank cluster launch per layer; kernels: one grid per stage; "
                          "program: each step is one persistent launch")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

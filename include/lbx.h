@@ -204,7 +204,20 @@ typedef struct lbx_attn_args {
   const float *rope_cs;      /* [n][head_dim/2] (cos, sin) pairs from
                                 lbx_rope_table for pos[], or NULL: computed
                                 in the kernel (same values)               */
+  /* Independent sequences in one launch (0 or 1: one sequence, as above).
+   * With n_seq = S > 1, n is the token count of EACH sequence and the rows
+   * of q, k_new, v_new, pos, tree_mask, rope_cs and out hold S*n tokens,
+   * sequence by sequence; sequence s's caches start cache_seq_stride
+   * elements after sequence s-1's (k_cache / v_cache are sequence 0's), and
+   * its cached-slot count is prefix_seq[s] (device; prefix_len bounds them
+   * all).  Each sequence's outputs are bit-identical to a launch of its
+   * own.  S <= LBX_ATTN_MAX_SEQ. */
+  int32_t n_seq;
+  int32_t _pad;
+  int64_t cache_seq_stride;
+  const int32_t *prefix_seq;
 } lbx_attn_args;
+#define LBX_ATTN_MAX_SEQ 256
 /* Workspace: zero-filled once at allocation (it holds self-resetting tickets). */
 size_t lbx_attn_workspace_size(const lbx_attn_args *a);
 int lbx_attn_decode(const lbx_attn_args *a, void *ws, size_t ws_bytes, cudaStream_t stream);
@@ -247,6 +260,30 @@ int lbx_accept_greedy_tree(const int64_t *cand, const int64_t *node_argmax,
 size_t lbx_linear_chain_workspace_size(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens);
 int lbx_linear_chain(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens, int32_t dtype,
                      void *const *acts, void *ws, size_t ws_bytes, cudaStream_t stream);
+
+/* ---- fused layer chain --------------------------------------------------
+ * No reference counterpart (the reference runs one layer per op call): a chain
+ * of single-projection layers, acts[i+1] = layer_i(acts[i]) as in
+ * lbx_linear_chain, as n_layers + 1 launches instead of two per layer.  Launch
+ * i runs layer i's U-stage and, from the outputs it has just formed, layer
+ * i+1's V-stage partial sums (one thread-block cluster of 8 CTAs per 256
+ * output rows; the first launch forms layer 0's partials from acts[0]).
+ * Every output is bit-identical to calling lbx_linear layer by layer.
+ * Requirements: in/out features multiples of 256 (in <= 8192), no prologue,
+ * store epilogue, 1-2 branches of at most 32 quantisation groups (128 ranks)
+ * together, 1..4 tokens, one activation dtype (LBX_F32 / LBX_BF16).
+ * lbx_chain_prepare writes, once, a copy of the chain's sign words laid out
+ * so that each CTA's share of a layer is contiguous (blob of
+ * lbx_chain_prepare_size bytes, 16-byte aligned); the layers' scale vectors
+ * are read from the descriptors.  The workspace (any contents) holds the
+ * partial sums between launches; calls sharing it must be ordered. */
+size_t lbx_chain_prepare_size(const lbx_proj *projs, int32_t n_layers);
+int lbx_chain_prepare(const lbx_proj *projs, int32_t n_layers, void *blob, size_t blob_bytes,
+                      cudaStream_t stream);
+size_t lbx_chain_fused_workspace_size(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens);
+int lbx_chain_fused(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens, int32_t dtype,
+                    void *const *acts, const void *blob, size_t blob_bytes, void *ws, size_t ws_bytes,
+                    cudaStream_t stream);
 
 /* ---- row-sharded LittleBitLinear over NVLink ----------------------------
  * No reference counterpart (the reference decodes on one CPU host): the
@@ -330,6 +367,25 @@ int lbx_forward(const lbx_model *m, const int64_t *tokens, int32_t n, int32_t st
                 const int32_t *start_dev, const int32_t *pos, const uint64_t *tree_mask,
                 float *hidden_out, float *logits, int64_t *argmax_out, void *ws,
                 size_t ws_bytes, cudaStream_t stream);
+
+/* Multi-sequence step (no reference counterpart: the reference decodes one
+ * sequence per process): n tokens of each of n_seq independent sequences in
+ * one step, so that every packed-weight read serves n_seq * n tokens (the
+ * linear calls batch LBX_MAX_TOKENS of them per launch).  Rows of tokens,
+ * pos, tree_mask and of the outputs are ordered sequence by sequence.
+ * Sequence s's KV caches start cache_seq_stride elements after sequence
+ * s-1's (the model's layer caches are sequence 0's; each is
+ * [kv_heads, max_seq, head_dim] bf16) and its first new slot is
+ * start_seq[s] (device int32; max_start bounds them all).  pos == NULL:
+ * rotary positions start_seq[s] + i.  tree_mask: each row's mask over its
+ * own sequence's n tokens, or NULL (causal).  Every sequence's outputs are
+ * bit-identical to an lbx_forward call for it alone.  Kernel path only;
+ * n_seq <= 64, n <= 64. */
+size_t lbx_forward_multi_workspace_size(const lbx_model *m, int32_t n_seq, int32_t n_tokens);
+int lbx_forward_multi(const lbx_model *m, const int64_t *tokens, int32_t n_seq, int32_t n, int32_t max_start,
+                      const int32_t *start_seq, int64_t cache_seq_stride, const int32_t *pos,
+                      const uint64_t *tree_mask, float *hidden_out, float *logits, int64_t *argmax_out,
+                      void *ws, size_t ws_bytes, cudaStream_t stream);
 
 /* Move KV rows inside the caches of every layer: for i < n, slot dst[i] <- slot
  * src[i] (all sources are read before any destination is written), used to

@@ -55,6 +55,7 @@ class AttnArgs(ctypes.Structure):
         ("pos", c_void_p), ("tree_mask", c_void_p),
         ("k_cache", c_void_p), ("v_cache", c_void_p), ("out", c_void_p),
         ("rope_cs", c_void_p),
+        ("n_seq", c_int32), ("_pad", c_int32), ("cache_seq_stride", c_int64), ("prefix_seq", c_void_p),
     ]
 
 
@@ -105,6 +106,11 @@ _SIGNATURES = {
     "lbx_linear_chain_workspace_size": (c_size_t, [POINTER(Proj), c_int32, c_int32]),
     "lbx_linear_chain": (c_int, [POINTER(Proj), c_int32, c_int32, c_int32, POINTER(c_void_p), c_void_p,
                                  c_size_t, c_void_p]),
+    "lbx_chain_prepare_size": (c_size_t, [POINTER(Proj), c_int32]),
+    "lbx_chain_prepare": (c_int, [POINTER(Proj), c_int32, c_void_p, c_size_t, c_void_p]),
+    "lbx_chain_fused_workspace_size": (c_size_t, [POINTER(Proj), c_int32, c_int32]),
+    "lbx_chain_fused": (c_int, [POINTER(Proj), c_int32, c_int32, c_int32, POINTER(c_void_p), c_void_p, c_size_t,
+                                c_void_p, c_size_t, c_void_p]),
     "lbx_linear_allgather": (c_int, [POINTER(Proj), POINTER(LinearArgs), c_int32, POINTER(c_void_p),
                                      c_int64, c_int32, c_int64, c_void_p, c_void_p, c_size_t, c_void_p]),
     "lbx_allgather_unpack": (c_int, [c_void_p, c_int64, c_int32, c_int32, c_int64, c_void_p, c_int64,
@@ -112,6 +118,10 @@ _SIGNATURES = {
     "lbx_forward_workspace_size": (c_size_t, [POINTER(Model), c_int32]),
     "lbx_forward": (c_int, [POINTER(Model), c_void_p, c_int32, c_int32, c_void_p, c_void_p,
                             c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "lbx_forward_multi_workspace_size": (c_size_t, [POINTER(Model), c_int32, c_int32]),
+    "lbx_forward_multi": (c_int, [POINTER(Model), c_void_p, c_int32, c_int32, c_int32, c_void_p, c_int64,
+                                  c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+                                  c_void_p]),
     "lbx_kv_move": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p,
                             c_void_p, c_int32, c_void_p]),
     "lbx_last_error": (c_int, [c_char_p, c_size_t]),

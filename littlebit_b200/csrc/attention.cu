@@ -48,6 +48,13 @@ struct AttnParams {
   float *part_o;     // [kvh][nchunk][R][d]
   float2 *part_ml;   // [kvh][nchunk][R]
   unsigned *ticket;  // [kvh][ATK_GROUPS], zero between launches
+  // independent sequences of one launch (nseq > 1): sequence s owns token rows
+  // [s*n, (s+1)*n), its caches start seq_stride elements after sequence s-1's,
+  // its cached-slot count is prefix_seq[s], and it has its own partials and
+  // tickets (part_seq / ml_seq elements and kvh * ATK_GROUPS words apart)
+  int nseq;
+  int64_t seq_stride, part_seq, ml_seq;
+  const int32_t *prefix_seq;
 };
 
 // cos/sin of pos * theta^(-2i/d) in double precision, rounded to float (HF
@@ -364,11 +371,39 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
   __syncthreads();  // the unit's shared buffers are free again
 }
 
+// the parameters of sequence s of a multi-sequence launch: one sequence's
+// attention exactly as a launch of its own would see it
+LBX_DEV AttnParams attn_seq(const AttnParams &p, int s) {
+  AttnParams q = p;
+  const int64_t rows = (int64_t)s * p.n;
+  q.q += rows * p.q_ld;
+  q.k_new += rows * p.kv_ld;
+  q.v_new += rows * p.kv_ld;
+  q.pos += rows;
+  if (q.tree) q.tree += rows;
+  if (q.rope) q.rope += rows * (p.d >> 1);
+  q.kc += s * p.seq_stride;
+  q.vc += s * p.seq_stride;
+  q.out += rows * p.heads * p.d;
+  q.prefix_dev = p.prefix_seq + s;
+  q.part_o += s * p.part_seq;
+  q.part_ml += s * p.ml_seq;
+  q.ticket += (int64_t)s * p.kvh * ATK_GROUPS;
+  q.nseq = 1;
+  return q;
+}
+
 __global__ void __launch_bounds__(ATHREADS) attn_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(16) float sm[];
   pdl_trigger();
   pdl_wait();
-  attn_unit(p, blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z), sm);
+  if (p.nseq > 1) {
+    const int s = blockIdx.z / p.ngroups, g = blockIdx.z - s * p.ngroups;
+    const AttnParams ps = attn_seq(p, s);
+    attn_unit(ps, blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * g), sm);
+  } else {
+    attn_unit(p, blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z), sm);
+  }
 }
 
 static int attn_sm_count() { return device_sm_count(); }
@@ -387,8 +422,9 @@ static void attn_fill(const lbx_attn_args *a, AttnParams &p) {
   // AMAX_ROWS, halved while the units would not cover the SMs twice (the
   // rows of one unit are scored one after another; each row's arithmetic is
   // the same whichever unit holds it)
+  p.nseq = a->n_seq > 1 ? a->n_seq : 1;
   int rows = p.R < AMAX_ROWS ? p.R : AMAX_ROWS;
-  while (rows > 1 && (int64_t)p.nchunk * p.kvh * ((p.R + rows - 1) / rows) < 2 * attn_sm_count() &&
+  while (rows > 1 && (int64_t)p.nchunk * p.kvh * p.nseq * ((p.R + rows - 1) / rows) < 2 * attn_sm_count() &&
          (p.R + (rows + 1) / 2 - 1) / ((rows + 1) / 2) <= ATK_GROUPS)
     rows = (rows + 1) / 2;
   p.rows = rows;
@@ -407,6 +443,8 @@ static void attn_fill(const lbx_attn_args *a, AttnParams &p) {
   p.vc = a->v_cache;
   p.out = a->out;
   p.prefix_dev = a->prefix_dev;
+  p.seq_stride = a->cache_seq_stride;
+  p.prefix_seq = a->prefix_seq;
 }
 
 // scratch: [tickets: fixed size and offset, whatever n is] [partials]
@@ -414,24 +452,26 @@ struct AttnWs {
   size_t tk, o, ml, total;
 };
 
-static size_t attn_ticket_bytes(int kv_heads) {
-  return ((size_t)kv_heads * ATK_GROUPS * 4 + 255) & ~(size_t)255;
+static size_t attn_ticket_bytes(int kv_heads, int n_seq = 1) {
+  return ((size_t)kv_heads * ATK_GROUPS * 4 * (n_seq > 1 ? n_seq : 1) + 255) & ~(size_t)255;
 }
 
+// partials: [seq][kvh][nchunk][R][d] floats, then [seq][kvh][nchunk][R] (max, sum)
 static size_t attn_partial_bytes(const lbx_attn_args *a, size_t *ml_off) {
   const int rep = a->heads / a->kv_heads;
   const int64_t R = (int64_t)a->n * rep;
   const int64_t nchunk = (a->prefix_len + a->n + ACH - 1) / ACH;
+  const int64_t S = a->n_seq > 1 ? a->n_seq : 1;
   auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
-  const size_t o = al((size_t)a->kv_heads * nchunk * R * a->head_dim * 4);
+  const size_t o = al((size_t)S * a->kv_heads * nchunk * R * a->head_dim * 4);
   if (ml_off) *ml_off = o;
-  return o + al((size_t)a->kv_heads * nchunk * R * 8);
+  return o + al((size_t)S * a->kv_heads * nchunk * R * 8);
 }
 
 static AttnWs attn_ws_layout(const lbx_attn_args *a) {
   AttnWs w;
   w.tk = 0;
-  w.o = attn_ticket_bytes(a->kv_heads);
+  w.o = attn_ticket_bytes(a->kv_heads, a->n_seq);
   size_t ml = 0;
   const size_t part = attn_partial_bytes(a, &ml);
   w.ml = w.o + ml;
@@ -453,6 +493,10 @@ static int attn_prep(const lbx_attn_args *a, void *partials, unsigned *tickets, 
                 "prefix_len + n exceeds max_seq");
   LBX_CHECK_ARG(a->q && a->k_new && a->v_new && a->pos && a->k_cache && a->v_cache && a->out,
                 "NULL pointer");
+  LBX_CHECK_ARG(a->n_seq <= 1 || (a->prefix_seq && a->cache_seq_stride >= (int64_t)a->kv_heads * a->max_seq *
+                                                                             a->head_dim),
+                "multi-sequence attention needs prefix_seq and a cache stride of at least one sequence's cache");
+  LBX_CHECK_ARG(a->n_seq >= 0 && a->n_seq <= LBX_ATTN_MAX_SEQ, "n_seq must be in [0,%d]", LBX_ATTN_MAX_SEQ);
   p = AttnParams{};
   attn_fill(a, p);
   LBX_CHECK_SUP(p.ngroups <= ATK_GROUPS, "too many query rows (n * heads/kv_heads)");
@@ -461,6 +505,8 @@ static int attn_prep(const lbx_attn_args *a, void *partials, unsigned *tickets, 
   p.part_o = reinterpret_cast<float *>(partials);
   p.part_ml = reinterpret_cast<float2 *>(reinterpret_cast<uint8_t *>(partials) + ml);
   p.ticket = tickets;
+  p.part_seq = (int64_t)p.kvh * p.nchunk * p.R * p.d;
+  p.ml_seq = (int64_t)p.kvh * p.nchunk * p.R;
   const int Rcap = p.rows;
   const int KP = p.d + 4;
   smem = ((size_t)(ACH + p.n) * KP + (size_t)(ACH + p.n) * p.d + (size_t)Rcap * KP + (size_t)Rcap * ACH) * 4 +
@@ -483,7 +529,7 @@ static int attn_launch(const lbx_attn_args *a, void *partials, unsigned *tickets
   LBX_CHECK_SUP(smem <= smax, "attention needs %zu bytes of shared memory (max %zu)", smem, smax);
   const bool pdl = a->use_pdl != 0;
   const cudaError_t e =
-      launch(attn_kernel, dim3(p.nchunk, p.kvh, p.ngroups), dim3(ATHREADS), smem, stream, pdl, p);
+      launch(attn_kernel, dim3(p.nchunk, p.kvh, p.ngroups * p.nseq), dim3(ATHREADS), smem, stream, pdl, p);
   return cuda_status(e, "attn launch");
 }
 

@@ -1,0 +1,697 @@
+// Fused layer chain: the U-stage of layer i and the V-stage of layer i+1 in
+// one launch.
+//
+// A chain of single-projection LittleBit layers, x_{i+1} = layer_i(x_i)
+// (quantization/modules/littlebit.py:95-121 per layer), runs as n + 1 launches
+// instead of 2n: a head launch computes layer 0's V-stage partials, then launch
+// i computes layer i's U-stage and, from its own outputs, layer i+1's V-stage
+// partials.  The grid is one thread-block cluster of FC_CS CTAs per 256 output
+// rows.
+//
+//  * V partials.  The V-stage quantises a = v2 ⊙ x with one scale per token
+//    per 256-column block and sums the blocks' exact integer products in block
+//    order (linear.cu, vstage_run).  Cluster c owns output rows [256c, 256c+256)
+//    of layer i, which are exactly block c of layer i+1's input, so it can form
+//    block c's product for every rank of layer i+1 as soon as its rows exist:
+//    P[c][t][r] = float(Σ_{j in block c} s_rj q_j) · (absmax / QMAX).  The CTAs
+//    of the cluster split the ranks (whole 128-rank groups).
+//  * z.  Launch i+1 adds the blocks' partials of its ranks in the V-stage's
+//    order (for each of the 16 block positions of a 4096-column pass, the passes
+//    in order, then the positions in order) and multiplies by mid: the V-stage's
+//    own float operations on the same values, so z has the same bits.
+//  * U.  Every CTA of a cluster owns some of the layer's 128-rank quantisation
+//    groups.  It derives each group's power-of-two exponent from the group's max
+//    |z| (as the U-stage does), quantises its groups and contracts them with the
+//    cluster's 256 U rows into exact int32 sums.  The sums and the exponents go
+//    to every CTA of the cluster over distributed shared memory; after one
+//    cluster barrier each CTA rounds every group to its branch's coarsest
+//    exponent with the U-stage's integer shift and forms y for all 256 rows with
+//    the U-stage's epilogue expression (u_result).  Exact integers add the same
+//    in any order, so y has the bits of the two stage grids.
+//  * Each CTA stores its 32 rows of y and quantises the cluster's 256 values
+//    (one block of layer i+1's input) for the next partials.
+//
+// Per layer this is one grid boundary and one cluster barrier, against two grid
+// boundaries for the stage grids.  Weights are copied into shared memory from a
+// prepared blob (lbx_chain_prepare) in which every CTA's share of U and V is
+// contiguous; the copies are issued before griddepcontrol.wait.
+
+#include <vector>
+
+namespace lbx {
+
+constexpr int FC_CS = 8;          // CTAs per cluster
+constexpr int FC_ROWS = 256;      // output rows per cluster (= one 256-column V block of the next layer)
+constexpr int FC_GMAX = 4;        // 128-rank groups per CTA, U side and V side
+constexpr int FC_GTOT = FC_CS * FC_GMAX;
+constexpr int FC_MAXK = 4;        // tokens per launch (one MMA column block)
+constexpr int FC_NBLK = 32;       // 256-column input blocks of a layer (in_features <= 8192)
+constexpr int FC_THREADS = 512;
+constexpr int FC_VPITCH = 12;     // words per V row in the blob (8 used: conflict-free fragment loads)
+constexpr int FC_UGW = FC_ROWS * 4;     // words of one U group slot (256 rows x 4 words)
+constexpr int FC_VGW = 128 * FC_VPITCH; // words of one V group slot (128 ranks x 12 words)
+
+struct FcGroup {  // one 128-rank quantisation group of a branch (U side)
+  int b;          // branch
+  int n;          // ranks in the group (<= 128)
+  int r0;         // first rank within the branch
+  int pidx;       // its first rank in the partial rank space
+};
+
+struct FcParams {
+  // U side of layer i (absent in the head launch)
+  const uint32_t *ublob;  // [N/256][ng][256 rows][4 words]
+  const float *u1[2];
+  const float *mid[2];
+  const float *bias;
+  const float *pin;       // partials of layer i: [nblk_in][k][pin_cols]
+  void *y;                // [k][N]
+  FcGroup g[FC_GTOT];     // groups in slot order (the CTAs' shares contiguous)
+  int gstart[FC_CS + 1];
+  int ng, nbr, pin_cols, nblk_in;
+  // V side of layer i+1 (absent in the last launch)
+  const uint32_t *vblob;  // [N/256][nvg][128 ranks][FC_VPITCH words]
+  const float *v2[2];     // [N] input scale of each V segment of layer i+1 (branch 0; branch 1
+                          // when it has its own V): every segment stages its own a = v2 * x
+  float *pout;            // [N/256][k][pout_cols]
+  int vg_p0[FC_GTOT];     // first rank (partial space) of each V group, slot order
+  int vg_n[FC_GTOT];
+  int vg_seg[FC_GTOT];    // V segment of each V group
+  int vstart[FC_CS + 1];
+  int nvg, nvseg, pout_cols;
+  // head launch: layer 0's input
+  const void *x;          // [k][N]
+  int k, adt, N;          // tokens, activation dtype, features of the rows this launch owns
+  int has_u, has_v;
+};
+
+// shared-memory layout of one CTA (bytes; weights first, then scratch)
+struct FcSmem {
+  int uw, vw, mid, u1, bias, v2, wbytes;      // weight region
+  int zf, actu, vx, ex, sa, actv, total;      // scratch
+};
+
+__host__ __device__ inline FcSmem fc_smem(int k, int ng) {
+  FcSmem L;
+  const int ws = act_ws(2 * k);
+  int o = 0;
+  L.uw = o;   o += FC_GMAX * FC_UGW * 4;
+  L.vw = o;   o += FC_GMAX * FC_VGW * 4;
+  L.mid = o;  o += FC_GMAX * 128 * 4;
+  L.u1 = o;   o += 2 * FC_ROWS * 4;
+  L.bias = o; o += FC_ROWS * 4;
+  L.v2 = o;   o += 2 * FC_ROWS * 4;
+  L.wbytes = o;
+  L.zf = o;   o += FC_GMAX * k * 128 * 4;
+  L.actu = o; o += FC_GMAX * 4 * ws * 4;
+  L.vx = o;   o += ng * FC_ROWS * k * 4;
+  L.ex = o;   o += ((ng * k * 4 + 15) / 16) * 16;
+  L.sa = o;   o += 2 * k * FC_ROWS * 4;
+  L.actv = o; o += 2 * 8 * ws * 4;
+  L.total = o;
+  return L;
+}
+
+__global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant__ FcParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int s_gmax[FC_GMAX][FC_MAXK];
+  __shared__ int s_usq[FC_GMAX][FC_MAXK];
+  __shared__ int s_ec[2][FC_MAXK];
+  __shared__ int s_vmax[2][FC_MAXK];
+  __shared__ int s_vsq[2][FC_MAXK];
+  __shared__ int s_ok;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int j = cl_rank();
+  const int c = blockIdx.x / FC_CS;
+  const int k = p.k;
+  const int ncols = 2 * k;
+  const int ws = act_ws(ncols);
+  const FcSmem L = fc_smem(k, p.ng);
+  uint32_t *uw = reinterpret_cast<uint32_t *>(smem + L.uw);
+  uint32_t *vw = reinterpret_cast<uint32_t *>(smem + L.vw);
+  float *smid = reinterpret_cast<float *>(smem + L.mid);
+  float *su1 = reinterpret_cast<float *>(smem + L.u1);
+  float *sbias = reinterpret_cast<float *>(smem + L.bias);
+  float *sv2 = reinterpret_cast<float *>(smem + L.v2);
+  float *zf = reinterpret_cast<float *>(smem + L.zf);        // [slot][t][128]
+  uint32_t *actu = reinterpret_cast<uint32_t *>(smem + L.actu);  // [slot][4 words][ws]
+  int *vx = reinterpret_cast<int *>(smem + L.vx);            // [group][row][t] exact sums
+  int *ex = reinterpret_cast<int *>(smem + L.ex);            // [group][t] exponents
+  float *sa = reinterpret_cast<float *>(smem + L.sa);        // [seg][t][256] a = v2 * x of the block
+  uint32_t *actv = reinterpret_cast<uint32_t *>(smem + L.actv);  // [seg][8 words][ws]
+
+  LBX_PROBE(20);
+  // cluster barrier A: this CTA has started, so the others may write into its
+  // shared memory (they do so only after waiting on A)
+  if (p.has_u) cl_arrive_relaxed();
+  const int gs = p.gstart[j], myg = p.has_u ? p.gstart[j + 1] - gs : 0;
+  const int vs = p.vstart[j], myv = p.has_v ? p.vstart[j + 1] - vs : 0;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (tid < FC_GMAX * FC_MAXK) {
+    (&s_gmax[0][0])[tid] = 0;
+    (&s_usq[0][0])[tid] = 0;
+  }
+  if (tid < 2 * FC_MAXK) {
+    (&s_vmax[0][0])[tid] = 0;
+    (&s_vsq[0][0])[tid] = 0;
+  }
+  __syncthreads();
+  // ---- weights (independent of every activation): before the dependency wait
+  if (tid == 0) {
+    uint32_t bytes = 0;
+    if (p.has_u) {
+      bytes += (uint32_t)myg * FC_UGW * 4u + (uint32_t)p.nbr * FC_ROWS * 4u + (p.bias ? FC_ROWS * 4u : 0u);
+      for (int s = 0; s < myg; ++s) bytes += (uint32_t)p.g[gs + s].n * 4u;
+    }
+    if (p.has_v) bytes += (uint32_t)myv * FC_VGW * 4u + (uint32_t)p.nvseg * FC_ROWS * 4u;
+    mbar_arrive_expect_tx(&bar, bytes);
+  }
+  __syncthreads();
+  if (warp == 0 && p.has_u) {
+    if (lane < myg) {
+      const FcGroup G = p.g[gs + lane];
+      bulk_g2s(uw + lane * FC_UGW, p.ublob + ((size_t)c * p.ng + gs + lane) * FC_UGW, FC_UGW * 4u, &bar);
+      bulk_g2s(smid + lane * 128, p.mid[G.b] + G.r0, (uint32_t)G.n * 4u, &bar);
+    } else if (lane == 8 || (lane == 9 && p.nbr > 1)) {
+      bulk_g2s(su1 + (lane - 8) * FC_ROWS, p.u1[lane - 8] + (size_t)c * FC_ROWS, FC_ROWS * 4u, &bar);
+    } else if (lane == 10 && p.bias) {
+      bulk_g2s(sbias, p.bias + (size_t)c * FC_ROWS, FC_ROWS * 4u, &bar);
+    }
+  } else if (warp == 1 && p.has_v) {
+    if (lane < myv)
+      bulk_g2s(vw + lane * FC_VGW, p.vblob + ((size_t)c * p.nvg + vs + lane) * FC_VGW, FC_VGW * 4u, &bar);
+    else if (lane == 8 || (lane == 9 && p.nvseg > 1))
+      bulk_g2s(sv2 + (lane - 8) * FC_ROWS, p.v2[lane - 8] + (size_t)c * FC_ROWS, FC_ROWS * 4u, &bar);
+  }
+  pdl_trigger();
+  pdl_wait();  // the previous launch's partials (and outputs) are complete
+  LBX_PROBE(21);
+  if (tid == 0) s_ok = mbar_wait_bounded(&bar, 0, 0x131) ? 1 : 0;
+  __syncthreads();
+  const bool ok = s_ok != 0;
+  LBX_PROBE(22);
+
+  if (p.has_u) {
+    // ---- z of this CTA's groups: the blocks' partials in the V-stage order
+    const int nblk = p.nblk_in;
+    const int npass = (nblk + 15) / 16;
+    for (int it = tid; it < myg * k * 128; it += FC_THREADS) {
+      const int sl = it / (k * 128), rem = it - sl * k * 128;
+      const int t = rem >> 7, r = rem & 127;
+      const FcGroup G = p.g[gs + sl];
+      float z = 0.f;
+      if (r < G.n) {
+        const float *src = p.pin + (size_t)t * p.pin_cols + G.pidx + r;
+        const size_t bstride = (size_t)k * p.pin_cols;
+        float pv[FC_NBLK];
+#pragma unroll
+        for (int b = 0; b < FC_NBLK; ++b) pv[b] = b < nblk ? __ldcg(src + b * bstride) : 0.f;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < 16; ++w) {
+          float tw = 0.f;
+#pragma unroll
+          for (int ps = 0; ps < FC_NBLK / 16; ++ps)
+            if (ps < npass && ps * 16 + w < nblk) tw += pv[ps * 16 + w];
+          v += tw;
+        }
+        z = smid[sl * 128 + r] * v;
+      }
+      zf[(sl * k + t) * 128 + r] = z;
+      // a warp's 32 items share (slot, token): the group maximum
+      const float m = warp_max(fabsf(z));
+      if (lane == 0) atomicMax(&s_gmax[sl][t], __float_as_int(m));
+    }
+    __syncthreads();
+    LBX_PROBE(23);
+    // exponents of this CTA's groups, to every CTA of the cluster
+    if (tid < myg * k) {
+      const int sl = tid / k, t = tid - sl * k;
+      const float m = __int_as_float(s_gmax[sl][t]);
+      s_gmax[sl][t] = m > 0.f ? u_group_exp(m) : UE_NONE;  // (now the exponent)
+    }
+    __syncthreads();
+    cl_wait();  // barrier A: every CTA of the cluster has started
+    if (tid < myg * k * FC_CS) {
+      const int d = tid / (myg * k), rem = tid - d * myg * k;
+      const int sl = rem / k, t = rem - sl * k;
+      *cl_map_w(ex + (gs + sl) * k + t, d) = s_gmax[sl][t];
+    }
+    // ---- digits of this CTA's groups (the U-stage's layout and rounding)
+    for (int it = warp; it < myg * k; it += FC_THREADS / 32) {
+      const int sl = it / k, t = it - sl * k;
+      const int Wd = lane >> 3, slot = lane & 7;
+      const int e = s_gmax[sl][t];
+      const float sc = e == UE_NONE ? 0.f : pow2f(e);
+      int hi[4], lo[4], sq = 0;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const int pos = 32 * Wd + 16 * (slot >> 2) + (slot & 3) + 4 * q4;
+        const int qv = __float2int_rn(zf[(sl * k + t) * 128 + pos] * sc);
+        sq += qv;
+        split_digits(qv, hi[q4], lo[q4]);
+      }
+      uint32_t *aw = actu + (sl * 4 + Wd) * ws + 2 * t;
+      aw[slot * ncols] = pack4(hi[0], hi[1], hi[2], hi[3]);
+      aw[slot * ncols + 1] = pack4(lo[0], lo[1], lo[2], lo[3]);
+      sq = __reduce_add_sync(0xffffffffu, sq);
+      if (lane == 0) s_usq[sl][t] = sq;
+    }
+    __syncthreads();
+    LBX_PROBE(24);
+    // ---- contraction: warp w = output rows 16w..16w+15 of the cluster, each
+    // of this CTA's groups on its own (exact int32), to every CTA's exchange
+    if (ok && warp < FC_ROWS / 16) {
+      const int g = lane >> 2, q = lane & 3;
+      for (int sl = 0; sl < myg; ++sl) {
+        int acc[1][4] = {{0, 0, 0, 0}};
+        const int G0[1] = {0};
+        const uint32_t *tile = uw + sl * FC_UGW + warp * 16 * 4;
+        sign_mma1<1>(acc, tile + g * 4, tile + (g + 8) * 4, actu + sl * 4 * ws, ws, ncols, G0, lane);
+        if (q < k) {
+          const int sq = s_usq[sl][q];
+          const int va = sq + 2 * (256 * acc[0][0] + acc[0][1]);
+          const int vb = sq + 2 * (256 * acc[0][2] + acc[0][3]);
+          int *base = vx + ((gs + sl) * FC_ROWS + warp * 16 + g) * k + q;
+#pragma unroll
+          for (int d = 0; d < FC_CS; ++d) {
+            int *rb = cl_map_w(base, d);
+            rb[0] = va;
+            rb[8 * k] = vb;
+          }
+        }
+      }
+    }
+    // cluster barrier B: every CTA's sums and exponents are in place
+    LBX_PROBE(25);
+    cl_arrive();
+    cl_wait();
+    LBX_PROBE(26);
+    // ---- coarsest exponent of each branch, then y for all 256 rows
+    if (tid < 2 * k) {
+      const int b = tid / k, t = tid - b * k;
+      int ec = UE_NONE;
+      for (int G = 0; G < p.ng; ++G)
+        if (p.g[G].b == b) ec = min(ec, ex[G * k + t]);
+      s_ec[b][t] = ec == UE_NONE ? 0 : ec;
+    }
+    __syncthreads();
+    for (int it = tid; it < FC_ROWS * k; it += FC_THREADS) {
+      const int t = it / FC_ROWS, r = it - t * FC_ROWS;
+      int I[2] = {0, 0};
+      for (int G = 0; G < p.ng; ++G) {
+        const int e = ex[G * k + t];
+        if (e != UE_NONE) {
+          const int b = p.g[G].b;
+          I[b] += rshr(vx[(G * FC_ROWS + r) * k + t], e - s_ec[b][t]);
+        }
+      }
+      float v = u_result(su1[r], I[0], s_ec[0][t], p.nbr > 1, su1[FC_ROWS + r], I[1], s_ec[1][t],
+                         p.bias != nullptr, sbias[r]);
+      if (!ok) v = __int_as_float(0x7fc00000);
+      float xv = v;  // the next layer's input value: as stored
+      const size_t off = (size_t)t * p.N + (size_t)c * FC_ROWS + r;
+      if (p.adt == LBX_F32) {
+        if ((r >> 5) == j) reinterpret_cast<float *>(p.y)[off] = v;
+      } else {
+        const uint16_t hb = f32_to_bf16(v);
+        if ((r >> 5) == j) reinterpret_cast<uint16_t *>(p.y)[off] = hb;
+        xv = bf16_to_f32(hb);
+      }
+      if (p.has_v)
+        for (int sg = 0; sg < p.nvseg; ++sg) sa[(sg * k + t) * FC_ROWS + r] = xv * sv2[sg * FC_ROWS + r];
+    }
+  } else if (p.has_v) {
+    // head launch: block c of layer 0's input
+    for (int it = tid; it < FC_ROWS * k; it += FC_THREADS) {
+      const int t = it / FC_ROWS, r = it - t * FC_ROWS;
+      const float xx = load_act(p.x, p.adt, (int64_t)t * p.N + (int64_t)c * FC_ROWS + r);
+      for (int sg = 0; sg < p.nvseg; ++sg) sa[(sg * k + t) * FC_ROWS + r] = xx * sv2[sg * FC_ROWS + r];
+    }
+  }
+  if (!p.has_v) return;
+
+  // ---- V-stage partials of the next layer for this CTA's rank groups
+  __syncthreads();
+  LBX_PROBE(27);
+  for (int it = tid; it < p.nvseg * k * FC_ROWS; it += FC_THREADS) {  // per (segment, token) block maximum
+    const int st = it / FC_ROWS;
+    const float m = warp_max(fabsf(sa[it]));
+    if (lane == 0) atomicMax(&s_vmax[st / k][st % k], __float_as_int(m));
+  }
+  __syncthreads();
+  for (int it = tid; it < p.nvseg * k * 64; it += FC_THREADS) {  // digits: (segment, token, word, slot)
+    const int st = it >> 6, Wd = (it >> 3) & 7, slot = it & 7;
+    const int sg = st / k, t = st % k;
+    const float m = __int_as_float(s_vmax[sg][t]);
+    const float sc = m > 0.f ? QMAX / m : 0.f;
+    int hi[4], lo[4], sq = 0;
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4) {
+      const int pos = 32 * Wd + 16 * (slot >> 2) + (slot & 3) + 4 * q4;
+      const int qv = __float2int_rn(sa[st * FC_ROWS + pos] * sc);
+      sq += qv;
+      split_digits(qv, hi[q4], lo[q4]);
+    }
+    uint32_t *aw = actv + (sg * 8 + Wd) * ws + 2 * t;
+    aw[slot * ncols] = pack4(hi[0], hi[1], hi[2], hi[3]);
+    aw[slot * ncols + 1] = pack4(lo[0], lo[1], lo[2], lo[3]);
+    sq = __reduce_add_sync(0xffffffffu, sq);  // a warp's 32 items share (segment, token)
+    if (lane == 0) atomicAdd(&s_vsq[sg][t], sq);
+  }
+  __syncthreads();
+  LBX_PROBE(28);
+  if (!ok) return;
+  const int g = lane >> 2, q = lane & 3;
+  for (int mt = warp; mt < myv * 8; mt += FC_THREADS / 32) {
+    const int sl = mt >> 3, rt = (mt & 7) * 16;
+    const int sg = p.vg_seg[vs + sl];
+    int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+    const int G01[2] = {0, 1};
+    const uint32_t *tile = vw + sl * FC_VGW + rt * FC_VPITCH;
+    sign_mma1<2>(acc, tile + g * FC_VPITCH, tile + (g + 8) * FC_VPITCH, actv + sg * 8 * ws, ws, ncols, G01,
+                 lane);
+    if (q < k) {
+      const int sq = s_vsq[sg][q];
+      const float inv = __int_as_float(s_vmax[sg][q]) / QMAX;
+      const int ia = sq + 2 * (256 * (acc[0][0] + acc[1][0]) + (acc[0][1] + acc[1][1]));
+      const int ib = sq + 2 * (256 * (acc[0][2] + acc[1][2]) + (acc[0][3] + acc[1][3]));
+      const int n = p.vg_n[vs + sl];
+      float *dst = p.pout + ((size_t)c * k + q) * p.pout_cols + p.vg_p0[vs + sl] + rt;
+      if (rt + g < n) dst[g] = 0.f + __fmul_rn(__int2float_rn(ia), inv);
+      if (rt + g + 8 < n) dst[g + 8] = 0.f + __fmul_rn(__int2float_rn(ib), inv);
+    }
+  }
+  LBX_PROBE(29);
+}
+
+// ---------------------------------------------------------------------------
+// host side: the plan of a layer (groups, their owners, blob offsets)
+// ---------------------------------------------------------------------------
+struct FcPlan {
+  int ng, nvg, nbr, pcols;
+  FcGroup g[FC_GTOT];
+  int gstart[FC_CS + 1];
+  int vg_seg[FC_GTOT], vg_r0[FC_GTOT], vg_p0[FC_GTOT], vg_n[FC_GTOT];
+  int vstart[FC_CS + 1];
+  size_t ublob_words, vblob_words;  // per layer
+};
+
+// Deal `n` items with sizes sz[] to FC_CS owners, largest first to the least
+// loaded owner (at most FC_GMAX each); order[] receives the items owner by owner.
+static bool fc_deal(int n, const int *sz, int *order, int *start) {
+  int owner[FC_GTOT], load[FC_CS] = {}, cnt[FC_CS] = {}, idx[FC_GTOT];
+  for (int i = 0; i < n; ++i) idx[i] = i;
+  std::stable_sort(idx, idx + n, [&](int a, int b) { return sz[a] > sz[b]; });
+  for (int ii = 0; ii < n; ++ii) {
+    const int i = idx[ii];
+    int best = -1;
+    for (int o = 0; o < FC_CS; ++o)
+      if (cnt[o] < FC_GMAX && (best < 0 || load[o] < load[best])) best = o;
+    if (best < 0) return false;
+    owner[i] = best;
+    load[best] += sz[i];
+    ++cnt[best];
+  }
+  int pos = 0;
+  for (int o = 0; o < FC_CS; ++o) {
+    start[o] = pos;
+    for (int i = 0; i < n; ++i)
+      if (owner[i] == o) order[pos++] = i;
+  }
+  start[FC_CS] = pos;
+  return true;
+}
+
+static int fc_plan(const lbx_proj &pr, FcPlan &P) {
+  P = FcPlan{};
+  LBX_CHECK_SUP(pr.in_features % FC_ROWS == 0 && pr.out_features % FC_ROWS == 0,
+                "fused chain: in/out features must be multiples of %d", FC_ROWS);
+  LBX_CHECK_SUP(pr.in_features / FC_ROWS <= FC_NBLK, "fused chain: in_features must be <= %d", FC_NBLK * FC_ROWS);
+  P.nbr = pr.n_branches;
+  const bool shared = pr.n_branches == 2 && !pr.br[1].v_sign;
+  // partial rank space: branch 0's ranks, then branch 1's when it has its own V
+  const int pbase[2] = {0, shared ? 0 : pr.br[0].rank};
+  P.pcols = pr.br[0].rank + (pr.n_branches == 2 && !shared ? pr.br[1].rank : 0);
+  FcGroup all[FC_GTOT];
+  int ng = 0;
+  for (int b = 0; b < pr.n_branches; ++b)
+    for (int r0 = 0; r0 < pr.br[b].rank; r0 += 128) {
+      LBX_CHECK_SUP(ng < FC_GTOT, "fused chain: more than %d quantisation groups in a layer", FC_GTOT);
+      all[ng++] = FcGroup{b, std::min(128, pr.br[b].rank - r0), r0, pbase[b] + r0};
+    }
+  int sz[FC_GTOT], order[FC_GTOT];
+  for (int i = 0; i < ng; ++i) sz[i] = all[i].n;
+  LBX_CHECK_SUP(fc_deal(ng, sz, order, P.gstart), "fused chain: groups do not fit %d per CTA", FC_GMAX);
+  for (int i = 0; i < ng; ++i) P.g[i] = all[order[i]];
+  P.ng = ng;
+  // V groups over the partial rank space
+  int vseg[FC_GTOT], vr0[FC_GTOT], vp0[FC_GTOT], vn[FC_GTOT], nvg = 0;
+  const int nseg = shared || pr.n_branches == 1 ? 1 : 2;
+  for (int sgi = 0; sgi < nseg; ++sgi)
+    for (int r0 = 0; r0 < pr.br[sgi].rank; r0 += 128) {
+      LBX_CHECK_SUP(nvg < FC_GTOT, "fused chain: more than %d V groups in a layer", FC_GTOT);
+      vseg[nvg] = sgi;
+      vr0[nvg] = r0;
+      vp0[nvg] = pbase[sgi] + r0;
+      vn[nvg] = std::min(128, pr.br[sgi].rank - r0);
+      ++nvg;
+    }
+  LBX_CHECK_SUP(fc_deal(nvg, vn, order, P.vstart), "fused chain: V groups do not fit %d per CTA", FC_GMAX);
+  for (int i = 0; i < nvg; ++i) {
+    P.vg_seg[i] = vseg[order[i]];
+    P.vg_r0[i] = vr0[order[i]];
+    P.vg_p0[i] = vp0[order[i]];
+    P.vg_n[i] = vn[order[i]];
+  }
+  P.nvg = nvg;
+  P.ublob_words = (size_t)(pr.out_features / FC_ROWS) * ng * FC_UGW;
+  P.vblob_words = (size_t)(pr.in_features / FC_ROWS) * nvg * FC_VGW;
+  return LBX_OK;
+}
+
+static int fc_validate(const lbx_proj *projs, int n_layers) {
+  LBX_CHECK_ARG(projs && n_layers >= 1, "need at least one layer");
+  int rc = validate(projs, 1);
+  if (rc) return rc;
+  for (int i = 0; i < n_layers; ++i) {
+    rc = validate(projs + i, 1);
+    if (rc) return rc;
+    if (i) LBX_CHECK_ARG(projs[i].in_features == projs[i - 1].out_features,
+                         "layer %d: in_features %d != previous out_features %d", i, projs[i].in_features,
+                         projs[i - 1].out_features);
+  }
+  return LBX_OK;
+}
+
+// blob of every layer: its U part (consumed by the layer's own launch) then
+// its V part (consumed by the launch before it)
+static size_t fc_blob_words(const lbx_proj *projs, int n_layers, size_t *uoff, size_t *voff) {
+  size_t tot = 0;
+  for (int i = 0; i < n_layers; ++i) {
+    FcPlan P;
+    if (fc_plan(projs[i], P)) return 0;
+    if (uoff) uoff[i] = tot;
+    tot += (P.ublob_words + 63) & ~(size_t)63;
+    if (voff) voff[i] = tot;
+    tot += (P.vblob_words + 63) & ~(size_t)63;
+  }
+  return tot;
+}
+
+// U part: [N/256][slot][256 rows][4 words] (words past the branch's row are 0)
+__global__ void fc_pack_u_kernel(const int32_t *u0, const int32_t *u1, int w0, int w1, FcPlan P, int nrows_blk,
+                                 uint32_t *dst) {
+  const size_t total = (size_t)nrows_blk * P.ng * FC_ROWS * 4;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int w = (int)(i & 3);
+    const size_t rr = i >> 2;
+    const int row = (int)(rr % FC_ROWS);
+    const size_t cs = rr / FC_ROWS;
+    const int s = (int)(cs % P.ng), c = (int)(cs / P.ng);
+    const FcGroup G = P.g[s];
+    const int word = G.r0 / 32 + w;
+    const int words = G.b ? w1 : w0;
+    const int32_t *src = G.b ? u1 : u0;
+    dst[i] = word < words ? (uint32_t)src[(size_t)(c * FC_ROWS + row) * words + word] : 0u;
+  }
+}
+
+// V part: [K/256][slot][128 ranks][FC_VPITCH words] (rows past the group and
+// pad words are 0)
+__global__ void fc_pack_v_kernel(const int32_t *v0, const int32_t *v1, int Wv, FcPlan P, int nblk, uint32_t *dst) {
+  const size_t total = (size_t)nblk * P.nvg * 128 * FC_VPITCH;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int w = (int)(i % FC_VPITCH);
+    const size_t rr = i / FC_VPITCH;
+    const int r = (int)(rr % 128);
+    const size_t cs = rr / 128;
+    const int s = (int)(cs % P.nvg), c = (int)(cs / P.nvg);
+    const int32_t *src = P.vg_seg[s] ? v1 : v0;
+    uint32_t v = 0u;
+    if (w < 8 && r < P.vg_n[s]) v = (uint32_t)src[(size_t)(P.vg_r0[s] + r) * Wv + c * 8 + w];
+    dst[i] = v;
+  }
+}
+
+static size_t fc_ws_bytes(const lbx_proj *projs, int n_layers, int k) {
+  size_t mx = 0;
+  for (int i = 0; i < n_layers; ++i) {
+    FcPlan P;
+    if (fc_plan(projs[i], P)) return 0;
+    mx = std::max(mx, (size_t)(projs[i].in_features / FC_ROWS) * k * P.pcols * 4);
+  }
+  return 2 * al256(mx);
+}
+
+}  // namespace lbx
+
+extern "C" size_t lbx_chain_prepare_size(const lbx_proj *projs, int32_t n_layers) {
+  using namespace lbx;
+  if (fc_validate(projs, n_layers)) return 0;
+  return fc_blob_words(projs, n_layers, nullptr, nullptr) * 4;
+}
+
+extern "C" int lbx_chain_prepare(const lbx_proj *projs, int32_t n_layers, void *blob, size_t blob_bytes,
+                                 cudaStream_t stream) {
+  using namespace lbx;
+  int rc = fc_validate(projs, n_layers);
+  if (rc) return rc;
+  std::vector<size_t> uo(n_layers), vo(n_layers);
+  const size_t words = fc_blob_words(projs, n_layers, uo.data(), vo.data());
+  if (!words) return LBX_EUNSUPPORTED;  // (the reason is in lbx_last_error)
+  LBX_CHECK_ARG(blob && aligned16(blob) && blob_bytes >= words * 4, "blob too small (%zu < %zu) or unaligned",
+                blob_bytes, words * 4);
+  uint32_t *b = reinterpret_cast<uint32_t *>(blob);
+  for (int i = 0; i < n_layers; ++i) {
+    const lbx_proj &pr = projs[i];
+    FcPlan P;
+    rc = fc_plan(pr, P);
+    if (rc) return rc;
+    const int w0 = (pr.br[0].rank + 31) / 32, w1 = pr.n_branches > 1 ? (pr.br[1].rank + 31) / 32 : 0;
+    fc_pack_u_kernel<<<296, 256, 0, stream>>>(pr.br[0].u_sign, pr.n_branches > 1 ? pr.br[1].u_sign : nullptr, w0,
+                                              w1, P, pr.out_features / FC_ROWS, b + uo[i]);
+    const bool own1 = pr.n_branches > 1 && pr.br[1].v_sign;
+    fc_pack_v_kernel<<<296, 256, 0, stream>>>(pr.br[0].v_sign, own1 ? pr.br[1].v_sign : nullptr,
+                                              pr.in_features / 32, P, pr.in_features / FC_ROWS, b + vo[i]);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_status(e, "chain prepare launch");
+  }
+  return LBX_OK;
+}
+
+extern "C" size_t lbx_chain_fused_workspace_size(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens) {
+  using namespace lbx;
+  if (fc_validate(projs, n_layers) || n_tokens < 1 || n_tokens > FC_MAXK) return 0;
+  return fc_ws_bytes(projs, n_layers, n_tokens);
+}
+
+extern "C" int lbx_chain_fused(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens, int32_t dtype,
+                               void *const *acts, const void *blob, size_t blob_bytes, void *ws, size_t ws_bytes,
+                               cudaStream_t stream) {
+  using namespace lbx;
+  int rc = fc_validate(projs, n_layers);
+  if (rc) return rc;
+  LBX_CHECK_SUP(n_tokens >= 1 && n_tokens <= FC_MAXK, "fused chain: 1..%d tokens", FC_MAXK);
+  LBX_CHECK_ARG(dtype == LBX_F32 || dtype == LBX_BF16, "bad dtype");
+  LBX_CHECK_ARG(acts && blob, "NULL argument");
+  for (int i = 0; i <= n_layers; ++i) LBX_CHECK_ARG(acts[i], "acts[%d] is NULL", i);
+  std::vector<size_t> uo(n_layers), vo(n_layers);
+  const size_t words = fc_blob_words(projs, n_layers, uo.data(), vo.data());
+  if (!words) return LBX_EUNSUPPORTED;  // (the reason is in lbx_last_error)
+  LBX_CHECK_ARG(blob_bytes >= words * 4, "blob too small (%zu < %zu)", blob_bytes, words * 4);
+  const size_t need = fc_ws_bytes(projs, n_layers, n_tokens);
+  LBX_CHECK_ARG(ws && ws_bytes >= need, "workspace too small (%zu < %zu)", ws_bytes, need);
+  const int k = n_tokens;
+  static DevCache<size_t> smax_cache;
+  size_t smax = 0;
+  rc = smax_cache.get(smax, [](size_t &out) {
+    const cudaError_t e = allow_max_smem(fc_kernel, &out);
+    return e != cudaSuccess ? cuda_status(e, "fused chain smem attribute") : (int)LBX_OK;
+  });
+  if (rc) return rc;
+  const uint32_t *b = reinterpret_cast<const uint32_t *>(blob);
+  float *part[2] = {reinterpret_cast<float *>(ws), reinterpret_cast<float *>(ws) + need / 8};
+  std::vector<FcPlan> plan(n_layers);
+  for (int i = 0; i < n_layers; ++i) {
+    rc = fc_plan(projs[i], plan[i]);
+    if (rc) return rc;
+  }
+  for (int i = -1; i < n_layers; ++i) {
+    FcParams p = {};
+    p.k = k;
+    p.adt = dtype;
+    const int nx = i + 1;  // the layer whose V partials this launch forms
+    if (i >= 0) {
+      const lbx_proj &pr = projs[i];
+      const FcPlan &P = plan[i];
+      p.has_u = 1;
+      p.ublob = b + uo[i];
+      p.nbr = pr.n_branches;
+      for (int bb = 0; bb < pr.n_branches; ++bb) {
+        p.u1[bb] = pr.br[bb].u1;
+        p.mid[bb] = pr.br[bb].mid;
+      }
+      p.bias = pr.bias;
+      p.pin = part[i & 1];
+      p.pin_cols = P.pcols;
+      p.nblk_in = pr.in_features / FC_ROWS;
+      p.y = acts[i + 1];
+      p.ng = P.ng;
+      for (int g = 0; g < P.ng; ++g) p.g[g] = P.g[g];
+      for (int o = 0; o <= FC_CS; ++o) p.gstart[o] = P.gstart[o];
+      p.N = pr.out_features;
+      LBX_CHECK_ARG(aligned16(pr.br[0].u1) && (pr.n_branches < 2 || aligned16(pr.br[1].u1)) &&
+                        (!pr.bias || aligned16(pr.bias)),
+                    "u1 / bias must be 16-byte aligned");
+    } else {
+      p.x = acts[0];
+      p.N = projs[0].in_features;
+    }
+    if (nx < n_layers) {
+      const lbx_proj &pn = projs[nx];
+      const FcPlan &Q = plan[nx];
+      p.has_v = 1;
+      p.vblob = b + vo[nx];
+      p.nvseg = pn.n_branches == 2 && pn.br[1].v_sign ? 2 : 1;
+      for (int sg = 0; sg < p.nvseg; ++sg) {
+        p.v2[sg] = pn.br[sg].v2;
+        LBX_CHECK_ARG(aligned16(pn.br[sg].v2), "v2 must be 16-byte aligned");
+      }
+      p.pout = part[nx & 1];
+      p.pout_cols = Q.pcols;
+      p.nvg = Q.nvg;
+      for (int g = 0; g < Q.nvg; ++g) {
+        p.vg_p0[g] = Q.vg_p0[g];
+        p.vg_n[g] = Q.vg_n[g];
+        p.vg_seg[g] = Q.vg_seg[g];
+      }
+      for (int o = 0; o <= FC_CS; ++o) p.vstart[o] = Q.vstart[o];
+    }
+    const int nclusters = p.N / FC_ROWS;
+    const FcSmem Ls = fc_smem(k, p.ng);
+    LBX_CHECK_SUP((size_t)Ls.total <= smax, "fused chain needs %d bytes of shared memory (max %zu)", Ls.total, smax);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[2];
+    cfg.gridDim = dim3(nclusters * FC_CS);
+    cfg.blockDim = dim3(FC_THREADS);
+    cfg.dynamicSmemBytes = Ls.total;
+    cfg.stream = stream;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = FC_CS;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, fc_kernel, p);
+    if (e != cudaSuccess) return cuda_status(e, "fused chain launch");
+  }
+  return LBX_OK;
+}

@@ -19,6 +19,7 @@
 namespace lbx {
 
 constexpr int FWD_MAX_TOKENS = 64;  // tokens per step (attention and tree-mask width)
+constexpr int FWD_MAX_SEQ = 64;     // independent sequences per multi-sequence step
 
 struct FwdLayout {
   size_t tk, sw, x, q, kk, vv, att, gate, up, pos, rope, lin, attn, lm, total;
@@ -27,45 +28,48 @@ struct FwdLayout {
 
 static size_t al(size_t v) { return (v + 255) & ~(size_t)255; }
 
-static FwdLayout fwd_layout(const lbx_model *m, int n) {
+// n tokens of each of S sequences (S = 1: one sequence)
+static FwdLayout fwd_layout(const lbx_model *m, int n, int S = 1) {
   FwdLayout L = {};
   const size_t H = m->hidden, I = m->intermediate, Q = (size_t)m->heads * m->head_dim,
                KV = (size_t)m->kv_heads * m->head_dim;
+  const int T = n * S;  // rows of every activation buffer
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off += al(bytes); return o; };
   // the attention tickets and the linear scratch come first: their bookkeeping
   // words (kept at zero between calls) must sit at the same offset whatever n
   // a call uses
-  L.tk = take(attn_ticket_bytes(m->kv_heads));
+  L.tk = take(attn_ticket_bytes(m->kv_heads, FWD_MAX_SEQ));
   L.sw = take(16);
   size_t lin = 0;
   for (int l = 0; l < m->n_layers; ++l) {
     const lbx_proj *pr = m->layers[l].proj;
-    lin = std::max(lin, lbx_linear_workspace_size(pr + 0, 3, n));
-    lin = std::max(lin, lbx_linear_workspace_size(pr + 3, 1, n));
-    lin = std::max(lin, lbx_linear_workspace_size(pr + 4, 2, n));
-    lin = std::max(lin, lbx_linear_workspace_size(pr + 6, 1, n));
+    lin = std::max(lin, lbx_linear_workspace_size(pr + 0, 3, T));
+    lin = std::max(lin, lbx_linear_workspace_size(pr + 3, 1, T));
+    lin = std::max(lin, lbx_linear_workspace_size(pr + 4, 2, T));
+    lin = std::max(lin, lbx_linear_workspace_size(pr + 6, 1, T));
   }
   L.lin_bytes = lin;
   L.lin = take(lin);
-  L.x = take((size_t)n * H * 4);
-  L.q = take((size_t)n * Q * 4);
-  L.kk = take((size_t)n * KV * 4);
-  L.vv = take((size_t)n * KV * 4);
-  L.att = take((size_t)n * Q * 4);
-  L.gate = take((size_t)n * I * 4);
-  L.up = take((size_t)n * I * 4);
-  L.pos = take((size_t)n * 4);
-  L.rope = take((size_t)n * m->head_dim * 4);
+  L.x = take((size_t)T * H * 4);
+  L.q = take((size_t)T * Q * 4);
+  L.kk = take((size_t)T * KV * 4);
+  L.vv = take((size_t)T * KV * 4);
+  L.att = take((size_t)T * Q * 4);
+  L.gate = take((size_t)T * I * 4);
+  L.up = take((size_t)T * I * 4);
+  L.pos = take((size_t)T * 4);
+  L.rope = take((size_t)T * m->head_dim * 4);
   lbx_attn_args aa = {};
   aa.n = n;
+  aa.n_seq = S;
   aa.heads = m->heads;
   aa.kv_heads = m->kv_heads;
   aa.head_dim = m->head_dim;
   aa.prefix_len = m->max_seq - n;
   L.attn_bytes = attn_partial_bytes(&aa, nullptr);
   L.attn = take(L.attn_bytes);
-  L.lm_bytes = lbx_lmhead_workspace_size(n, m->vocab);
+  L.lm_bytes = lbx_lmhead_workspace_size(T, m->vocab);
   L.lm = take(L.lm_bytes);
   L.total = off;
   return L;
@@ -74,6 +78,12 @@ static FwdLayout fwd_layout(const lbx_model *m, int n) {
 __global__ void iota_kernel(int32_t *pos, int start, const int32_t *start_dev, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) pos[i] = (start_dev ? *start_dev : start) + i;
+}
+
+// positions of S sequences of n tokens: row s*n + i at start_seq[s] + i
+__global__ void iota_seq_kernel(int32_t *pos, const int32_t *start_seq, int n, int S) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e < n * S) pos[e] = start_seq[e / n] + e % n;
 }
 
 // every (layer, kv head, k|v) row block: stage all source rows, then write
@@ -118,12 +128,16 @@ extern "C" int lbx_kv_move(uint16_t *const *k_caches, uint16_t *const *v_caches,
 }
 
 namespace lbx {
-// one step of n <= FWD_MAX_TOKENS tokens (checked by the caller)
+// one step of n <= FWD_MAX_TOKENS tokens (checked by the caller); with S > 1,
+// n tokens of each of S independent sequences (start_seq: their first slots,
+// seq_stride: elements between their caches), rows ordered by sequence
 static int forward_chunk(const lbx_model *m, const int64_t *tokens, int32_t n, int32_t start,
                          const int32_t *start_dev, const int32_t *pos, const uint64_t *tree_mask,
                          float *hidden_out, float *logits, int64_t *argmax_out, void *ws,
-                         size_t ws_bytes, cudaStream_t stream) {
-  const FwdLayout L = fwd_layout(m, n);
+                         size_t ws_bytes, cudaStream_t stream, int S = 1,
+                         const int32_t *start_seq = nullptr, int64_t seq_stride = 0) {
+  const FwdLayout L = fwd_layout(m, n, S);
+  const int T = n * S;
   LBX_CHECK_ARG(ws && ws_bytes >= L.total, "workspace too small (%zu < %zu)", ws_bytes, L.total);
   uint8_t *w = reinterpret_cast<uint8_t *>(ws);
   float *x = reinterpret_cast<float *>(w + L.x);
@@ -141,16 +155,19 @@ static int forward_chunk(const lbx_model *m, const int64_t *tokens, int32_t n, i
   void *lm_ws = w + L.lm;
   const int pdl = m->use_pdl;
 
-  int rc = lbx_embed(m->embed, tokens, n, m->hidden, m->vocab, x, stream);
+  int rc = lbx_embed(m->embed, tokens, T, m->hidden, m->vocab, x, stream);
   if (rc) return rc;
   if (!pos) {
-    iota_kernel<<<(n + 127) / 128, 128, 0, stream>>>(posb, start, start_dev, n);
+    if (S > 1)
+      iota_seq_kernel<<<(T + 127) / 128, 128, 0, stream>>>(posb, start_seq, n, S);
+    else
+      iota_kernel<<<(n + 127) / 128, 128, 0, stream>>>(posb, start, start_dev, n);
     rc = cuda_status(cudaGetLastError(), "iota launch");
     if (rc) return rc;
     pos = posb;
   }
   // RoPE (cos, sin) of this step's positions, once for all layers
-  rc = lbx_rope_table(pos, n, m->head_dim, m->rope_theta, rope, stream);
+  rc = lbx_rope_table(pos, T, m->head_dim, m->rope_theta, rope, stream);
   if (rc) return rc;
   for (int l = 0; l < m->n_layers; ++l) {
     const lbx_layer &ly = m->layers[l];
@@ -158,7 +175,7 @@ static int forward_chunk(const lbx_model *m, const int64_t *tokens, int32_t n, i
     lbx_linear_args a = {};
     a.exec = m->exec_mode == LBX_EXEC_KERNELS ? LBX_EXEC_KERNELS : LBX_EXEC_AUTO;
     a.n_proj = 3;
-    a.n_tokens = n;
+    a.n_tokens = T;
     a.x_dtype = LBX_F32;
     a.y_dtype = LBX_F32;
     a.prologue = LBX_PRO_RMSNORM;
@@ -193,13 +210,19 @@ static int forward_chunk(const lbx_model *m, const int64_t *tokens, int32_t n, i
     aa.k_cache = ly.k_cache;
     aa.v_cache = ly.v_cache;
     aa.out = att;
+    if (S > 1) {
+      aa.n_seq = S;
+      aa.prefix_seq = start_seq;
+      aa.cache_seq_stride = seq_stride;
+      aa.prefix_dev = nullptr;
+    }
     rc = attn_launch(&aa, attn_part, attn_tk, stream);
     if (rc) return rc;
     // x += o(att)
     lbx_linear_args o = {};
     o.exec = a.exec;
     o.n_proj = 1;
-    o.n_tokens = n;
+    o.n_tokens = T;
     o.x_dtype = LBX_F32;
     o.y_dtype = LBX_F32;
     o.prologue = LBX_PRO_NONE;
@@ -228,11 +251,11 @@ static int forward_chunk(const lbx_model *m, const int64_t *tokens, int32_t n, i
     if (rc) return rc;
   }
   if (hidden_out) {
-    rc = lbx_rmsnorm(x, m->final_norm, n, m->hidden, m->rms_eps, hidden_out, stream);
+    rc = lbx_rmsnorm(x, m->final_norm, T, m->hidden, m->rms_eps, hidden_out, stream);
     if (rc) return rc;
   }
   if (logits || argmax_out) {
-    rc = lbx_lmhead_argmax(x, m->final_norm, m->rms_eps, n, m->hidden, m->lm_head, m->vocab,
+    rc = lbx_lmhead_argmax(x, m->final_norm, m->rms_eps, T, m->hidden, m->lm_head, m->vocab,
                            logits, argmax_out, lm_ws, L.lm_bytes, pdl, stream);
     if (rc) return rc;
   }
@@ -455,6 +478,36 @@ static int forward_program(const lbx_model *m, const int64_t *tokens, int32_t n,
   return launch_program(P, gridbar_of(lin), io, stream);
 }
 }  // namespace lbx
+
+extern "C" size_t lbx_forward_multi_workspace_size(const lbx_model *m, int32_t n_seq, int32_t n_tokens) {
+  if (!m || !m->layers || n_seq < 1 || n_seq > lbx::FWD_MAX_SEQ || n_tokens < 1 ||
+      n_tokens > lbx::FWD_MAX_TOKENS)
+    return 0;
+  return lbx::fwd_layout(m, n_tokens, n_seq).total;
+}
+
+extern "C" int lbx_forward_multi(const lbx_model *m, const int64_t *tokens, int32_t n_seq, int32_t n,
+                                 int32_t max_start, const int32_t *start_seq, int64_t cache_seq_stride,
+                                 const int32_t *pos, const uint64_t *tree_mask, float *hidden_out,
+                                 float *logits, int64_t *argmax_out, void *ws, size_t ws_bytes,
+                                 cudaStream_t stream) {
+  using namespace lbx;
+  LBX_CHECK_ARG(m && m->layers, "model is NULL");
+  LBX_CHECK_ARG(n_seq >= 1 && n_seq <= FWD_MAX_SEQ, "n_seq must be in [1,%d]", FWD_MAX_SEQ);
+  LBX_CHECK_ARG(n >= 1 && n <= FWD_MAX_TOKENS && tokens, "n must be in [1,%d]", FWD_MAX_TOKENS);
+  LBX_CHECK_ARG(start_seq, "start_seq is NULL");
+  LBX_CHECK_ARG(max_start >= 0 && max_start + n <= m->max_seq, "max_start + n exceeds max_seq");
+  LBX_CHECK_ARG(cache_seq_stride >= (int64_t)m->kv_heads * m->max_seq * m->head_dim,
+                "cache_seq_stride is smaller than one sequence's cache");
+  LBX_CHECK_ARG(m->heads % m->kv_heads == 0, "heads must be a multiple of kv_heads");
+  LBX_CHECK_ARG(m->embed && m->final_norm, "embed/final_norm required");
+  LBX_CHECK_ARG(!(logits || argmax_out) || m->lm_head, "lm_head required for logits/argmax");
+  LBX_CHECK_SUP(m->exec_mode != LBX_EXEC_PROGRAM, "multi-sequence steps run on the kernel path");
+  const size_t need = fwd_layout(m, n, n_seq).total;
+  LBX_CHECK_ARG(ws && ws_bytes >= need, "workspace too small (%zu < %zu)", ws_bytes, need);
+  return forward_chunk(m, tokens, n, max_start, nullptr, pos, tree_mask, hidden_out, logits, argmax_out, ws,
+                       ws_bytes, stream, n_seq, start_seq, cache_seq_stride);
+}
 
 extern "C" int lbx_forward(const lbx_model *m, const int64_t *tokens, int32_t n, int32_t start,
                            const int32_t *start_dev, const int32_t *pos, const uint64_t *tree_mask,

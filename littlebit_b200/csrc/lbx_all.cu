@@ -6,6 +6,7 @@
 #include "capi.cu"
 #include "pack.cu"
 #include "linear.cu"
+#include "chain.cu"
 #include "misc.cu"
 #include "attention.cu"
 #include "lmhead.cu"

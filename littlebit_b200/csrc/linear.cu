@@ -682,6 +682,16 @@ LBX_DEV float pow2f(int e) { return __int_as_float((e + 127) << 23); }  // e in 
 // v / 2^s rounded half up, s >= 0 (|v| < 2^24)
 LBX_DEV int rshr(int v, int s) { return s == 0 ? v : s > 30 ? 0 : (v + (1 << (s - 1))) >> s; }
 
+// One output value from the exact branch sums I_b at exponents e_b: the single
+// expression every executor evaluates, so that all of them round alike.
+LBX_DEV float u_result(float u1a, int I0, int e0, bool two, float u1b, int I1, int e1, bool has_bias,
+                       float bias) {
+  float v = u1a * ldexpf(__int2float_rn(I0), -e0);
+  if (two) v += u1b * ldexpf(__int2float_rn(I1), -e1);
+  if (has_bias) v += bias;
+  return v;
+}
+
 LBX_DEV int useg_of(const UParams &p, int unit) {
   int s = 0;
   while (s + 1 < p.nseg && unit >= p.seg[s + 1].cta0) ++s;
@@ -986,9 +996,8 @@ LBX_DEV bool ustage_run(const UParams &p, int unit, int nunits, uint8_t *W, uint
       for (int hrow = 0; hrow < 2; ++hrow) {
         const int nl = g + 8 * hrow;
         const int n = n0 + nl;
-        float v = myu1[nl] * ldexpf(__int2float_rn(I0[cb][hrow]), -sh.u_ec[0][t]);
-        if (sg.nbr > 1) v += myu1[16 + nl] * ldexpf(__int2float_rn(I1[cb][hrow]), -sh.u_ec[1][t]);
-        if (sg.bias) v += myu1[32 + nl];
+        float v = u_result(myu1[nl], I0[cb][hrow], sh.u_ec[0][t], sg.nbr > 1, myu1[16 + nl], I1[cb][hrow],
+                           sh.u_ec[1][t], sg.bias != nullptr, myu1[32 + nl]);
         if (p.epi == LBX_EPI_SILU0 && si == 0) v = v / (1.0f + expf(-v));
         const int64_t off = (int64_t)t * sg.y_ld + n;
         if constexpr (PEER) {  // NVLink stores of (call number, value) words

@@ -435,9 +435,8 @@ __global__ void __launch_bounds__(VTHREADS, LBX_SL_MINBLOCKS) slice_kernel(const
         }
         const int rr = c0 + r;
         const int n = rt0 * 16 + rr;
-        float v = su1[rr] * ldexpf(__int2float_rn(I0), -s_ec[0][t]);
-        if (P.nbr > 1) v += su1[p.rmax + rr] * ldexpf(__int2float_rn(I1), -s_ec[1][t]);
-        if (P.bias) v += su1[2 * p.rmax + rr];
+        float v = u_result(su1[rr], I0, s_ec[0][t], P.nbr > 1, su1[p.rmax + rr], I1, s_ec[1][t],
+                           P.bias != nullptr, su1[2 * p.rmax + rr]);
         if (p.epi == LBX_EPI_SILU0 && C.proj == 0) v = v / (1.0f + expf(-v));
         const int64_t off = (int64_t)t * P.y_ld + n;
         if (p.ydt == LBX_F32) {

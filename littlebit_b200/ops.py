@@ -236,6 +236,48 @@ def linear_chain(layers: Sequence[PackedLinear], acts: Sequence[torch.Tensor],
                                    _stream(acts[0].device)), "linear_chain")
 
 
+class FusedChain:
+    """A chain of single-projection layers run by the fused chain executor
+    (lbx_chain_fused): layer i's U-stage and layer i+1's V-stage partials in
+    one launch, bit-identical to running the layers one by one.  The sign
+    words are copied once into the executor's layout (lbx_chain_prepare)."""
+
+    def __init__(self, layers: Sequence[PackedLinear]):
+        self.layers = list(layers)
+        self.arr = projs_array(self.layers)
+        n = len(self.layers)
+        nb = int(lib().lbx_chain_prepare_size(self.arr, n))
+        if nb == 0:
+            raise RuntimeError(f"layer chain does not fit the fused chain executor: {L.last_error()}")
+        dev = self.layers[0].device
+        self.blob = torch.empty(nb // 4, dtype=torch.int32, device=dev)
+        L.check(lib().lbx_chain_prepare(self.arr, n, _p(self.blob), nb, _stream(dev)), "chain_prepare")
+        self._ws = {}
+
+    def workspace(self, k: int) -> torch.Tensor:
+        if k not in self._ws:
+            nb = int(lib().lbx_chain_fused_workspace_size(self.arr, len(self.layers), k))
+            if nb == 0:
+                raise RuntimeError(f"fused chain: {k} tokens unsupported: {L.last_error()}")
+            self._ws[k] = torch.empty(nb, dtype=torch.uint8, device=self.layers[0].device)
+        return self._ws[k]
+
+    def run(self, acts: Sequence[torch.Tensor], ptrs=None, stream=None) -> None:
+        """acts[i+1] = layers[i](acts[i]); all activations [k, features] of one dtype."""
+        n = len(self.layers)
+        if len(acts) != n + 1:
+            raise ValueError("need len(layers) + 1 activation buffers")
+        for i, t in enumerate(acts):
+            _cuda(f"acts[{i}]", t)
+        k = acts[0].shape[0]
+        ws = self.workspace(k)
+        if ptrs is None:
+            ptrs = (ctypes.c_void_p * (n + 1))(*[t.data_ptr() for t in acts])
+        st = _stream(acts[0].device) if stream is None else ctypes.c_void_p(stream.cuda_stream)
+        L.check(lib().lbx_chain_fused(self.arr, n, k, _dt(acts[0]), ptrs, _p(self.blob), self.blob.numel() * 4,
+                                      _p(ws), ws.numel(), st), "chain_fused")
+
+
 def linear_workspace_bytes(projs: Sequence[PackedLinear], n_tokens: int) -> int:
     return int(lib().lbx_linear_workspace_size(projs_array(projs), len(projs), n_tokens))
 

@@ -1,0 +1,105 @@
+"""The fused chain executor (lbx_chain_fused): layer i's U-stage and layer
+i+1's V-stage partial sums in one launch.  Every activation of the chain must
+equal, bit for bit, the layer-by-layer result of the two stage grids
+(lbx_linear_verify with LBX_EXEC_KERNELS), which the linear tests hold to the
+float64 oracle."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _chain(dims, ranks, shared=False, bias=False, seed=0):
+    from littlebit_b200 import synthetic
+
+    g = torch.Generator().manual_seed(seed)
+    layers = []
+    for i in range(len(dims) - 1):
+        brs = synthetic.layer(dims[i], dims[i + 1], ranks, g, shared_residual=shared)
+        b = (0.1 * torch.randn(dims[i + 1], generator=g)) if bias else None
+        layers.append(synthetic.to_packed_linear(dims[i], dims[i + 1], brs, DEV, bias=b))
+    return layers, g
+
+
+def _layerwise(ops, layers, x):
+    from littlebit_b200 import _lib as L
+
+    outs = [x]
+    for lay in layers:
+        y = torch.empty(x.shape[0], lay.out_features, dtype=x.dtype, device=DEV)
+        ops.linear_group([lay], outs[-1], [y], exec_mode=L.LBX_EXEC_KERNELS)
+        outs.append(y)
+    return outs
+
+
+@pytest.mark.parametrize("k", [1, 2, 4])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_fused_chain_c2_bitwise(k, dtype):
+    """C2 layers (4096 -> 4096, draft rank 208 + independent residual rank 1840)."""
+    from littlebit_b200 import ops
+
+    layers, g = _chain([4096] * 5, [208, 1840], seed=10 + k)
+    fc = ops.FusedChain(layers)
+    x = torch.randn(k, 4096, generator=g).to(DEV, dtype)
+    ref = _layerwise(ops, layers, x)
+    acts = [x] + [torch.full_like(r, float("nan")) for r in ref[1:]]
+    fc.run(acts)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    for i in range(1, len(acts)):
+        assert torch.isfinite(acts[i].float()).all(), i
+        assert torch.equal(acts[i].view(torch.int16 if dtype == torch.bfloat16 else torch.int32),
+                           ref[i].view(torch.int16 if dtype == torch.bfloat16 else torch.int32)), (k, i)
+
+
+@pytest.mark.parametrize("k", [1, 3])
+def test_fused_chain_shared_factor_bias_and_widths_bitwise(k):
+    """The config-4 shared-factor residual (U_R on the draft's V-stage) with a
+    bias, through widths 4096 -> 8192 -> 1024 -> 4096 (a two-pass input, and
+    blocks fewer than one pass), and a single-branch layer."""
+    from littlebit_b200 import ops
+
+    layers, g = _chain([4096, 8192, 1024, 4096], [208, 208], shared=True, bias=True, seed=40 + k)
+    single, _ = _chain([4096, 4096], [392], seed=50 + k)
+    layers = layers + single
+    fc = ops.FusedChain(layers)
+    x = torch.randn(k, 4096, generator=g).to(DEV)
+    ref = _layerwise(ops, layers, x)
+    acts = [x] + [torch.empty_like(r) for r in ref[1:]]
+    fc.run(acts)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    for i in range(1, len(acts)):
+        assert torch.equal(acts[i].view(torch.int32), ref[i].view(torch.int32)), (k, i)
+
+
+def test_fused_chain_repeated_calls_and_single_layer():
+    """Back-to-back calls reuse the partial-sum workspace; a one-layer chain is
+    the head launch plus one layer launch."""
+    from littlebit_b200 import ops
+
+    layers, g = _chain([4096, 4096], [208, 1840], seed=60)
+    fc = ops.FusedChain(layers)
+    for it in range(3):
+        x = torch.randn(2, 4096, generator=g).to(DEV, torch.bfloat16)
+        ref = _layerwise(ops, layers, x)
+        acts = [x, torch.empty_like(ref[1])]
+        fc.run(acts)
+        torch.cuda.synchronize()
+        assert torch.equal(acts[1].view(torch.int16), ref[1].view(torch.int16)), it
+
+
+def test_fused_chain_rejects_unsupported():
+    from littlebit_b200 import ops
+
+    layers, _ = _chain([4096, 4096], [208], seed=70)
+    fc = ops.FusedChain(layers)
+    x = torch.zeros(5, 4096, device=DEV)
+    with pytest.raises(RuntimeError, match="tokens"):
+        fc.run([x, torch.empty_like(x)])
+    odd, _ = _chain([4096, 4112], [208], seed=71)   # out_features not a multiple of 256
+    wide, _ = _chain([11008, 4096], [280], seed=72)  # in_features above 8192
+    for bad in (odd, wide):
+        with pytest.raises(RuntimeError, match="fused chain"):
+            ops.FusedChain(bad)
