@@ -88,7 +88,7 @@ struct FcParams {
 // shared-memory layout of one CTA (bytes; weights first, then scratch)
 struct FcSmem {
   int uw, vw, mid, u1, bias, v2, wbytes;      // weight region
-  int zf, actu, vx, ex, sa, actv, total;      // scratch
+  int zf, actu, xs, ex, sa, actv, total;      // scratch
 };
 
 __host__ __device__ inline FcSmem fc_smem(int k, int ng) {
@@ -104,22 +104,62 @@ __host__ __device__ inline FcSmem fc_smem(int k, int ng) {
   L.wbytes = o;
   L.zf = o;   o += FC_GMAX * k * 128 * 4;
   L.actu = o; o += FC_GMAX * 4 * ws * 4;
-  L.vx = o;   o += ng * FC_ROWS * k * 4;
+  L.xs = o;   o += (ng ? FC_CS : 0) * FC_ROWS * k * 8;
   L.ex = o;   o += ((ng * k * 4 + 15) / 16) * 16;
   L.sa = o;   o += 2 * k * FC_ROWS * 4;
-  L.actv = o; o += 2 * 8 * ws * 4;
+  L.actv = o; o += (FC_THREADS / 32) * 8 * ws * 4;
   L.total = o;
   return L;
 }
 
+// shared::cluster address of `p` (this CTA's shared memory) in CTA `rank` of the cluster
+LBX_DEV uint32_t cl_addr(const void *p, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+// asynchronous stores into a cluster CTA's shared memory, each counted (in
+// bytes) on that CTA's mbarrier
+LBX_DEV void st_async_b32(uint32_t addr, int v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr), "r"(v),
+               "r"(bar)
+               : "memory");
+}
+LBX_DEV void st_async_v2(uint32_t addr, int a, int b, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+               "r"(a), "r"(b), "r"(bar)
+               : "memory");
+}
+// bounded wait on a phase of an mbarrier that other CTAs of the cluster
+// complete (acquire at cluster scope); false, with `code` in the device error
+// word, if the phase did not complete within the limit
+LBX_DEV bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, int code) {
+  for (uint32_t it = 0; it < (1u << 22); ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  atomicCAS(&g_lbx_device_error, 0, code);
+  return false;
+}
+
+LBX_DEV void fc_vpart(const FcParams &p, int c, int k, int ws, int myv, int vs, const uint32_t *vw,
+                      const float *sa, uint32_t *act, int lane);
+
 __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant__ FcParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar;
+  __shared__ __align__(8) uint64_t xbar[2];  // exponents, then the CTAs' rounded sums (filled by st.async)
   __shared__ int s_gmax[FC_GMAX][FC_MAXK];
   __shared__ int s_usq[FC_GMAX][FC_MAXK];
   __shared__ int s_ec[2][FC_MAXK];
-  __shared__ int s_vmax[2][FC_MAXK];
-  __shared__ int s_vsq[2][FC_MAXK];
+  __shared__ int s_gb[FC_GTOT];  // branch of each group (slot order)
   __shared__ int s_ok;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -137,30 +177,35 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
   float *sv2 = reinterpret_cast<float *>(smem + L.v2);
   float *zf = reinterpret_cast<float *>(smem + L.zf);        // [slot][t][128]
   uint32_t *actu = reinterpret_cast<uint32_t *>(smem + L.actu);  // [slot][4 words][ws]
-  int *vx = reinterpret_cast<int *>(smem + L.vx);            // [group][row][t] exact sums
+  int *xs = reinterpret_cast<int *>(smem + L.xs);            // [cta][row][t][branch] rounded sums
   int *ex = reinterpret_cast<int *>(smem + L.ex);            // [group][t] exponents
   float *sa = reinterpret_cast<float *>(smem + L.sa);        // [seg][t][256] a = v2 * x of the block
-  uint32_t *actv = reinterpret_cast<uint32_t *>(smem + L.actv);  // [seg][8 words][ws]
+  uint32_t *actv = reinterpret_cast<uint32_t *>(smem + L.actv);  // [warp][8 words][ws] (each warp's copy)
 
   LBX_PROBE(20);
-  // cluster barrier A: this CTA has started, so the others may write into its
-  // shared memory (they do so only after waiting on A)
-  if (p.has_u) cl_arrive_relaxed();
   const int gs = p.gstart[j], myg = p.has_u ? p.gstart[j + 1] - gs : 0;
   const int vs = p.vstart[j], myv = p.has_v ? p.vstart[j + 1] - vs : 0;
   if (tid == 0) {
     mbar_init(&bar, 1);
+    if (p.has_u) {
+      mbar_init(&xbar[0], 1);
+      mbar_init(&xbar[1], 1);
+    }
     fence_mbar_init();
+    if (p.has_u) {  // the bytes every CTA of the cluster will store here
+      mbar_arrive_expect_tx(&xbar[0], (uint32_t)p.ng * k * 4u);
+      mbar_arrive_expect_tx(&xbar[1], (uint32_t)FC_CS * FC_ROWS * k * 8u);
+    }
   }
   if (tid < FC_GMAX * FC_MAXK) {
     (&s_gmax[0][0])[tid] = 0;
     (&s_usq[0][0])[tid] = 0;
   }
-  if (tid < 2 * FC_MAXK) {
-    (&s_vmax[0][0])[tid] = 0;
-    (&s_vsq[0][0])[tid] = 0;
-  }
+  if (tid < FC_GTOT) s_gb[tid] = tid < p.ng ? p.g[tid].b : 0;
   __syncthreads();
+  // cluster barrier A: this CTA has started and set up its barriers, so the
+  // others may store into its shared memory (they do so only after waiting on A)
+  if (p.has_u) cl_arrive_relaxed();
   // ---- weights (independent of every activation): before the dependency wait
   if (tid == 0) {
     uint32_t bytes = 0;
@@ -198,8 +243,11 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
 
   if (p.has_u) {
     // ---- z of this CTA's groups: the blocks' partials in the V-stage order
+    // (for each of the 16 block positions of a 4096-column pass, 0 + the
+    // passes in order; then the positions in order).  A pass's 16 loads are
+    // all in flight together.
     const int nblk = p.nblk_in;
-    const int npass = (nblk + 15) / 16;
+    const size_t bstride = (size_t)k * p.pin_cols;
     for (int it = tid; it < myg * k * 128; it += FC_THREADS) {
       const int sl = it / (k * 128), rem = it - sl * k * 128;
       const int t = rem >> 7, r = rem & 127;
@@ -207,19 +255,25 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
       float z = 0.f;
       if (r < G.n) {
         const float *src = p.pin + (size_t)t * p.pin_cols + G.pidx + r;
-        const size_t bstride = (size_t)k * p.pin_cols;
-        float pv[FC_NBLK];
+        float tw[16];
+        {
+          float pv[16];
 #pragma unroll
-        for (int b = 0; b < FC_NBLK; ++b) pv[b] = b < nblk ? __ldcg(src + b * bstride) : 0.f;
+          for (int w = 0; w < 16; ++w) pv[w] = w < nblk ? __ldcg(src + w * bstride) : 0.f;
+#pragma unroll
+          for (int w = 0; w < 16; ++w) tw[w] = 0.f + pv[w];
+        }
+        for (int b0 = 16; b0 < nblk; b0 += 16) {
+          float pv[16];
+#pragma unroll
+          for (int w = 0; w < 16; ++w) pv[w] = b0 + w < nblk ? __ldcg(src + (b0 + w) * bstride) : 0.f;
+#pragma unroll
+          for (int w = 0; w < 16; ++w)
+            if (b0 + w < nblk) tw[w] += pv[w];
+        }
         float v = 0.f;
 #pragma unroll
-        for (int w = 0; w < 16; ++w) {
-          float tw = 0.f;
-#pragma unroll
-          for (int ps = 0; ps < FC_NBLK / 16; ++ps)
-            if (ps < npass && ps * 16 + w < nblk) tw += pv[ps * 16 + w];
-          v += tw;
-        }
+        for (int w = 0; w < 16; ++w) v += tw[w];
         z = smid[sl * 128 + r] * v;
       }
       zf[(sl * k + t) * 128 + r] = z;
@@ -229,24 +283,17 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
     }
     __syncthreads();
     LBX_PROBE(23);
-    // exponents of this CTA's groups, to every CTA of the cluster
-    if (tid < myg * k) {
-      const int sl = tid / k, t = tid - sl * k;
-      const float m = __int_as_float(s_gmax[sl][t]);
-      s_gmax[sl][t] = m > 0.f ? u_group_exp(m) : UE_NONE;  // (now the exponent)
-    }
-    __syncthreads();
-    cl_wait();  // barrier A: every CTA of the cluster has started
-    if (tid < myg * k * FC_CS) {
-      const int d = tid / (myg * k), rem = tid - d * myg * k;
-      const int sl = rem / k, t = rem - sl * k;
-      *cl_map_w(ex + (gs + sl) * k + t, d) = s_gmax[sl][t];
-    }
-    // ---- digits of this CTA's groups (the U-stage's layout and rounding)
+    cl_wait();  // barrier A: every CTA of the cluster has started (its barriers are set up)
+    // ---- per (group, token), one warp: the exponent (to every CTA of the
+    // cluster) and the digits (the U-stage's layout and rounding)
     for (int it = warp; it < myg * k; it += FC_THREADS / 32) {
       const int sl = it / k, t = it - sl * k;
+      const float m = __int_as_float(s_gmax[sl][t]);
+      const int e = m > 0.f ? u_group_exp(m) : UE_NONE;
+      __syncwarp();
+      if (lane == 0) s_gmax[sl][t] = e;  // (from here on: the group's exponent)
+      if (lane < FC_CS) st_async_b32(cl_addr(ex + (gs + sl) * k + t, lane), e, cl_addr(&xbar[0], lane));
       const int Wd = lane >> 3, slot = lane & 7;
-      const int e = s_gmax[sl][t];
       const float sc = e == UE_NONE ? 0.f : pow2f(e);
       int hi[4], lo[4], sq = 0;
 #pragma unroll
@@ -265,55 +312,88 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
     __syncthreads();
     LBX_PROBE(24);
     // ---- contraction: warp w = output rows 16w..16w+15 of the cluster, each
-    // of this CTA's groups on its own (exact int32), to every CTA's exchange
-    if (ok && warp < FC_ROWS / 16) {
-      const int g = lane >> 2, q = lane & 3;
-      for (int sl = 0; sl < myg; ++sl) {
+    // of this CTA's groups on its own (exact int32, kept in registers)
+    const int g = lane >> 2, q = lane & 3;
+    int va[FC_GMAX], vb[FC_GMAX];
+#pragma unroll
+    for (int sl = 0; sl < FC_GMAX; ++sl) {
+      va[sl] = vb[sl] = 0;
+      if (sl < myg) {
         int acc[1][4] = {{0, 0, 0, 0}};
         const int G0[1] = {0};
         const uint32_t *tile = uw + sl * FC_UGW + warp * 16 * 4;
         sign_mma1<1>(acc, tile + g * 4, tile + (g + 8) * 4, actu + sl * 4 * ws, ws, ncols, G0, lane);
-        if (q < k) {
-          const int sq = s_usq[sl][q];
-          const int va = sq + 2 * (256 * acc[0][0] + acc[0][1]);
-          const int vb = sq + 2 * (256 * acc[0][2] + acc[0][3]);
-          int *base = vx + ((gs + sl) * FC_ROWS + warp * 16 + g) * k + q;
+        const int sq = q < k ? s_usq[sl][q] : 0;
+        va[sl] = sq + 2 * (256 * acc[0][0] + acc[0][1]);
+        vb[sl] = sq + 2 * (256 * acc[0][2] + acc[0][3]);
+      }
+    }
+    LBX_PROBE(25);
+    // ---- every group's exponent (from every CTA), then per branch and
+    // token the coarsest one
+    bool okx = mbar_wait_cluster(&xbar[0], 0, 0x132);
+    if (warp == 0) {
+      for (int t = 0; t < k; ++t) {
+        const int e = lane < p.ng ? ex[lane * k + t] : UE_NONE;
+        const int b = lane < p.ng ? s_gb[lane] : 0;
+        const int e0 = __reduce_min_sync(0xffffffffu, b == 0 ? e : UE_NONE);
+        const int e1 = __reduce_min_sync(0xffffffffu, b == 1 ? e : UE_NONE);
+        if (lane == 0) {
+          s_ec[0][t] = e0 == UE_NONE ? 0 : e0;
+          s_ec[1][t] = e1 == UE_NONE ? 0 : e1;
+        }
+      }
+    }
+    okx = __syncthreads_and(okx);
+    LBX_PROBE(26);
+    // ---- this CTA's groups rounded to their branch's coarsest exponent (the
+    // U-stage's integer shift) and added per branch, to every CTA
+    if (q < k) {
+      int I[2][2] = {{0, 0}, {0, 0}};  // [row g / g+8][branch]
 #pragma unroll
-          for (int d = 0; d < FC_CS; ++d) {
-            int *rb = cl_map_w(base, d);
-            rb[0] = va;
-            rb[8 * k] = vb;
+      for (int sl = 0; sl < FC_GMAX; ++sl) {
+        if (sl < myg) {
+          const int e = s_gmax[sl][q];  // (this group's exponent: see the digit loop)
+          if (e != UE_NONE) {
+            const int b = s_gb[gs + sl];
+            const int sft = e - s_ec[b][q];
+            const int ra = rshr(va[sl], sft), rb = rshr(vb[sl], sft);
+            if (b) {
+              I[0][1] += ra;
+              I[1][1] += rb;
+            } else {
+              I[0][0] += ra;
+              I[1][0] += rb;
+            }
           }
         }
       }
+      const int row = warp * 16 + g;
+#pragma unroll
+      for (int d = 0; d < FC_CS; ++d) {
+        const uint32_t bar = cl_addr(&xbar[1], d);
+        st_async_v2(cl_addr(xs + ((j * FC_ROWS + row) * k + q) * 2, d), I[0][0], I[0][1], bar);
+        st_async_v2(cl_addr(xs + ((j * FC_ROWS + row + 8) * k + q) * 2, d), I[1][0], I[1][1], bar);
+      }
     }
-    // cluster barrier B: every CTA's sums and exponents are in place
-    LBX_PROBE(25);
+    // cluster barrier C (waited at the exit): no CTA leaves while another may
+    // still store into its shared memory
     cl_arrive();
-    cl_wait();
-    LBX_PROBE(26);
-    // ---- coarsest exponent of each branch, then y for all 256 rows
-    if (tid < 2 * k) {
-      const int b = tid / k, t = tid - b * k;
-      int ec = UE_NONE;
-      for (int G = 0; G < p.ng; ++G)
-        if (p.g[G].b == b) ec = min(ec, ex[G * k + t]);
-      s_ec[b][t] = ec == UE_NONE ? 0 : ec;
-    }
-    __syncthreads();
+    // ---- every CTA's sums, then y for all 256 rows
+    okx = __syncthreads_and(mbar_wait_cluster(&xbar[1], 0, 0x133) && okx);
+    LBX_PROBE(28);
     for (int it = tid; it < FC_ROWS * k; it += FC_THREADS) {
       const int t = it / FC_ROWS, r = it - t * FC_ROWS;
-      int I[2] = {0, 0};
-      for (int G = 0; G < p.ng; ++G) {
-        const int e = ex[G * k + t];
-        if (e != UE_NONE) {
-          const int b = p.g[G].b;
-          I[b] += rshr(vx[(G * FC_ROWS + r) * k + t], e - s_ec[b][t]);
-        }
+      int I0 = 0, I1 = 0;
+#pragma unroll
+      for (int d = 0; d < FC_CS; ++d) {
+        const int2 v = *reinterpret_cast<const int2 *>(xs + ((d * FC_ROWS + r) * k + t) * 2);
+        I0 += v.x;
+        I1 += v.y;
       }
-      float v = u_result(su1[r], I[0], s_ec[0][t], p.nbr > 1, su1[FC_ROWS + r], I[1], s_ec[1][t],
-                         p.bias != nullptr, sbias[r]);
-      if (!ok) v = __int_as_float(0x7fc00000);
+      const int e0 = s_ec[0][t], e1 = s_ec[1][t];
+      float v = u_result(su1[r], I0, e0, p.nbr > 1, su1[FC_ROWS + r], I1, e1, p.bias != nullptr, sbias[r]);
+      if (!ok || !okx) v = __int_as_float(0x7fc00000);
       float xv = v;  // the next layer's input value: as stored
       const size_t off = (size_t)t * p.N + (size_t)c * FC_ROWS + r;
       if (p.adt == LBX_F32) {
@@ -334,60 +414,75 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
       for (int sg = 0; sg < p.nvseg; ++sg) sa[(sg * k + t) * FC_ROWS + r] = xx * sv2[sg * FC_ROWS + r];
     }
   }
-  if (!p.has_v) return;
+  if (p.has_v) {
+    __syncthreads();
+    LBX_PROBE(27);
+    if (ok) fc_vpart(p, c, k, ws, myv, vs, vw, sa, actv + warp * 8 * ws, lane);
+  }
+  LBX_PROBE(29);
+  if (p.has_u) cl_wait();  // barrier C
+}
 
-  // ---- V-stage partials of the next layer for this CTA's rank groups
-  __syncthreads();
-  LBX_PROBE(27);
-  for (int it = tid; it < p.nvseg * k * FC_ROWS; it += FC_THREADS) {  // per (segment, token) block maximum
-    const int st = it / FC_ROWS;
-    const float m = warp_max(fabsf(sa[it]));
-    if (lane == 0) atomicMax(&s_vmax[st / k][st % k], __float_as_int(m));
-  }
-  __syncthreads();
-  for (int it = tid; it < p.nvseg * k * 64; it += FC_THREADS) {  // digits: (segment, token, word, slot)
-    const int st = it >> 6, Wd = (it >> 3) & 7, slot = it & 7;
-    const int sg = st / k, t = st % k;
-    const float m = __int_as_float(s_vmax[sg][t]);
-    const float sc = m > 0.f ? QMAX / m : 0.f;
-    int hi[4], lo[4], sq = 0;
-#pragma unroll
-    for (int q4 = 0; q4 < 4; ++q4) {
-      const int pos = 32 * Wd + 16 * (slot >> 2) + (slot & 3) + 4 * q4;
-      const int qv = __float2int_rn(sa[st * FC_ROWS + pos] * sc);
-      sq += qv;
-      split_digits(qv, hi[q4], lo[q4]);
-    }
-    uint32_t *aw = actv + (sg * 8 + Wd) * ws + 2 * t;
-    aw[slot * ncols] = pack4(hi[0], hi[1], hi[2], hi[3]);
-    aw[slot * ncols + 1] = pack4(lo[0], lo[1], lo[2], lo[3]);
-    sq = __reduce_add_sync(0xffffffffu, sq);  // a warp's 32 items share (segment, token)
-    if (lane == 0) atomicAdd(&s_vsq[sg][t], sq);
-  }
-  __syncthreads();
-  LBX_PROBE(28);
-  if (!ok) return;
+// V-stage partials of the next layer for this CTA's rank groups, warp by warp:
+// each warp quantises the block itself (its private copy of the digits), so
+// the block maximum, the digits and the contraction need no CTA barrier
+LBX_DEV void fc_vpart(const FcParams &p, int c, int k, int ws, int myv, int vs, const uint32_t *vw,
+                      const float *sa, uint32_t *act, int lane) {
+  const int warp = threadIdx.x >> 5, ncols = 2 * k;
   const int g = lane >> 2, q = lane & 3;
+  int cur = -1;
+  int sq_t = 0;      // lane q (< k): digit sum of token q
+  float inv_t = 0.f; // lane q (< k): scale of token q
   for (int mt = warp; mt < myv * 8; mt += FC_THREADS / 32) {
     const int sl = mt >> 3, rt = (mt & 7) * 16;
     const int sg = p.vg_seg[vs + sl];
+    if (sg != cur) {  // this warp's digits of segment sg
+      cur = sg;
+      for (int t = 0; t < k; ++t) {
+        const float *a = sa + (sg * k + t) * FC_ROWS;
+        float m = 0.f;
+#pragma unroll
+        for (int i = 0; i < FC_ROWS / 32; ++i) m = fmaxf(m, fabsf(a[lane + 32 * i]));
+        m = warp_max(m);
+        const float sc = m > 0.f ? QMAX / m : 0.f;
+        int sq = 0;
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {  // 64 (word, slot) items, two per lane
+          const int itm = lane + 32 * h2;
+          const int Wd = itm >> 3, slot = itm & 7;
+          int hi[4], lo[4];
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const int pos = 32 * Wd + 16 * (slot >> 2) + (slot & 3) + 4 * q4;
+            const int qv = __float2int_rn(a[pos] * sc);
+            sq += qv;
+            split_digits(qv, hi[q4], lo[q4]);
+          }
+          uint32_t *aw = act + Wd * ws + 2 * t;
+          aw[slot * ncols] = pack4(hi[0], hi[1], hi[2], hi[3]);
+          aw[slot * ncols + 1] = pack4(lo[0], lo[1], lo[2], lo[3]);
+        }
+        sq = __reduce_add_sync(0xffffffffu, sq);
+        if (q == t) {
+          sq_t = sq;
+          inv_t = m / QMAX;
+        }
+      }
+      __syncwarp();
+    }
     int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
     const int G01[2] = {0, 1};
     const uint32_t *tile = vw + sl * FC_VGW + rt * FC_VPITCH;
-    sign_mma1<2>(acc, tile + g * FC_VPITCH, tile + (g + 8) * FC_VPITCH, actv + sg * 8 * ws, ws, ncols, G01,
-                 lane);
+    sign_mma1<2>(acc, tile + g * FC_VPITCH, tile + (g + 8) * FC_VPITCH, act, ws, ncols, G01, lane);
     if (q < k) {
-      const int sq = s_vsq[sg][q];
-      const float inv = __int_as_float(s_vmax[sg][q]) / QMAX;
-      const int ia = sq + 2 * (256 * (acc[0][0] + acc[1][0]) + (acc[0][1] + acc[1][1]));
-      const int ib = sq + 2 * (256 * (acc[0][2] + acc[1][2]) + (acc[0][3] + acc[1][3]));
+      const int ia = sq_t + 2 * (256 * (acc[0][0] + acc[1][0]) + (acc[0][1] + acc[1][1]));
+      const int ib = sq_t + 2 * (256 * (acc[0][2] + acc[1][2]) + (acc[0][3] + acc[1][3]));
       const int n = p.vg_n[vs + sl];
       float *dst = p.pout + ((size_t)c * k + q) * p.pout_cols + p.vg_p0[vs + sl] + rt;
-      if (rt + g < n) dst[g] = 0.f + __fmul_rn(__int2float_rn(ia), inv);
-      if (rt + g + 8 < n) dst[g + 8] = 0.f + __fmul_rn(__int2float_rn(ib), inv);
+      if (rt + g < n) dst[g] = 0.f + __fmul_rn(__int2float_rn(ia), inv_t);
+      if (rt + g + 8 < n) dst[g + 8] = 0.f + __fmul_rn(__int2float_rn(ib), inv_t);
     }
   }
-  LBX_PROBE(29);
 }
 
 // ---------------------------------------------------------------------------
