@@ -666,6 +666,80 @@ def run_decode70b(args, dev, rank, ws):
     return out
 
 
+def run_c5(args, dev, rank, ws):
+    """BASELINE config 5 on the Llama-2-70B shape: 64 independent sequences split
+    data-parallel over the ranks (64/N per GPU), each GPU decoding its share as
+    one batch (lbx_forward_multi: every packed-weight read serves all of its
+    sequences).  0.1-bit draft + 0.9-bit residual target (per-layer residual),
+    chain speculation with gamma 4 against batched target-only greedy decoding;
+    every sequence's tokens must be identical between the two.  The 512-token
+    prompt prefill is replaced by a seeded random bf16 KV prefix of 511 slots
+    per sequence (the decode work per token depends only on the cached length;
+    the draft's caches hold the same prefix)."""
+    from littlebit_b200.batch_decode import BatchDecoder, greedy_generate, speculative_generate
+    from littlebit_b200.cuda_models import _branch0_view
+    from littlebit_b200.model import LLAMA2_70B, LittleBitDecoder, synthetic_runtime_state
+
+    shape = LLAMA2_70B
+    r_d, r_r = _ranks_at(shape, 0.1), _ranks_at(shape, 0.9)
+    st = synthetic_runtime_state(shape, {k: [r_d[k], r_r[k]] for k in r_d}, seed=91, device=dev,
+                                 unit_gain=True)
+    for k in list(st):
+        if k.endswith(".u1_r"):
+            st[k] = st[k] * args.res_scale
+    S_total, gamma, P, G = 64, 4, 512, args.c5_new
+    S = S_total // ws
+    max_seq = P + (gamma + 1) * G + 16
+    dec = LittleBitDecoder(shape, st, device=dev, max_seq=16)  # weights only (the batches own the caches)
+    del st
+    tgt = BatchDecoder(dec, S, max_seq)
+    drf = BatchDecoder(_branch0_view(dec, 16), S, max_seq)
+    tgt.fill_synthetic_prefix(P - 1, seed=3000 + rank)
+    drf.copy_prefix_from(tgt, P - 1)
+    g = torch.Generator().manual_seed(4000 + rank)
+    last = torch.randint(0, shape.vocab_size, (S,), generator=g).to(dev)
+    prev = torch.randint(0, shape.vocab_size, (S,), generator=g).to(dev)
+
+    def timed(fn):
+        barrier(ws)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        out = fn()
+        torch.cuda.synchronize()
+        return out, max_over_ranks(time.perf_counter() - t0, ws)
+
+    # warm-up (kernel attributes, workspaces), then the timed runs
+    greedy_generate(tgt, last, P - 1, 2)
+    speculative_generate(drf, tgt, prev, last, P - 1, 2, gamma)
+    greedy_generate(drf, last, P - 1, 2)
+    greedy, t_g = timed(lambda: greedy_generate(tgt, last, P - 1, G))
+    _, t_d = timed(lambda: greedy_generate(drf, last, P - 1, G))
+    (spec, sst), t_s = timed(lambda: speculative_generate(drf, tgt, prev, last, P - 1, G, gamma))
+    same = bool(torch.equal(spec, greedy))
+    if not same:
+        raise RuntimeError("C5 batched speculation differs from batched target-only greedy")
+    lm = shape.vocab_size * shape.hidden_size * 2
+    kv_tok = 2 * shape.num_hidden_layers * shape.num_key_value_heads * shape.head_dim * 2
+    step_bytes = dec.packed_bytes() + dec.scale_bytes() + lm + S * kv_tok * (P + G // 2)
+    peak_gbs, _ = peaks()
+    tps_g = S_total * G / t_g
+    return {"workload": f"Llama-2-70B shape, {S_total} independent sequences ({S} per GPU, one batch), "
+                        f"{P}-token context (random bf16 KV prefix standing in for the prefill), {G} new "
+                        f"tokens each, greedy",
+            "unit": "tokens/s (all sequences, all GPUs)", "sequences_per_gpu": S,
+            "target_packed_gb": round(dec.packed_bytes() / 1e9, 2),
+            "target_greedy": round(tps_g, 2), "draft_greedy": round(S_total * G / t_d, 2),
+            "spec_chain_gamma4": {"tokens_per_s": round(S_total * G / t_s, 2),
+                                  "acceptance_rate": round(sst["acceptance_rate"], 4),
+                                  "mean_acceptance_length": round(sst["mean_acceptance_length"], 3),
+                                  "num_steps": sst["num_steps"], "token_identical": same},
+            "target_step_ms": round(t_g / G * 1e3, 2),
+            "target_hbm_frac_per_gpu": round(step_bytes * (G / t_g) / 1e9 / peak_gbs, 4),
+            "bytes_per_target_step": step_bytes,
+            "timing": "wall clock around each generate call, max over ranks; residual u1 x"
+                      f"{args.res_scale}, unit-gain scales"}
+
+
 # ---------------------------------------------------------------------------
 # row-sharded 8192 -> 28672 LittleBitLinear (N > 1)
 # ---------------------------------------------------------------------------
@@ -948,6 +1022,8 @@ def run_ours(args):
     assert ops.device_error() == 0, "device error word set during the bench"
     if not torch.isfinite(acts[-1].float()).all():
         raise RuntimeError("non-finite output in the layer chain")
+    if not float(acts[-1].float().abs().mean()) > 1e-3 * float(acts[0].float().abs().mean()):
+        raise RuntimeError("the layer chain's activations collapsed to zero (the timing would skip work)")
     y_main = acts[-1].clone()
     # the other executors: timed the same way, and they must give the same bits
     exec_t = {}
@@ -1031,6 +1107,7 @@ def run_ours(args):
         dense["speedup_of_packed_kernels"] = round(dense["us_per_layer"] / (per_launch_s * 1e6), 2)
     decode = run_decode(args, dev, rank, ws) if args.decode else None
     decode70 = run_decode70b(args, dev, rank, ws) if args.decode70b else None
+    c5 = run_c5(args, dev, rank, ws) if args.c5 else None
     row_shard = run_row_shard(args, dev, rank, ws) if ws > 1 else None
 
     if rank == 0:
@@ -1074,6 +1151,7 @@ def run_ours(args):
             "dense_bf16_ref": dense,
             "decode": decode,
             "decode_70b": decode70,
+            "c5_70b_dp": c5,
             "row_shard": row_shard,
             "gpu_launches": {"program": 1, "kernels": 2 * P, "cluster": P, "fused": P + 1}[args.exec] * args.steps,
             "clocks": clocks,
@@ -1104,6 +1182,9 @@ def main():
     ap.add_argument("--decode70b", type=int, default=0,
                     help="also run the 70B-shape decode section (about a minute more)")
     ap.add_argument("--new70", type=int, default=32, help="tokens generated in the 70B section")
+    ap.add_argument("--c5", type=int, default=1, help="BASELINE config 5: 64 sequences of the 70B shape, "
+                                                      "data-parallel over the ranks, batched per GPU")
+    ap.add_argument("--c5-new", type=int, default=32, help="tokens generated per sequence in config 5")
     ap.add_argument("--dense-ref", type=int, default=1,
                     help="also time the reference's GPU path (bf16 dense GEMMs) on the same layer")
     ap.add_argument("--prompt", type=int, default=128)

@@ -49,7 +49,8 @@ constexpr int FC_NBLK = 32;       // 256-column input blocks of a layer (in_feat
 constexpr int FC_THREADS = 512;
 constexpr int FC_VPITCH = 12;     // words per V row in the blob (8 used: conflict-free fragment loads)
 constexpr int FC_UGW = FC_ROWS * 4;     // words of one U group slot (256 rows x 4 words)
-constexpr int FC_VGW = 128 * FC_VPITCH; // words of one V group slot (128 ranks x 12 words)
+constexpr int FC_VTW = 16 * FC_VPITCH;  // words of one V tile (16 ranks x 12 words)
+constexpr int FC_VTC = 32;              // V tiles per CTA at most (two per warp)
 
 struct FcGroup {  // one 128-rank quantisation group of a branch (U side)
   int b;          // branch
@@ -70,15 +71,15 @@ struct FcParams {
   int gstart[FC_CS + 1];
   int ng, nbr, pin_cols, nblk_in;
   // V side of layer i+1 (absent in the last launch)
-  const uint32_t *vblob;  // [N/256][nvg][128 ranks][FC_VPITCH words]
+  const uint32_t *vblob;  // [N/256][nvt][16 ranks][FC_VPITCH words]
   const float *v2[2];     // [N] input scale of each V segment of layer i+1 (branch 0; branch 1
                           // when it has its own V): every segment stages its own a = v2 * x
   float *pout;            // [N/256][k][pout_cols]
-  int vg_p0[FC_GTOT];     // first rank (partial space) of each V group, slot order
-  int vg_n[FC_GTOT];
-  int vg_seg[FC_GTOT];    // V segment of each V group
-  int vstart[FC_CS + 1];
-  int nvg, nvseg, pout_cols;
+  // V tiles: 16 ranks each, segment 0's ranks then segment 1's (partial rank
+  // space); CTA j of a cluster takes tiles [nvt*j/8, nvt*(j+1)/8)
+  int nvt, vt0;           // tiles in all, tiles of segment 0
+  int vr[2], vpb[2];      // ranks and first partial rank of each segment
+  int nvseg, pout_cols;
   // head launch: layer 0's input
   const void *x;          // [k][N]
   int k, adt, N;          // tokens, activation dtype, features of the rows this launch owns
@@ -96,7 +97,7 @@ __host__ __device__ inline FcSmem fc_smem(int k, int ng) {
   const int ws = act_ws(2 * k);
   int o = 0;
   L.uw = o;   o += FC_GMAX * FC_UGW * 4;
-  L.vw = o;   o += FC_GMAX * FC_VGW * 4;
+  L.vw = o;   o += FC_VTC * FC_VTW * 4;
   L.mid = o;  o += FC_GMAX * 128 * 4;
   L.u1 = o;   o += 2 * FC_ROWS * 4;
   L.bias = o; o += FC_ROWS * 4;
@@ -131,25 +132,33 @@ LBX_DEV void st_async_v2(uint32_t addr, int a, int b, uint32_t bar) {
                : "memory");
 }
 // bounded wait on a phase of an mbarrier that other CTAs of the cluster
-// complete (acquire at cluster scope); false, with `code` in the device error
-// word, if the phase did not complete within the limit
+// complete (acquire at cluster scope), polled with test_wait: the data is
+// usually in flight already, and a suspending try_wait may sleep past its
+// arrival.  False, with `code` in the device error word, after 1 s.
 LBX_DEV bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, int code) {
-  for (uint32_t it = 0; it < (1u << 22); ++it) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
         : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
     if (ok) return true;
+    if ((it & 1023u) == 0) {
+      uint64_t t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (it == 0) t0 = t;
+      else if (t - t0 > 1000000000ull) break;
+    }
   }
   atomicCAS(&g_lbx_device_error, 0, code);
   return false;
 }
 
-LBX_DEV void fc_vpart(const FcParams &p, int c, int k, int ws, int myv, int vs, const uint32_t *vw,
+LBX_DEV void fc_vpart(const FcParams &p, int c, int k, int ws, int vs, int ve, const uint32_t *vw,
                       const float *sa, uint32_t *act, int lane);
 
 __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant__ FcParams p) {
@@ -184,7 +193,7 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
 
   LBX_PROBE(20);
   const int gs = p.gstart[j], myg = p.has_u ? p.gstart[j + 1] - gs : 0;
-  const int vs = p.vstart[j], myv = p.has_v ? p.vstart[j + 1] - vs : 0;
+  const int vs = p.nvt * j / FC_CS, ve = p.has_v ? p.nvt * (j + 1) / FC_CS : vs;
   if (tid == 0) {
     mbar_init(&bar, 1);
     if (p.has_u) {
@@ -213,7 +222,7 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
       bytes += (uint32_t)myg * FC_UGW * 4u + (uint32_t)p.nbr * FC_ROWS * 4u + (p.bias ? FC_ROWS * 4u : 0u);
       for (int s = 0; s < myg; ++s) bytes += (uint32_t)p.g[gs + s].n * 4u;
     }
-    if (p.has_v) bytes += (uint32_t)myv * FC_VGW * 4u + (uint32_t)p.nvseg * FC_ROWS * 4u;
+    if (p.has_v) bytes += (uint32_t)(ve - vs) * FC_VTW * 4u + (uint32_t)p.nvseg * FC_ROWS * 4u;
     mbar_arrive_expect_tx(&bar, bytes);
   }
   __syncthreads();
@@ -228,8 +237,8 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
       bulk_g2s(sbias, p.bias + (size_t)c * FC_ROWS, FC_ROWS * 4u, &bar);
     }
   } else if (warp == 1 && p.has_v) {
-    if (lane < myv)
-      bulk_g2s(vw + lane * FC_VGW, p.vblob + ((size_t)c * p.nvg + vs + lane) * FC_VGW, FC_VGW * 4u, &bar);
+    if (lane == 0 && ve > vs)  // this CTA's tiles are contiguous in the blob
+      bulk_g2s(vw, p.vblob + ((size_t)c * p.nvt + vs) * FC_VTW, (uint32_t)(ve - vs) * FC_VTW * 4u, &bar);
     else if (lane == 8 || (lane == 9 && p.nvseg > 1))
       bulk_g2s(sv2 + (lane - 8) * FC_ROWS, p.v2[lane - 8] + (size_t)c * FC_ROWS, FC_ROWS * 4u, &bar);
   }
@@ -417,7 +426,7 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
   if (p.has_v) {
     __syncthreads();
     LBX_PROBE(27);
-    if (ok) fc_vpart(p, c, k, ws, myv, vs, vw, sa, actv + warp * 8 * ws, lane);
+    if (ok) fc_vpart(p, c, k, ws, vs, ve, vw, sa, actv + warp * 8 * ws, lane);
   }
   LBX_PROBE(29);
   if (p.has_u) cl_wait();  // barrier C
@@ -426,16 +435,17 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
 // V-stage partials of the next layer for this CTA's rank groups, warp by warp:
 // each warp quantises the block itself (its private copy of the digits), so
 // the block maximum, the digits and the contraction need no CTA barrier
-LBX_DEV void fc_vpart(const FcParams &p, int c, int k, int ws, int myv, int vs, const uint32_t *vw,
+LBX_DEV void fc_vpart(const FcParams &p, int c, int k, int ws, int vs, int ve, const uint32_t *vw,
                       const float *sa, uint32_t *act, int lane) {
   const int warp = threadIdx.x >> 5, ncols = 2 * k;
   const int g = lane >> 2, q = lane & 3;
   int cur = -1;
   int sq_t = 0;      // lane q (< k): digit sum of token q
   float inv_t = 0.f; // lane q (< k): scale of token q
-  for (int mt = warp; mt < myv * 8; mt += FC_THREADS / 32) {
-    const int sl = mt >> 3, rt = (mt & 7) * 16;
-    const int sg = p.vg_seg[vs + sl];
+  for (int mt = vs + warp; mt < ve; mt += FC_THREADS / 32) {
+    const int sg = mt < p.vt0 ? 0 : 1;
+    const int r0 = 16 * (sg ? mt - p.vt0 : mt);   // first rank of the tile in its segment
+    const int n = min(16, p.vr[sg] - r0);
     if (sg != cur) {  // this warp's digits of segment sg
       cur = sg;
       for (int t = 0; t < k; ++t) {
@@ -472,15 +482,14 @@ LBX_DEV void fc_vpart(const FcParams &p, int c, int k, int ws, int myv, int vs, 
     }
     int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
     const int G01[2] = {0, 1};
-    const uint32_t *tile = vw + sl * FC_VGW + rt * FC_VPITCH;
+    const uint32_t *tile = vw + (mt - vs) * FC_VTW;
     sign_mma1<2>(acc, tile + g * FC_VPITCH, tile + (g + 8) * FC_VPITCH, act, ws, ncols, G01, lane);
     if (q < k) {
       const int ia = sq_t + 2 * (256 * (acc[0][0] + acc[1][0]) + (acc[0][1] + acc[1][1]));
       const int ib = sq_t + 2 * (256 * (acc[0][2] + acc[1][2]) + (acc[0][3] + acc[1][3]));
-      const int n = p.vg_n[vs + sl];
-      float *dst = p.pout + ((size_t)c * k + q) * p.pout_cols + p.vg_p0[vs + sl] + rt;
-      if (rt + g < n) dst[g] = 0.f + __fmul_rn(__int2float_rn(ia), inv_t);
-      if (rt + g + 8 < n) dst[g + 8] = 0.f + __fmul_rn(__int2float_rn(ib), inv_t);
+      float *dst = p.pout + ((size_t)c * k + q) * p.pout_cols + p.vpb[sg] + r0;
+      if (g < n) dst[g] = 0.f + __fmul_rn(__int2float_rn(ia), inv_t);
+      if (g + 8 < n) dst[g + 8] = 0.f + __fmul_rn(__int2float_rn(ib), inv_t);
     }
   }
 }
@@ -489,11 +498,10 @@ LBX_DEV void fc_vpart(const FcParams &p, int c, int k, int ws, int myv, int vs, 
 // host side: the plan of a layer (groups, their owners, blob offsets)
 // ---------------------------------------------------------------------------
 struct FcPlan {
-  int ng, nvg, nbr, pcols;
+  int ng, nbr, pcols;
   FcGroup g[FC_GTOT];
   int gstart[FC_CS + 1];
-  int vg_seg[FC_GTOT], vg_r0[FC_GTOT], vg_p0[FC_GTOT], vg_n[FC_GTOT];
-  int vstart[FC_CS + 1];
+  int nvt, vt0, vr[2], vpb[2];  // V tiles (see FcParams)
   size_t ublob_words, vblob_words;  // per layer
 };
 
@@ -545,28 +553,18 @@ static int fc_plan(const lbx_proj &pr, FcPlan &P) {
   LBX_CHECK_SUP(fc_deal(ng, sz, order, P.gstart), "fused chain: groups do not fit %d per CTA", FC_GMAX);
   for (int i = 0; i < ng; ++i) P.g[i] = all[order[i]];
   P.ng = ng;
-  // V groups over the partial rank space
-  int vseg[FC_GTOT], vr0[FC_GTOT], vp0[FC_GTOT], vn[FC_GTOT], nvg = 0;
+  // V tiles over the partial rank space (16 ranks each, per segment)
   const int nseg = shared || pr.n_branches == 1 ? 1 : 2;
-  for (int sgi = 0; sgi < nseg; ++sgi)
-    for (int r0 = 0; r0 < pr.br[sgi].rank; r0 += 128) {
-      LBX_CHECK_SUP(nvg < FC_GTOT, "fused chain: more than %d V groups in a layer", FC_GTOT);
-      vseg[nvg] = sgi;
-      vr0[nvg] = r0;
-      vp0[nvg] = pbase[sgi] + r0;
-      vn[nvg] = std::min(128, pr.br[sgi].rank - r0);
-      ++nvg;
-    }
-  LBX_CHECK_SUP(fc_deal(nvg, vn, order, P.vstart), "fused chain: V groups do not fit %d per CTA", FC_GMAX);
-  for (int i = 0; i < nvg; ++i) {
-    P.vg_seg[i] = vseg[order[i]];
-    P.vg_r0[i] = vr0[order[i]];
-    P.vg_p0[i] = vp0[order[i]];
-    P.vg_n[i] = vn[order[i]];
+  for (int sgi = 0; sgi < nseg; ++sgi) {
+    P.vr[sgi] = pr.br[sgi].rank;
+    P.vpb[sgi] = pbase[sgi];
   }
-  P.nvg = nvg;
+  P.vt0 = (P.vr[0] + 15) / 16;
+  P.nvt = P.vt0 + (nseg > 1 ? (P.vr[1] + 15) / 16 : 0);
+  LBX_CHECK_SUP((P.nvt + FC_CS - 1) / FC_CS <= FC_VTC, "fused chain: more than %d ranks in a layer's V-stages",
+                FC_VTC * FC_CS * 16);
   P.ublob_words = (size_t)(pr.out_features / FC_ROWS) * ng * FC_UGW;
-  P.vblob_words = (size_t)(pr.in_features / FC_ROWS) * nvg * FC_VGW;
+  P.vblob_words = (size_t)(pr.in_features / FC_ROWS) * P.nvt * FC_VTW;
   return LBX_OK;
 }
 
@@ -617,19 +615,21 @@ __global__ void fc_pack_u_kernel(const int32_t *u0, const int32_t *u1, int w0, i
   }
 }
 
-// V part: [K/256][slot][128 ranks][FC_VPITCH words] (rows past the group and
-// pad words are 0)
+// V part: [K/256][tile][16 ranks][FC_VPITCH words] (rows past the segment's
+// rank and the pad words are 0)
 __global__ void fc_pack_v_kernel(const int32_t *v0, const int32_t *v1, int Wv, FcPlan P, int nblk, uint32_t *dst) {
-  const size_t total = (size_t)nblk * P.nvg * 128 * FC_VPITCH;
+  const size_t total = (size_t)nblk * P.nvt * FC_VTW;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int w = (int)(i % FC_VPITCH);
     const size_t rr = i / FC_VPITCH;
-    const int r = (int)(rr % 128);
-    const size_t cs = rr / 128;
-    const int s = (int)(cs % P.nvg), c = (int)(cs / P.nvg);
-    const int32_t *src = P.vg_seg[s] ? v1 : v0;
+    const int r = (int)(rr % 16);
+    const size_t ct = rr / 16;
+    const int mt = (int)(ct % P.nvt), c = (int)(ct / P.nvt);
+    const int sg = mt < P.vt0 ? 0 : 1;
+    const int rank = 16 * (sg ? mt - P.vt0 : mt) + r;
+    const int32_t *src = sg ? v1 : v0;
     uint32_t v = 0u;
-    if (w < 8 && r < P.vg_n[s]) v = (uint32_t)src[(size_t)(P.vg_r0[s] + r) * Wv + c * 8 + w];
+    if (w < 8 && rank < P.vr[sg]) v = (uint32_t)src[(size_t)rank * Wv + c * 8 + w];
     dst[i] = v;
   }
 }
@@ -760,13 +760,12 @@ extern "C" int lbx_chain_fused(const lbx_proj *projs, int32_t n_layers, int32_t 
       }
       p.pout = part[nx & 1];
       p.pout_cols = Q.pcols;
-      p.nvg = Q.nvg;
-      for (int g = 0; g < Q.nvg; ++g) {
-        p.vg_p0[g] = Q.vg_p0[g];
-        p.vg_n[g] = Q.vg_n[g];
-        p.vg_seg[g] = Q.vg_seg[g];
+      p.nvt = Q.nvt;
+      p.vt0 = Q.vt0;
+      for (int sg = 0; sg < 2; ++sg) {
+        p.vr[sg] = Q.vr[sg];
+        p.vpb[sg] = Q.vpb[sg];
       }
-      for (int o = 0; o <= FC_CS; ++o) p.vstart[o] = Q.vstart[o];
     }
     const int nclusters = p.N / FC_ROWS;
     const FcSmem Ls = fc_smem(k, p.ng);
