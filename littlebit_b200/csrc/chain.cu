@@ -108,7 +108,7 @@ __host__ __device__ inline FcSmem fc_smem(int k, int ng) {
   L.xs = o;   o += (ng ? FC_CS : 0) * FC_ROWS * k * 8;
   L.ex = o;   o += ((ng * k * 4 + 15) / 16) * 16;
   L.sa = o;   o += 2 * k * FC_ROWS * 4;
-  L.actv = o; o += (FC_THREADS / 32) * 8 * ws * 4;
+  L.actv = o; o += 2 * 8 * ws * 4;
   L.total = o;
   return L;
 }
@@ -159,7 +159,7 @@ LBX_DEV bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, int code) {
 }
 
 LBX_DEV void fc_vpart(const FcParams &p, int c, int k, int ws, int vs, int ve, const uint32_t *vw,
-                      const float *sa, uint32_t *act, int lane);
+                      const uint32_t *actv, const int *vmax, const int *vsq, int lane);
 
 __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant__ FcParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -169,6 +169,7 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
   __shared__ int s_usq[FC_GMAX][FC_MAXK];
   __shared__ int s_ec[2][FC_MAXK];
   __shared__ int s_gb[FC_GTOT];  // branch of each group (slot order)
+  __shared__ int s_vmax[2 * FC_MAXK], s_vsq[2 * FC_MAXK];  // per (V segment, token)
   __shared__ int s_ok;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -189,7 +190,7 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
   int *xs = reinterpret_cast<int *>(smem + L.xs);            // [cta][row][t][branch] rounded sums
   int *ex = reinterpret_cast<int *>(smem + L.ex);            // [group][t] exponents
   float *sa = reinterpret_cast<float *>(smem + L.sa);        // [seg][t][256] a = v2 * x of the block
-  uint32_t *actv = reinterpret_cast<uint32_t *>(smem + L.actv);  // [warp][8 words][ws] (each warp's copy)
+  uint32_t *actv = reinterpret_cast<uint32_t *>(smem + L.actv);  // [segment][8 words][ws]
 
   LBX_PROBE(20);
   const int gs = p.gstart[j], myg = p.has_u ? p.gstart[j + 1] - gs : 0;
@@ -211,6 +212,7 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
     (&s_usq[0][0])[tid] = 0;
   }
   if (tid < FC_GTOT) s_gb[tid] = tid < p.ng ? p.g[tid].b : 0;
+  if (tid < 2 * FC_MAXK) s_vmax[tid] = s_vsq[tid] = 0;
   __syncthreads();
   // cluster barrier A: this CTA has started and set up its barriers, so the
   // others may store into its shared memory (they do so only after waiting on A)
@@ -357,8 +359,8 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
     LBX_PROBE(26);
     // ---- this CTA's groups rounded to their branch's coarsest exponent (the
     // U-stage's integer shift) and added per branch, to every CTA
+    int I[2][2] = {{0, 0}, {0, 0}};  // [row g / g+8][branch], token q
     if (q < k) {
-      int I[2][2] = {{0, 0}, {0, 0}};  // [row g / g+8][branch]
 #pragma unroll
       for (int sl = 0; sl < FC_GMAX; ++sl) {
         if (sl < myg) {
@@ -377,12 +379,33 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
           }
         }
       }
+    }
+    {
+      // all four lanes of a row pair store: lane q sends every token's sums
+      // (fetched from lane (g, t)) to the CTAs d = q, q + 4
+      int A[FC_MAXK][4];
+#pragma unroll
+      for (int t = 0; t < FC_MAXK; ++t) {
+        if (t < k) {  // (uniform)
+          const int src = (lane & ~3) | t;
+          A[t][0] = __shfl_sync(0xffffffffu, I[0][0], src);
+          A[t][1] = __shfl_sync(0xffffffffu, I[0][1], src);
+          A[t][2] = __shfl_sync(0xffffffffu, I[1][0], src);
+          A[t][3] = __shfl_sync(0xffffffffu, I[1][1], src);
+        }
+      }
       const int row = warp * 16 + g;
 #pragma unroll
-      for (int d = 0; d < FC_CS; ++d) {
+      for (int dd = 0; dd < FC_CS / 4; ++dd) {
+        const int d = q + 4 * dd;
         const uint32_t bar = cl_addr(&xbar[1], d);
-        st_async_v2(cl_addr(xs + ((j * FC_ROWS + row) * k + q) * 2, d), I[0][0], I[0][1], bar);
-        st_async_v2(cl_addr(xs + ((j * FC_ROWS + row + 8) * k + q) * 2, d), I[1][0], I[1][1], bar);
+#pragma unroll
+        for (int t = 0; t < FC_MAXK; ++t) {
+          if (t < k) {
+            st_async_v2(cl_addr(xs + ((j * FC_ROWS + row) * k + t) * 2, d), A[t][0], A[t][1], bar);
+            st_async_v2(cl_addr(xs + ((j * FC_ROWS + row + 8) * k + t) * 2, d), A[t][2], A[t][3], bar);
+          }
+        }
       }
     }
     // cluster barrier C (waited at the exit): no CTA leaves while another may
@@ -426,7 +449,34 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
   if (p.has_v) {
     __syncthreads();
     LBX_PROBE(27);
-    if (ok) fc_vpart(p, c, k, ws, vs, ve, vw, sa, actv + warp * 8 * ws, lane);
+    // the block's digits, once per segment and token: (segment, token) block
+    // maxima, then (segment, token, word, slot) items
+    for (int it = tid; it < p.nvseg * k * FC_ROWS; it += FC_THREADS) {
+      const float m = warp_max(fabsf(sa[it]));
+      if (lane == 0) atomicMax(&s_vmax[it / FC_ROWS], __float_as_int(m));
+    }
+    __syncthreads();
+    for (int it = tid; it < p.nvseg * k * 64; it += FC_THREADS) {
+      const int st = it >> 6, Wd = (it >> 3) & 7, slot = it & 7;
+      const int sg = st / k, t = st - sg * k;
+      const float m = __int_as_float(s_vmax[st]);
+      const float sc = m > 0.f ? QMAX / m : 0.f;
+      int hi[4], lo[4], sq = 0;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const int pos = 32 * Wd + 16 * (slot >> 2) + (slot & 3) + 4 * q4;
+        const int qv = __float2int_rn(sa[st * FC_ROWS + pos] * sc);
+        sq += qv;
+        split_digits(qv, hi[q4], lo[q4]);
+      }
+      uint32_t *aw = actv + (sg * 8 + Wd) * ws + 2 * t;
+      aw[slot * ncols] = pack4(hi[0], hi[1], hi[2], hi[3]);
+      aw[slot * ncols + 1] = pack4(lo[0], lo[1], lo[2], lo[3]);
+      sq = __reduce_add_sync(0xffffffffu, sq);  // a warp's 32 items share (segment, token)
+      if (lane == 0) atomicAdd(&s_vsq[st], sq);
+    }
+    __syncthreads();
+    if (ok) fc_vpart(p, c, k, ws, vs, ve, vw, actv, s_vmax, s_vsq, lane);
   }
   LBX_PROBE(29);
   if (p.has_u) cl_wait();  // barrier C
@@ -435,61 +485,30 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
 // V-stage partials of the next layer for this CTA's rank groups, warp by warp:
 // each warp quantises the block itself (its private copy of the digits), so
 // the block maximum, the digits and the contraction need no CTA barrier
+// V-stage partials of the next layer for this CTA's rank tiles, one tile per
+// warp at a time, from the block's digits (actv [segment][8 words][ws], the
+// per (segment, token) maxima and digit sums)
 LBX_DEV void fc_vpart(const FcParams &p, int c, int k, int ws, int vs, int ve, const uint32_t *vw,
-                      const float *sa, uint32_t *act, int lane) {
+                      const uint32_t *actv, const int *vmax, const int *vsq, int lane) {
   const int warp = threadIdx.x >> 5, ncols = 2 * k;
   const int g = lane >> 2, q = lane & 3;
-  int cur = -1;
-  int sq_t = 0;      // lane q (< k): digit sum of token q
-  float inv_t = 0.f; // lane q (< k): scale of token q
   for (int mt = vs + warp; mt < ve; mt += FC_THREADS / 32) {
     const int sg = mt < p.vt0 ? 0 : 1;
     const int r0 = 16 * (sg ? mt - p.vt0 : mt);   // first rank of the tile in its segment
     const int n = min(16, p.vr[sg] - r0);
-    if (sg != cur) {  // this warp's digits of segment sg
-      cur = sg;
-      for (int t = 0; t < k; ++t) {
-        const float *a = sa + (sg * k + t) * FC_ROWS;
-        float m = 0.f;
-#pragma unroll
-        for (int i = 0; i < FC_ROWS / 32; ++i) m = fmaxf(m, fabsf(a[lane + 32 * i]));
-        m = warp_max(m);
-        const float sc = m > 0.f ? QMAX / m : 0.f;
-        int sq = 0;
-#pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {  // 64 (word, slot) items, two per lane
-          const int itm = lane + 32 * h2;
-          const int Wd = itm >> 3, slot = itm & 7;
-          int hi[4], lo[4];
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            const int pos = 32 * Wd + 16 * (slot >> 2) + (slot & 3) + 4 * q4;
-            const int qv = __float2int_rn(a[pos] * sc);
-            sq += qv;
-            split_digits(qv, hi[q4], lo[q4]);
-          }
-          uint32_t *aw = act + Wd * ws + 2 * t;
-          aw[slot * ncols] = pack4(hi[0], hi[1], hi[2], hi[3]);
-          aw[slot * ncols + 1] = pack4(lo[0], lo[1], lo[2], lo[3]);
-        }
-        sq = __reduce_add_sync(0xffffffffu, sq);
-        if (q == t) {
-          sq_t = sq;
-          inv_t = m / QMAX;
-        }
-      }
-      __syncwarp();
-    }
     int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
     const int G01[2] = {0, 1};
     const uint32_t *tile = vw + (mt - vs) * FC_VTW;
-    sign_mma1<2>(acc, tile + g * FC_VPITCH, tile + (g + 8) * FC_VPITCH, act, ws, ncols, G01, lane);
+    sign_mma1<2>(acc, tile + g * FC_VPITCH, tile + (g + 8) * FC_VPITCH, actv + sg * 8 * ws, ws, ncols, G01,
+                 lane);
     if (q < k) {
-      const int ia = sq_t + 2 * (256 * (acc[0][0] + acc[1][0]) + (acc[0][1] + acc[1][1]));
-      const int ib = sq_t + 2 * (256 * (acc[0][2] + acc[1][2]) + (acc[0][3] + acc[1][3]));
+      const int sq = vsq[sg * k + q];
+      const float inv = __int_as_float(vmax[sg * k + q]) / QMAX;
+      const int ia = sq + 2 * (256 * (acc[0][0] + acc[1][0]) + (acc[0][1] + acc[1][1]));
+      const int ib = sq + 2 * (256 * (acc[0][2] + acc[1][2]) + (acc[0][3] + acc[1][3]));
       float *dst = p.pout + ((size_t)c * k + q) * p.pout_cols + p.vpb[sg] + r0;
-      if (g < n) dst[g] = 0.f + __fmul_rn(__int2float_rn(ia), inv_t);
-      if (g + 8 < n) dst[g + 8] = 0.f + __fmul_rn(__int2float_rn(ib), inv_t);
+      if (g < n) dst[g] = 0.f + __fmul_rn(__int2float_rn(ia), inv);
+      if (g + 8 < n) dst[g + 8] = 0.f + __fmul_rn(__int2float_rn(ib), inv);
     }
   }
 }
