@@ -6,8 +6,14 @@ rank 208 and a residual branch of rank 1840 (independent V_R), random packed
 POOL distinct layer instances (x_{i+1} = y_i, like a deep stack), so each
 step streams POOL x 2.28 MB of packed weights — 128 layers = 292 MB, more
 than twice the 126 MB L2, so every step reads the weights from HBM (no L2
-flush needed).  A step is one CUDA graph replay (2 kernels per layer, chained
-with programmatic dependent launch).
+flush needed).  A step is one CUDA graph replay: by default the fused chain
+executor (lbx_chain_fused: one launch per layer, layer i's U-stage with layer
+i+1's V-stage partials, chained with programmatic dependent launch); the
+two-stage grids, the cluster executor and the persistent program are timed
+beside it and must give the same bits.  Scales are |N(1,0.1)| with mid and u1
+divided by sqrt(in) and sqrt(rank x branches) so that every layer has unit
+gain: with the raw scales the chain's activations overflow within ~11 layers
+and collapse to zero, which lets the kernels skip work.
 
 value   = algorithmic bytes of all layers of all ranks / max-over-ranks time
           (packed bits without word padding + fp32 scales + activations in/out)
@@ -15,8 +21,8 @@ e2e     = the same metric through the C-ABI call itself: every step copies
           x from pinned host memory to the device, the host calls
           lbx_linear_verify (ctypes) once per layer of the chain, and the
           last layer's y is copied back to pinned host memory (8 KB each
-          way per step at k=1); no CUDA graph.  e2e_graph is the same step
-          captured in a CUDA graph.
+          way per step at k=1); no CUDA graph.  e2e_graph is the default
+          executor's step with the same copies, captured in a CUDA graph.
 configs = the other BASELINE layer configs, each as its own chain: C1 (fp32,
           r=208), C2 verify at k=5 and k=8, the shared-factor target layer of
           config 4 (draft r=208 + residual U_R of the same rank on the draft's
@@ -79,7 +85,8 @@ def peaks():
 def traffic_from_profiles(k: int, exec_name: str):
     """DRAM bytes per layer of the committed ncu capture of this executor
     (None when there is none: the persistent program has no per-layer launch)."""
-    name = {"kernels": f"linear_c2_k{k}.md", "cluster": f"linear_cluster_c2_k{k}.md"}.get(exec_name)
+    name = {"kernels": f"linear_c2_k{k}.md", "cluster": f"linear_cluster_c2_k{k}.md",
+            "fused": f"chain_fused_c2_k{k}.md"}.get(exec_name)
     if name is None:
         return None
     f = ROOT / "profiles" / name
@@ -950,11 +957,25 @@ def run_configs(args, dev, stream, ws, main_pool, peak, peak_kind):
     steps, warm = max(5, args.steps // 2), args.warmup
 
     def one(name, pool, k, dtype, ranks, shared, desc):
+        from littlebit_b200 import ops
+
         ch = Chain(pool, k, dtype, dev)
-        t = timed_graph(lambda: ch.run(L.LBX_EXEC_KERNELS, stream), stream, warm, steps, ws)
+        t_k = timed_graph(lambda: ch.run(L.LBX_EXEC_KERNELS, stream), stream, warm, steps, ws)
+        y_k = ch.acts[-1].clone()
+        t, exe = t_k, "two stage grids per layer"
+        if k <= 4:  # the fused chain executor (same bits) when the call fits it
+            fc = ops.FusedChain(pool)
+            ptrs = (ctypes.c_void_p * (len(pool) + 1))(*[a.data_ptr() for a in ch.acts])
+            t_f = timed_graph(lambda: fc.run(ch.acts, ptrs=ptrs, stream=stream), stream, warm, steps, ws)
+            if not torch.equal(ch.acts[-1], y_k):
+                raise RuntimeError(f"{name}: fused chain and stage grids disagree")
+            if t_f < t_k:
+                t, exe = t_f, "fused chain (one launch per layer)"
+            del fc
         us = t * 1e3 / (steps * len(pool))
         b, packed = layer_bytes(k, ranks, shared, 4 if dtype == torch.float32 else 2)
         e = roofline_entry(b, us, peak, peak_kind)
+        e.update({"exec": exe, "stage_grids_us": round(t_k * 1e3 / (steps * len(pool)), 3)})
         e.update({"workload": desc, "tokens": k, "pool_layers": len(pool),
                   "pool_mb": round(len(pool) * (b - (4 if dtype == torch.float32 else 2) * k * (IN_F + OUT_F)) / 1e6, 1),
                   "gbs_aggregate": round(b * len(pool) * steps * ws / (t * 1e-3) / 1e9, 2),
@@ -1054,34 +1075,51 @@ def run_ours(args):
                      "doing no arithmetic (lbx_linear_floor): launches only, and with each unit's weight "
                      "bulk copies and their wait")
 
-    # ---- e2e through the C-ABI call: pinned host x -> device, the host calls
-    # lbx_linear_verify for every layer (ctypes), device y -> pinned host
+    # ---- e2e through the C ABI with host buffers, no CUDA graph: every step
+    # copies x from pinned host memory, makes the library call(s) of the
+    # chain from the host (ctypes), and copies the last y back to pinned host
+    # memory.  Two forms: the chain entry point (lbx_chain_fused, one call
+    # per step, the default executor), and one lbx_linear_verify call per
+    # layer (the reference's one-op-per-layer usage).
     hx = torch.empty(k, IN_F, dtype=torch.bfloat16).pin_memory()
     hx.copy_(acts[0].cpu())
     hy = torch.empty(k, OUT_F, dtype=torch.bfloat16).pin_memory()
 
-    def e2e_step():
-        with torch.cuda.stream(stream):
-            acts[0].copy_(hx, non_blocking=True)
-            ch.run(L.LBX_EXEC_KERNELS, stream, args.pdl)
-            hy.copy_(acts[-1], non_blocking=True)
+    def e2e_time(run_chain):
+        def e2e_step():
+            with torch.cuda.stream(stream):
+                acts[0].copy_(hx, non_blocking=True)
+                run_chain()
+                hy.copy_(acts[-1], non_blocking=True)
 
-    for _ in range(args.warmup):
-        e2e_step()
-    torch.cuda.synchronize()
-    barrier(ws)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t_wall0 = time.perf_counter()
-    e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    t_wall = time.perf_counter() - t_wall0
-    t2 = max_over_ranks(e0.elapsed_time(e1), ws)
-    barrier(ws)
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(ws)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t_wall0 = time.perf_counter()
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t_wall = time.perf_counter() - t_wall0
+        t_dev = max_over_ranks(e0.elapsed_time(e1), ws)
+        barrier(ws)
+        return t_dev, t_wall
+
+    if fchain is not None:
+        t2, t_wall = e2e_time(step_fused)
+        e2e_path = (f"pinned host x -> device; the host calls lbx_chain_fused (C ABI, ctypes) once for the "
+                    f"{P}-layer chain, no CUDA graph; last y -> pinned host; every step")
+    else:
+        t2, t_wall = e2e_time(lambda: ch.run(L.LBX_EXEC_KERNELS, stream, args.pdl))
+        e2e_path = (f"pinned host x -> device; the host calls lbx_linear_verify (C ABI, ctypes) for each of "
+                    f"the {P} layers, no CUDA graph; last y -> pinned host; every step")
     e2e_val = b_layer * P * args.steps * ws / (t2 * 1e-3) / 1e9
+    t3, t3_wall = e2e_time(lambda: ch.run(L.LBX_EXEC_KERNELS, stream, args.pdl))
+    e2e_layer_val = b_layer * P * args.steps * ws / (t3 * 1e-3) / 1e9
 
     def e2e_graph_step():
         acts[0].copy_(hx, non_blocking=True)
@@ -1140,9 +1178,12 @@ def run_ours(args):
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": 2 * k * IN_F, "d2h_bytes_per_step": 2 * k * OUT_F,
                     "ms_per_step": round(t2 / args.steps, 4),
-                    "host_wall_ms_per_step": round(t_wall * 1e3 / args.steps, 4),
-                    "path": f"pinned host x -> device; the host calls lbx_linear_verify (C ABI, ctypes) for "
-                            f"each of the {P} layers, no CUDA graph; last y -> pinned host; every step"},
+                    "host_wall_ms_per_step": round(t_wall * 1e3 / args.steps, 4), "path": e2e_path},
+            "e2e_per_layer_calls": {
+                "value": round(e2e_layer_val, 2), "unit": "GB/s", "ms_per_step": round(t3 / args.steps, 4),
+                "host_wall_ms_per_step": round(t3_wall * 1e3 / args.steps, 4),
+                "path": f"the same copies; the host calls lbx_linear_verify (C ABI, ctypes) for each of the {P} "
+                        f"layers (two stage grids per call), no CUDA graph"},
             "e2e_graph": {"value": round(e2e_graph_val, 2), "unit": "GB/s",
                           "ms_per_step": round(tg / args.steps, 4),
                           "path": "the same step (copies + chain) captured in one CUDA graph"},
@@ -1172,7 +1213,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--pool", type=int, default=128)
     ap.add_argument("--pdl", type=int, default=1)
-    ap.add_argument("--exec", default="kernels", choices=["kernels", "cluster", "program", "fused"],
+    ap.add_argument("--exec", default="fused", choices=["kernels", "cluster", "program", "fused"],
                     help="cluster: one split-rank cluster launch per layer; kernels: one grid per stage; "
                          "program: each step is one persistent launch")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

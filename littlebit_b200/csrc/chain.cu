@@ -47,9 +47,10 @@ constexpr int FC_GTOT = FC_CS * FC_GMAX;
 constexpr int FC_MAXK = 4;        // tokens per launch (one MMA column block)
 constexpr int FC_NBLK = 32;       // 256-column input blocks of a layer (in_features <= 8192)
 constexpr int FC_THREADS = 512;
-constexpr int FC_VPITCH = 12;     // words per V row in the blob (8 used: conflict-free fragment loads)
+constexpr int FC_VPITCH = 8;      // words per V row in the blob (rows 4-7 and 12-15 of a tile hold their
+                                  // two 4-word halves swapped: conflict-free fragment loads, no padding)
 constexpr int FC_UGW = FC_ROWS * 4;     // words of one U group slot (256 rows x 4 words)
-constexpr int FC_VTW = 16 * FC_VPITCH;  // words of one V tile (16 ranks x 12 words)
+constexpr int FC_VTW = 16 * FC_VPITCH;  // words of one V tile (16 ranks x 8 words)
 constexpr int FC_VTC = 32;              // V tiles per CTA at most (two per warp)
 
 struct FcGroup {  // one 128-rank quantisation group of a branch (U side)
@@ -408,9 +409,11 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
         }
       }
     }
-    // cluster barrier C (waited at the exit): no CTA leaves while another may
-    // still store into its shared memory
-    cl_arrive();
+    // cluster barrier C (waited at the exit): no CTA leaves before every CTA
+    // of the cluster has issued its stores into the others' shared memory.
+    // Relaxed: the stores a CTA receives are all counted on its own barriers,
+    // which it waits for before it reaches the exit.
+    cl_arrive_relaxed();
     // ---- every CTA's sums, then y for all 256 rows
     okx = __syncthreads_and(mbar_wait_cluster(&xbar[1], 0, 0x133) && okx);
     LBX_PROBE(28);
@@ -500,7 +503,7 @@ LBX_DEV void fc_vpart(const FcParams &p, int c, int k, int ws, int vs, int ve, c
     const int G01[2] = {0, 1};
     const uint32_t *tile = vw + (mt - vs) * FC_VTW;
     sign_mma1<2>(acc, tile + g * FC_VPITCH, tile + (g + 8) * FC_VPITCH, actv + sg * 8 * ws, ws, ncols, G01,
-                 lane);
+                 lane, (g & 4));
     if (q < k) {
       const int sq = vsq[sg * k + q];
       const float inv = __int_as_float(vmax[sg * k + q]) / QMAX;
@@ -634,8 +637,9 @@ __global__ void fc_pack_u_kernel(const int32_t *u0, const int32_t *u1, int w0, i
   }
 }
 
-// V part: [K/256][tile][16 ranks][FC_VPITCH words] (rows past the segment's
-// rank and the pad words are 0)
+// V part: [K/256][tile][16 ranks][8 words], rows 4-7 and 12-15 with their two
+// 4-word halves swapped (word w of row r at w ^ (r & 4)); rows past the
+// segment's rank are 0
 __global__ void fc_pack_v_kernel(const int32_t *v0, const int32_t *v1, int Wv, FcPlan P, int nblk, uint32_t *dst) {
   const size_t total = (size_t)nblk * P.nvt * FC_VTW;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -647,8 +651,9 @@ __global__ void fc_pack_v_kernel(const int32_t *v0, const int32_t *v1, int Wv, F
     const int sg = mt < P.vt0 ? 0 : 1;
     const int rank = 16 * (sg ? mt - P.vt0 : mt) + r;
     const int32_t *src = sg ? v1 : v0;
+    const int wl = w ^ (r & 4);  // the logical word stored at this position
     uint32_t v = 0u;
-    if (w < 8 && rank < P.vr[sg]) v = (uint32_t)src[(size_t)rank * Wv + c * 8 + w];
+    if (rank < P.vr[sg]) v = (uint32_t)src[(size_t)rank * Wv + c * 8 + wl];
     dst[i] = v;
   }
 }
@@ -715,13 +720,24 @@ extern "C" int lbx_chain_fused(const lbx_proj *projs, int32_t n_layers, int32_t 
   LBX_CHECK_ARG(dtype == LBX_F32 || dtype == LBX_BF16, "bad dtype");
   LBX_CHECK_ARG(acts && blob, "NULL argument");
   for (int i = 0; i <= n_layers; ++i) LBX_CHECK_ARG(acts[i], "acts[%d] is NULL", i);
-  std::vector<size_t> uo(n_layers), vo(n_layers);
-  const size_t words = fc_blob_words(projs, n_layers, uo.data(), vo.data());
-  if (!words) return LBX_EUNSUPPORTED;  // (the reason is in lbx_last_error)
-  LBX_CHECK_ARG(blob_bytes >= words * 4, "blob too small (%zu < %zu)", blob_bytes, words * 4);
-  const size_t need = fc_ws_bytes(projs, n_layers, n_tokens);
-  LBX_CHECK_ARG(ws && ws_bytes >= need, "workspace too small (%zu < %zu)", ws_bytes, need);
+  // every layer's plan once: blob offsets (as fc_blob_words lays them out)
+  // and the partial-sum buffers (as fc_ws_bytes sizes them)
   const int k = n_tokens;
+  std::vector<FcPlan> plan(n_layers);
+  std::vector<size_t> uo(n_layers), vo(n_layers);
+  size_t words = 0, pmax = 0;
+  for (int i = 0; i < n_layers; ++i) {
+    rc = fc_plan(projs[i], plan[i]);
+    if (rc) return rc;
+    uo[i] = words;
+    words += (plan[i].ublob_words + 63) & ~(size_t)63;
+    vo[i] = words;
+    words += (plan[i].vblob_words + 63) & ~(size_t)63;
+    pmax = std::max(pmax, (size_t)(projs[i].in_features / FC_ROWS) * k * plan[i].pcols * 4);
+  }
+  LBX_CHECK_ARG(blob_bytes >= words * 4, "blob too small (%zu < %zu)", blob_bytes, words * 4);
+  const size_t need = 2 * al256(pmax);
+  LBX_CHECK_ARG(ws && ws_bytes >= need, "workspace too small (%zu < %zu)", ws_bytes, need);
   static DevCache<size_t> smax_cache;
   size_t smax = 0;
   rc = smax_cache.get(smax, [](size_t &out) {
@@ -731,11 +747,6 @@ extern "C" int lbx_chain_fused(const lbx_proj *projs, int32_t n_layers, int32_t 
   if (rc) return rc;
   const uint32_t *b = reinterpret_cast<const uint32_t *>(blob);
   float *part[2] = {reinterpret_cast<float *>(ws), reinterpret_cast<float *>(ws) + need / 8};
-  std::vector<FcPlan> plan(n_layers);
-  for (int i = 0; i < n_layers; ++i) {
-    rc = fc_plan(projs[i], plan[i]);
-    if (rc) return rc;
-  }
   for (int i = -1; i < n_layers; ++i) {
     FcParams p = {};
     p.k = k;

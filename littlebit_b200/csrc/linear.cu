@@ -150,17 +150,20 @@ LBX_DEV void sign_kstep1(int (&acc)[NG][4], const uint32_t (&wa)[NG], const uint
     mma_s8(acc[i], a0, a1, a2, a3, b0, b1);
   }
 }
+// swz: the sign rows' words are stored permuted (word w of the rows at w ^ swz;
+// the fused chain's V tiles swap the two 4-word halves of rows 4-7 and 12-15
+// so that the fragment loads hit distinct banks without a padded pitch)
 template <int NG>
 LBX_DEV void sign_mma1(int (&acc)[NG][4], const uint32_t *rowg, const uint32_t *rowg8,
-                       const uint32_t *act, int ws, int ncols, const int (&G)[NG], int lane) {
+                       const uint32_t *act, int ws, int ncols, const int (&G)[NG], int lane, int swz = 0) {
   const int q = lane & 3, n8 = lane >> 2;
   uint32_t wa[NG], wb[NG];
   const uint32_t *aw[NG];
 #pragma unroll
   for (int i = 0; i < NG; ++i) {
     const int w = 4 * G[i] + q;
-    wa[i] = rowg[w];
-    wb[i] = rowg8[w];
+    wa[i] = rowg[w ^ swz];
+    wb[i] = rowg8[w ^ swz];
     aw[i] = act + w * ws;
   }
   sign_kstep1<0, NG>(acc, wa, wb, aw, ncols, n8);

@@ -1,0 +1,108 @@
+"""Small, fixed launch sequences of every kernel family, for profiler captures.
+
+    python -m littlebit_b200.profile_cases [all|c2|vsplit|70b|fused|decode]
+
+Each case builds seeded random layers (Bernoulli(0.5) signs, |N(1,0.1)|
+scales) on cuda:0 and launches each kernel a few times in a known order, so a
+capture (for instance ``ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum
+--clock-control none python -m littlebit_b200.profile_cases all``) lists
+every kernel of the library with a small device footprint (about 0.3 GB).
+
+  c2      the C2 layer (4096 -> 4096, ranks 208 + 1840, bf16) on the two
+          stage grids at k = 1, 5 and 8 tokens
+  vsplit  the 7B draft down projection (11008 -> 4096, rank 280, x * x2
+          prologue): the pass-split V-stage
+  70b     the 70B gate/up target call (8192 -> 2 x 28672, ranks 616 + 5736,
+          RMSNorm prologue, silu(gate) epilogue) at k = 1 and 5
+  fused   a chain of 8 unit-gain C2 layers on the fused chain executor, k = 1
+  decode  two multi-sequence decoder steps (4 sequences) of a small model:
+          attention with the sequence dimension, embedding, lm_head
+"""
+from __future__ import annotations
+
+import sys
+
+import torch
+
+from . import _lib as L
+from . import ops, synthetic
+
+
+def _layer(K, N, ranks, g, dev):
+    return synthetic.to_packed_linear(K, N, synthetic.layer(K, N, ranks, g), dev)
+
+
+def case_c2(dev, g):
+    c2 = _layer(4096, 4096, [208, 1840], g, dev)
+    for k in (1, 5, 8):
+        x = torch.randn(k, 4096, generator=g).to(dev, torch.bfloat16)
+        y = torch.empty(k, 4096, device=dev, dtype=torch.bfloat16)
+        ops.linear_group([c2], x, [y], exec_mode=L.LBX_EXEC_KERNELS)
+
+
+def case_vsplit(dev, g):
+    dn = _layer(11008, 4096, [280], g, dev)
+    x = torch.randn(1, 11008, generator=g).to(dev)
+    x2 = torch.randn(1, 11008, generator=g).to(dev)
+    y = torch.empty(1, 4096, device=dev)
+    ops.linear_group([dn], x, [y], prologue=L.LBX_PRO_MUL, x2=x2, exec_mode=L.LBX_EXEC_KERNELS)
+
+
+def case_70b(dev, g):
+    gate, up = _layer(8192, 28672, [616, 5736], g, dev), _layer(8192, 28672, [616, 5736], g, dev)
+    w = torch.ones(8192, device=dev)
+    for k in (1, 5):
+        x = torch.randn(k, 8192, generator=g).to(dev)
+        ys = [torch.empty(k, 28672, device=dev) for _ in range(2)]
+        ops.linear_group([gate, up], x, ys, prologue=L.LBX_PRO_RMSNORM, norm_w=w, epilogue=L.LBX_EPI_SILU0,
+                         exec_mode=L.LBX_EXEC_KERNELS)
+
+
+def case_fused(dev, g):
+    layers = []
+    for _ in range(8):
+        brs = synthetic.layer(4096, 4096, [208, 1840], g)
+        for b in brs:  # unit gain: the chain's activations stay finite
+            b["mid"] = b["mid"] / 64.0
+            b["u1"] = b["u1"] / (2 * b["rank"]) ** 0.5
+        layers.append(synthetic.to_packed_linear(4096, 4096, brs, dev))
+    fc = ops.FusedChain(layers)
+    acts = [torch.randn(1, 4096, generator=g).to(dev, torch.bfloat16)] + \
+        [torch.empty(1, 4096, device=dev, dtype=torch.bfloat16) for _ in layers]
+    fc.run(acts)
+
+
+def case_decode(dev, g):
+    from .batch_decode import BatchDecoder
+    from .model import DecoderShape, LittleBitDecoder, synthetic_runtime_state
+
+    shape = DecoderShape(2, 512, 1024, 8, 2, 2048)
+    ranks = {"q_proj": [64, 64], "k_proj": [32, 32], "v_proj": [32, 32], "o_proj": [64, 64],
+             "gate_proj": [96, 96], "up_proj": [96, 96], "down_proj": [96, 96]}
+    st = synthetic_runtime_state(shape, ranks, seed=1, unit_gain=True)
+    dec = LittleBitDecoder(shape, st, device=dev, max_seq=16)
+    bd = BatchDecoder(dec, 4, max_seq=256)
+    bd.fill_synthetic_prefix(127, seed=2)
+    tok = torch.randint(0, shape.vocab_size, (4,), generator=g).to(dev)
+    am = torch.empty(4, dtype=torch.int64, device=dev)
+    for i in range(2):
+        bd.step(tok, torch.full((4,), 127 + i, dtype=torch.int32, device=dev), 127 + i, 1, argmax=am)
+        tok = am.clone()
+
+
+CASES = {"c2": case_c2, "vsplit": case_vsplit, "70b": case_70b, "fused": case_fused, "decode": case_decode}
+
+
+def main(argv):
+    which = argv[1] if len(argv) > 1 else "all"
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(0)
+    for name, fn in CASES.items():
+        if which in ("all", name):
+            fn(dev, g)
+    torch.cuda.synchronize()
+    print("ok", which)
+
+
+if __name__ == "__main__":
+    main(sys.argv)

@@ -63,9 +63,12 @@ def speculative_decode(draft_model, target_model, input_ids: torch.Tensor,
                        eos_token_id: int = 2, verbose: bool = False):
     """Draft ``draft_length`` tokens, verify with the target, accept the longest
     matching prefix plus one target token (greedy) or rejection-sample (sampling)."""
-    if greedy and _is_cuda_pair(draft_model, target_model):
-        return _speculative_decode_cuda(draft_model, target_model, input_ids, max_new_tokens,
-                                        draft_length, eos_token_id, verbose)
+    if _is_cuda_pair(draft_model, target_model):
+        if greedy:
+            return _speculative_decode_cuda(draft_model, target_model, input_ids, max_new_tokens,
+                                            draft_length, eos_token_id, verbose)
+        return _speculative_decode_cuda_sampling(draft_model, target_model, input_ids, max_new_tokens,
+                                                 draft_length, temperature, eos_token_id, verbose)
     device = input_ids.device
     gen = []
     total_draft = total_acc = steps = 0
@@ -222,6 +225,98 @@ def _speculative_decode_cuda(draft, target, input_ids, max_new_tokens, draft_len
     el = time.time() - t0
     out = torch.cat([input_ids, torch.tensor([gen], device=device, dtype=input_ids.dtype)], dim=1)
     return out, _stats(gen, total_draft, total_acc, steps, el, draft_length)
+
+
+def _speculative_decode_cuda_sampling(draft, target, input_ids, max_new_tokens, draft_length, temperature, eos,
+                                      verbose, generator: Optional[torch.Generator] = None):
+    """Sampling-mode chain speculation with the drafting, the verification and
+    the acceptance test on the device; the host reads the round's outcome once.
+
+    Per round (speculative_decoding.py:331-363): the draft samples k tokens
+    d_i ~ q_i = softmax(draft logits / T); the target gives p_i for the seed
+    and the drafts in one batched step; draft i is accepted while
+    u_i < min(1, p_i(d_i) / q_i(d_i)) (u_i uniform); at the first rejection a
+    token is drawn from norm(max(p_a - q_a, 0)), and after k acceptances a
+    bonus token from p_k."""
+    ids = input_ids[0].tolist()
+    device = input_ids.device
+    dev = draft.device
+    V = draft._vocab_size
+    Tm = max(float(temperature), 1e-8)
+    draft.reset()
+    target.reset_cache()
+    t0 = time.time()
+    P = len(ids) - 1
+    draft._sync_prefix(ids, P)
+    target.prefill_ids(ids, P)
+    K = draft_length
+    tok = torch.empty(K + 1, dtype=torch.int64, device=dev)
+    dlog = torch.empty(K, V, dtype=torch.float32, device=dev)
+    tlog = torch.empty(K + 1, V, dtype=torch.float32, device=dev)
+    host = torch.empty(2 + K, dtype=torch.int64).pin_memory()
+    pending = None
+    gen = []
+    total_draft = total_acc = steps = 0
+    tok[0] = ids[-1]
+    while len(gen) < max_new_tokens:
+        steps += 1
+        k = min(K, max_new_tokens - len(gen))
+        if pending is not None:
+            draft.dec.step(pending, P - 1)
+            pending = None
+        for i in range(k):  # sample the drafts on the device
+            draft.dec.step(tok[i:i + 1], P + i, logits=dlog[i:i + 1])
+            q = F.softmax(dlog[i] / Tm, dim=-1)
+            tok[i + 1:i + 2] = torch.multinomial(q, 1, generator=generator)
+        target._step(tok[:k + 1], P, logits=tlog[:k + 1])
+        pr = F.softmax(tlog[:k + 1] / Tm, dim=-1)
+        qd = F.softmax(dlog[:k] / Tm, dim=-1)
+        d = tok[1:k + 1]
+        pt = pr[:k].gather(1, d[:, None])[:, 0]
+        pq = qd.gather(1, d[:, None])[:, 0]
+        u = torch.rand(k, device=dev, generator=generator)
+        ok = (u < torch.clamp(pt / pq.clamp_min(1e-10), max=1.0)).to(torch.int64)
+        a = torch.cumprod(ok, 0).sum()
+        # the token after the accepted drafts: residual sample at a rejection,
+        # bonus from p_k after k acceptances
+        ai = a.clamp(max=k - 1)
+        resid = torch.clamp(pr[ai] - qd[ai], min=0)
+        resid = resid / (resid.sum() + 1e-10)
+        dist = torch.where(a < k, resid, pr[k])
+        nxt = torch.multinomial(dist, 1, generator=generator)[0]
+        host[0:1].copy_(a.view(1), non_blocking=True)
+        host[1:2].copy_(nxt.view(1), non_blocking=True)
+        host[2:2 + k].copy_(d, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        acc_n, nx = int(host[0]), int(host[1])
+        drafts = host[2:2 + k].tolist()
+        acc = 0
+        for i in range(k):
+            if i < acc_n:
+                acc += 1
+                gen.append(drafts[i])
+                if drafts[i] == eos:
+                    break
+            else:
+                gen.append(nx)
+                break
+        if acc == k and len(gen) < max_new_tokens:
+            gen.append(nx)
+        total_draft += k
+        total_acc += acc
+        if verbose:
+            print(f"step {steps}: drafted {k}, accepted {acc}, generated {len(gen)}")
+        if gen[-1] == eos:
+            break
+        if acc == k:
+            pending = tok[k:k + 1].clone()
+        P = P + acc + 1
+        tok[0] = gen[-1]
+    for u_ in target._units:
+        u_.pos = P
+    el = time.time() - t0
+    out = torch.cat([input_ids, torch.tensor([gen], device=device, dtype=input_ids.dtype)], dim=1)
+    return out, _stats(gen, total_draft, total_acc, steps, el, draft_length, {"decode_mode": "sampling"})
 
 
 def accept_chain(draft_toks: torch.Tensor, target_argmax: torch.Tensor, out: torch.Tensor):

@@ -165,3 +165,31 @@ def test_littlebit_module_reference_state_dict(golden):
         # its own state_dict round-trips the packed words bit-exactly
         sd2 = lin.state_dict()
         assert torch.equal(sd2["U_packed"].cpu(), sd["U_packed"]) and torch.equal(sd2["V_packed"].cpu(), sd["V_packed"])
+
+
+def test_sampling_mode_device_loop_limits():
+    """Sampling-mode chain speculation on the device (drafting, verification
+    and the acceptance test of speculative_decoding.py:331-363 on the GPU).
+    Two limits pin it: at a vanishing temperature every distribution is one-hot
+    and the output is target-only greedy; with the draft equal to the target
+    every draft passes the ratio test."""
+    from littlebit_b200.cuda_models import CudaDraftModel, CudaTargetModel
+    from littlebit_b200.speculative_decoding import autoregressive_generate, speculative_decode
+
+    shape, st, drf, tgt = _models_combined(unit_gain=True)
+    ids = _prompt(shape, n=12, seed=3)
+    ar, _ = autoregressive_generate(tgt, ids, None, max_new_tokens=32, eos_token_id=-1)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    from littlebit_b200 import speculative_decoding as sd
+
+    sp, stats = sd._speculative_decode_cuda_sampling(drf, tgt, ids, 32, 4, 1e-6, -1, False, generator=g)
+    assert sp.tolist() == ar.tolist()
+    assert stats["decode_mode"] == "sampling"
+    # the draft is a second copy of the target model: every ratio p/q is 1
+    from littlebit_b200.model import LittleBitDecoder
+
+    same = CudaDraftModel.from_decoder(LittleBitDecoder(shape, st, max_seq=512), use_graphs=False)
+    sp2, st2 = speculative_decode(same, tgt, ids, None, max_new_tokens=32, draft_length=4, temperature=1.0,
+                                  greedy=False, eos_token_id=-1)
+    assert st2["acceptance_rate"] == 1.0 and st2["total_tokens_generated"] == 32
+    assert sp2.shape[1] == ids.shape[1] + 32
