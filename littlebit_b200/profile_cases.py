@@ -1,6 +1,6 @@
 """Small, fixed launch sequences of every kernel family, for profiler captures.
 
-    python -m littlebit_b200.profile_cases [all|c2|vsplit|70b|fused|decode]
+    python -m littlebit_b200.profile_cases [all|c2|vsplit|70b|fused|decode|allgather]
 
 Each case builds seeded random layers (Bernoulli(0.5) signs, |N(1,0.1)|
 scales) on cuda:0 and launches each kernel a few times in a known order, so a
@@ -17,6 +17,8 @@ every kernel of the library with a small device footprint (about 0.3 GB).
   fused   a chain of 8 unit-gain C2 layers on the fused chain executor, k = 1
   decode  two multi-sequence decoder steps (4 sequences) of a small model:
           attention with the sequence dimension, embedding, lm_head
+  allgather  the row-sharded 8192 -> 28672 layer with the all-gather fused
+          into its U-stage, two shards emulated on one GPU in stream order
 """
 from __future__ import annotations
 
@@ -90,7 +92,40 @@ def case_decode(dev, g):
         tok = am.clone()
 
 
-CASES = {"c2": case_c2, "vsplit": case_vsplit, "70b": case_70b, "fused": case_fused, "decode": case_decode}
+def case_allgather(dev, g):
+    """The row-sharded 8192 -> 28672 layer (rank 616) with its all-gather fused
+    into the U-stage, two shards emulated on one GPU in stream order (every word
+    is written before the unpack that reads it starts)."""
+    import ctypes
+
+    from .sharded import RowShardedLinear
+
+    K, N, G, k = 8192, 28672, 2, 1
+    full = _layer(K, N, [616], g, dev)
+    shards = [RowShardedLinear(full, G, r) for r in range(G)]
+    half = k * N
+    xbufs = [torch.zeros(2 * half, dtype=torch.int64, device=dev) for _ in range(G)]
+    states = [torch.zeros(2, dtype=torch.int32, device=dev) for _ in range(G)]
+    peers = (ctypes.c_void_p * G)(*[b.data_ptr() for b in xbufs])
+    wss = [torch.zeros(ops.linear_workspace_bytes([s.local], k), dtype=torch.uint8, device=dev) for s in shards]
+    lib = ops.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    x = torch.randn(k, K, generator=g).to(dev)
+    for rank, sh in enumerate(shards):
+        a = L.LinearArgs()
+        a.n_proj, a.n_tokens, a.x_dtype, a.y_dtype = 1, k, L.LBX_F32, L.LBX_F32
+        a.epilogue, a.use_pdl, a.x = L.LBX_EPI_STORE, 0, x.data_ptr()
+        L.check(lib.lbx_linear_allgather(ops.projs_array([sh.local]), ctypes.byref(a), G, peers, half, sh.lo, N,
+                                         states[rank].data_ptr(), wss[rank].data_ptr(), wss[rank].numel(), st),
+                "allgather")
+    ys = [torch.empty(k, N, device=dev) for _ in range(G)]
+    for rank in range(G):
+        L.check(lib.lbx_allgather_unpack(xbufs[rank].data_ptr(), half, k, N, N, ys[rank].data_ptr(), N,
+                                         states[rank].data_ptr(), 0, st), "unpack")
+
+
+CASES = {"c2": case_c2, "vsplit": case_vsplit, "70b": case_70b, "fused": case_fused, "decode": case_decode,
+         "allgather": case_allgather}
 
 
 def main(argv):
