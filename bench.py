@@ -948,9 +948,44 @@ def roofline_entry(b_layer: int, us: float, peak: float, peak_kind: str, traffic
             "mean_launch_us": round(us, 3)}
 
 
+def cpu_layer_gbs(k: int, ranks, shared: bool, esz: int, budget_s: float = 2.0, nlayers: int = 8):
+    """The reference's CPU op (oracle/_ref littlebit_linear) on a config's layer:
+    GB/s over a few distinct layers for about budget_s seconds (None when the
+    op is not built or a branch shares its V, which the op cannot express)."""
+    from oracle import build_ref  # CPU baseline only
+
+    if shared or not build_ref.load():
+        return None
+    from littlebit_b200 import synthetic as syn
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(9)
+    layers = [syn.layer(IN_F, OUT_F, list(ranks), g) for _ in range(nlayers)]
+    op = torch.ops.littlebit_cpu_ops.littlebit_linear
+    x = torch.randn(k, IN_F, generator=g)
+
+    def one_pass():
+        for lay in layers:
+            for b in lay:
+                op(x, b["v2"][None], b["v_sign"], IN_F, b["mid"][None], b["u_sign"], b["rank"], b["u1"][None])
+
+    one_pass()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        one_pass()
+        times.append(time.perf_counter() - t0)
+    b, _ = layer_bytes(k, ranks, shared, esz)
+    return {"value": round(b * nlayers / statistics.median(times) / 1e9, 3), "unit": "GB/s",
+            "cores": torch.get_num_threads(), "kind": "reference",
+            "sample": f"{len(times)} passes (median) over {nlayers} distinct layers, k={k}"}
+
+
 def run_configs(args, dev, stream, ws, main_pool, peak, peak_kind):
     """The other BASELINE layer configs, each a chain of distinct layers timed
-    like the headline (CUDA graph of the C-ABI calls, weights streamed from HBM)."""
+    like the headline (CUDA graph of the C-ABI calls, weights streamed from HBM),
+    with the reference's CPU op on the same layer beside each (rank 0, N=1)."""
     from littlebit_b200 import _lib as L
 
     out = {}
@@ -980,6 +1015,8 @@ def run_configs(args, dev, stream, ws, main_pool, peak, peak_kind):
                   "pool_mb": round(len(pool) * (b - (4 if dtype == torch.float32 else 2) * k * (IN_F + OUT_F)) / 1e6, 1),
                   "gbs_aggregate": round(b * len(pool) * steps * ws / (t * 1e-3) / 1e9, 2),
                   "finite": bool(torch.isfinite(ch.acts[-1].float()).all())})
+        if ws == 1 and not args.no_cpu:
+            e["cpu_baseline"] = cpu_layer_gbs(k, ranks, shared, 4 if dtype == torch.float32 else 2)
         out[name] = e
         del ch
 

@@ -90,7 +90,7 @@ struct FcParams {
 // shared-memory layout of one CTA (bytes; weights first, then scratch)
 struct FcSmem {
   int uw, vw, mid, u1, bias, v2, wbytes;      // weight region
-  int zf, actu, xs, ex, sa, actv, total;      // scratch
+  int actu, xs, ex, sa, actv, total;          // scratch
 };
 
 __host__ __device__ inline FcSmem fc_smem(int k, int ng) {
@@ -104,7 +104,6 @@ __host__ __device__ inline FcSmem fc_smem(int k, int ng) {
   L.bias = o; o += FC_ROWS * 4;
   L.v2 = o;   o += 2 * FC_ROWS * 4;
   L.wbytes = o;
-  L.zf = o;   o += FC_GMAX * k * 128 * 4;
   L.actu = o; o += FC_GMAX * 4 * ws * 4;
   L.xs = o;   o += (ng ? FC_CS : 0) * FC_ROWS * k * 8;
   L.ex = o;   o += ((ng * k * 4 + 15) / 16) * 16;
@@ -112,6 +111,17 @@ __host__ __device__ inline FcSmem fc_smem(int k, int ng) {
   L.actv = o; o += 2 * 8 * ws * 4;
   L.total = o;
   return L;
+}
+
+// barrier 1 + q (q = 0..3) of the 128 threads of warps 4q..4q+3 (constant
+// barrier ids, so that the kernel reserves five barriers, not sixteen)
+LBX_DEV void quad_barrier(int q) {
+  switch (q) {
+    case 0: asm volatile("bar.sync 1, 128;" ::: "memory"); break;
+    case 1: asm volatile("bar.sync 2, 128;" ::: "memory"); break;
+    case 2: asm volatile("bar.sync 3, 128;" ::: "memory"); break;
+    default: asm volatile("bar.sync 4, 128;" ::: "memory"); break;
+  }
 }
 
 // shared::cluster address of `p` (this CTA's shared memory) in CTA `rank` of the cluster
@@ -159,6 +169,30 @@ LBX_DEV bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, int code) {
   return false;
 }
 
+// the same for an mbarrier completed by this CTA's own bulk copies
+LBX_DEV bool mbar_poll_cta(uint64_t *bar, uint32_t parity, int code) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((it & 1023u) == 0) {
+      uint64_t t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (it == 0) t0 = t;
+      else if (t - t0 > 1000000000ull) break;
+    }
+  }
+  atomicCAS(&g_lbx_device_error, 0, code);
+  return false;
+}
+
 LBX_DEV void fc_vpart(const FcParams &p, int c, int k, int ws, int vs, int ve, const uint32_t *vw,
                       const uint32_t *actv, const int *vmax, const int *vsq, int lane);
 
@@ -168,6 +202,7 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
   __shared__ __align__(8) uint64_t xbar[2];  // exponents, then the CTAs' rounded sums (filled by st.async)
   __shared__ int s_gmax[FC_GMAX][FC_MAXK];
   __shared__ int s_usq[FC_GMAX][FC_MAXK];
+  __shared__ int s_gexp[FC_GMAX][FC_MAXK];  // exponent of each of this CTA's groups
   __shared__ int s_ec[2][FC_MAXK];
   __shared__ int s_gb[FC_GTOT];  // branch of each group (slot order)
   __shared__ int s_vmax[2 * FC_MAXK], s_vsq[2 * FC_MAXK];  // per (V segment, token)
@@ -186,7 +221,6 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
   float *su1 = reinterpret_cast<float *>(smem + L.u1);
   float *sbias = reinterpret_cast<float *>(smem + L.bias);
   float *sv2 = reinterpret_cast<float *>(smem + L.v2);
-  float *zf = reinterpret_cast<float *>(smem + L.zf);        // [slot][t][128]
   uint32_t *actu = reinterpret_cast<uint32_t *>(smem + L.actu);  // [slot][4 words][ws]
   int *xs = reinterpret_cast<int *>(smem + L.xs);            // [cta][row][t][branch] rounded sums
   int *ex = reinterpret_cast<int *>(smem + L.ex);            // [group][t] exponents
@@ -248,25 +282,33 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
   pdl_trigger();
   pdl_wait();  // the previous launch's partials (and outputs) are complete
   LBX_PROBE(21);
-  if (tid == 0) s_ok = mbar_wait_bounded(&bar, 0, 0x131) ? 1 : 0;
+  if (tid == 0) s_ok = mbar_poll_cta(&bar, 0, 0x131) ? 1 : 0;
   __syncthreads();
   const bool ok = s_ok != 0;
   LBX_PROBE(22);
 
   if (p.has_u) {
-    // ---- z of this CTA's groups: the blocks' partials in the V-stage order
-    // (for each of the 16 block positions of a 4096-column pass, 0 + the
-    // passes in order; then the positions in order).  A pass's 16 loads are
-    // all in flight together.
+    cl_wait();  // barrier A: every CTA of the cluster has started (its barriers are set up)
+    // ---- per (group, token), four warps: z of the group's 128 ranks (the
+    // blocks' partials in the V-stage order: for each of the 16 block
+    // positions of a 4096-column pass, 0 + the passes in order, then the
+    // positions in order; a pass's 16 loads in flight together), the group
+    // maximum, the exponent (to every CTA of the cluster) and the digits in
+    // the U-stage's layout and rounding.  Warp wq holds word wq of the group:
+    // lane (slot, e) the rank 32 wq + 16 (slot >> 2) + (slot & 3) + 4 e.
     const int nblk = p.nblk_in;
     const size_t bstride = (size_t)k * p.pin_cols;
-    for (int it = tid; it < myg * k * 128; it += FC_THREADS) {
-      const int sl = it / (k * 128), rem = it - sl * k * 128;
-      const int t = rem >> 7, r = rem & 127;
+    const int quad = warp >> 2, wq = warp & 3;
+    const int slot = lane >> 2, e4 = lane & 3;
+    const int pos = 32 * wq + 16 * (slot >> 2) + (slot & 3) + 4 * e4;
+    for (int it0 = 0; it0 < myg * k; it0 += FC_THREADS / 128) {
+      const int it = it0 + quad;  // (uniform per quad)
+      if (it >= myg * k) break;
+      const int sl = it / k, t = it - sl * k;
       const FcGroup G = p.g[gs + sl];
       float z = 0.f;
-      if (r < G.n) {
-        const float *src = p.pin + (size_t)t * p.pin_cols + G.pidx + r;
+      if (pos < G.n) {
+        const float *src = p.pin + (size_t)t * p.pin_cols + G.pidx + pos;
         float tw[16];
         {
           float pv[16];
@@ -286,42 +328,37 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
         float v = 0.f;
 #pragma unroll
         for (int w = 0; w < 16; ++w) v += tw[w];
-        z = smid[sl * 128 + r] * v;
+        z = smid[sl * 128 + pos] * v;
       }
-      zf[(sl * k + t) * 128 + r] = z;
-      // a warp's 32 items share (slot, token): the group maximum
       const float m = warp_max(fabsf(z));
       if (lane == 0) atomicMax(&s_gmax[sl][t], __float_as_int(m));
+      quad_barrier(quad);  // the quad's four maxima are in
+      const float gm = __int_as_float(s_gmax[sl][t]);
+      const int e = gm > 0.f ? u_group_exp(gm) : UE_NONE;
+      if (wq == 0) {
+        if (lane < FC_CS) st_async_b32(cl_addr(ex + (gs + sl) * k + t, lane), e, cl_addr(&xbar[0], lane));
+        if (lane == 0) s_gexp[sl][t] = e;
+      }
+      const float sc = e == UE_NONE ? 0.f : pow2f(e);
+      const int qv = __float2int_rn(z * sc);
+      int hi, lo;
+      split_digits(qv, hi, lo);
+      // the four digits of a slot word come from lanes (slot, 0..3)
+      const int base = lane & ~3;
+      const int h0 = __shfl_sync(0xffffffffu, hi, base), h1 = __shfl_sync(0xffffffffu, hi, base + 1);
+      const int h2 = __shfl_sync(0xffffffffu, hi, base + 2), h3 = __shfl_sync(0xffffffffu, hi, base + 3);
+      const int l0 = __shfl_sync(0xffffffffu, lo, base), l1 = __shfl_sync(0xffffffffu, lo, base + 1);
+      const int l2 = __shfl_sync(0xffffffffu, lo, base + 2), l3 = __shfl_sync(0xffffffffu, lo, base + 3);
+      if (e4 == 0) {
+        uint32_t *aw = actu + (sl * 4 + wq) * ws + 2 * t;
+        aw[slot * ncols] = pack4(h0, h1, h2, h3);
+        aw[slot * ncols + 1] = pack4(l0, l1, l2, l3);
+      }
+      const int sq = __reduce_add_sync(0xffffffffu, qv);
+      if (lane == 0) atomicAdd(&s_usq[sl][t], sq);
     }
     __syncthreads();
     LBX_PROBE(23);
-    cl_wait();  // barrier A: every CTA of the cluster has started (its barriers are set up)
-    // ---- per (group, token), one warp: the exponent (to every CTA of the
-    // cluster) and the digits (the U-stage's layout and rounding)
-    for (int it = warp; it < myg * k; it += FC_THREADS / 32) {
-      const int sl = it / k, t = it - sl * k;
-      const float m = __int_as_float(s_gmax[sl][t]);
-      const int e = m > 0.f ? u_group_exp(m) : UE_NONE;
-      __syncwarp();
-      if (lane == 0) s_gmax[sl][t] = e;  // (from here on: the group's exponent)
-      if (lane < FC_CS) st_async_b32(cl_addr(ex + (gs + sl) * k + t, lane), e, cl_addr(&xbar[0], lane));
-      const int Wd = lane >> 3, slot = lane & 7;
-      const float sc = e == UE_NONE ? 0.f : pow2f(e);
-      int hi[4], lo[4], sq = 0;
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        const int pos = 32 * Wd + 16 * (slot >> 2) + (slot & 3) + 4 * q4;
-        const int qv = __float2int_rn(zf[(sl * k + t) * 128 + pos] * sc);
-        sq += qv;
-        split_digits(qv, hi[q4], lo[q4]);
-      }
-      uint32_t *aw = actu + (sl * 4 + Wd) * ws + 2 * t;
-      aw[slot * ncols] = pack4(hi[0], hi[1], hi[2], hi[3]);
-      aw[slot * ncols + 1] = pack4(lo[0], lo[1], lo[2], lo[3]);
-      sq = __reduce_add_sync(0xffffffffu, sq);
-      if (lane == 0) s_usq[sl][t] = sq;
-    }
-    __syncthreads();
     LBX_PROBE(24);
     // ---- contraction: warp w = output rows 16w..16w+15 of the cluster, each
     // of this CTA's groups on its own (exact int32, kept in registers)
@@ -365,7 +402,7 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
 #pragma unroll
       for (int sl = 0; sl < FC_GMAX; ++sl) {
         if (sl < myg) {
-          const int e = s_gmax[sl][q];  // (this group's exponent: see the digit loop)
+          const int e = s_gexp[sl][q];
           if (e != UE_NONE) {
             const int b = s_gb[gs + sl];
             const int sft = e - s_ec[b][q];
@@ -439,26 +476,31 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
         xv = bf16_to_f32(hb);
       }
       if (p.has_v)
-        for (int sg = 0; sg < p.nvseg; ++sg) sa[(sg * k + t) * FC_ROWS + r] = xv * sv2[sg * FC_ROWS + r];
+        for (int sg = 0; sg < p.nvseg; ++sg) {  // the next layer's a = v2 * x and its block maximum
+          const float a = xv * sv2[sg * FC_ROWS + r];
+          sa[(sg * k + t) * FC_ROWS + r] = a;
+          const float m = warp_max(fabsf(a));  // (a warp's 32 items share the token)
+          if (lane == 0) atomicMax(&s_vmax[sg * k + t], __float_as_int(m));
+        }
     }
   } else if (p.has_v) {
     // head launch: block c of layer 0's input
     for (int it = tid; it < FC_ROWS * k; it += FC_THREADS) {
       const int t = it / FC_ROWS, r = it - t * FC_ROWS;
       const float xx = load_act(p.x, p.adt, (int64_t)t * p.N + (int64_t)c * FC_ROWS + r);
-      for (int sg = 0; sg < p.nvseg; ++sg) sa[(sg * k + t) * FC_ROWS + r] = xx * sv2[sg * FC_ROWS + r];
+      for (int sg = 0; sg < p.nvseg; ++sg) {
+        const float a = xx * sv2[sg * FC_ROWS + r];
+        sa[(sg * k + t) * FC_ROWS + r] = a;
+        const float m = warp_max(fabsf(a));
+        if (lane == 0) atomicMax(&s_vmax[sg * k + t], __float_as_int(m));
+      }
     }
   }
   if (p.has_v) {
     __syncthreads();
     LBX_PROBE(27);
-    // the block's digits, once per segment and token: (segment, token) block
-    // maxima, then (segment, token, word, slot) items
-    for (int it = tid; it < p.nvseg * k * FC_ROWS; it += FC_THREADS) {
-      const float m = warp_max(fabsf(sa[it]));
-      if (lane == 0) atomicMax(&s_vmax[it / FC_ROWS], __float_as_int(m));
-    }
-    __syncthreads();
+    // the block's digits, once per (segment, token, word, slot) item (the
+    // block maxima were taken with a = v2 * x)
     for (int it = tid; it < p.nvseg * k * 64; it += FC_THREADS) {
       const int st = it >> 6, Wd = (it >> 3) & 7, slot = it & 7;
       const int sg = st / k, t = st - sg * k;

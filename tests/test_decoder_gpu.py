@@ -154,3 +154,4 @@ def test_program_matches_kernel_path_bitwise(tiny, shared):
     pos = 66 + tb["tree_position_ids"]
     outs = [m.forward_tokens(ids[:T], 66, pos=pos, tree_mask=tmask) for m in (mk, mp)]
     assert torch.equal(outs[0]["logits"], outs[1]["logits"])
+
