@@ -99,8 +99,9 @@ typedef struct lbx_linear_args {
   int32_t exec;        /* LBX_EXEC_AUTO: one cluster launch when the call fits
                         * it, else the two stage grids; LBX_EXEC_KERNELS: the
                         * two stage grids; LBX_EXEC_CLUSTER: the cluster launch
-                        * or LBX_EUNSUPPORTED; LBX_EXEC_KERNELS_ONE_CTA_V (see
-                        * below).  All give the same bits.                    */
+                        * or LBX_EUNSUPPORTED; LBX_EXEC_KERNELS_ONE_CTA_V,
+                        * LBX_EXEC_TC, LBX_EXEC_NO_TC (see below).  All give
+                        * the same bits.                                      */
   int32_t _pad;
 } lbx_linear_args;
 
@@ -351,6 +352,14 @@ typedef struct lbx_model {
  * passes in one CTA (inputs wider than 4096 columns otherwise run a cluster of
  * one CTA per pass on small grids).  Same bits; for validation. */
 #define LBX_EXEC_KERNELS_ONE_CTA_V 4
+/* lbx_linear_args.exec only: the tensor-core executor (tcgen05 kind::i8,
+ * up to 64 tokens per launch) for any token count; AUTO and KERNELS select it
+ * for calls of 32 tokens or more when the workspace holds a batch
+ * (lbx_linear_workspace_size counts it from 32 tokens).  Same bits. */
+#define LBX_EXEC_TC 5
+/* lbx_linear_args.exec only: the two stage grids at every token count (never
+ * the tensor-core executor).  Same bits; for validation. */
+#define LBX_EXEC_NO_TC 6
 
 /* Workspace of lbx_forward: zero-filled once at allocation, like lbx_linear's. */
 size_t lbx_forward_workspace_size(const lbx_model *m /* host */, int32_t n_tokens);

@@ -19,6 +19,7 @@ LBX_PRO_NONE, LBX_PRO_RMSNORM, LBX_PRO_SILU_MUL, LBX_PRO_MUL = 0, 1, 2, 3
 LBX_EPI_STORE, LBX_EPI_ADD, LBX_EPI_SILU0 = 0, 1, 2
 LBX_EXEC_AUTO, LBX_EXEC_KERNELS, LBX_EXEC_PROGRAM, LBX_EXEC_CLUSTER = 0, 1, 2, 3
 LBX_EXEC_KERNELS_ONE_CTA_V = 4
+LBX_EXEC_TC, LBX_EXEC_NO_TC = 5, 6
 
 
 class Branch(ctypes.Structure):

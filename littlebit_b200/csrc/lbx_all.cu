@@ -7,6 +7,7 @@
 #include "pack.cu"
 #include "linear.cu"
 #include "chain.cu"
+#include "wide.cu"
 #include "misc.cu"
 #include "attention.cu"
 #include "lmhead.cu"

@@ -1360,8 +1360,9 @@ static int check_args(const lbx_proj *projs, const lbx_linear_args *a) {
                 "bad epilogue (ADD needs fp32 y)");
   for (int i = 0; i < a->n_proj; ++i) LBX_CHECK_ARG(a->y[i], "y[%d] is NULL", i);
   LBX_CHECK_ARG(a->exec == LBX_EXEC_AUTO || a->exec == LBX_EXEC_KERNELS || a->exec == LBX_EXEC_CLUSTER ||
-                    a->exec == LBX_EXEC_KERNELS_ONE_CTA_V,
-                "bad exec (LBX_EXEC_AUTO, _KERNELS, _CLUSTER or _KERNELS_ONE_CTA_V)");
+                    a->exec == LBX_EXEC_KERNELS_ONE_CTA_V || a->exec == LBX_EXEC_TC ||
+                    a->exec == LBX_EXEC_NO_TC,
+                "bad exec (LBX_EXEC_AUTO, _KERNELS, _CLUSTER, _KERNELS_ONE_CTA_V, _TC or _NO_TC)");
   return LBX_OK;
 }
 
@@ -1937,11 +1938,23 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
 
 }  // namespace lbx
 
+// the tensor-core executor (wide.cu)
+#ifndef LBX_WIDE_MIN_TOKENS
+#define LBX_WIDE_MIN_TOKENS 32  // AUTO / KERNELS calls with at least this many tokens run on it
+#endif
+namespace lbx {
+static size_t wide_ws_bytes(const lbx_proj *projs, int n_proj, int k);
+static int wide_try(const lbx_proj *projs, const lbx_linear_args *a, void *ws, size_t ws_bytes,
+                    cudaStream_t stream, bool &handled);
+}  // namespace lbx
+
 extern "C" size_t lbx_linear_workspace_size(const lbx_proj *projs, int32_t n_proj,
                                             int32_t n_tokens) {
   if (!projs || n_proj < 1 || n_proj > LBX_MAX_PROJ || n_tokens < 1) return 0;
   const int k = n_tokens < LBX_MAX_TOKENS ? n_tokens : LBX_MAX_TOKENS;
-  return lbx::ws_bytes_for(projs, n_proj, k);
+  size_t s = lbx::ws_bytes_for(projs, n_proj, k);
+  if (n_tokens >= LBX_WIDE_MIN_TOKENS) s = std::max(s, lbx::wide_ws_bytes(projs, n_proj, n_tokens));
+  return s;
 }
 
 extern "C" int lbx_linear_verify(const lbx_proj *projs, const lbx_linear_args *a, void *ws,
@@ -1949,6 +1962,9 @@ extern "C" int lbx_linear_verify(const lbx_proj *projs, const lbx_linear_args *a
   using namespace lbx;
   int rc = check_args(projs, a);
   if (rc) return rc;
+  bool handled = false;
+  rc = wide_try(projs, a, ws, ws_bytes, stream, handled);
+  if (handled) return rc;
   const size_t need = ws_bytes_call(projs, a);
   LBX_CHECK_ARG(ws && ws_bytes >= need, "workspace too small (%zu < %zu)", ws_bytes, need);
   // token batches: up to LBX_MAX_TOKENS, fewer when a batch's stages would not
