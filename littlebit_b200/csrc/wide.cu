@@ -38,7 +38,7 @@
 
 namespace lbx {
 
-constexpr int WD_THREADS = 256;   // 8 warps: 4 TMEM lane quarters x 2 token halves
+constexpr int WD_THREADS = 512;   // 16 warps: 4 TMEM lane quarters x 4 token quarters
 constexpr int WD_MAXK = 64;       // tokens per tensor-core batch
 constexpr int WD_NBV = 4;         // B-operand buffers of the V kernel
 constexpr int WD_NBU = 8;         // B-operand buffers of the U kernel
@@ -80,6 +80,12 @@ LBX_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: 
 // 32 lanes x NC consecutive 32-bit columns: thread i gets lane (base lane + i)
 template <int NC>
 LBX_DEV void tmem_ld(uint32_t taddr, uint32_t *r);
+template <>
+LBX_DEV void tmem_ld<4>(uint32_t a, uint32_t *r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
 template <>
 LBX_DEV void tmem_ld<8>(uint32_t a, uint32_t *r) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
@@ -147,6 +153,25 @@ LBX_DEV void wd_expand(uint32_t w, uint4 &c0, uint4 &c1) {
   c0 = make_uint4(pm1bits4(w), pm1bits4(w >> 1), pm1bits4(w >> 2), pm1bits4(w >> 3));
   c1 = make_uint4(pm1bits4(w >> 16), pm1bits4(w >> 17), pm1bits4(w >> 18), pm1bits4(w >> 19));
 }
+// asynchronous global -> shared copies of this thread's own sign words (the
+// thread reads them back after cp.async.wait_group; no barrier involved).
+// src_bytes 0 fills zeros without reading.
+LBX_DEV void cpa16(void *dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+LBX_DEV void cpa8(void *dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+LBX_DEV void cpa4(void *dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+LBX_DEV void cpa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+LBX_DEV void cpa_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 LBX_DEV uint8_t *align1024(uint8_t *p) {
   return p + ((1024u - (smem_u32(p) & 1023u)) & 1023u);
 }
@@ -279,25 +304,29 @@ __global__ void __launch_bounds__(WX_THREADS) wx_stage_kernel(const __grid_const
 }
 
 // ---------------------------------------------------------------------------
-// V-stage on the tensor cores.  Thread (row = tid % 128, half = tid / 128):
-// expands half of its sign row's block (one 128-byte atom row), and in the
-// epilogue reads TMEM lane `row` for tokens [half*KP/2, (half+1)*KP/2).
+// V-stage on the tensor cores.  Thread (row = tid % 128, quarter = tid / 128)
+// expands 2 of the 8 sign words of its row's block and, in the epilogue,
+// reads TMEM lane `row` (its warp's lane quarter) for tokens
+// [quarter*KP/4, (quarter+1)*KP/4).
 // ---------------------------------------------------------------------------
 template <int KP>
 __global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant__ WParams p) {
-  constexpr int N = 2 * KP, KH = KP / 2;
+  constexpr int N = 2 * KP, KQ = KP / 4;
   constexpr int SB = N * 256 + 1024;  // B buffer: image (two atoms of N x 128 B), then the block scales
   constexpr uint32_t IDESC = idesc_i8(N);
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sA = align1024(smem_raw);  // 2 x (2 atoms x 128 rows x 128 B)
   uint8_t *sB = sA + 2 * 32768;        // WD_NBV x SB
+  uint2 *sQ = reinterpret_cast<uint2 *>(sB + WD_NBV * SB);  // [WD_PD][threads] sign-word ring
   __shared__ __align__(8) uint64_t bbar[WD_NBV];
   __shared__ __align__(8) uint64_t mbar[2];
   __shared__ uint32_t tbase;
   __shared__ uint16_t blist[WD_MAXBLK];
   __shared__ int gmx[2][KP];
+  __shared__ int gex[KP];
+  __shared__ float gsc[KP];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int row = tid & 127, half = tid >> 7;
+  const int row = tid & 127, qd = tid >> 7;
   int si = 0;
   while (si + 1 < p.nseg && (int)blockIdx.x >= p.seg[si + 1].tile0) ++si;
   const WSeg &sg = p.seg[si];
@@ -327,17 +356,15 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant
   const uint32_t tmem = tbase;
 
   const int32_t *vrow = sg.v_sign + (int64_t)(rvalid ? rr : 0) * p.Wv;
+  // this thread's 2 sign words of block i into ring slot i % WD_PD (one commit group per block)
   auto load_bits = [&](int i) {
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (i < nb && rvalid) {
-      const int w0 = 8 * (blist[i] & 0x7fff) + 4 * half;
-      if (w0 < p.Wv) v = __ldg(reinterpret_cast<const uint4 *>(vrow + w0));
-    }
-    return v;
+    const int w0 = i < nb ? 8 * (blist[i] & 0x7fff) + 2 * qd : 0;
+    const bool v = i < nb && rvalid && w0 < p.Wv;
+    cpa8(&sQ[(i % WD_PD) * WD_THREADS + tid], vrow + (v ? w0 : 0), v ? 8u : 0u);
+    cpa_commit();
   };
-  uint4 q[WD_PD];
 #pragma unroll
-  for (int j = 0; j < WD_PD; ++j) q[j] = load_bits(j);
+  for (int j = 0; j + 1 < WD_PD; ++j) load_bits(j);
   const int rec_copy = p.rec_bytes;
   int nissued = 0, nused = 0, ncommit = 0;  // (thread 0) B copies issued / waited for, MMA commits
   auto issue_b = [&](int i) {
@@ -353,9 +380,9 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant
   if (tid == 0)
     for (int j = 0; j < 2 && j < nb; ++j) issue_b(j);
 
-  float T[KH], V[KH];
+  float T[KQ], V[KQ];
 #pragma unroll
-  for (int i = 0; i < KH; ++i) T[i] = V[i] = 0.f;
+  for (int i = 0; i < KQ; ++i) T[i] = V[i] = 0.f;
 
   int mine = 1;  // this thread's waits all completed
   // (warp-uniform outcome: tcgen05.ld is a whole-warp instruction)
@@ -368,16 +395,19 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant
       mine = 0;
       return;
     }
-    const float *inv = reinterpret_cast<const float *>(sB + (j % WD_NBV) * SB + N * 256) + half * KH;
-    uint32_t r[KP];
-    tmem_ld_cols<KP>(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((j & 1) * N + half * KP), r);
+    const float *inv = reinterpret_cast<const float *>(sB + (j % WD_NBV) * SB + N * 256) + qd * KQ;
+    uint32_t r[2 * KQ];
+    tmem_ld_cols<2 * KQ>(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((j & 1) * N + qd * 2 * KQ), r);
     tmem_ld_wait();
     const bool last = (blist[j] & 0x8000) != 0;
 #pragma unroll
-    for (int i = 0; i < KH; ++i) {
+    for (int i = 0; i < KQ; ++i) {
       const int val = 256 * (int)r[2 * i] + (int)r[2 * i + 1];
       T[i] += __fmul_rn(__int2float_rn(val), inv[i]);
-      if (last) {
+    }
+    if (last) {
+#pragma unroll
+      for (int i = 0; i < KQ; ++i) {
         V[i] += T[i];
         T[i] = 0.f;
       }
@@ -386,17 +416,21 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant
 
   bool ok = true;
   for (int i = 0; i < nb; ++i) {
-    const uint4 qn = load_bits(i + WD_PD);
+    if (i == 10) LBX_PROBE(45);
+    load_bits(i + WD_PD - 1);
+    cpa_wait<WD_PD - 1>();  // block i's words have landed
+    if (i == 10) LBX_PROBE(46);
     {  // expand block i into A buffer i & 1 (its previous MMA, block i-2, has completed)
-      uint8_t *a = sA + (i & 1) * 32768 + half * 16384;
-      const uint32_t wv[4] = {q[0].x, q[0].y, q[0].z, q[0].w};
-#pragma unroll
-      for (int wi = 0; wi < 4; ++wi) {
-        uint4 c0, c1;
-        wd_expand(wv[wi], c0, c1);
-        *reinterpret_cast<uint4 *>(a + sw128_off(row, 32 * wi)) = c0;
-        *reinterpret_cast<uint4 *>(a + sw128_off(row, 32 * wi + 16)) = c1;
-      }
+      uint8_t *a = sA + (i & 1) * 32768 + (qd >> 1) * 16384;
+      const uint2 q = sQ[(i % WD_PD) * WD_THREADS + tid];
+      const int c0 = 32 * 2 * (qd & 1);
+      uint4 e0, e1;
+      wd_expand(q.x, e0, e1);
+      *reinterpret_cast<uint4 *>(a + sw128_off(row, c0)) = e0;
+      *reinterpret_cast<uint4 *>(a + sw128_off(row, c0 + 16)) = e1;
+      wd_expand(q.y, e0, e1);
+      *reinterpret_cast<uint4 *>(a + sw128_off(row, c0 + 32)) = e0;
+      *reinterpret_cast<uint4 *>(a + sw128_off(row, c0 + 48)) = e1;
     }
     fence_proxy_async();
     tc_fence_before();
@@ -404,11 +438,13 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant
       ok = false;
       break;
     }
+    if (i == 10) LBX_PROBE(47);
     if (tid == 0) {
       // B of block i+2 into the buffer of block i-2 (its MMA and epilogue are done)
       if (i + 2 < nb) issue_b(i + 2);
       tc_fence_after();
       if (mbar_poll_cta(&bbar[i % WD_NBV], (uint32_t)(i / WD_NBV) & 1u, 0x701)) {
+        if (i == 10) LBX_PROBE(48);
         ++nused;
         const uint32_t aB = smem_u32(sA + (i & 1) * 32768), bB = smem_u32(sB + (i % WD_NBV) * SB);
 #pragma unroll
@@ -424,10 +460,9 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant
       }
     }
     if (i >= 1) epilogue(i - 1);
-#pragma unroll
-    for (int j = 0; j + 1 < WD_PD; ++j) q[j] = q[j + 1];
-    q[WD_PD - 1] = qn;
+    if (i == 10) LBX_PROBE(49);
   }
+  cpa_wait<0>();
   if (ok) ok = __syncthreads_and(mine);
   if (ok) epilogue(nb - 1);
   LBX_PROBE(43);
@@ -447,8 +482,8 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant
   const float m0 = rvalid ? sg.mid0[rr] : 0.f;
   const float m1 = rvalid && sg.mid1 ? sg.mid1[rr] : 0.f;
 #pragma unroll
-  for (int i = 0; i < KH; ++i) {
-    const int t = half * KH + i;
+  for (int i = 0; i < KQ; ++i) {
+    const int t = qd * KQ + i;
     float vv = V[i];
     if (rms && t < k) vv *= __ldcg(sg.rs + t);
     T[i] = vv;
@@ -457,23 +492,27 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant
   for (int sd = 0; sd < nside; ++sd) {
     const float mm = sd ? m1 : m0;
 #pragma unroll
-    for (int i = 0; i < KH; ++i) {
-      const int t = half * KH + i;
+    for (int i = 0; i < KQ; ++i) {
+      const int t = qd * KQ + i;
       const float z = rvalid && t < k ? mm * T[i] : 0.f;
       V[i] = z;
       const int mb = __reduce_max_sync(0xffffffffu, __float_as_int(fabsf(z)));
       if (lane == 0 && mb) atomicMax(&gmx[sd][t], mb);
     }
     __syncthreads();
+    if (tid < KP) {  // the group exponent of each token, once
+      const float gm = __int_as_float(gmx[sd][tid]);
+      const int ex = tid < k && gm > 0.f ? u_group_exp(gm) : UE_NONE;
+      gex[tid] = ex;
+      gsc[tid] = ex == UE_NONE ? 0.f : pow2f(ex);
+    }
+    __syncthreads();
     uint8_t *im = img + sd * 16384;
     const int pos = 32 * (row >> 5) + wd_pos(row & 31);
 #pragma unroll
-    for (int i = 0; i < KH; ++i) {
-      const int t = half * KH + i;
-      const float gm = __int_as_float(gmx[sd][t]);
-      const int ex = gm > 0.f ? u_group_exp(gm) : UE_NONE;
-      const float sc = ex == UE_NONE ? 0.f : pow2f(ex);
-      const int qv = t < k ? __float2int_rn(V[i] * sc) : 0;
+    for (int i = 0; i < KQ; ++i) {
+      const int t = qd * KQ + i;
+      const int qv = t < k ? __float2int_rn(V[i] * gsc[t]) : 0;
       int hi, lo;
       split_digits(qv, hi, lo);
       im[sw128_off(2 * t, pos)] = (uint8_t)hi;
@@ -483,33 +522,34 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant
     uint8_t *rec = (sd ? sg.urec1 : sg.urec0) + (size_t)grp * p.urec_bytes;
     for (int o = 16 * tid; o < N * 128; o += 16 * WD_THREADS)
       *reinterpret_cast<uint4 *>(rec + o) = *reinterpret_cast<const uint4 *>(im + o);
-    if (tid < KP) {
-      const float gm = __int_as_float(gmx[sd][tid]);
-      reinterpret_cast<int *>(rec + N * 128)[tid] = tid < k && gm > 0.f ? u_group_exp(gm) : UE_NONE;
-    }
+    if (tid < KP) reinterpret_cast<int *>(rec + N * 128)[tid] = gex[tid];
+    __syncthreads();  // (gex / gsc are rewritten by the next side)
   }
   LBX_PROBE(44);
 }
 
 // ---------------------------------------------------------------------------
-// U-stage on the tensor cores.  Thread (row, half) as in wv_kernel; rows are
-// output rows, the K dimension one quantisation group (128 ranks) per step.
+// U-stage on the tensor cores.  Thread (row, quarter) as in wv_kernel; rows
+// are output rows, the K dimension one quantisation group (128 ranks) per
+// step, each thread expanding one of the group's 4 sign words of its row.
 // ---------------------------------------------------------------------------
 template <int KP>
 __global__ void __launch_bounds__(WD_THREADS, 1) wu_kernel(const __grid_constant__ WParams p) {
-  constexpr int N = 2 * KP, KH = KP / 2;
+  constexpr int N = 2 * KP, KQ = KP / 4;
   constexpr int SBU = ((N * 128 + KP * 4) + 1023) & ~1023;  // B buffer: image, then the group exponents
   constexpr uint32_t IDESC = idesc_i8(N);
   constexpr int PF = WD_NBU - 2;  // B copies in flight ahead of the MMA
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sA = align1024(smem_raw);  // 2 x (128 rows x 128 B)
   uint8_t *sB = sA + 2 * 16384;        // WD_NBU x SBU
+  uint32_t *sQ = reinterpret_cast<uint32_t *>(sB + WD_NBU * SBU);  // [WD_PD][threads] sign-word ring
   __shared__ __align__(8) uint64_t bbar[WD_NBU];
   __shared__ __align__(8) uint64_t mbar[2];
   __shared__ uint32_t tbase;
   __shared__ int ec[2][KP];
+  __shared__ int2 rtab[WD_THREADS / 32][KQ];  // per warp: (add, shift) of the group being rounded
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int row = tid & 127, half = tid >> 7;
+  const int row = tid & 127, qd = tid >> 7;
   int pi = 0;
   while (pi + 1 < p.nproj && (int)blockIdx.x >= p.up[pi + 1].tile0) ++pi;
   const WUProj &pj = p.up[pi];
@@ -517,7 +557,6 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wu_kernel(const __grid_constant
   const bool nvalid = n < pj.out;
   const int k = p.k;
   const int ng0 = pj.ng[0], ngt = pj.ng[0] + (pj.nbr > 1 ? pj.ng[1] : 0);
-  (void)lane;
   LBX_PROBE(50);
 
   if (tid == 0) {
@@ -532,21 +571,18 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wu_kernel(const __grid_constant
   tc_fence_after();
   const uint32_t tmem = tbase;
 
-  // this thread's two sign words of group G (words 4g + 2*half, +1 of its row)
+  // this thread's sign word of group G (word 4g + quarter of its row) into
+  // ring slot G % WD_PD (one commit group per group)
   auto load_bits = [&](int G) {
-    uint2 v = make_uint2(0u, 0u);
-    if (G < ngt && nvalid) {
-      const int b = G < ng0 ? 0 : 1, g = b ? G - ng0 : G;
-      const int w0 = 4 * g + 2 * half, W = pj.words[b];
-      const int32_t *src = pj.u_sign[b] + (int64_t)n * W + w0;
-      if (w0 < W) v.x = (uint32_t)__ldg(src);
-      if (w0 + 1 < W) v.y = (uint32_t)__ldg(src + 1);
-    }
-    return v;
+    const int b = G < ng0 ? 0 : 1, g = b ? G - ng0 : G;
+    const int w0 = 4 * g + qd, W = pj.words[b];
+    const bool v = G < ngt && nvalid && w0 < W;
+    cpa4(&sQ[(G % WD_PD) * WD_THREADS + tid], v ? pj.u_sign[b] + (int64_t)n * W + w0 : pj.u_sign[0],
+         v ? 4u : 0u);
+    cpa_commit();
   };
-  uint2 q[WD_PD];
 #pragma unroll
-  for (int j = 0; j < WD_PD; ++j) q[j] = load_bits(j);
+  for (int j = 0; j + 1 < WD_PD; ++j) load_bits(j);
   int nissued = 0, nused = 0, ncommit = 0;  // (thread 0) B copies issued / waited for, MMA commits
   auto issue_b = [&](int G) {
     const int buf = G % WD_NBU;
@@ -573,9 +609,9 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wu_kernel(const __grid_constant
   }
   LBX_PROBE(52);
 
-  int I0[KH], I1[KH];
+  int I0[KQ], I1[KQ];
 #pragma unroll
-  for (int i = 0; i < KH; ++i) I0[i] = I1[i] = 0;
+  for (int i = 0; i < KQ; ++i) I0[i] = I1[i] = 0;
 
   int mine = 1;  // this thread's waits all completed
   // (warp-uniform outcome: tcgen05.ld is a whole-warp instruction)
@@ -589,34 +625,47 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wu_kernel(const __grid_constant
       return;
     }
     const int b = G < ng0 ? 0 : 1;
-    const int *ue = reinterpret_cast<const int *>(sB + (G % WD_NBU) * SBU + N * 128) + half * KH;
-    const int *ecb = &ec[b][half * KH];
-    uint32_t r[KP];
-    tmem_ld_cols<KP>(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((G & 1) * N + half * KP), r);
+    uint32_t r[2 * KQ];
+    tmem_ld_cols<2 * KQ>(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((G & 1) * N + qd * 2 * KQ), r);
+    // the rounding of this group for the warp's tokens: rshr(v, e - ec) as
+    // (v + add) >> shift (shift 31 with add 2^30 gives 0 for every |v| < 2^30;
+    // an all-zero group has v = 0)
+    if (lane < KQ) {
+      const int t = qd * KQ + lane;
+      const int ex = reinterpret_cast<const int *>(sB + (G % WD_NBU) * SBU + N * 128)[t];
+      const int s = ex == UE_NONE ? 0 : min(ex - ec[b][t], 31);
+      rtab[warp][lane] = make_int2(s > 0 ? 1 << (s - 1) : 0, s);
+    }
+    __syncwarp();
     tmem_ld_wait();
+    if (b) {
 #pragma unroll
-    for (int i = 0; i < KH; ++i) {
-      const int ex = ue[i];
-      if (ex != UE_NONE) {
-        const int v = rshr(256 * (int)r[2 * i] + (int)r[2 * i + 1], ex - ecb[i]);
-        if (b) I1[i] += v;
-        else I0[i] += v;
+      for (int i = 0; i < KQ; ++i) {
+        const int2 as = rtab[warp][i];
+        I1[i] += (256 * (int)r[2 * i] + (int)r[2 * i + 1] + as.x) >> as.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < KQ; ++i) {
+        const int2 as = rtab[warp][i];
+        I0[i] += (256 * (int)r[2 * i] + (int)r[2 * i + 1] + as.x) >> as.y;
       }
     }
+    __syncwarp();  // (rtab is rewritten by the next group)
   };
 
   bool ok = true;
   for (int G = 0; G < ngt; ++G) {
-    const uint2 qn = load_bits(G + WD_PD);
+    if (G == 20) LBX_PROBE(55);
+    load_bits(G + WD_PD - 1);
+    cpa_wait<WD_PD - 1>();  // group G's words have landed
+    if (G == 20) LBX_PROBE(56);
     {  // expand group G into A buffer G & 1 (its previous MMA, group G-2, has completed)
       uint8_t *a = sA + (G & 1) * 16384;
-      uint4 c0, c1;
-      wd_expand(q[0].x, c0, c1);
-      *reinterpret_cast<uint4 *>(a + sw128_off(row, 64 * half)) = c0;
-      *reinterpret_cast<uint4 *>(a + sw128_off(row, 64 * half + 16)) = c1;
-      wd_expand(q[0].y, c0, c1);
-      *reinterpret_cast<uint4 *>(a + sw128_off(row, 64 * half + 32)) = c0;
-      *reinterpret_cast<uint4 *>(a + sw128_off(row, 64 * half + 48)) = c1;
+      uint4 e0, e1;
+      wd_expand(sQ[(G % WD_PD) * WD_THREADS + tid], e0, e1);
+      *reinterpret_cast<uint4 *>(a + sw128_off(row, 32 * qd)) = e0;
+      *reinterpret_cast<uint4 *>(a + sw128_off(row, 32 * qd + 16)) = e1;
     }
     fence_proxy_async();
     tc_fence_before();
@@ -624,11 +673,13 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wu_kernel(const __grid_constant
       ok = false;
       break;
     }
+    if (G == 20) LBX_PROBE(57);
     if (tid == 0) {
       // B of group G+PF into the buffer of group G-2 (its MMA and epilogue are done)
       if (G + PF < ngt) issue_b(G + PF);
       tc_fence_after();
       if (mbar_poll_cta(&bbar[G % WD_NBU], (uint32_t)(G / WD_NBU) & 1u, 0x711)) {
+        if (G == 20) LBX_PROBE(58);
         ++nused;
         const uint32_t aB = smem_u32(sA + (G & 1) * 16384), bB = smem_u32(sB + (G % WD_NBU) * SBU);
 #pragma unroll
@@ -642,10 +693,9 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wu_kernel(const __grid_constant
       }
     }
     if (G >= 1) epilogue(G - 1);
-#pragma unroll
-    for (int j = 0; j + 1 < WD_PD; ++j) q[j] = q[j + 1];
-    q[WD_PD - 1] = qn;
+    if (G == 20) LBX_PROBE(59);
   }
+  cpa_wait<0>();
   if (ok) ok = __syncthreads_and(mine);
   if (ok && ngt > 0) epilogue(ngt - 1);
   LBX_PROBE(53);
@@ -662,8 +712,8 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wu_kernel(const __grid_constant
   const float u1b = pj.nbr > 1 ? pj.u1[1][n] : 0.f;
   const float bias = pj.bias ? pj.bias[n] : 0.f;
 #pragma unroll
-  for (int i = 0; i < KH; ++i) {
-    const int t = half * KH + i;
+  for (int i = 0; i < KQ; ++i) {
+    const int t = qd * KQ + i;
     if (t >= k) break;
     float v = u_result(u1a, I0[i], ec[0][t], pj.nbr > 1, u1b, I1[i], ec[1][t], pj.bias != nullptr, bias);
     if (p.epi == LBX_EPI_SILU0 && pi == 0) v = v / (1.0f + expf(-v));
@@ -685,9 +735,12 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wu_kernel(const __grid_constant
 static int wide_kp(int k) { return k <= 8 ? 8 : k <= 16 ? 16 : k <= 32 ? 32 : 64; }
 static int wide_rec_bytes(int KP) { return (2 * KP * 256 + KP * 4 + 15) & ~15; }
 static int wide_urec_bytes(int KP) { return (2 * KP * 128 + KP * 4 + 15) & ~15; }
-static size_t wv_smem(int KP) { return 1024 + 2 * 32768 + (size_t)WD_NBV * (2 * KP * 256 + 1024); }
+static size_t wv_smem(int KP) {
+  return 1024 + 2 * 32768 + (size_t)WD_NBV * (2 * KP * 256 + 1024) + (size_t)WD_PD * WD_THREADS * 8;
+}
 static size_t wu_smem(int KP) {
-  return 1024 + 2 * 16384 + (size_t)WD_NBU * (((2 * KP * 128 + KP * 4) + 1023) & ~1023);
+  return 1024 + 2 * 16384 + (size_t)WD_NBU * (((2 * KP * 128 + KP * 4) + 1023) & ~1023) +
+         (size_t)WD_PD * WD_THREADS * 4;
 }
 
 // scratch of one tensor-core batch of k tokens (0: the call does not fit it)
