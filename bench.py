@@ -805,16 +805,25 @@ def run_row_shard(args, dev, rank, ws, reps: int = 200):
     t_fused = timed(lambda: fsh.forward(x, yf))
     ref = gat.permute(1, 0, 2).reshape(1, N)
     same = bool(torch.equal(fsh.forward(x, yf), ref))
+    # the whole layer on this GPU alone: the sharded result must be its bits
+    yfull = torch.empty(1, N, device=dev)
+    t_unsharded = timed(lambda: ops.linear_group([full], x, [yfull]))
+    same_full = bool(torch.equal(yf, yfull))
     dev_err = ops.device_error(dev)
     fsh.close()
-    if not same or dev_err:
-        raise RuntimeError(f"fused all-gather disagrees with NCCL (equal={same}, device error {dev_err:#x})")
+    if not same or not same_full or dev_err:
+        raise RuntimeError(f"fused all-gather disagrees (equal to NCCL {same}, to the unsharded layer {same_full}, "
+                           f"device error {dev_err:#x})")
     alg = (r * K + 7) // 8 + (N * r + 7) // 8 + 4 * (K + r + N) + 4 * K + 4 * N
     return {"workload": f"LittleBitLinear {K}->{N} r={r}, k=1 fp32, U rows split over {ws} GPUs, "
                         f"V replicated, y all-gathered",
             "us_per_call": round(t_fused, 3), "local_kernel_us": round(t_local, 3),
             "nccl_us_per_call": round(t_all, 3), "nccl_allgather_us": round(t_ag, 3),
             "fused_us_per_call": round(t_fused, 3), "fused_equals_nccl": same,
+            "fused_equals_unsharded": same_full, "unsharded_us_per_call": round(t_unsharded, 3),
+            "exchange_us": round(t_fused - t_local, 3),
+            "limiter": "the replicated V-stage and the two stage launches: the layer is latency-bound at one "
+                       "token (2.8 MB in ~10 us), so splitting its rows shortens only the U-stage body",
             "allgather_bytes_per_rank": 4 * N // ws,
             "gbs_whole_layer": round(alg / (t_fused * 1e-6) / 1e9, 2), "algorithmic_bytes": alg,
             "timing": f"CUDA events over {reps} calls ({per} per CUDA graph), max over ranks"}

@@ -38,7 +38,6 @@
 
 namespace lbx {
 
-constexpr int WD_THREADS = 512;   // 16 warps: 4 TMEM lane quarters x 4 token quarters
 constexpr int WD_MAXK = 64;       // tokens per tensor-core batch
 constexpr int WD_NBV = 4;         // B-operand buffers of the V kernel
 constexpr int WD_NBU = 8;         // B-operand buffers of the U kernel
@@ -304,37 +303,78 @@ __global__ void __launch_bounds__(WX_THREADS) wx_stage_kernel(const __grid_const
 }
 
 // ---------------------------------------------------------------------------
-// V-stage on the tensor cores.  Thread (row = tid % 128, quarter = tid / 128)
-// expands 2 of the 8 sign words of its row's block and, in the epilogue,
-// reads TMEM lane `row` (its warp's lane quarter) for tokens
-// [quarter*KP/4, (quarter+1)*KP/4).
+// Warp roles of the tensor-core stages: warps 0-15 expand the sign rows
+// (operand A) and read the accumulators back; warp 16 issues the operand-B
+// copies and the MMAs.  They meet only at mbarriers:
+//   afull[j]  the 512 expanding threads have written A buffer j
+//   dfull[j]  the MMAs into TMEM buffer j (and their reads of A buffer j and
+//             of the B buffer) completed (tcgen05.commit)
+//   dfree[j]  the 512 reading threads have loaded TMEM buffer j and read what
+//             they need of the step's B buffer
+// Every wait gives up after 1 s or as soon as another thread gave up (the
+// CTA's abort flag), so a fault anywhere ends the kernel promptly.
+// ---------------------------------------------------------------------------
+constexpr int WD_CW = 512;                // expanding / reading threads
+constexpr int WD_TPB = WD_CW + 32;        // plus the issuing warp
+
+// (try_wait suspends the thread in hardware until the phase completes or a
+// short time limit passes, so waiting warps leave the issue slots to the
+// working ones)
+LBX_DEV bool wd_wait(uint64_t *bar, uint32_t parity, int code, volatile int *abort) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 7u) == 0) {
+      if (*abort) return false;
+      uint64_t t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (it == 0) t0 = t;
+      else if (t - t0 > 1000000000ull) {
+        *abort = 1;
+        atomicCAS(&g_lbx_device_error, 0, code);
+        return false;
+      }
+    }
+  }
+}
+LBX_DEV void mbar_arrive1(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// V-stage on the tensor cores.  Expanding thread (row = tid % 128, quarter =
+// tid / 128) expands 2 of the 8 sign words of its row's block and reads TMEM
+// lane `row` (its warp's lane quarter) for tokens [quarter*KP/4, +KP/4).
 // ---------------------------------------------------------------------------
 template <int KP>
-__global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant__ WParams p) {
+__global__ void __launch_bounds__(WD_TPB, 1) wv_kernel(const __grid_constant__ WParams p) {
   constexpr int N = 2 * KP, KQ = KP / 4;
   constexpr int SB = N * 256 + 1024;  // B buffer: image (two atoms of N x 128 B), then the block scales
   constexpr uint32_t IDESC = idesc_i8(N);
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sA = align1024(smem_raw);  // 2 x (2 atoms x 128 rows x 128 B)
   uint8_t *sB = sA + 2 * 32768;        // WD_NBV x SB
-  uint2 *sQ = reinterpret_cast<uint2 *>(sB + WD_NBV * SB);  // [WD_PD][threads] sign-word ring
+  uint2 *sQ = reinterpret_cast<uint2 *>(sB + WD_NBV * SB);  // [WD_PD][WD_CW] sign-word ring
   __shared__ __align__(8) uint64_t bbar[WD_NBV];
-  __shared__ __align__(8) uint64_t mbar[2];
+  __shared__ __align__(8) uint64_t afull[2], dfull[2], dfree[2];
   __shared__ uint32_t tbase;
+  __shared__ int abort_flag;
   __shared__ uint16_t blist[WD_MAXBLK];
   __shared__ int gmx[2][KP];
   __shared__ int gex[KP];
   __shared__ float gsc[KP];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int row = tid & 127, qd = tid >> 7;
+  const bool cw = tid < WD_CW;
+  const int row = tid & 127, qd = (tid >> 7) & 3;
   int si = 0;
   while (si + 1 < p.nseg && (int)blockIdx.x >= p.seg[si + 1].tile0) ++si;
   const WSeg &sg = p.seg[si];
   const int grp = (int)blockIdx.x - sg.tile0;
   const int rr = grp * 128 + row;
-  const bool rvalid = rr < sg.rank;
+  const bool rvalid = cw && rr < sg.rank;
   const int nb = p.nblk;
   const int k = p.k;
+  volatile int *abrt = &abort_flag;
   LBX_PROBE(40);
 
   if (tid == 0) {
@@ -344,12 +384,16 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant
     for (int w = 0; w < 16; ++w)
       for (int b = w; b < nb; b += 16) blist[i++] = (uint16_t)(b | (b + 16 >= nb ? 0x8000 : 0));
     for (int j = 0; j < WD_NBV; ++j) mbar_init(&bbar[j], 1);
-    mbar_init(&mbar[0], 1);
-    mbar_init(&mbar[1], 1);
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&afull[j], WD_CW);
+      mbar_init(&dfull[j], 1);
+      mbar_init(&dfree[j], WD_CW);
+    }
     fence_mbar_init();
+    abort_flag = 0;
   }
   if (tid < 2 * KP) (&gmx[0][0])[tid] = 0;
-  if (warp == 0) tmem_alloc(&tbase, 2 * N);
+  if (warp == 16) tmem_alloc(&tbase, 2 * N);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -360,92 +404,45 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant
   auto load_bits = [&](int i) {
     const int w0 = i < nb ? 8 * (blist[i] & 0x7fff) + 2 * qd : 0;
     const bool v = i < nb && rvalid && w0 < p.Wv;
-    cpa8(&sQ[(i % WD_PD) * WD_THREADS + tid], vrow + (v ? w0 : 0), v ? 8u : 0u);
+    cpa8(&sQ[(i % WD_PD) * WD_CW + tid], vrow + (v ? w0 : 0), v ? 8u : 0u);
     cpa_commit();
   };
+  if (cw) {
 #pragma unroll
-  for (int j = 0; j + 1 < WD_PD; ++j) load_bits(j);
-  const int rec_copy = p.rec_bytes;
-  int nissued = 0, nused = 0, ncommit = 0;  // (thread 0) B copies issued / waited for, MMA commits
-  auto issue_b = [&](int i) {
-    const int buf = i % WD_NBV;
-    mbar_arrive_expect_tx(&bbar[buf], (uint32_t)rec_copy);
-    bulk_g2s(sB + buf * SB, sg.xrec + (size_t)(blist[i] & 0x7fff) * p.rec_bytes, (uint32_t)rec_copy, &bbar[buf]);
-    ++nissued;
-  };
+    for (int j = 0; j + 1 < WD_PD; ++j) load_bits(j);
+  }
   LBX_PROBE(41);
   pdl_trigger();
   pdl_wait();  // x records come from the staging grid
   LBX_PROBE(42);
-  if (tid == 0)
-    for (int j = 0; j < 2 && j < nb; ++j) issue_b(j);
 
   float T[KQ], V[KQ];
 #pragma unroll
   for (int i = 0; i < KQ; ++i) T[i] = V[i] = 0.f;
 
-  int mine = 1;  // this thread's waits all completed
-  // (warp-uniform outcome: tcgen05.ld is a whole-warp instruction)
-  auto epilogue = [&](int j) {
-    bool okw = mbar_poll_cta(&mbar[j & 1], (uint32_t)(j >> 1) & 1u, 0x702) &&
-               mbar_poll_cta(&bbar[j % WD_NBV], (uint32_t)(j / WD_NBV) & 1u, 0x703);
-    okw = __all_sync(0xffffffffu, okw);
-    tc_fence_after();
-    if (!okw) {
-      mine = 0;
-      return;
-    }
-    const float *inv = reinterpret_cast<const float *>(sB + (j % WD_NBV) * SB + N * 256) + qd * KQ;
-    uint32_t r[2 * KQ];
-    tmem_ld_cols<2 * KQ>(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((j & 1) * N + qd * 2 * KQ), r);
-    tmem_ld_wait();
-    const bool last = (blist[j] & 0x8000) != 0;
-#pragma unroll
-    for (int i = 0; i < KQ; ++i) {
-      const int val = 256 * (int)r[2 * i] + (int)r[2 * i + 1];
-      T[i] += __fmul_rn(__int2float_rn(val), inv[i]);
-    }
-    if (last) {
-#pragma unroll
-      for (int i = 0; i < KQ; ++i) {
-        V[i] += T[i];
-        T[i] = 0.f;
+  if (warp == 16) {
+    // ---- issuing warp (lane 0 acts, the warp stays converged)
+    int nissued = 0, ncommit = 0;
+    auto issue_b = [&](int i) {
+      if (lane == 0) {
+        const int buf = i % WD_NBV;
+        mbar_arrive_expect_tx(&bbar[buf], (uint32_t)p.rec_bytes);
+        bulk_g2s(sB + buf * SB, sg.xrec + (size_t)(blist[i] & 0x7fff) * p.rec_bytes, (uint32_t)p.rec_bytes,
+                 &bbar[buf]);
       }
-    }
-  };
-
-  bool ok = true;
-  for (int i = 0; i < nb; ++i) {
-    if (i == 10) LBX_PROBE(45);
-    load_bits(i + WD_PD - 1);
-    cpa_wait<WD_PD - 1>();  // block i's words have landed
-    if (i == 10) LBX_PROBE(46);
-    {  // expand block i into A buffer i & 1 (its previous MMA, block i-2, has completed)
-      uint8_t *a = sA + (i & 1) * 32768 + (qd >> 1) * 16384;
-      const uint2 q = sQ[(i % WD_PD) * WD_THREADS + tid];
-      const int c0 = 32 * 2 * (qd & 1);
-      uint4 e0, e1;
-      wd_expand(q.x, e0, e1);
-      *reinterpret_cast<uint4 *>(a + sw128_off(row, c0)) = e0;
-      *reinterpret_cast<uint4 *>(a + sw128_off(row, c0 + 16)) = e1;
-      wd_expand(q.y, e0, e1);
-      *reinterpret_cast<uint4 *>(a + sw128_off(row, c0 + 32)) = e0;
-      *reinterpret_cast<uint4 *>(a + sw128_off(row, c0 + 48)) = e1;
-    }
-    fence_proxy_async();
-    tc_fence_before();
-    if (!__syncthreads_and(mine)) {  // a wait ran out: stop (uniform)
-      ok = false;
-      break;
-    }
-    if (i == 10) LBX_PROBE(47);
-    if (tid == 0) {
-      // B of block i+2 into the buffer of block i-2 (its MMA and epilogue are done)
-      if (i + 2 < nb) issue_b(i + 2);
+      ++nissued;
+    };
+    for (int j = 0; j < WD_NBV && j < nb; ++j) issue_b(j);
+    for (int i = 0; i < nb; ++i) {
+      if (i >= 2) {  // TMEM buffer i & 1 and the B buffer of block i-2 are free again
+        if (!__all_sync(0xffffffffu, wd_wait(&dfree[i & 1], (uint32_t)((i - 2) >> 1) & 1u, 0x706, abrt))) break;
+        if (i + 2 < nb) issue_b(i + 2);
+      }
+      if (!__all_sync(0xffffffffu, wd_wait(&afull[i & 1], (uint32_t)(i >> 1) & 1u, 0x707, abrt))) break;
+      if (!__all_sync(0xffffffffu, wd_wait(&bbar[i % WD_NBV], (uint32_t)(i / WD_NBV) & 1u, 0x701, abrt))) break;
+      __syncwarp();
       tc_fence_after();
-      if (mbar_poll_cta(&bbar[i % WD_NBV], (uint32_t)(i / WD_NBV) & 1u, 0x701)) {
-        if (i == 10) LBX_PROBE(48);
-        ++nused;
+      if (lane == 0) {
         const uint32_t aB = smem_u32(sA + (i & 1) * 32768), bB = smem_u32(sB + (i % WD_NBV) * SB);
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
@@ -453,26 +450,84 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant
           umma_i8(tmem + (uint32_t)((i & 1) * N), sw128_desc(aB + at * 16384 + ko),
                   sw128_desc(bB + at * N * 128 + ko), IDESC, s > 0 ? 1u : 0u);
         }
-        umma_commit(&mbar[i & 1]);
-        ++ncommit;
-      } else {
-        mine = 0;
+        umma_commit(&dfull[i & 1]);
       }
+      ++ncommit;
+      __syncwarp();
     }
-    if (i >= 1) epilogue(i - 1);
-    if (i == 10) LBX_PROBE(49);
+    if (*abrt && lane == 0) {  // work in flight ends before shared memory and TMEM are released
+      const int nused = ncommit;
+      for (int j = nused; j < nissued; ++j) mbar_poll_cta(&bbar[j % WD_NBV], (uint32_t)(j / WD_NBV) & 1u, 0x704);
+      if (ncommit > 0) mbar_poll_cta(&dfull[(ncommit - 1) & 1], (uint32_t)((ncommit - 1) >> 1) & 1u, 0x705);
+    }
+    __syncwarp();
+  } else {
+    // ---- expanding / reading warps
+    auto epilogue = [&](int j) {
+      bool okw = wd_wait(&dfull[j & 1], (uint32_t)(j >> 1) & 1u, 0x702, abrt) &&
+                 wd_wait(&bbar[j % WD_NBV], (uint32_t)(j / WD_NBV) & 1u, 0x703, abrt);
+      okw = __all_sync(0xffffffffu, okw);
+      tc_fence_after();
+      if (!okw) return false;
+      const float *inv = reinterpret_cast<const float *>(sB + (j % WD_NBV) * SB + N * 256) + qd * KQ;
+      float iv[KQ];
+#pragma unroll
+      for (int i = 0; i < KQ; ++i) iv[i] = inv[i];
+      const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((j & 1) * N + qd * 2 * KQ);
+      uint32_t r[2 * KQ];
+      tmem_ld_cols<2 * KQ>(ta, r);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive1(&dfree[j & 1]);
+#pragma unroll
+      for (int i = 0; i < KQ; ++i) {
+        const int val = 256 * (int)r[2 * i] + (int)r[2 * i + 1];
+        T[i] += __fmul_rn(__int2float_rn(val), iv[i]);
+      }
+      if (blist[j] & 0x8000) {
+#pragma unroll
+        for (int i = 0; i < KQ; ++i) {
+          V[i] += T[i];
+          T[i] = 0.f;
+        }
+      }
+      return true;
+    };
+    for (int i = 0; i < nb; ++i) {
+      if (i == 10) LBX_PROBE(45);
+      load_bits(i + WD_PD - 1);
+      cpa_wait<WD_PD - 1>();  // block i's words have landed
+      // A buffer i & 1 is free once the MMAs of block i-2 completed
+      if (i >= 2 && !__all_sync(0xffffffffu, wd_wait(&dfull[i & 1], (uint32_t)((i - 2) >> 1) & 1u, 0x708, abrt)))
+        break;
+      if (i == 10) LBX_PROBE(46);
+      {
+        uint8_t *a = sA + (i & 1) * 32768 + (qd >> 1) * 16384;
+        const uint2 q = sQ[(i % WD_PD) * WD_CW + tid];
+        const int c0 = 64 * (qd & 1);
+        uint4 e0, e1;
+        wd_expand(q.x, e0, e1);
+        *reinterpret_cast<uint4 *>(a + sw128_off(row, c0)) = e0;
+        *reinterpret_cast<uint4 *>(a + sw128_off(row, c0 + 16)) = e1;
+        wd_expand(q.y, e0, e1);
+        *reinterpret_cast<uint4 *>(a + sw128_off(row, c0 + 32)) = e0;
+        *reinterpret_cast<uint4 *>(a + sw128_off(row, c0 + 48)) = e1;
+      }
+      fence_proxy_async();
+      mbar_arrive1(&afull[i & 1]);
+      if (i == 10) LBX_PROBE(47);
+      if (i >= 1 && !epilogue(i - 1)) break;
+      if (i == 10) LBX_PROBE(49);
+    }
+    if (!*abrt) epilogue(nb - 1);
+    cpa_wait<0>();
   }
-  cpa_wait<0>();
-  if (ok) ok = __syncthreads_and(mine);
-  if (ok) epilogue(nb - 1);
   LBX_PROBE(43);
   tc_fence_before();
-  ok = __syncthreads_and(ok && mine);
-  if (tid == 0 && !ok) {  // copies and MMAs still in flight end before shared memory and TMEM are released
-    for (int j = nused; j < nissued; ++j) mbar_poll_cta(&bbar[j % WD_NBV], (uint32_t)(j / WD_NBV) & 1u, 0x704);
-    if (ncommit > 0) mbar_poll_cta(&mbar[(ncommit - 1) & 1], (uint32_t)((ncommit - 1) >> 1) & 1u, 0x705);
-  }
-  if (warp == 0) tmem_dealloc(tmem, 2 * N);
+  __syncthreads();
+  tc_fence_after();
+  const bool ok = !*abrt;
+  if (warp == 16) tmem_dealloc(tmem, 2 * N);
   if (!ok) return;
 
   // ---- z = mid (.) v (RMSNorm: v * rs first), the group exponent per token
@@ -485,19 +540,21 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant
   for (int i = 0; i < KQ; ++i) {
     const int t = qd * KQ + i;
     float vv = V[i];
-    if (rms && t < k) vv *= __ldcg(sg.rs + t);
+    if (rms && cw && t < k) vv *= __ldcg(sg.rs + t);
     T[i] = vv;
   }
   uint8_t *img = sA;  // staging images of the two sides (the A buffers are free)
   for (int sd = 0; sd < nside; ++sd) {
     const float mm = sd ? m1 : m0;
+    if (cw) {
 #pragma unroll
-    for (int i = 0; i < KQ; ++i) {
-      const int t = qd * KQ + i;
-      const float z = rvalid && t < k ? mm * T[i] : 0.f;
-      V[i] = z;
-      const int mb = __reduce_max_sync(0xffffffffu, __float_as_int(fabsf(z)));
-      if (lane == 0 && mb) atomicMax(&gmx[sd][t], mb);
+      for (int i = 0; i < KQ; ++i) {
+        const int t = qd * KQ + i;
+        const float z = rvalid && t < k ? mm * T[i] : 0.f;
+        V[i] = z;
+        const int mb = __reduce_max_sync(0xffffffffu, __float_as_int(fabsf(z)));
+        if (lane == 0 && mb) atomicMax(&gmx[sd][t], mb);
+      }
     }
     __syncthreads();
     if (tid < KP) {  // the group exponent of each token, once
@@ -508,19 +565,21 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant
     }
     __syncthreads();
     uint8_t *im = img + sd * 16384;
-    const int pos = 32 * (row >> 5) + wd_pos(row & 31);
+    if (cw) {
+      const int pos = 32 * (row >> 5) + wd_pos(row & 31);
 #pragma unroll
-    for (int i = 0; i < KQ; ++i) {
-      const int t = qd * KQ + i;
-      const int qv = t < k ? __float2int_rn(V[i] * gsc[t]) : 0;
-      int hi, lo;
-      split_digits(qv, hi, lo);
-      im[sw128_off(2 * t, pos)] = (uint8_t)hi;
-      im[sw128_off(2 * t + 1, pos)] = (uint8_t)lo;
+      for (int i = 0; i < KQ; ++i) {
+        const int t = qd * KQ + i;
+        const int qv = t < k ? __float2int_rn(V[i] * gsc[t]) : 0;
+        int hi, lo;
+        split_digits(qv, hi, lo);
+        im[sw128_off(2 * t, pos)] = (uint8_t)hi;
+        im[sw128_off(2 * t + 1, pos)] = (uint8_t)lo;
+      }
     }
     __syncthreads();
     uint8_t *rec = (sd ? sg.urec1 : sg.urec0) + (size_t)grp * p.urec_bytes;
-    for (int o = 16 * tid; o < N * 128; o += 16 * WD_THREADS)
+    for (int o = 16 * tid; o < N * 128; o += 16 * WD_TPB)
       *reinterpret_cast<uint4 *>(rec + o) = *reinterpret_cast<const uint4 *>(im + o);
     if (tid < KP) reinterpret_cast<int *>(rec + N * 128)[tid] = gex[tid];
     __syncthreads();  // (gex / gsc are rewritten by the next side)
@@ -529,43 +588,50 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wv_kernel(const __grid_constant
 }
 
 // ---------------------------------------------------------------------------
-// U-stage on the tensor cores.  Thread (row, quarter) as in wv_kernel; rows
-// are output rows, the K dimension one quantisation group (128 ranks) per
-// step, each thread expanding one of the group's 4 sign words of its row.
+// U-stage on the tensor cores.  Expanding thread (row, quarter) as in
+// wv_kernel; rows are output rows, the K dimension one quantisation group
+// (128 ranks) per step, each thread expanding one of the group's 4 sign
+// words of its row.
 // ---------------------------------------------------------------------------
 template <int KP>
-__global__ void __launch_bounds__(WD_THREADS, 1) wu_kernel(const __grid_constant__ WParams p) {
+__global__ void __launch_bounds__(WD_TPB, 1) wu_kernel(const __grid_constant__ WParams p) {
   constexpr int N = 2 * KP, KQ = KP / 4;
   constexpr int SBU = ((N * 128 + KP * 4) + 1023) & ~1023;  // B buffer: image, then the group exponents
   constexpr uint32_t IDESC = idesc_i8(N);
-  constexpr int PF = WD_NBU - 2;  // B copies in flight ahead of the MMA
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sA = align1024(smem_raw);  // 2 x (128 rows x 128 B)
   uint8_t *sB = sA + 2 * 16384;        // WD_NBU x SBU
-  uint32_t *sQ = reinterpret_cast<uint32_t *>(sB + WD_NBU * SBU);  // [WD_PD][threads] sign-word ring
+  uint32_t *sQ = reinterpret_cast<uint32_t *>(sB + WD_NBU * SBU);  // [WD_PD][WD_CW] sign-word ring
   __shared__ __align__(8) uint64_t bbar[WD_NBU];
-  __shared__ __align__(8) uint64_t mbar[2];
+  __shared__ __align__(8) uint64_t afull[2], dfull[2], dfree[2];
   __shared__ uint32_t tbase;
+  __shared__ int abort_flag;
   __shared__ int ec[2][KP];
-  __shared__ int2 rtab[WD_THREADS / 32][KQ];  // per warp: (add, shift) of the group being rounded
+  __shared__ int2 rtab[WD_CW / 32][KQ];  // per warp: (add, shift) of the group being rounded
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int row = tid & 127, qd = tid >> 7;
+  const bool cw = tid < WD_CW;
+  const int row = tid & 127, qd = (tid >> 7) & 3;
   int pi = 0;
   while (pi + 1 < p.nproj && (int)blockIdx.x >= p.up[pi + 1].tile0) ++pi;
   const WUProj &pj = p.up[pi];
   const int n = ((int)blockIdx.x - pj.tile0) * 128 + row;
-  const bool nvalid = n < pj.out;
+  const bool nvalid = cw && n < pj.out;
   const int k = p.k;
   const int ng0 = pj.ng[0], ngt = pj.ng[0] + (pj.nbr > 1 ? pj.ng[1] : 0);
+  volatile int *abrt = &abort_flag;
   LBX_PROBE(50);
 
   if (tid == 0) {
     for (int j = 0; j < WD_NBU; ++j) mbar_init(&bbar[j], 1);
-    mbar_init(&mbar[0], 1);
-    mbar_init(&mbar[1], 1);
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&afull[j], WD_CW);
+      mbar_init(&dfull[j], 1);
+      mbar_init(&dfree[j], WD_CW);
+    }
     fence_mbar_init();
+    abort_flag = 0;
   }
-  if (warp == 0) tmem_alloc(&tbase, 2 * N);
+  if (warp == 16) tmem_alloc(&tbase, 2 * N);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -577,25 +643,16 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wu_kernel(const __grid_constant
     const int b = G < ng0 ? 0 : 1, g = b ? G - ng0 : G;
     const int w0 = 4 * g + qd, W = pj.words[b];
     const bool v = G < ngt && nvalid && w0 < W;
-    cpa4(&sQ[(G % WD_PD) * WD_THREADS + tid], v ? pj.u_sign[b] + (int64_t)n * W + w0 : pj.u_sign[0],
-         v ? 4u : 0u);
+    cpa4(&sQ[(G % WD_PD) * WD_CW + tid], v ? pj.u_sign[b] + (int64_t)n * W + w0 : pj.u_sign[0], v ? 4u : 0u);
     cpa_commit();
   };
+  if (cw) {
 #pragma unroll
-  for (int j = 0; j + 1 < WD_PD; ++j) load_bits(j);
-  int nissued = 0, nused = 0, ncommit = 0;  // (thread 0) B copies issued / waited for, MMA commits
-  auto issue_b = [&](int G) {
-    const int buf = G % WD_NBU;
-    const int b = G < ng0 ? 0 : 1, g = b ? G - ng0 : G;
-    mbar_arrive_expect_tx(&bbar[buf], (uint32_t)p.urec_bytes);
-    bulk_g2s(sB + buf * SBU, pj.urec[b] + (size_t)g * p.urec_bytes, (uint32_t)p.urec_bytes, &bbar[buf]);
-    ++nissued;
-  };
+    for (int j = 0; j + 1 < WD_PD; ++j) load_bits(j);
+  }
   LBX_PROBE(51);
   pdl_trigger();
   pdl_wait();  // U records come from the V grid
-  if (tid == 0)
-    for (int j = 0; j < PF && j < ngt; ++j) issue_b(j);
   // per (branch, token) the coarsest group exponent
   if (tid < 2 * KP) {
     const int b = tid / KP, t = tid - b * KP;
@@ -607,105 +664,121 @@ __global__ void __launch_bounds__(WD_THREADS, 1) wu_kernel(const __grid_constant
     }
     ec[b][t] = e == UE_NONE ? 0 : e;
   }
+  __syncthreads();
   LBX_PROBE(52);
 
   int I0[KQ], I1[KQ];
 #pragma unroll
   for (int i = 0; i < KQ; ++i) I0[i] = I1[i] = 0;
 
-  int mine = 1;  // this thread's waits all completed
-  // (warp-uniform outcome: tcgen05.ld is a whole-warp instruction)
-  auto epilogue = [&](int G) {
-    bool okw = mbar_poll_cta(&mbar[G & 1], (uint32_t)(G >> 1) & 1u, 0x712) &&
-               mbar_poll_cta(&bbar[G % WD_NBU], (uint32_t)(G / WD_NBU) & 1u, 0x713);
-    okw = __all_sync(0xffffffffu, okw);
-    tc_fence_after();
-    if (!okw) {
-      mine = 0;
-      return;
-    }
-    const int b = G < ng0 ? 0 : 1;
-    uint32_t r[2 * KQ];
-    tmem_ld_cols<2 * KQ>(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((G & 1) * N + qd * 2 * KQ), r);
-    // the rounding of this group for the warp's tokens: rshr(v, e - ec) as
-    // (v + add) >> shift (shift 31 with add 2^30 gives 0 for every |v| < 2^30;
-    // an all-zero group has v = 0)
-    if (lane < KQ) {
-      const int t = qd * KQ + lane;
-      const int ex = reinterpret_cast<const int *>(sB + (G % WD_NBU) * SBU + N * 128)[t];
-      const int s = ex == UE_NONE ? 0 : min(ex - ec[b][t], 31);
-      rtab[warp][lane] = make_int2(s > 0 ? 1 << (s - 1) : 0, s);
-    }
-    __syncwarp();
-    tmem_ld_wait();
-    if (b) {
-#pragma unroll
-      for (int i = 0; i < KQ; ++i) {
-        const int2 as = rtab[warp][i];
-        I1[i] += (256 * (int)r[2 * i] + (int)r[2 * i + 1] + as.x) >> as.y;
+  if (warp == 16) {
+    // ---- issuing warp (lane 0 acts, the warp stays converged)
+    int nissued = 0, ncommit = 0;
+    auto issue_b = [&](int G) {
+      if (lane == 0) {
+        const int buf = G % WD_NBU;
+        const int b = G < ng0 ? 0 : 1, g = b ? G - ng0 : G;
+        mbar_arrive_expect_tx(&bbar[buf], (uint32_t)p.urec_bytes);
+        bulk_g2s(sB + buf * SBU, pj.urec[b] + (size_t)g * p.urec_bytes, (uint32_t)p.urec_bytes, &bbar[buf]);
       }
-    } else {
-#pragma unroll
-      for (int i = 0; i < KQ; ++i) {
-        const int2 as = rtab[warp][i];
-        I0[i] += (256 * (int)r[2 * i] + (int)r[2 * i + 1] + as.x) >> as.y;
+      ++nissued;
+    };
+    for (int j = 0; j < WD_NBU && j < ngt; ++j) issue_b(j);
+    for (int G = 0; G < ngt; ++G) {
+      if (G >= 2) {  // TMEM buffer G & 1 and the B buffer of group G-2 are free again
+        if (!__all_sync(0xffffffffu, wd_wait(&dfree[G & 1], (uint32_t)((G - 2) >> 1) & 1u, 0x716, abrt))) break;
+        if (G - 2 + WD_NBU < ngt) issue_b(G - 2 + WD_NBU);
       }
-    }
-    __syncwarp();  // (rtab is rewritten by the next group)
-  };
-
-  bool ok = true;
-  for (int G = 0; G < ngt; ++G) {
-    if (G == 20) LBX_PROBE(55);
-    load_bits(G + WD_PD - 1);
-    cpa_wait<WD_PD - 1>();  // group G's words have landed
-    if (G == 20) LBX_PROBE(56);
-    {  // expand group G into A buffer G & 1 (its previous MMA, group G-2, has completed)
-      uint8_t *a = sA + (G & 1) * 16384;
-      uint4 e0, e1;
-      wd_expand(sQ[(G % WD_PD) * WD_THREADS + tid], e0, e1);
-      *reinterpret_cast<uint4 *>(a + sw128_off(row, 32 * qd)) = e0;
-      *reinterpret_cast<uint4 *>(a + sw128_off(row, 32 * qd + 16)) = e1;
-    }
-    fence_proxy_async();
-    tc_fence_before();
-    if (!__syncthreads_and(mine)) {  // a wait ran out: stop (uniform)
-      ok = false;
-      break;
-    }
-    if (G == 20) LBX_PROBE(57);
-    if (tid == 0) {
-      // B of group G+PF into the buffer of group G-2 (its MMA and epilogue are done)
-      if (G + PF < ngt) issue_b(G + PF);
+      if (!__all_sync(0xffffffffu, wd_wait(&afull[G & 1], (uint32_t)(G >> 1) & 1u, 0x717, abrt))) break;
+      if (!__all_sync(0xffffffffu, wd_wait(&bbar[G % WD_NBU], (uint32_t)(G / WD_NBU) & 1u, 0x711, abrt))) break;
+      __syncwarp();
       tc_fence_after();
-      if (mbar_poll_cta(&bbar[G % WD_NBU], (uint32_t)(G / WD_NBU) & 1u, 0x711)) {
-        if (G == 20) LBX_PROBE(58);
-        ++nused;
+      if (lane == 0) {
         const uint32_t aB = smem_u32(sA + (G & 1) * 16384), bB = smem_u32(sB + (G % WD_NBU) * SBU);
 #pragma unroll
         for (int s = 0; s < 4; ++s)
           umma_i8(tmem + (uint32_t)((G & 1) * N), sw128_desc(aB + 32 * s), sw128_desc(bB + 32 * s), IDESC,
                   s > 0 ? 1u : 0u);
-        umma_commit(&mbar[G & 1]);
-        ++ncommit;
-      } else {
-        mine = 0;
+        umma_commit(&dfull[G & 1]);
       }
+      ++ncommit;
+      __syncwarp();
     }
-    if (G >= 1) epilogue(G - 1);
-    if (G == 20) LBX_PROBE(59);
+    if (*abrt && lane == 0) {  // work in flight ends before shared memory and TMEM are released
+      for (int j = ncommit; j < nissued; ++j) mbar_poll_cta(&bbar[j % WD_NBU], (uint32_t)(j / WD_NBU) & 1u, 0x714);
+      if (ncommit > 0) mbar_poll_cta(&dfull[(ncommit - 1) & 1], (uint32_t)((ncommit - 1) >> 1) & 1u, 0x715);
+    }
+    __syncwarp();
+  } else {
+    // ---- expanding / reading warps
+    auto epilogue = [&](int G) {
+      bool okw = wd_wait(&dfull[G & 1], (uint32_t)(G >> 1) & 1u, 0x712, abrt) &&
+                 wd_wait(&bbar[G % WD_NBU], (uint32_t)(G / WD_NBU) & 1u, 0x713, abrt);
+      okw = __all_sync(0xffffffffu, okw);
+      tc_fence_after();
+      if (!okw) return false;
+      const int b = G < ng0 ? 0 : 1;
+      // the rounding of this group for the warp's tokens: rshr(v, e - ec) as
+      // (v + add) >> shift (shift 31 with add 2^30 gives 0 for every |v| < 2^30;
+      // an all-zero group has v = 0)
+      if (lane < KQ) {
+        const int t = qd * KQ + lane;
+        const int ex = reinterpret_cast<const int *>(sB + (G % WD_NBU) * SBU + N * 128)[t];
+        const int s = ex == UE_NONE ? 0 : min(ex - ec[b][t], 31);
+        rtab[warp][lane] = make_int2(s > 0 ? 1 << (s - 1) : 0, s);
+      }
+      uint32_t r[2 * KQ];
+      tmem_ld_cols<2 * KQ>(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((G & 1) * N + qd * 2 * KQ), r);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive1(&dfree[G & 1]);
+      __syncwarp();
+      if (b) {
+#pragma unroll
+        for (int i = 0; i < KQ; ++i) {
+          const int2 as = rtab[warp][i];
+          I1[i] += (256 * (int)r[2 * i] + (int)r[2 * i + 1] + as.x) >> as.y;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < KQ; ++i) {
+          const int2 as = rtab[warp][i];
+          I0[i] += (256 * (int)r[2 * i] + (int)r[2 * i + 1] + as.x) >> as.y;
+        }
+      }
+      __syncwarp();  // (rtab is rewritten by the next group)
+      return true;
+    };
+    for (int G = 0; G < ngt; ++G) {
+      if (G == 20) LBX_PROBE(55);
+      load_bits(G + WD_PD - 1);
+      cpa_wait<WD_PD - 1>();  // group G's words have landed
+      // A buffer G & 1 is free once the MMAs of group G-2 completed
+      if (G >= 2 && !__all_sync(0xffffffffu, wd_wait(&dfull[G & 1], (uint32_t)((G - 2) >> 1) & 1u, 0x718, abrt)))
+        break;
+      if (G == 20) LBX_PROBE(56);
+      {
+        uint8_t *a = sA + (G & 1) * 16384;
+        uint4 e0, e1;
+        wd_expand(sQ[(G % WD_PD) * WD_CW + tid], e0, e1);
+        *reinterpret_cast<uint4 *>(a + sw128_off(row, 32 * qd)) = e0;
+        *reinterpret_cast<uint4 *>(a + sw128_off(row, 32 * qd + 16)) = e1;
+      }
+      fence_proxy_async();
+      mbar_arrive1(&afull[G & 1]);
+      if (G == 20) LBX_PROBE(57);
+      if (G >= 1 && !epilogue(G - 1)) break;
+      if (G == 20) LBX_PROBE(59);
+    }
+    if (!*abrt && ngt > 0) epilogue(ngt - 1);
+    cpa_wait<0>();
   }
-  cpa_wait<0>();
-  if (ok) ok = __syncthreads_and(mine);
-  if (ok && ngt > 0) epilogue(ngt - 1);
   LBX_PROBE(53);
   tc_fence_before();
-  ok = __syncthreads_and(ok && mine);
-  if (tid == 0 && !ok) {  // copies and MMAs still in flight end before shared memory and TMEM are released
-    for (int j = nused; j < nissued; ++j) mbar_poll_cta(&bbar[j % WD_NBU], (uint32_t)(j / WD_NBU) & 1u, 0x714);
-    if (ncommit > 0) mbar_poll_cta(&mbar[(ncommit - 1) & 1], (uint32_t)((ncommit - 1) >> 1) & 1u, 0x715);
-  }
-  if (warp == 0) tmem_dealloc(tmem, 2 * N);
+  __syncthreads();
+  tc_fence_after();
+  const bool ok = !*abrt;
+  if (warp == 16) tmem_dealloc(tmem, 2 * N);
   if (!ok || !nvalid) return;
 
   const float u1a = pj.u1[0][n];
@@ -736,11 +809,11 @@ static int wide_kp(int k) { return k <= 8 ? 8 : k <= 16 ? 16 : k <= 32 ? 32 : 64
 static int wide_rec_bytes(int KP) { return (2 * KP * 256 + KP * 4 + 15) & ~15; }
 static int wide_urec_bytes(int KP) { return (2 * KP * 128 + KP * 4 + 15) & ~15; }
 static size_t wv_smem(int KP) {
-  return 1024 + 2 * 32768 + (size_t)WD_NBV * (2 * KP * 256 + 1024) + (size_t)WD_PD * WD_THREADS * 8;
+  return 1024 + 2 * 32768 + (size_t)WD_NBV * (2 * KP * 256 + 1024) + (size_t)WD_PD * WD_CW * 8;
 }
 static size_t wu_smem(int KP) {
   return 1024 + 2 * 16384 + (size_t)WD_NBU * (((2 * KP * 128 + KP * 4) + 1023) & ~1023) +
-         (size_t)WD_PD * WD_THREADS * 4;
+         (size_t)WD_PD * WD_CW * 4;
 }
 
 // scratch of one tensor-core batch of k tokens (0: the call does not fit it)
@@ -774,9 +847,9 @@ static int wide_launch(const WParams &wp, int vtiles, int utiles, bool pdl, cuda
   if (rc) return rc;
   cudaError_t e = launch(wx_stage_kernel, dim3(wp.k, wp.nseg), dim3(WX_THREADS), 0, stream, pdl, wp);
   if (e != cudaSuccess) return cuda_status(e, "x staging launch");
-  e = launch(wv_kernel<KP>, dim3(vtiles), dim3(WD_THREADS), wv_smem(KP), stream, pdl, wp);
+  e = launch(wv_kernel<KP>, dim3(vtiles), dim3(WD_TPB), wv_smem(KP), stream, pdl, wp);
   if (e != cudaSuccess) return cuda_status(e, "tensor-core V-stage launch");
-  e = launch(wu_kernel<KP>, dim3(utiles), dim3(WD_THREADS), wu_smem(KP), stream, pdl, wp);
+  e = launch(wu_kernel<KP>, dim3(utiles), dim3(WD_TPB), wu_smem(KP), stream, pdl, wp);
   if (e != cudaSuccess) return cuda_status(e, "tensor-core U-stage launch");
   return LBX_OK;
 }

@@ -1,6 +1,6 @@
 """Small, fixed launch sequences of every kernel family, for profiler captures.
 
-    python -m littlebit_b200.profile_cases [all|c2|vsplit|70b|fused|decode|allgather]
+    python -m littlebit_b200.profile_cases [all|c2|vsplit|70b|fused|decode|allgather|tc]
 
 Each case builds seeded random layers (Bernoulli(0.5) signs, |N(1,0.1)|
 scales) on cuda:0 and launches each kernel a few times in a known order, so a
@@ -19,6 +19,9 @@ every kernel of the library with a small device footprint (about 0.3 GB).
           attention with the sequence dimension, embedding, lm_head
   allgather  the row-sharded 8192 -> 28672 layer with the all-gather fused
           into its U-stage, two shards emulated on one GPU in stream order
+  tc      the tensor-core executor (LBX_EXEC_TC) on the 70B down projection
+          (28672 -> 8192, ranks 616 + 5712, x * x2 prologue) at 64 tokens,
+          twice: x staging, tcgen05 V-stage, tcgen05 U-stage
 """
 from __future__ import annotations
 
@@ -124,8 +127,19 @@ def case_allgather(dev, g):
                                          states[rank].data_ptr(), 0, st), "unpack")
 
 
+def case_tc(dev, g):
+    dn = _layer(28672, 8192, [616, 5712], g, dev)
+    k = 64
+    x = torch.randn(k, 28672, generator=g).to(dev, torch.bfloat16)
+    x2 = torch.randn(k, 28672, generator=g).to(dev, torch.bfloat16)
+    y = torch.empty(k, 8192, device=dev, dtype=torch.bfloat16)
+    ws = torch.zeros(ops.linear_workspace_bytes([dn], k), dtype=torch.uint8, device=dev)
+    for _ in range(2):
+        ops.linear_group([dn], x, [y], ws=ws, x2=x2, prologue=L.LBX_PRO_MUL, exec_mode=L.LBX_EXEC_TC)
+
+
 CASES = {"c2": case_c2, "vsplit": case_vsplit, "70b": case_70b, "fused": case_fused, "decode": case_decode,
-         "allgather": case_allgather}
+         "allgather": case_allgather, "tc": case_tc}
 
 
 def main(argv):
