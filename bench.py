@@ -754,8 +754,10 @@ def run_row_shard(args, dev, rank, ws, reps: int = 200):
     """The 70B-MLP-shaped LittleBitLinear at this world size: U rows split over
     the ranks, V replicated, the y slices all-gathered, timed two ways — the
     local layer followed by an NCCL all-gather, and the all-gather fused into
-    the U-stage (tagged NVLink stores + an unpack kernel; ``us_per_call``).
-    GB/s counts the whole layer's algorithmic bytes once per call."""
+    the U-stage (tagged NVLink stores + an unpack kernel; ``us_per_call``) —
+    beside the whole layer on one GPU, at one token (the top-level keys) and
+    at a 16-token verify batch (``k16``).  GB/s counts the whole layer's
+    algorithmic bytes once per call."""
     import torch.distributed as dist
     from littlebit_b200 import synthetic
     from littlebit_b200 import ops
@@ -765,11 +767,8 @@ def run_row_shard(args, dev, rank, ws, reps: int = 200):
     g = torch.Generator().manual_seed(4242)
     full = synthetic.to_packed_linear(K, N, synthetic.layer(K, N, [r], g), dev)
     sh = RowShardedLinear(full, ws, rank)
-    x = torch.randn(1, K, generator=g).to(dev)
-    part = sh.local_forward(x)
-    gat = torch.empty(ws, 1, N // ws, device=dev)
+    fsh = FusedRowShardedLinear(full, ws, rank, max_tokens=16)
     stream = torch.cuda.current_stream(dev)
-
     per = 20  # calls per CUDA graph
 
     def timed(fn):
@@ -796,36 +795,45 @@ def run_row_shard(args, dev, rank, ws, reps: int = 200):
         del graph  # a graph holding NCCL calls goes before the process group
         return t
 
-    t_local = timed(lambda: sh.local_forward(x, part))
-    t_ag = timed(lambda: dist.all_gather_into_tensor(gat, part))
-    t_all = timed(lambda: (sh.local_forward(x, part), dist.all_gather_into_tensor(gat, part)))
-    # the all-gather fused into the U-stage; must agree with the NCCL path bitwise
-    fsh = FusedRowShardedLinear(full, ws, rank, max_tokens=1)
-    yf = torch.empty(1, N, device=dev)
-    t_fused = timed(lambda: fsh.forward(x, yf))
-    ref = gat.permute(1, 0, 2).reshape(1, N)
-    same = bool(torch.equal(fsh.forward(x, yf), ref))
-    # the whole layer on this GPU alone: the sharded result must be its bits
-    yfull = torch.empty(1, N, device=dev)
-    t_unsharded = timed(lambda: ops.linear_group([full], x, [yfull]))
-    same_full = bool(torch.equal(yf, yfull))
-    dev_err = ops.device_error(dev)
+    def measure(k):
+        x = torch.randn(k, K, generator=g).to(dev)
+        part = sh.local_forward(x)
+        gat = torch.empty(ws, k, N // ws, device=dev)
+        t_local = timed(lambda: sh.local_forward(x, part))
+        t_ag = timed(lambda: dist.all_gather_into_tensor(gat, part))
+        t_all = timed(lambda: (sh.local_forward(x, part), dist.all_gather_into_tensor(gat, part)))
+        # the all-gather fused into the U-stage; must agree with the NCCL path bitwise
+        yf = torch.empty(k, N, device=dev)
+        t_fused = timed(lambda: fsh.forward(x, yf))
+        ref = gat.permute(1, 0, 2).reshape(k, N)
+        same = bool(torch.equal(fsh.forward(x, yf), ref))
+        # the whole layer on this GPU alone: the sharded result must be its bits
+        yfull = torch.empty(k, N, device=dev)
+        t_unsharded = timed(lambda: ops.linear_group([full], x, [yfull]))
+        same_full = bool(torch.equal(yf, yfull))
+        dev_err = ops.device_error(dev)
+        if not same or not same_full or dev_err:
+            raise RuntimeError(f"fused all-gather disagrees at k={k} (equal to NCCL {same}, to the unsharded "
+                               f"layer {same_full}, device error {dev_err:#x})")
+        alg = (r * K + 7) // 8 + (N * r + 7) // 8 + 4 * (K + r + N) + 4 * K * k + 4 * N * k
+        return {"us_per_call": round(t_fused, 3), "local_kernel_us": round(t_local, 3),
+                "nccl_us_per_call": round(t_all, 3), "nccl_allgather_us": round(t_ag, 3),
+                "fused_us_per_call": round(t_fused, 3), "fused_equals_nccl": same,
+                "fused_equals_unsharded": same_full, "unsharded_us_per_call": round(t_unsharded, 3),
+                "exchange_us": round(t_fused - t_local, 3),
+                "allgather_bytes_per_rank": 4 * N * k // ws,
+                "gbs_whole_layer": round(alg / (t_fused * 1e-6) / 1e9, 2), "algorithmic_bytes": alg}
+
+    k1 = measure(1)
+    k16 = measure(16)
     fsh.close()
-    if not same or not same_full or dev_err:
-        raise RuntimeError(f"fused all-gather disagrees (equal to NCCL {same}, to the unsharded layer {same_full}, "
-                           f"device error {dev_err:#x})")
-    alg = (r * K + 7) // 8 + (N * r + 7) // 8 + 4 * (K + r + N) + 4 * K + 4 * N
-    return {"workload": f"LittleBitLinear {K}->{N} r={r}, k=1 fp32, U rows split over {ws} GPUs, "
-                        f"V replicated, y all-gathered",
-            "us_per_call": round(t_fused, 3), "local_kernel_us": round(t_local, 3),
-            "nccl_us_per_call": round(t_all, 3), "nccl_allgather_us": round(t_ag, 3),
-            "fused_us_per_call": round(t_fused, 3), "fused_equals_nccl": same,
-            "fused_equals_unsharded": same_full, "unsharded_us_per_call": round(t_unsharded, 3),
-            "exchange_us": round(t_fused - t_local, 3),
-            "limiter": "the replicated V-stage and the two stage launches: the layer is latency-bound at one "
-                       "token (2.8 MB in ~10 us), so splitting its rows shortens only the U-stage body",
-            "allgather_bytes_per_rank": 4 * N // ws,
-            "gbs_whole_layer": round(alg / (t_fused * 1e-6) / 1e9, 2), "algorithmic_bytes": alg,
+    return {"workload": f"LittleBitLinear {K}->{N} r={r}, fp32, U rows split over {ws} GPUs, "
+                        f"V replicated, y all-gathered; k=1 (top level) and k=16 (k16)",
+            **k1,
+            "limiter": "the replicated V-stage and the stage launches: at one token the layer is latency-bound "
+                       "(2.8 MB in ~10 us), so splitting its rows shortens only the U-stage body; at 16 tokens "
+                       "the U-stage body is the larger part and shrinks with the rows",
+            "k16": k16,
             "timing": f"CUDA events over {reps} calls ({per} per CUDA graph), max over ranks"}
 
 

@@ -353,9 +353,11 @@ typedef struct lbx_model {
  * one CTA per pass on small grids).  Same bits; for validation. */
 #define LBX_EXEC_KERNELS_ONE_CTA_V 4
 /* lbx_linear_args.exec only: the tensor-core executor (tcgen05 kind::i8,
- * up to 64 tokens per launch) for any token count; AUTO and KERNELS select it
- * for calls of 32 tokens or more when the workspace holds a batch
- * (lbx_linear_workspace_size counts it from 32 tokens).  Same bits. */
+ * up to 64 tokens per launch) for any token count.  AUTO and KERNELS select
+ * it for calls of 32 tokens or more, and of 16 or more when the call is large
+ * (sum over projections of (in + out features) x ranks >= 2.5e7), provided the
+ * workspace holds a batch; lbx_linear_workspace_size counts it for exactly
+ * those calls.  Same bits. */
 #define LBX_EXEC_TC 5
 /* lbx_linear_args.exec only: the two stage grids at every token count (never
  * the tensor-core executor).  Same bits; for validation. */

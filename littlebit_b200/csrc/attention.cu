@@ -32,6 +32,7 @@ constexpr int ACH = 64;        // keys per chunk
 constexpr int ATHREADS = 128;
 constexpr int AMAX_ROWS = 64;  // query rows (tokens x GQA group) per CTA at most; more rows -> more CTAs
 constexpr int ATK_GROUPS = 64; // ticket slots per kv head (row groups of one launch)
+constexpr int ARB = 8;         // query rows of one token sharing each key / value load
 
 struct AttnParams {
   int n, heads, kvh, d, max_seq, prefix, rep, R, nchunk, ngroups;
@@ -99,6 +100,8 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
   uint8_t *sel = reinterpret_cast<uint8_t *>(map + Rcap * ACH);  // n x 64: t-th visible new token
   __shared__ int s_cnt[64];
   __shared__ int s_last;
+  __shared__ int s_bstart[AMAX_ROWS + 1];  // row blocks: rows of one token, at most ARB each
+  __shared__ int s_nb;
 
   const int prefix = p.prefix_dev ? __ldcg(p.prefix_dev) : p.prefix;
   const int total = prefix + p.n;
@@ -125,6 +128,18 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
       for (int j = 0; j <= i; ++j) sel[i * 64 + cnt++] = (uint8_t)j;
     }
     s_cnt[i] = cnt;
+  }
+  // row blocks (the rows of one token share the key / value row of every
+  // rank, so one load serves the block's rows)
+  if (tid == 0) {
+    int nbk = 0;
+    for (int r = 0; r < Rg;) {
+      s_bstart[nbk++] = r;
+      const int i = (rlo + r) / p.rep;
+      r = min(min(Rg, (i + 1) * p.rep - rlo), r + ARB);
+    }
+    s_bstart[nbk] = Rg;
+    s_nb = nbk;
   }
   // queries of this row group, rotated
   for (int e = tid; e < Rg * half; e += nthr) {
@@ -195,10 +210,14 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
   __syncthreads();
 
   // scores by rank: every quantity below depends only on the key's rank in
-  // the query's visible sequence
-  for (int e = tid; e < Rg * ACH; e += nthr) {
-    const int r = e / ACH, jj = e - r * ACH;
-    const int i = (rlo + r) / p.rep;
+  // the query's visible sequence.  A thread takes one rank for a whole row
+  // block (one key row, loaded once per step); each score is the same fmaf
+  // chain over the head dimension as a thread per (row, rank) would form.
+  const int nbk = s_nb;
+  for (int e = tid; e < nbk * ACH; e += nthr) {
+    const int bi = e / ACH, jj = e - bi * ACH;
+    const int ra = s_bstart[bi], nr = s_bstart[bi + 1] - ra;
+    const int i = (rlo + ra) / p.rep;
     const int rank = r0 + jj;
     int row = -1;
     if (rank < prefix) {
@@ -207,22 +226,31 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
       const int t = rank - prefix;
       if (has_new && t < s_cnt[i]) row = ACH + sel[i * 64 + t];
     }
-    map[r * ACH + jj] = (int16_t)row;
-    float sc = -INFINITY;
+    map[bi * ACH + jj] = (int16_t)row;
+    float a[ARB];
+#pragma unroll
+    for (int u = 0; u < ARB; ++u) a[u] = 0.f;
     if (row >= 0) {
-      const float4 *q4 = reinterpret_cast<const float4 *>(Qs + r * KP);
       const float4 *k4 = reinterpret_cast<const float4 *>(Ka + row * KP);
-      float a = 0.f;
       for (int t = 0; t < d / 4; ++t) {
-        const float4 qv = q4[t], kv = k4[t];
-        a = fmaf(qv.x, kv.x, a);
-        a = fmaf(qv.y, kv.y, a);
-        a = fmaf(qv.z, kv.z, a);
-        a = fmaf(qv.w, kv.w, a);
+        const float4 kv = k4[t];
+#pragma unroll
+        for (int u = 0; u < ARB; ++u) {
+          if (u < nr) {
+            const float4 qv = reinterpret_cast<const float4 *>(Qs + (ra + u) * KP)[t];
+            float x = a[u];
+            x = fmaf(qv.x, kv.x, x);
+            x = fmaf(qv.y, kv.y, x);
+            x = fmaf(qv.z, kv.z, x);
+            x = fmaf(qv.w, kv.w, x);
+            a[u] = x;
+          }
+        }
       }
-      sc = a * p.scale;
     }
-    Pm[r * ACH + jj] = sc;
+#pragma unroll
+    for (int u = 0; u < ARB; ++u)
+      if (u < nr) Pm[(ra + u) * ACH + jj] = row >= 0 ? a[u] * p.scale : -INFINITY;
   }
   __syncthreads();
 
@@ -243,18 +271,40 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
   }
   __syncthreads();
 
-  // Σ p·v in rank order (ranks without a key carry p = 0)
-  for (int e = tid; e < Rg * d; e += nthr) {
-    const int r = e / d, t = e - r * d;
-    const float *pr = Pm + r * ACH;
-    const int16_t *mr = map + r * ACH;
-    float a = 0.f;
-#pragma unroll 8
-    for (int jj = 0; jj < ACH; ++jj) {
-      const int row = mr[jj];
-      a = fmaf(pr[jj], Va[(row < 0 ? 0 : row) * d + t], a);
+  // Σ p·v in rank order (ranks without a key carry p = 0).  A thread takes
+  // one head-dimension column for a whole row block (one value load per rank
+  // serves the block's rows); each output is the same fmaf chain over the
+  // ranks as a thread per (row, column) would form.
+  for (int e = tid; e < nbk * d; e += nthr) {
+    const int bi = e / d, t = e - bi * d;
+    const int ra = s_bstart[bi], nr = s_bstart[bi + 1] - ra;
+    const int16_t *mr = map + bi * ACH;
+    float a[ARB];
+#pragma unroll
+    for (int u = 0; u < ARB; ++u) a[u] = 0.f;
+    for (int j0 = 0; j0 < ACH; j0 += 4) {
+      float v[4];
+#pragma unroll
+      for (int jq = 0; jq < 4; ++jq) {
+        const int row = mr[j0 + jq];
+        v[jq] = Va[(row < 0 ? 0 : row) * d + t];
+      }
+#pragma unroll
+      for (int u = 0; u < ARB; ++u) {
+        if (u < nr) {
+          const float4 pq = *reinterpret_cast<const float4 *>(Pm + (ra + u) * ACH + j0);
+          float x = a[u];
+          x = fmaf(pq.x, v[0], x);
+          x = fmaf(pq.y, v[1], x);
+          x = fmaf(pq.z, v[2], x);
+          x = fmaf(pq.w, v[3], x);
+          a[u] = x;
+        }
+      }
     }
-    p.part_o[(pbase + rlo + r) * d + t] = a;
+#pragma unroll
+    for (int u = 0; u < ARB; ++u)
+      if (u < nr) p.part_o[(pbase + rlo + ra + u) * d + t] = a[u];
   }
 
   // the last live chunk of (h, g) merges the partials, in chunk order

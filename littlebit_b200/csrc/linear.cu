@@ -1939,10 +1939,8 @@ static int run_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0, 
 }  // namespace lbx
 
 // the tensor-core executor (wide.cu)
-#ifndef LBX_WIDE_MIN_TOKENS
-#define LBX_WIDE_MIN_TOKENS 32  // AUTO / KERNELS calls with at least this many tokens run on it
-#endif
 namespace lbx {
+static bool wide_auto(const lbx_proj *projs, int n_proj, int n_tokens);
 static size_t wide_ws_bytes(const lbx_proj *projs, int n_proj, int k);
 static int wide_try(const lbx_proj *projs, const lbx_linear_args *a, void *ws, size_t ws_bytes,
                     cudaStream_t stream, bool &handled);
@@ -1953,7 +1951,7 @@ extern "C" size_t lbx_linear_workspace_size(const lbx_proj *projs, int32_t n_pro
   if (!projs || n_proj < 1 || n_proj > LBX_MAX_PROJ || n_tokens < 1) return 0;
   const int k = n_tokens < LBX_MAX_TOKENS ? n_tokens : LBX_MAX_TOKENS;
   size_t s = lbx::ws_bytes_for(projs, n_proj, k);
-  if (n_tokens >= LBX_WIDE_MIN_TOKENS) s = std::max(s, lbx::wide_ws_bytes(projs, n_proj, n_tokens));
+  if (lbx::wide_auto(projs, n_proj, n_tokens)) s = std::max(s, lbx::wide_ws_bytes(projs, n_proj, n_tokens));
   return s;
 }
 

@@ -41,6 +41,7 @@ namespace lbx {
 constexpr int WD_MAXK = 64;       // tokens per tensor-core batch
 constexpr int WD_NBV = 4;         // B-operand buffers of the V kernel
 constexpr int WD_NBU = 8;         // B-operand buffers of the U kernel
+constexpr int WD_NAU = 4;         // A-operand / TMEM accumulator buffers of the U kernel
 constexpr int WD_MAXBLK = 512;    // 256-column blocks (in_features <= 131072)
 constexpr int WX_THREADS = 512;
 constexpr int WD_PD = 4;          // sign-word loads in flight ahead of the expansion (blocks / groups)
@@ -598,12 +599,13 @@ __global__ void __launch_bounds__(WD_TPB, 1) wu_kernel(const __grid_constant__ W
   constexpr int N = 2 * KP, KQ = KP / 4;
   constexpr int SBU = ((N * 128 + KP * 4) + 1023) & ~1023;  // B buffer: image, then the group exponents
   constexpr uint32_t IDESC = idesc_i8(N);
+  constexpr int NA = WD_NAU, D = WD_NAU - 1;  // A / TMEM buffers; groups the read-back trails the expansion by
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *sA = align1024(smem_raw);  // 2 x (128 rows x 128 B)
-  uint8_t *sB = sA + 2 * 16384;        // WD_NBU x SBU
+  uint8_t *sA = align1024(smem_raw);  // NA x (128 rows x 128 B)
+  uint8_t *sB = sA + NA * 16384;       // WD_NBU x SBU
   uint32_t *sQ = reinterpret_cast<uint32_t *>(sB + WD_NBU * SBU);  // [WD_PD][WD_CW] sign-word ring
   __shared__ __align__(8) uint64_t bbar[WD_NBU];
-  __shared__ __align__(8) uint64_t afull[2], dfull[2], dfree[2];
+  __shared__ __align__(8) uint64_t afull[NA], dfull[NA], dfree[NA];
   __shared__ uint32_t tbase;
   __shared__ int abort_flag;
   __shared__ int ec[2][KP];
@@ -623,7 +625,7 @@ __global__ void __launch_bounds__(WD_TPB, 1) wu_kernel(const __grid_constant__ W
 
   if (tid == 0) {
     for (int j = 0; j < WD_NBU; ++j) mbar_init(&bbar[j], 1);
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < NA; ++j) {
       mbar_init(&afull[j], WD_CW);
       mbar_init(&dfull[j], 1);
       mbar_init(&dfree[j], WD_CW);
@@ -631,7 +633,7 @@ __global__ void __launch_bounds__(WD_TPB, 1) wu_kernel(const __grid_constant__ W
     fence_mbar_init();
     abort_flag = 0;
   }
-  if (warp == 16) tmem_alloc(&tbase, 2 * N);
+  if (warp == 16) tmem_alloc(&tbase, NA * N);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -685,34 +687,35 @@ __global__ void __launch_bounds__(WD_TPB, 1) wu_kernel(const __grid_constant__ W
     };
     for (int j = 0; j < WD_NBU && j < ngt; ++j) issue_b(j);
     for (int G = 0; G < ngt; ++G) {
-      if (G >= 2) {  // TMEM buffer G & 1 and the B buffer of group G-2 are free again
-        if (!__all_sync(0xffffffffu, wd_wait(&dfree[G & 1], (uint32_t)((G - 2) >> 1) & 1u, 0x716, abrt))) break;
-        if (G - 2 + WD_NBU < ngt) issue_b(G - 2 + WD_NBU);
+      const int a = G % NA;
+      if (G >= NA) {  // TMEM buffer a and the B buffer of group G-NA are free again
+        if (!__all_sync(0xffffffffu, wd_wait(&dfree[a], (uint32_t)((G - NA) / NA) & 1u, 0x716, abrt))) break;
+        if (G - NA + WD_NBU < ngt) issue_b(G - NA + WD_NBU);
       }
-      if (!__all_sync(0xffffffffu, wd_wait(&afull[G & 1], (uint32_t)(G >> 1) & 1u, 0x717, abrt))) break;
+      if (!__all_sync(0xffffffffu, wd_wait(&afull[a], (uint32_t)(G / NA) & 1u, 0x717, abrt))) break;
       if (!__all_sync(0xffffffffu, wd_wait(&bbar[G % WD_NBU], (uint32_t)(G / WD_NBU) & 1u, 0x711, abrt))) break;
       __syncwarp();
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t aB = smem_u32(sA + (G & 1) * 16384), bB = smem_u32(sB + (G % WD_NBU) * SBU);
+        const uint32_t aB = smem_u32(sA + a * 16384), bB = smem_u32(sB + (G % WD_NBU) * SBU);
 #pragma unroll
         for (int s = 0; s < 4; ++s)
-          umma_i8(tmem + (uint32_t)((G & 1) * N), sw128_desc(aB + 32 * s), sw128_desc(bB + 32 * s), IDESC,
+          umma_i8(tmem + (uint32_t)(a * N), sw128_desc(aB + 32 * s), sw128_desc(bB + 32 * s), IDESC,
                   s > 0 ? 1u : 0u);
-        umma_commit(&dfull[G & 1]);
+        umma_commit(&dfull[a]);
       }
       ++ncommit;
       __syncwarp();
     }
     if (*abrt && lane == 0) {  // work in flight ends before shared memory and TMEM are released
       for (int j = ncommit; j < nissued; ++j) mbar_poll_cta(&bbar[j % WD_NBU], (uint32_t)(j / WD_NBU) & 1u, 0x714);
-      if (ncommit > 0) mbar_poll_cta(&dfull[(ncommit - 1) & 1], (uint32_t)((ncommit - 1) >> 1) & 1u, 0x715);
+      if (ncommit > 0) mbar_poll_cta(&dfull[(ncommit - 1) % NA], (uint32_t)((ncommit - 1) / NA) & 1u, 0x715);
     }
     __syncwarp();
   } else {
     // ---- expanding / reading warps
     auto epilogue = [&](int G) {
-      bool okw = wd_wait(&dfull[G & 1], (uint32_t)(G >> 1) & 1u, 0x712, abrt) &&
+      bool okw = wd_wait(&dfull[G % NA], (uint32_t)(G / NA) & 1u, 0x712, abrt) &&
                  wd_wait(&bbar[G % WD_NBU], (uint32_t)(G / WD_NBU) & 1u, 0x713, abrt);
       okw = __all_sync(0xffffffffu, okw);
       tc_fence_after();
@@ -728,10 +731,10 @@ __global__ void __launch_bounds__(WD_TPB, 1) wu_kernel(const __grid_constant__ W
         rtab[warp][lane] = make_int2(s > 0 ? 1 << (s - 1) : 0, s);
       }
       uint32_t r[2 * KQ];
-      tmem_ld_cols<2 * KQ>(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((G & 1) * N + qd * 2 * KQ), r);
+      tmem_ld_cols<2 * KQ>(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((G % NA) * N + qd * 2 * KQ), r);
       tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive1(&dfree[G & 1]);
+      mbar_arrive1(&dfree[G % NA]);
       __syncwarp();
       if (b) {
 #pragma unroll
@@ -753,24 +756,25 @@ __global__ void __launch_bounds__(WD_TPB, 1) wu_kernel(const __grid_constant__ W
       if (G == 20) LBX_PROBE(55);
       load_bits(G + WD_PD - 1);
       cpa_wait<WD_PD - 1>();  // group G's words have landed
-      // A buffer G & 1 is free once the MMAs of group G-2 completed
-      if (G >= 2 && !__all_sync(0xffffffffu, wd_wait(&dfull[G & 1], (uint32_t)((G - 2) >> 1) & 1u, 0x718, abrt)))
+      // A buffer G % NA is free once the MMAs of group G-NA completed
+      if (G >= NA && !__all_sync(0xffffffffu, wd_wait(&dfull[G % NA], (uint32_t)((G - NA) / NA) & 1u, 0x718, abrt)))
         break;
       if (G == 20) LBX_PROBE(56);
       {
-        uint8_t *a = sA + (G & 1) * 16384;
+        uint8_t *a = sA + (G % NA) * 16384;
         uint4 e0, e1;
         wd_expand(sQ[(G % WD_PD) * WD_CW + tid], e0, e1);
         *reinterpret_cast<uint4 *>(a + sw128_off(row, 32 * qd)) = e0;
         *reinterpret_cast<uint4 *>(a + sw128_off(row, 32 * qd + 16)) = e1;
       }
       fence_proxy_async();
-      mbar_arrive1(&afull[G & 1]);
+      mbar_arrive1(&afull[G % NA]);
       if (G == 20) LBX_PROBE(57);
-      if (G >= 1 && !epilogue(G - 1)) break;
+      if (G >= D && !epilogue(G - D)) break;
       if (G == 20) LBX_PROBE(59);
     }
-    if (!*abrt && ngt > 0) epilogue(ngt - 1);
+    for (int j = ngt > D ? ngt - D : 0; j < ngt && !*abrt; ++j)
+      if (!epilogue(j)) break;
     cpa_wait<0>();
   }
   LBX_PROBE(53);
@@ -778,7 +782,7 @@ __global__ void __launch_bounds__(WD_TPB, 1) wu_kernel(const __grid_constant__ W
   __syncthreads();
   tc_fence_after();
   const bool ok = !*abrt;
-  if (warp == 16) tmem_dealloc(tmem, 2 * N);
+  if (warp == 16) tmem_dealloc(tmem, NA * N);
   if (!ok || !nvalid) return;
 
   const float u1a = pj.u1[0][n];
@@ -812,7 +816,7 @@ static size_t wv_smem(int KP) {
   return 1024 + 2 * 32768 + (size_t)WD_NBV * (2 * KP * 256 + 1024) + (size_t)WD_PD * WD_CW * 8;
 }
 static size_t wu_smem(int KP) {
-  return 1024 + 2 * 16384 + (size_t)WD_NBU * (((2 * KP * 128 + KP * 4) + 1023) & ~1023) +
+  return 1024 + (size_t)WD_NAU * 16384 + (size_t)WD_NBU * (((2 * KP * 128 + KP * 4) + 1023) & ~1023) +
          (size_t)WD_PD * WD_CW * 4;
 }
 
@@ -933,16 +937,46 @@ static int wide_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0,
   }
 }
 
+#ifndef LBX_WIDE_MIN_TOKENS
+#define LBX_WIDE_MIN_TOKENS 32  // the tensor-core executor from this many tokens on every call
+#endif
+#ifndef LBX_WIDE_BIG_TOKENS
+#define LBX_WIDE_BIG_TOKENS 16  // ... and from this many on calls of at least LBX_WIDE_BIG_WORK
+#endif
+#ifndef LBX_WIDE_BIG_WORK
+#define LBX_WIDE_BIG_WORK 25000000.0  // sum over projections of (in + out features) x (sum of ranks)
+#endif
+// Whether AUTO / KERNELS run a call of n_tokens on the tensor-core executor.
+// Its cost is nearly flat up to 32 tokens (one pass over the weights per
+// batch of 64), the stage grids' grows with every 16 tokens; measured on
+// B200 the executor wins from 32 tokens on every shape and from 16 on the
+// 7B- and 70B-class calls (7B q/k/v 74.4 -> 41.6 us, 7B down 120.0 -> 75.2,
+// 70B o 88.1 -> 70.3, 70B gate/up 415 -> 219), while a single C2-sized
+// projection (4096 + 4096 features x 2048 ranks) stays faster on the stage
+// grids at 16 (38.1 vs 40.5 us).
+static bool wide_auto(const lbx_proj *projs, int n_proj, int n_tokens) {
+  if (!projs || n_proj < 1 || n_proj > LBX_MAX_PROJ) return false;
+  if (n_tokens >= LBX_WIDE_MIN_TOKENS) return true;
+  if (n_tokens < LBX_WIDE_BIG_TOKENS) return false;
+  double work = 0;
+  for (int i = 0; i < n_proj; ++i) {
+    int r = 0;
+    for (int b = 0; b < projs[i].n_branches && b < 2; ++b) r += projs[i].br[b].rank;
+    work += (double)(projs[i].in_features + projs[i].out_features) * r;
+  }
+  return work >= LBX_WIDE_BIG_WORK;
+}
+
 // The tensor-core executor for this call, if it applies: LBX_EXEC_TC always
 // (LBX_EUNSUPPORTED when it cannot run the call); LBX_EXEC_AUTO / _KERNELS
-// when the call has at least LBX_WIDE_MIN_TOKENS tokens and the workspace
-// holds a batch.  *handled tells whether the call ran (or failed) here.
+// when wide_auto selects it and the workspace holds a batch.  *handled tells
+// whether the call ran (or failed) here.
 static int wide_try(const lbx_proj *projs, const lbx_linear_args *a, void *ws, size_t ws_bytes,
                     cudaStream_t stream, bool &handled) {
   handled = false;
   const bool forced = a->exec == LBX_EXEC_TC;
   if (!forced && !((a->exec == LBX_EXEC_AUTO || a->exec == LBX_EXEC_KERNELS) &&
-                   a->n_tokens >= LBX_WIDE_MIN_TOKENS))
+                   wide_auto(projs, a->n_proj, a->n_tokens)))
     return LBX_OK;
   const size_t need = wide_ws_bytes(projs, a->n_proj, a->n_tokens);
   if (need == 0 || ws_bytes < need) {

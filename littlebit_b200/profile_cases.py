@@ -1,6 +1,6 @@
 """Small, fixed launch sequences of every kernel family, for profiler captures.
 
-    python -m littlebit_b200.profile_cases [all|c2|vsplit|70b|fused|decode|allgather|tc]
+    python -m littlebit_b200.profile_cases [all|c2|vsplit|70b|fused|decode|allgather|tc|c5]
 
 Each case builds seeded random layers (Bernoulli(0.5) signs, |N(1,0.1)|
 scales) on cuda:0 and launches each kernel a few times in a known order, so a
@@ -22,6 +22,10 @@ every kernel of the library with a small device footprint (about 0.3 GB).
   tc      the tensor-core executor (LBX_EXEC_TC) on the 70B down projection
           (28672 -> 8192, ranks 616 + 5712, x * x2 prologue) at 64 tokens,
           twice: x staging, tcgen05 V-stage, tcgen05 U-stage
+  c5      two decode steps of a 2-layer Llama-2-70B-shaped target (0.1 + 0.9 bit
+          ranks) for 64 sequences at 511 cached slots: the linears on the
+          tensor-core executor, attention with the sequence dimension, the lm_head
+          and argmax (not part of "all": ~2 GB on the device)
 """
 from __future__ import annotations
 
@@ -138,8 +142,38 @@ def case_tc(dev, g):
         ops.linear_group([dn], x, [y], ws=ws, x2=x2, prologue=L.LBX_PRO_MUL, exec_mode=L.LBX_EXEC_TC)
 
 
+def case_c5(dev, g):
+    import dataclasses
+
+    from .batch_decode import BatchDecoder
+    from .littlebit import LittleBitLinear
+    from .model import LLAMA2_70B, LittleBitDecoder, synthetic_runtime_state
+
+    shape = dataclasses.replace(LLAMA2_70B, num_hidden_layers=2)
+    H, I = shape.hidden_size, shape.intermediate_size
+    qd, kvd = shape.num_attention_heads * shape.head_dim, shape.num_key_value_heads * shape.head_dim
+    dims = {"q_proj": (H, qd), "k_proj": (H, kvd), "v_proj": (H, kvd), "o_proj": (qd, H),
+            "gate_proj": (H, I), "up_proj": (H, I), "down_proj": (I, H)}
+    rk = lambda b: {nm: LittleBitLinear._finalize_split_dim(LittleBitLinear._estimate_split_dim(a, o, b, False),
+                                                              1024, 8) for nm, (a, o) in dims.items()}
+    rd, rr = rk(0.1), rk(0.9)
+    st = synthetic_runtime_state(shape, {nm: [rd[nm], rr[nm]] for nm in dims}, seed=91, device=dev,
+                                 unit_gain=True)
+    dec = LittleBitDecoder(shape, st, device=dev, max_seq=16)
+    del st
+    S = 64
+    bd = BatchDecoder(dec, S, 640)
+    bd.fill_synthetic_prefix(511, seed=3)
+    tok = torch.randint(0, shape.vocab_size, (S,), generator=g).to(dev)
+    am = torch.empty(S, dtype=torch.int64, device=dev)
+    st = torch.full((S,), 511, dtype=torch.int32, device=dev)
+    for _ in range(2):
+        bd.step(tok, st, 511, 1, argmax=am)
+
+
 CASES = {"c2": case_c2, "vsplit": case_vsplit, "70b": case_70b, "fused": case_fused, "decode": case_decode,
-         "allgather": case_allgather, "tc": case_tc}
+         "allgather": case_allgather, "tc": case_tc, "c5": case_c5}
+ALL_SKIPS = ("c5",)
 
 
 def main(argv):
@@ -147,7 +181,7 @@ def main(argv):
     dev = torch.device("cuda", 0)
     g = torch.Generator().manual_seed(0)
     for name, fn in CASES.items():
-        if which in ("all", name):
+        if which == name or (which == "all" and name not in ALL_SKIPS):
             fn(dev, g)
     torch.cuda.synchronize()
     print("ok", which)
