@@ -24,6 +24,8 @@
 // the rounded values it computed itself, so no CTA reads a cache slot written
 // in the same launch.
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace lbx {
@@ -80,11 +82,20 @@ __global__ void rope_table_kernel(const int32_t *__restrict__ pos, int n, int d,
   if (e < n * half) out[e] = rope_cs_d(pos[e / half], e % half, d, theta);
 }
 
+// bf16 element counts rounded up to 16 bytes
+__host__ __device__ inline int attn_al8(int n) { return (n + 7) & ~7; }
+
 // one unit = (chunk c, kv head h, row group g); S holds its staging buffers.
+// B16: keys and values are staged as bf16 (half the shared memory: more units
+// per SM, for launches of many sequences); otherwise as fp32 (no conversion
+// at use: the lower latency of a single sequence's decode).  Both give the
+// same values, so the same bits.
 // Chunks at or past the live length do nothing; the last live chunk of (h, g)
 // to finish merges the partials.  Runs with any multiple of 32 threads.
+template <bool B16>
 LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
-  const int d = p.d, half = d / 2, KP = d + 4;  // key / query row pitch (float4-aligned)
+  const int d = p.d, half = d / 2, KP = d + 4;  // query row pitch (float4-aligned)
+  const int KPB = d + 4;  // key row pitch in bf16 (66 words at d = 128: conflict-free 8-byte loads)
   const int c = unit % p.nchunk;
   const int h = (unit / p.nchunk) % p.kvh;
   const int g = unit / (p.nchunk * p.kvh);
@@ -92,9 +103,12 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
   const int Rg = min(p.rows, p.R - rlo);
   const int Rcap = p.rows;
   const int tid = threadIdx.x, nthr = blockDim.x;
-  float *Ka = sm;                               // (ACH + n) x KP: cached rows 0..63, new tokens 64..
-  float *Va = Ka + (ACH + p.n) * KP;            // (ACH + n) x d
-  float *Qs = Va + (ACH + p.n) * d;             // Rcap x KP
+  // keys (ACH + n rows: cached ranks 0..63, new tokens 64..) and values
+  uint16_t *Kb = reinterpret_cast<uint16_t *>(sm);  // B16: (ACH + n) x KPB bf16
+  uint16_t *Vb = Kb + attn_al8((ACH + p.n) * KPB);  // B16: (ACH + n) x d bf16
+  float *Ka = sm;                                   // fp32: (ACH + n) x KP
+  float *Va = Ka + (ACH + p.n) * KP;                // fp32: (ACH + n) x d
+  float *Qs = B16 ? reinterpret_cast<float *>(Vb + attn_al8((ACH + p.n) * d)) : Va + (ACH + p.n) * d;  // Rcap x KP
   float *Pm = Qs + Rcap * KP;                   // Rcap x ACH
   int16_t *map = reinterpret_cast<int16_t *>(Pm + Rcap * ACH);  // Rcap x ACH: row of Ka/Va, -1 = none
   uint8_t *sel = reinterpret_cast<uint8_t *>(map + Rcap * ACH);  // n x 64: t-th visible new token
@@ -177,12 +191,17 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
       const int e = e0 + u * nthr;
       if (e >= ACH * d4) break;
       const int jj = e / d4, j4 = e - jj * d4;
-      *reinterpret_cast<float4 *>(Ka + jj * KP + 4 * j4) =
-          make_float4(__uint_as_float(kq[u].x << 16), __uint_as_float(kq[u].x & 0xFFFF0000u),
-                      __uint_as_float(kq[u].y << 16), __uint_as_float(kq[u].y & 0xFFFF0000u));
-      *reinterpret_cast<float4 *>(Va + jj * d + 4 * j4) =
-          make_float4(__uint_as_float(vq[u].x << 16), __uint_as_float(vq[u].x & 0xFFFF0000u),
-                      __uint_as_float(vq[u].y << 16), __uint_as_float(vq[u].y & 0xFFFF0000u));
+      if constexpr (B16) {
+        *reinterpret_cast<uint2 *>(Kb + jj * KPB + 4 * j4) = kq[u];
+        *reinterpret_cast<uint2 *>(Vb + jj * d + 4 * j4) = vq[u];
+      } else {
+        *reinterpret_cast<float4 *>(Ka + jj * KP + 4 * j4) =
+            make_float4(__uint_as_float(kq[u].x << 16), __uint_as_float(kq[u].x & 0xFFFF0000u),
+                        __uint_as_float(kq[u].y << 16), __uint_as_float(kq[u].y & 0xFFFF0000u));
+        *reinterpret_cast<float4 *>(Va + jj * d + 4 * j4) =
+            make_float4(__uint_as_float(vq[u].x << 16), __uint_as_float(vq[u].x & 0xFFFF0000u),
+                        __uint_as_float(vq[u].y << 16), __uint_as_float(vq[u].y & 0xFFFF0000u));
+      }
     }
   }
   // the new tokens: rotate, round to bf16; the unit whose slot range holds
@@ -203,8 +222,13 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
         uint16_t *vw = p.vc + cache_base + (int64_t)slot * d;
         kw[j] = b1; kw[j + half] = b2; vw[j] = c1; vw[j + half] = c2;
       }
-      Ka[(ACH + i) * KP + j] = bf16_to_f32(b1); Ka[(ACH + i) * KP + j + half] = bf16_to_f32(b2);
-      Va[(ACH + i) * d + j] = bf16_to_f32(c1); Va[(ACH + i) * d + j + half] = bf16_to_f32(c2);
+      if constexpr (B16) {
+        Kb[(ACH + i) * KPB + j] = b1; Kb[(ACH + i) * KPB + j + half] = b2;
+        Vb[(ACH + i) * d + j] = c1; Vb[(ACH + i) * d + j + half] = c2;
+      } else {
+        Ka[(ACH + i) * KP + j] = bf16_to_f32(b1); Ka[(ACH + i) * KP + j + half] = bf16_to_f32(b2);
+        Va[(ACH + i) * d + j] = bf16_to_f32(c1); Va[(ACH + i) * d + j + half] = bf16_to_f32(c2);
+      }
     }
   }
   __syncthreads();
@@ -214,8 +238,10 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
   // block (one key row, loaded once per step); each score is the same fmaf
   // chain over the head dimension as a thread per (row, rank) would form.
   const int nbk = s_nb;
-  for (int e = tid; e < nbk * ACH; e += nthr) {
-    const int bi = e / ACH, jj = e - bi * ACH;
+  // (the row count of a block as a compile-time bound: a one-row block, every
+  // row of a multi-head-attention step, runs no predicated-off rows)
+  auto score_block = [&](auto nrc, int bi, int jj) {
+    constexpr int NR = decltype(nrc)::value;
     const int ra = s_bstart[bi], nr = s_bstart[bi + 1] - ra;
     const int i = (rlo + ra) / p.rep;
     const int rank = r0 + jj;
@@ -227,15 +253,23 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
       if (has_new && t < s_cnt[i]) row = ACH + sel[i * 64 + t];
     }
     map[bi * ACH + jj] = (int16_t)row;
-    float a[ARB];
+    float a[NR];
 #pragma unroll
-    for (int u = 0; u < ARB; ++u) a[u] = 0.f;
+    for (int u = 0; u < NR; ++u) a[u] = 0.f;
     if (row >= 0) {
+      const uint2 *k2 = reinterpret_cast<const uint2 *>(Kb + row * KPB);
       const float4 *k4 = reinterpret_cast<const float4 *>(Ka + row * KP);
       for (int t = 0; t < d / 4; ++t) {
-        const float4 kv = k4[t];
+        float4 kv;
+        if constexpr (B16) {
+          const uint2 kw = k2[t];
+          kv = make_float4(__uint_as_float(kw.x << 16), __uint_as_float(kw.x & 0xFFFF0000u),
+                           __uint_as_float(kw.y << 16), __uint_as_float(kw.y & 0xFFFF0000u));
+        } else {
+          kv = k4[t];
+        }
 #pragma unroll
-        for (int u = 0; u < ARB; ++u) {
+        for (int u = 0; u < NR; ++u) {
           if (u < nr) {
             const float4 qv = reinterpret_cast<const float4 *>(Qs + (ra + u) * KP)[t];
             float x = a[u];
@@ -249,8 +283,16 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
       }
     }
 #pragma unroll
-    for (int u = 0; u < ARB; ++u)
+    for (int u = 0; u < NR; ++u)
       if (u < nr) Pm[(ra + u) * ACH + jj] = row >= 0 ? a[u] * p.scale : -INFINITY;
+  };
+  for (int e = tid; e < nbk * ACH; e += nthr) {
+    const int bi = e / ACH, jj = e - bi * ACH;
+    const int nr = s_bstart[bi + 1] - s_bstart[bi];
+    if (nr == 1) score_block(std::integral_constant<int, 1>{}, bi, jj);
+    else if (nr <= 2) score_block(std::integral_constant<int, 2>{}, bi, jj);
+    else if (nr <= 4) score_block(std::integral_constant<int, 4>{}, bi, jj);
+    else score_block(std::integral_constant<int, ARB>{}, bi, jj);
   }
   __syncthreads();
 
@@ -275,22 +317,22 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
   // one head-dimension column for a whole row block (one value load per rank
   // serves the block's rows); each output is the same fmaf chain over the
   // ranks as a thread per (row, column) would form.
-  for (int e = tid; e < nbk * d; e += nthr) {
-    const int bi = e / d, t = e - bi * d;
+  auto pv_block = [&](auto nrc, int bi, int t) {
+    constexpr int NR = decltype(nrc)::value;
     const int ra = s_bstart[bi], nr = s_bstart[bi + 1] - ra;
     const int16_t *mr = map + bi * ACH;
-    float a[ARB];
+    float a[NR];
 #pragma unroll
-    for (int u = 0; u < ARB; ++u) a[u] = 0.f;
+    for (int u = 0; u < NR; ++u) a[u] = 0.f;
     for (int j0 = 0; j0 < ACH; j0 += 4) {
       float v[4];
 #pragma unroll
       for (int jq = 0; jq < 4; ++jq) {
         const int row = mr[j0 + jq];
-        v[jq] = Va[(row < 0 ? 0 : row) * d + t];
+        v[jq] = B16 ? bf16_to_f32(Vb[(row < 0 ? 0 : row) * d + t]) : Va[(row < 0 ? 0 : row) * d + t];
       }
 #pragma unroll
-      for (int u = 0; u < ARB; ++u) {
+      for (int u = 0; u < NR; ++u) {
         if (u < nr) {
           const float4 pq = *reinterpret_cast<const float4 *>(Pm + (ra + u) * ACH + j0);
           float x = a[u];
@@ -303,8 +345,16 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
       }
     }
 #pragma unroll
-    for (int u = 0; u < ARB; ++u)
+    for (int u = 0; u < NR; ++u)
       if (u < nr) p.part_o[(pbase + rlo + ra + u) * d + t] = a[u];
+  };
+  for (int e = tid; e < nbk * d; e += nthr) {
+    const int bi = e / d, t = e - bi * d;
+    const int nr = s_bstart[bi + 1] - s_bstart[bi];
+    if (nr == 1) pv_block(std::integral_constant<int, 1>{}, bi, t);
+    else if (nr <= 2) pv_block(std::integral_constant<int, 2>{}, bi, t);
+    else if (nr <= 4) pv_block(std::integral_constant<int, 4>{}, bi, t);
+    else pv_block(std::integral_constant<int, ARB>{}, bi, t);
   }
 
   // the last live chunk of (h, g) merges the partials, in chunk order
@@ -318,15 +368,16 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
   // O += w*o, out = O / L)
   // staged merge for long sequences (more than 16 chunks: the per-output
   // form below then needs 6 or more L2 round trips per output), when its
-  // tables fit in Ka/Va
-  const bool staged = nlive > 16 && 2 * Rg * nlive + Rg <= (ACH + p.n) * (KP + d);
+  // tables fit in the key / value buffers
+  const int scratch = B16 ? (attn_al8((ACH + p.n) * KPB) + (ACH + p.n) * d) / 2 : (ACH + p.n) * (KP + d);  // floats
+  const bool staged = nlive > 16 && 2 * Rg * nlive + Rg <= scratch;
   if (s_last && staged) {
     __threadfence();
     // per (row, chunk) (m, l) into shared memory, all loads in flight; per
     // row M, the weights (-1: a chunk without keys) and L; then each output
     // loads its chunks' partial sums a batch at a time
-    float *wsm = Ka;                     // [Rg][nlive]: m, then w
-    float *lsm = Ka + Rg * nlive;        // [Rg][nlive]: l
+    float *wsm = reinterpret_cast<float *>(Kb);  // [Rg][nlive]: m, then w
+    float *lsm = wsm + Rg * nlive;               // [Rg][nlive]: l
     float *Lsm = lsm + Rg * nlive;       // [Rg]
 #pragma unroll 4
     for (int i = tid; i < Rg * nlive; i += nthr) {
@@ -443,16 +494,17 @@ LBX_DEV AttnParams attn_seq(const AttnParams &p, int s) {
   return q;
 }
 
-__global__ void __launch_bounds__(ATHREADS) attn_kernel(const __grid_constant__ AttnParams p) {
+template <bool B16>
+__global__ void __launch_bounds__(ATHREADS, B16 ? 4 : 1) attn_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(16) float sm[];
   pdl_trigger();
   pdl_wait();
   if (p.nseq > 1) {
     const int s = blockIdx.z / p.ngroups, g = blockIdx.z - s * p.ngroups;
     const AttnParams ps = attn_seq(p, s);
-    attn_unit(ps, blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * g), sm);
+    attn_unit<B16>(ps, blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * g), sm);
   } else {
-    attn_unit(p, blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z), sm);
+    attn_unit<B16>(p, blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z), sm);
   }
 }
 
@@ -531,8 +583,9 @@ static AttnWs attn_ws_layout(const lbx_attn_args *a) {
 
 // validated parameters of one attention op with explicit scratch pointers
 // (lbx_forward keeps the tickets at a fixed offset of its own workspace)
+// b16: the shared-memory size of the bf16-staged unit (attn_unit<true>)
 static int attn_prep(const lbx_attn_args *a, void *partials, unsigned *tickets, AttnParams &p,
-                     size_t &smem) {
+                     size_t &smem, bool b16 = false) {
   LBX_CHECK_ARG(a, "args is NULL");
   LBX_CHECK_ARG(a->n >= 1 && a->n <= 64, "n must be in [1,64]");
   LBX_CHECK_ARG(a->kv_heads >= 1 && a->heads >= a->kv_heads && a->heads % a->kv_heads == 0,
@@ -558,28 +611,35 @@ static int attn_prep(const lbx_attn_args *a, void *partials, unsigned *tickets, 
   p.part_seq = (int64_t)p.kvh * p.nchunk * p.R * p.d;
   p.ml_seq = (int64_t)p.kvh * p.nchunk * p.R;
   const int Rcap = p.rows;
-  const int KP = p.d + 4;
-  smem = ((size_t)(ACH + p.n) * KP + (size_t)(ACH + p.n) * p.d + (size_t)Rcap * KP + (size_t)Rcap * ACH) * 4 +
-         (size_t)Rcap * ACH * 2 + (size_t)p.n * 64;
+  const int KP = p.d + 4, KPB = p.d + 4;
+  const size_t kv = b16 ? ((size_t)attn_al8((ACH + p.n) * KPB) + (size_t)attn_al8((ACH + p.n) * p.d)) * 2
+                        : ((size_t)(ACH + p.n) * KP + (size_t)(ACH + p.n) * p.d) * 4;
+  smem = kv + ((size_t)Rcap * KP + (size_t)Rcap * ACH) * 4 + (size_t)Rcap * ACH * 2 + (size_t)p.n * 64;
   return LBX_OK;
 }
 
 static int attn_launch(const lbx_attn_args *a, void *partials, unsigned *tickets, cudaStream_t stream) {
   AttnParams p;
   size_t smem = 0;
-  int rc = attn_prep(a, partials, tickets, p, smem);
+  // many sequences: bf16 staging (more units per SM); one sequence: fp32 (lower latency)
+  const bool b16 = a->n_seq > 1;
+  int rc = attn_prep(a, partials, tickets, p, smem, b16);
   if (rc) return rc;
   static DevCache<size_t> smax_cache;
   size_t smax = 0;
   rc = smax_cache.get(smax, [](size_t &out) {
-    cudaError_t e = allow_max_smem(attn_kernel, &out);
+    size_t o2 = 0;
+    cudaError_t e = allow_max_smem(attn_kernel<false>, &out);
+    if (e == cudaSuccess) e = allow_max_smem(attn_kernel<true>, &o2);
+    out = std::min(out, o2);
     return e != cudaSuccess ? cuda_status(e, "attn smem attribute") : (int)LBX_OK;
   });
   if (rc) return rc;
   LBX_CHECK_SUP(smem <= smax, "attention needs %zu bytes of shared memory (max %zu)", smem, smax);
   const bool pdl = a->use_pdl != 0;
-  const cudaError_t e =
-      launch(attn_kernel, dim3(p.nchunk, p.kvh, p.ngroups * p.nseq), dim3(ATHREADS), smem, stream, pdl, p);
+  const dim3 grid(p.nchunk, p.kvh, p.ngroups * p.nseq);
+  const cudaError_t e = b16 ? launch(attn_kernel<true>, grid, dim3(ATHREADS), smem, stream, pdl, p)
+                            : launch(attn_kernel<false>, grid, dim3(ATHREADS), smem, stream, pdl, p);
   return cuda_status(e, "attn launch");
 }
 

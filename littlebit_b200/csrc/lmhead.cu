@@ -180,7 +180,7 @@ extern "C" int lbx_lmhead_argmax(const float *x, const float *norm_w, float eps,
   static DevCache<int> attr;
   int attr_done = 0;
   const int arc = attr.get(attr_done, [](int &out) {
-    for (auto k : {lmhead_kernel<1>, lmhead_kernel<2>, lmhead_kernel<4>, lmhead_kernel<8>}) {
+    for (auto k : {lmhead_kernel<1>, lmhead_kernel<2>, lmhead_kernel<4>, lmhead_kernel<6>, lmhead_kernel<8>}) {
       cudaError_t e = allow_max_smem(k);
       if (e != cudaSuccess) return cuda_status(e, "lmhead smem attribute");
     }
@@ -190,9 +190,11 @@ extern "C" int lbx_lmhead_argmax(const float *x, const float *norm_w, float eps,
   if (arc) return arc;
   const bool pdl = use_pdl != 0;
   const int nb = lm_blocks();
-  // tokens per pass: the normalised hidden states of a pass live in shared memory
+  // tokens per pass: the normalised hidden states of a pass live in shared
+  // memory (8, 6, 4, 2 or 1 of them; 6 at hidden 8192).  Each token's logits
+  // are the same fmaf chains whatever the pass holds.
   int per = LM_TOK;
-  while (per > 1 && (size_t)per * hidden * 4 > 200 * 1024) per >>= 1;
+  while (per > 1 && (size_t)per * hidden * 4 > 200 * 1024) per = per == 8 ? 6 : per == 6 ? 4 : per >> 1;
   for (int t0 = 0; t0 < n; t0 += per) {
     const int nt = std::min(per, n - t0);
     LmParams p = {};
@@ -206,9 +208,9 @@ extern "C" int lbx_lmhead_argmax(const float *x, const float *norm_w, float eps,
     p.w = w_bf16;
     p.logits = logits ? logits + (int64_t)t0 * vocab : nullptr;
     p.best = reinterpret_cast<unsigned long long *>(ws);
-    const int NT = nt <= 1 ? 1 : nt <= 2 ? 2 : nt <= 4 ? 4 : 8;  // rows >= nt staged as 0
+    const int NT = nt <= 1 ? 1 : nt <= 2 ? 2 : nt <= 4 ? 4 : nt <= 6 && per == 6 ? 6 : 8;  // rows >= nt staged as 0
     auto kern = NT == 1 ? lmhead_kernel<1> : NT == 2 ? lmhead_kernel<2> : NT == 4 ? lmhead_kernel<4>
-                                                                             : lmhead_kernel<8>;
+                : NT == 6 ? lmhead_kernel<6> : lmhead_kernel<8>;
     const size_t smem = (size_t)NT * hidden * 4;
     cudaError_t e = launch(kern, dim3(nb), dim3(LM_WARPS * 32), smem, stream, pdl, p);
     if (e != cudaSuccess) return cuda_status(e, "lmhead launch");

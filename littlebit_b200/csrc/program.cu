@@ -243,7 +243,7 @@ LBX_DEV bool run_unit(const Phase &P, const ProgIo &io, int u, uint8_t *W, uint8
     case PH_U:
       return ustage_run<NCB>(P.u, u, P.units, W, S, sh);
     case PH_ATTN:
-      attn_unit(P.a, u, reinterpret_cast<float *>(S));
+      attn_unit<false>(P.a, u, reinterpret_cast<float *>(S));
       return true;
     case PH_START:
       start_unit(P.st, io, u);
