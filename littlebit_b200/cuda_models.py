@@ -280,55 +280,90 @@ class CudaDraftModel:
                     temperature: float = 1.0) -> torch.Tensor:
         """generate_draft_tree on the device: the root's top-k fill depth 1, then each
         depth level is expanded by ONE tree-masked forward over all nodes up to that
-        depth (the reference runs one full-prefix forward per expanded node)."""
-        from .tree_utils import tree_bitmasks
-
+        depth (the reference runs one full-prefix forward per expanded node), one
+        batched top-k over the level's parents and one indexed fill of their
+        children.  Everything but the tokens depends only on the tree's shape and is
+        planned once per shape (``_tree_plan``)."""
         ids = input_ids[0].tolist()
         P = len(ids) - 1
         self._sync_prefix(ids, P)
         dev = self.device
+        plan = _tree_plan(tree_buffers, top_k, dev)
         root = self.dec.forward_tokens([ids[-1]], P, want_logits=True, want_argmax=False)["logits"]
         self.unit.pos = P + 1
         self._cached_ids = ids[:]
-        sc = tree_buffers["sorted_tree_choices"]
-        T = tree_buffers["tree_len"]
-        depth_of = [0] + [len(c) for c in sc]
-        index = {tuple(c): i + 1 for i, c in enumerate(sc)}
-        cand = torch.zeros(T, dtype=torch.int64, device=dev)
+        inv_t = 1.0 / max(temperature, 1e-5)
+        cand = torch.zeros(plan["T"], dtype=torch.int64, device=dev)
         cand[0] = ids[-1]
-        ktop = torch.topk(root[0] / max(temperature, 1e-5), top_k).indices
-        for c in sc:
-            if len(c) == 1:
-                cand[index[tuple(c)]] = ktop[c[0]]
-        mask = tree_buffers["tree_attn_mask"]
-        full_bits = tree_bitmasks(mask)  # over all T nodes (root = bit 0)
-        maxd = max(depth_of)
-        for d in range(1, maxd):
-            nodes = [i for i in range(1, T) if depth_of[i] <= d]
-            # nodes occupy slots P+1 .. in index order; drop the root bit (it is cached)
-            remap = {j: r for r, j in enumerate(nodes)}
-            bits = []
-            for i in nodes:
-                b = int(full_bits[i]) & ((1 << 64) - 1)
-                v = 0
-                for j in nodes:
-                    if (b >> j) & 1:
-                        v |= 1 << remap[j]
-                bits.append(v - (1 << 64) if v >= (1 << 63) else v)
-            pos = [P + depth_of[i] for i in nodes]
-            out = self.dec.forward_tokens(cand[nodes], P + 1, pos=pos, tree_mask=bits,
-                                          want_logits=True, want_argmax=False)["logits"]
-            for r, i in enumerate(nodes):
-                if depth_of[i] != d:
-                    continue
-                path = tuple(sc[i - 1])
-                kids = [c for c in sc if len(c) == d + 1 and tuple(c[:d]) == path]
-                if not kids:
-                    continue
-                kt = torch.topk(out[r] / max(temperature, 1e-5), top_k).indices
-                for c in kids:
-                    cand[index[tuple(c)]] = kt[c[-1]]
+        ktop = torch.topk(root[0] * inv_t if temperature != 1.0 else root[0], top_k).indices
+        cand[plan["d1_nodes"]] = ktop[plan["d1_ranks"]]
+        for lv in plan["levels"]:
+            out = self.dec.forward_tokens(cand[lv["nodes"]], P + 1, pos=[P + o for o in lv["depth"]],
+                                          tree_mask=lv["bits"], want_logits=True, want_argmax=False)["logits"]
+            if lv["kids"] is None:
+                continue
+            par = out[lv["parent_rows"]]
+            kt = torch.topk(par * inv_t if temperature != 1.0 else par, top_k).indices
+            cand[lv["kids"]] = kt[lv["kid_parent"], lv["kid_rank"]]
         return cand[None]
+
+
+_TREE_PLANS: Dict = {}
+
+
+def _tree_plan(tree_buffers: Dict, top_k: int, dev) -> Dict:
+    """Per tree shape: for each depth level the nodes of the level's forward (all
+    nodes up to that depth, in index order), their tree-mask bits over those
+    nodes, their depths, the rows of the level's parents and, per child, its node
+    index, its parent's row among those and its top-k rank."""
+    from .tree_utils import tree_bitmasks
+
+    sc = tree_buffers["sorted_tree_choices"]
+    key = (tuple(tuple(c) for c in sc), int(tree_buffers["tree_len"]), int(top_k), str(dev))
+    plan = _TREE_PLANS.get(key)
+    if plan is not None:
+        return plan
+    T = tree_buffers["tree_len"]
+    depth_of = [0] + [len(c) for c in sc]
+    index = {tuple(c): i + 1 for i, c in enumerate(sc)}
+    full_bits = tree_bitmasks(tree_buffers["tree_attn_mask"])  # over all T nodes (root = bit 0)
+    d1 = [c for c in sc if len(c) == 1]
+    t64 = lambda v: torch.tensor(v, dtype=torch.int64, device=dev)
+    levels = []
+    for d in range(1, max(depth_of)):
+        nodes = [i for i in range(1, T) if depth_of[i] <= d]
+        # nodes occupy slots P+1 .. in index order; drop the root bit (it is cached)
+        remap = {j: r for r, j in enumerate(nodes)}
+        bits = []
+        for i in nodes:
+            b = int(full_bits[i]) & ((1 << 64) - 1)
+            v = 0
+            for j in nodes:
+                if (b >> j) & 1:
+                    v |= 1 << remap[j]
+            bits.append(v - (1 << 64) if v >= (1 << 63) else v)
+        parent_rows, kids, kid_parent, kid_rank = [], [], [], []
+        for r, i in enumerate(nodes):
+            if depth_of[i] != d:
+                continue
+            path = tuple(sc[i - 1])
+            ch = [c for c in sc if len(c) == d + 1 and tuple(c[:d]) == path]
+            if not ch:
+                continue
+            for c in ch:
+                kids.append(index[tuple(c)])
+                kid_parent.append(len(parent_rows))
+                kid_rank.append(c[-1])
+            parent_rows.append(r)
+        levels.append({"nodes": t64(nodes), "bits": bits, "depth": [depth_of[i] for i in nodes],
+                       "parent_rows": t64(parent_rows) if kids else None,
+                       "kids": t64(kids) if kids else None,
+                       "kid_parent": t64(kid_parent) if kids else None,
+                       "kid_rank": t64(kid_rank) if kids else None})
+    plan = {"T": T, "levels": levels, "d1_nodes": t64([index[tuple(c)] for c in d1]),
+            "d1_ranks": t64([c[0] for c in d1])}
+    _TREE_PLANS[key] = plan
+    return plan
 
 
 class CudaTargetModel:
@@ -470,8 +505,14 @@ class CudaTargetModel:
         from .tree_utils import tree_bitmasks
 
         T = cand.numel()
-        pos = (P + tree_buffers["tree_position_ids"].to(self.device)).to(torch.int32)
-        bits = tree_bitmasks(tree_buffers["tree_attn_mask"]).to(self.device)
+        key = (tuple(tuple(c) for c in tree_buffers["sorted_tree_choices"]), T, str(self.device))
+        cached = self._verify_plan if getattr(self, "_verify_plan_key", None) == key else None
+        if cached is None:  # per tree shape: position offsets and mask bits on the device
+            cached = (tree_buffers["tree_position_ids"].to(self.device).to(torch.int32),
+                      tree_bitmasks(tree_buffers["tree_attn_mask"]).to(self.device))
+            self._verify_plan, self._verify_plan_key = cached, key
+        pos = P + cached[0]
+        bits = cached[1]
         am = torch.empty(T, dtype=torch.int64, device=self.device)
         self._step(cand, P, argmax=am, pos=pos, tree_mask=bits)
         return am

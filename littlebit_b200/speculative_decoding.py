@@ -396,10 +396,12 @@ def speculative_decode_tree(draft_model, target_model, input_ids: torch.Tensor,
         node_am = target_model.verify_tree(cand, P, tree_buffers)
         padded = torch.cat([cand, torch.full((1,), -1, dtype=torch.int64, device=dev)])
         cart = padded[retrieve]  # retrieve uses -1 for padding -> the appended -1
-        res = accept_greedy_tree(cart.contiguous(), node_am, retrieve.contiguous()).tolist()
+        res_d = accept_greedy_tree(cart.contiguous(), node_am, retrieve.contiguous())
+        both = torch.cat([res_d, cand.to(torch.int64)]).tolist()  # one device read: outcome and candidates
+        res, cand_h = both[:res_d.numel()], both[res_d.numel():]
         best, alen, bonus = res[0], res[1], res[2]
         nodes = [int(v) for v in res[3:3 + alen]]
-        acc_toks = [int(cand[j]) for j in nodes]
+        acc_toks = [cand_h[j] for j in nodes]
         stop = False
         for t in acc_toks:
             gen.append(t)
