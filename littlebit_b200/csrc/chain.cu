@@ -137,10 +137,11 @@ LBX_DEV void st_async_b32(uint32_t addr, int v, uint32_t bar) {
                "r"(bar)
                : "memory");
 }
-LBX_DEV void st_async_v2(uint32_t addr, int a, int b, uint32_t bar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(addr),
-               "r"(a), "r"(b), "r"(bar)
-               : "memory");
+LBX_DEV void st_async_v4(uint32_t addr, int a, int b, int c, int d, uint32_t bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+      "r"(a), "r"(b), "r"(c), "r"(d), "r"(bar)
+      : "memory");
 }
 // bounded wait on a phase of an mbarrier that other CTAs of the cluster
 // complete (acquire at cluster scope), polled with test_wait: the data is
@@ -359,7 +360,6 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
     }
     __syncthreads();
     LBX_PROBE(23);
-    LBX_PROBE(24);
     // ---- contraction: warp w = output rows 16w..16w+15 of the cluster, each
     // of this CTA's groups on its own (exact int32, kept in registers)
     const int g = lane >> 2, q = lane & 3;
@@ -432,20 +432,22 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
           A[t][3] = __shfl_sync(0xffffffffu, I[1][1], src);
         }
       }
-      const int row = warp * 16 + g;
+      // one 16-byte store per (destination, token): both rows of the lane's
+      // row pair (warp * 16 + g and + 8), both branches; xs is laid out as
+      // [source CTA][row pair][token][4]
+      const int rp = warp * 8 + g;
 #pragma unroll
       for (int dd = 0; dd < FC_CS / 4; ++dd) {
         const int d = q + 4 * dd;
         const uint32_t bar = cl_addr(&xbar[1], d);
 #pragma unroll
-        for (int t = 0; t < FC_MAXK; ++t) {
-          if (t < k) {
-            st_async_v2(cl_addr(xs + ((j * FC_ROWS + row) * k + t) * 2, d), A[t][0], A[t][1], bar);
-            st_async_v2(cl_addr(xs + ((j * FC_ROWS + row + 8) * k + t) * 2, d), A[t][2], A[t][3], bar);
-          }
-        }
+        for (int t = 0; t < FC_MAXK; ++t)
+          if (t < k)
+            st_async_v4(cl_addr(xs + ((j * (FC_ROWS / 2) + rp) * k + t) * 4, d), A[t][0], A[t][1], A[t][2],
+                        A[t][3], bar);
       }
     }
+    LBX_PROBE(24);
     // cluster barrier C (waited at the exit): no CTA leaves before every CTA
     // of the cluster has issued its stores into the others' shared memory.
     // Relaxed: the stores a CTA receives are all counted on its own barriers,
@@ -456,10 +458,11 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
     LBX_PROBE(28);
     for (int it = tid; it < FC_ROWS * k; it += FC_THREADS) {
       const int t = it / FC_ROWS, r = it - t * FC_ROWS;
+      const int rp = (r >> 4) * 8 + (r & 7), hf = (r >> 3) & 1;  // row pair, and which of its rows
       int I0 = 0, I1 = 0;
 #pragma unroll
       for (int d = 0; d < FC_CS; ++d) {
-        const int2 v = *reinterpret_cast<const int2 *>(xs + ((d * FC_ROWS + r) * k + t) * 2);
+        const int2 v = *reinterpret_cast<const int2 *>(xs + ((d * (FC_ROWS / 2) + rp) * k + t) * 4 + 2 * hf);
         I0 += v.x;
         I1 += v.y;
       }
