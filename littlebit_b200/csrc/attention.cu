@@ -257,16 +257,14 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
 #pragma unroll
     for (int u = 0; u < NR; ++u) a[u] = 0.f;
     if (row >= 0) {
-      const uint2 *k2 = reinterpret_cast<const uint2 *>(Kb + row * KPB);
-      const float4 *k4 = reinterpret_cast<const float4 *>(Ka + row * KP);
       for (int t = 0; t < d / 4; ++t) {
         float4 kv;
         if constexpr (B16) {
-          const uint2 kw = k2[t];
+          const uint2 kw = reinterpret_cast<const uint2 *>(Kb + row * KPB)[t];
           kv = make_float4(__uint_as_float(kw.x << 16), __uint_as_float(kw.x & 0xFFFF0000u),
                            __uint_as_float(kw.y << 16), __uint_as_float(kw.y & 0xFFFF0000u));
         } else {
-          kv = k4[t];
+          kv = reinterpret_cast<const float4 *>(Ka + row * KP)[t];
         }
 #pragma unroll
         for (int u = 0; u < NR; ++u) {

@@ -202,7 +202,8 @@ struct WParams {
   WSeg seg[2 * LBX_MAX_PROJ];
   WUProj up[LBX_MAX_PROJ];
   int nseg, nproj;
-  int K, Wv, nblk, k, KP;
+  int K, Wv, nblk, k, KP;  // KP: tokens of the records (the batch padded to 8, 16, 32 or 64)
+  int vts, uts;            // token splits of the V and U grids: a CTA takes KP / splits tokens
   int xdt, prologue, ydt, epi;
   float eps;
   const void *x, *x2;
@@ -367,14 +368,17 @@ __global__ void __launch_bounds__(WD_TPB, 1) wv_kernel(const __grid_constant__ W
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool cw = tid < WD_CW;
   const int row = tid & 127, qd = (tid >> 7) & 3;
+  // CTA = (tile, token split): tokens t0 .. t0+KP of the batch's KPR
+  const int tile = (int)blockIdx.x / p.vts, t0 = ((int)blockIdx.x - tile * p.vts) * KP;
+  const int NR = 2 * p.KP;  // rows of the records' operand images
   int si = 0;
-  while (si + 1 < p.nseg && (int)blockIdx.x >= p.seg[si + 1].tile0) ++si;
+  while (si + 1 < p.nseg && tile >= p.seg[si + 1].tile0) ++si;
   const WSeg &sg = p.seg[si];
-  const int grp = (int)blockIdx.x - sg.tile0;
+  const int grp = tile - sg.tile0;
   const int rr = grp * 128 + row;
   const bool rvalid = cw && rr < sg.rank;
   const int nb = p.nblk;
-  const int k = p.k;
+  const int k = p.k - t0;  // valid tokens from t0 on (may exceed KP)
   volatile int *abrt = &abort_flag;
   LBX_PROBE(40);
 
@@ -424,12 +428,17 @@ __global__ void __launch_bounds__(WD_TPB, 1) wv_kernel(const __grid_constant__ W
   if (warp == 16) {
     // ---- issuing warp (lane 0 acts, the warp stays converged)
     int nissued = 0, ncommit = 0;
+    // this CTA's rows of each image atom, and its tokens' block scales (rows
+    // 2*t0 .. are a whole number of 8-row swizzle atoms, so the copies keep the layout)
     auto issue_b = [&](int i) {
       if (lane == 0) {
         const int buf = i % WD_NBV;
-        mbar_arrive_expect_tx(&bbar[buf], (uint32_t)p.rec_bytes);
-        bulk_g2s(sB + buf * SB, sg.xrec + (size_t)(blist[i] & 0x7fff) * p.rec_bytes, (uint32_t)p.rec_bytes,
-                 &bbar[buf]);
+        const uint8_t *rec = sg.xrec + (size_t)(blist[i] & 0x7fff) * p.rec_bytes;
+        uint8_t *dst = sB + buf * SB;
+        mbar_arrive_expect_tx(&bbar[buf], (uint32_t)(2 * N * 128 + KP * 4));
+        bulk_g2s(dst, rec + (size_t)2 * t0 * 128, N * 128u, &bbar[buf]);
+        bulk_g2s(dst + N * 128, rec + (size_t)NR * 128 + (size_t)2 * t0 * 128, N * 128u, &bbar[buf]);
+        bulk_g2s(dst + N * 256, rec + (size_t)NR * 256 + (size_t)t0 * 4, KP * 4u, &bbar[buf]);
       }
       ++nissued;
     };
@@ -541,7 +550,7 @@ __global__ void __launch_bounds__(WD_TPB, 1) wv_kernel(const __grid_constant__ W
   for (int i = 0; i < KQ; ++i) {
     const int t = qd * KQ + i;
     float vv = V[i];
-    if (rms && cw && t < k) vv *= __ldcg(sg.rs + t);
+    if (rms && cw && t < k) vv *= __ldcg(sg.rs + t0 + t);
     T[i] = vv;
   }
   uint8_t *img = sA;  // staging images of the two sides (the A buffers are free)
@@ -579,10 +588,11 @@ __global__ void __launch_bounds__(WD_TPB, 1) wv_kernel(const __grid_constant__ W
       }
     }
     __syncthreads();
+    // (this CTA's tokens' rows of the record image: bytes 2*t0*128 on, the layout kept)
     uint8_t *rec = (sd ? sg.urec1 : sg.urec0) + (size_t)grp * p.urec_bytes;
     for (int o = 16 * tid; o < N * 128; o += 16 * WD_TPB)
-      *reinterpret_cast<uint4 *>(rec + o) = *reinterpret_cast<const uint4 *>(im + o);
-    if (tid < KP) reinterpret_cast<int *>(rec + N * 128)[tid] = gex[tid];
+      *reinterpret_cast<uint4 *>(rec + (size_t)2 * t0 * 128 + o) = *reinterpret_cast<const uint4 *>(im + o);
+    if (tid < KP) reinterpret_cast<int *>(rec + (size_t)NR * 128)[t0 + tid] = gex[tid];
     __syncthreads();  // (gex / gsc are rewritten by the next side)
   }
   LBX_PROBE(44);
@@ -613,12 +623,15 @@ __global__ void __launch_bounds__(WD_TPB, 1) wu_kernel(const __grid_constant__ W
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool cw = tid < WD_CW;
   const int row = tid & 127, qd = (tid >> 7) & 3;
+  // CTA = (tile, token split): tokens t0 .. t0+KP of the batch's KPR
+  const int tile = (int)blockIdx.x / p.uts, t0 = ((int)blockIdx.x - tile * p.uts) * KP;
+  const int NR = 2 * p.KP;  // rows of the records' operand images
   int pi = 0;
-  while (pi + 1 < p.nproj && (int)blockIdx.x >= p.up[pi + 1].tile0) ++pi;
+  while (pi + 1 < p.nproj && tile >= p.up[pi + 1].tile0) ++pi;
   const WUProj &pj = p.up[pi];
-  const int n = ((int)blockIdx.x - pj.tile0) * 128 + row;
+  const int n = (tile - pj.tile0) * 128 + row;
   const bool nvalid = cw && n < pj.out;
-  const int k = p.k;
+  const int k = p.k - t0;  // valid tokens from t0 on (may exceed KP)
   const int ng0 = pj.ng[0], ngt = pj.ng[0] + (pj.nbr > 1 ? pj.ng[1] : 0);
   volatile int *abrt = &abort_flag;
   LBX_PROBE(50);
@@ -662,7 +675,8 @@ __global__ void __launch_bounds__(WD_TPB, 1) wu_kernel(const __grid_constant__ W
     if (t < k && b < pj.nbr) {
       const int ng = pj.ng[b];
       for (int g = 0; g < ng; ++g)
-        e = min(e, __ldcg(reinterpret_cast<const int *>(pj.urec[b] + (size_t)g * p.urec_bytes + N * 128) + t));
+        e = min(e, __ldcg(reinterpret_cast<const int *>(pj.urec[b] + (size_t)g * p.urec_bytes + (size_t)NR * 128) +
+                          t0 + t));
     }
     ec[b][t] = e == UE_NONE ? 0 : e;
   }
@@ -680,8 +694,11 @@ __global__ void __launch_bounds__(WD_TPB, 1) wu_kernel(const __grid_constant__ W
       if (lane == 0) {
         const int buf = G % WD_NBU;
         const int b = G < ng0 ? 0 : 1, g = b ? G - ng0 : G;
-        mbar_arrive_expect_tx(&bbar[buf], (uint32_t)p.urec_bytes);
-        bulk_g2s(sB + buf * SBU, pj.urec[b] + (size_t)g * p.urec_bytes, (uint32_t)p.urec_bytes, &bbar[buf]);
+        // this CTA's rows of the image (whole 8-row swizzle atoms), then its tokens' exponents
+        const uint8_t *rec = pj.urec[b] + (size_t)g * p.urec_bytes;
+        mbar_arrive_expect_tx(&bbar[buf], (uint32_t)(N * 128 + KP * 4));
+        bulk_g2s(sB + buf * SBU, rec + (size_t)2 * t0 * 128, N * 128u, &bbar[buf]);
+        bulk_g2s(sB + buf * SBU + N * 128, rec + (size_t)NR * 128 + (size_t)t0 * 4, KP * 4u, &bbar[buf]);
       }
       ++nissued;
     };
@@ -794,7 +811,7 @@ __global__ void __launch_bounds__(WD_TPB, 1) wu_kernel(const __grid_constant__ W
     if (t >= k) break;
     float v = u_result(u1a, I0[i], ec[0][t], pj.nbr > 1, u1b, I1[i], ec[1][t], pj.bias != nullptr, bias);
     if (p.epi == LBX_EPI_SILU0 && pi == 0) v = v / (1.0f + expf(-v));
-    const int64_t off = (int64_t)t * pj.y_ld + n;
+    const int64_t off = (int64_t)(t0 + t) * pj.y_ld + n;
     if (p.ydt == LBX_F32) {
       float *y = reinterpret_cast<float *>(pj.y) + off;
       if (p.epi == LBX_EPI_ADD) v += *y;
@@ -837,25 +854,43 @@ static size_t wide_ws_bytes(const lbx_proj *projs, int n_proj, int k) {
   return tot;
 }
 
-template <int KP>
-static int wide_launch(const WParams &wp, int vtiles, int utiles, bool pdl, cudaStream_t stream) {
+template <int KPS>
+static int wv_launch(const WParams &wp, int vtiles, bool pdl, cudaStream_t stream) {
   static DevCache<int> attr;
   int dummy = 0;
-  int rc = attr.get(dummy, [](int &) {
-    cudaError_t e = cudaFuncSetAttribute(wv_kernel<KP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)wv_smem(KP));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(wu_kernel<KP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wu_smem(KP));
-    return cuda_status(e, "tensor-core stage attributes");
+  const int rc = attr.get(dummy, [](int &) {
+    return cuda_status(cudaFuncSetAttribute(wv_kernel<KPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)wv_smem(KPS)),
+                       "tensor-core V-stage attribute");
   });
   if (rc) return rc;
-  cudaError_t e = launch(wx_stage_kernel, dim3(wp.k, wp.nseg), dim3(WX_THREADS), 0, stream, pdl, wp);
-  if (e != cudaSuccess) return cuda_status(e, "x staging launch");
-  e = launch(wv_kernel<KP>, dim3(vtiles), dim3(WD_TPB), wv_smem(KP), stream, pdl, wp);
-  if (e != cudaSuccess) return cuda_status(e, "tensor-core V-stage launch");
-  e = launch(wu_kernel<KP>, dim3(utiles), dim3(WD_TPB), wu_smem(KP), stream, pdl, wp);
-  if (e != cudaSuccess) return cuda_status(e, "tensor-core U-stage launch");
-  return LBX_OK;
+  return cuda_status(launch(wv_kernel<KPS>, dim3(vtiles * wp.vts), dim3(WD_TPB), wv_smem(KPS), stream, pdl, wp),
+                     "tensor-core V-stage launch");
+}
+template <int KPS>
+static int wu_launch(const WParams &wp, int utiles, bool pdl, cudaStream_t stream) {
+  static DevCache<int> attr;
+  int dummy = 0;
+  const int rc = attr.get(dummy, [](int &) {
+    return cuda_status(cudaFuncSetAttribute(wu_kernel<KPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)wu_smem(KPS)),
+                       "tensor-core U-stage attribute");
+  });
+  if (rc) return rc;
+  return cuda_status(launch(wu_kernel<KPS>, dim3(utiles * wp.uts), dim3(WD_TPB), wu_smem(KPS), stream, pdl, wp),
+                     "tensor-core U-stage launch");
+}
+
+// Token splits of a grid of `tiles` CTAs: while the grid would fill at most
+// half of the SMs, each tile's tokens are split over twice as many CTAs (at
+// least 8 tokens each, the last split holding tokens).  Every token's
+// arithmetic is the same in any split.  Measured on the 70B down projection
+// at 64 tokens (50 V tiles, 64 U tiles): see the design notes.
+static int wide_split(int tiles, int KPR, int k) {
+  const int sms = device_sm_count();
+  int ts = 1;
+  while (ts < 8 && KPR / (2 * ts) >= 8 && tiles * ts * 2 <= sms && (2 * ts - 1) * (KPR / (2 * ts)) < k) ts *= 2;
+  return ts;
 }
 
 // one batch of k <= WD_MAXK tokens starting at token tok0
@@ -929,11 +964,23 @@ static int wide_batch(const lbx_proj *projs, const lbx_linear_args *a, int tok0,
   }
   wp.nproj = n_proj;
   const bool pdl = a->use_pdl != 0;
-  switch (KP) {
-    case 8: return wide_launch<8>(wp, vtiles, utiles, pdl, stream);
-    case 16: return wide_launch<16>(wp, vtiles, utiles, pdl, stream);
-    case 32: return wide_launch<32>(wp, vtiles, utiles, pdl, stream);
-    default: return wide_launch<64>(wp, vtiles, utiles, pdl, stream);
+  wp.vts = wide_split(vtiles, KP, k);
+  wp.uts = wide_split(utiles, KP, k);
+  cudaError_t e = launch(wx_stage_kernel, dim3(wp.k, wp.nseg), dim3(WX_THREADS), 0, stream, pdl, wp);
+  if (e != cudaSuccess) return cuda_status(e, "x staging launch");
+  int rc;
+  switch (KP / wp.vts) {
+    case 8: rc = wv_launch<8>(wp, vtiles, pdl, stream); break;
+    case 16: rc = wv_launch<16>(wp, vtiles, pdl, stream); break;
+    case 32: rc = wv_launch<32>(wp, vtiles, pdl, stream); break;
+    default: rc = wv_launch<64>(wp, vtiles, pdl, stream); break;
+  }
+  if (rc) return rc;
+  switch (KP / wp.uts) {
+    case 8: return wu_launch<8>(wp, utiles, pdl, stream);
+    case 16: return wu_launch<16>(wp, utiles, pdl, stream);
+    case 32: return wu_launch<32>(wp, utiles, pdl, stream);
+    default: return wu_launch<64>(wp, utiles, pdl, stream);
   }
 }
 
