@@ -240,9 +240,10 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
   const int nbk = s_nb;
   // (the row count of a block as a compile-time bound: a one-row block, every
   // row of a multi-head-attention step, runs no predicated-off rows)
-  auto score_block = [&](auto nrc, int bi, int jj) {
+  // rows ra .. ra+nr of block bi (the block's map row is written once, by its
+  // first part)
+  auto score_block = [&](auto nrc, int bi, int jj, int ra, int nr) {
     constexpr int NR = decltype(nrc)::value;
-    const int ra = s_bstart[bi], nr = s_bstart[bi + 1] - ra;
     const int i = (rlo + ra) / p.rep;
     const int rank = r0 + jj;
     int row = -1;
@@ -252,7 +253,7 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
       const int t = rank - prefix;
       if (has_new && t < s_cnt[i]) row = ACH + sel[i * 64 + t];
     }
-    map[bi * ACH + jj] = (int16_t)row;
+    if (ra == s_bstart[bi]) map[bi * ACH + jj] = (int16_t)row;
     float a[NR];
 #pragma unroll
     for (int u = 0; u < NR; ++u) a[u] = 0.f;
@@ -284,13 +285,18 @@ LBX_DEV void attn_unit(const AttnParams &p, int unit, float *sm) {
     for (int u = 0; u < NR; ++u)
       if (u < nr) Pm[(ra + u) * ACH + jj] = row >= 0 ? a[u] * p.scale : -INFINITY;
   };
-  for (int e = tid; e < nbk * ACH; e += nthr) {
-    const int bi = e / ACH, jj = e - bi * ACH;
-    const int nr = s_bstart[bi + 1] - s_bstart[bi];
-    if (nr == 1) score_block(std::integral_constant<int, 1>{}, bi, jj);
-    else if (nr <= 2) score_block(std::integral_constant<int, 2>{}, bi, jj);
-    else if (nr <= 4) score_block(std::integral_constant<int, 4>{}, bi, jj);
-    else score_block(std::integral_constant<int, ARB>{}, bi, jj);
+  // with threads to spare, each block's rows are scored in two halves (a
+  // decode step's GQA block of 8 rows fills 64 of 128 threads otherwise)
+  const int S = nbk * ACH * 2 <= nthr ? 2 : 1, HR = ARB / S;
+  for (int e = tid; e < nbk * ACH * S; e += nthr) {
+    const int bh = e / ACH, jj = e - bh * ACH;
+    const int bi = bh / S, h = bh - bi * S;
+    const int ra = s_bstart[bi] + h * HR, nr = min(s_bstart[bi + 1] - ra, HR);
+    if (nr <= 0) continue;
+    if (nr == 1) score_block(std::integral_constant<int, 1>{}, bi, jj, ra, nr);
+    else if (nr <= 2) score_block(std::integral_constant<int, 2>{}, bi, jj, ra, nr);
+    else if (nr <= 4) score_block(std::integral_constant<int, 4>{}, bi, jj, ra, nr);
+    else score_block(std::integral_constant<int, ARB>{}, bi, jj, ra, nr);
   }
   __syncthreads();
 
