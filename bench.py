@@ -1015,14 +1015,16 @@ def run_configs(args, dev, stream, ws, main_pool, peak, peak_kind):
         t_k = timed_graph(lambda: ch.run(L.LBX_EXEC_KERNELS, stream), stream, warm, steps, ws)
         y_k = ch.acts[-1].clone()
         t, exe = t_k, "two stage grids per layer"
-        if k <= 4:  # the fused chain executor (same bits) when the call fits it
+        if k <= 8:  # the fused chain executor (same bits) when the call fits it
             fc = ops.FusedChain(pool)
             ptrs = (ctypes.c_void_p * (len(pool) + 1))(*[a.data_ptr() for a in ch.acts])
             t_f = timed_graph(lambda: fc.run(ch.acts, ptrs=ptrs, stream=stream), stream, warm, steps, ws)
             if not torch.equal(ch.acts[-1], y_k):
                 raise RuntimeError(f"{name}: fused chain and stage grids disagree")
             if t_f < t_k:
-                t, exe = t_f, "fused chain (one launch per layer)"
+                t, exe = t_f, ("fused chain (one launch per layer)" if k == 1 else
+                               f"fused chain as two concurrent sub-chains of {(k + 1) // 2} and {k // 2} tokens "
+                               f"(one launch per layer each)")
             del fc
         us = t * 1e3 / (steps * len(pool))
         b, packed = layer_bytes(k, ranks, shared, 4 if dtype == torch.float32 else 2)
@@ -1080,7 +1082,7 @@ def run_ours(args):
     def step_program():  # the whole chain as one persistent program
         ops.linear_chain(pool, acts, ws=wsc, arr=arr_all, ptrs=ptrs)
 
-    fchain = ops.FusedChain(pool) if k <= 4 else None  # sign words copied once into its layout
+    fchain = ops.FusedChain(pool) if k <= 8 else None  # sign words copied once into its layout
 
     def step_fused():  # n + 1 launches: layer i's U-stage with layer i+1's V partials
         fchain.run(acts, ptrs=ptrs, stream=stream)
@@ -1105,8 +1107,8 @@ def run_ours(args):
     for name, fn in execs.items():
         if name == args.exec:
             continue
-        if name in ("cluster", "fused") and k > 4:
-            continue  # the cluster and fused executors take k <= 4
+        if (name == "cluster" and k > 4) or (name == "fused" and k > 8):
+            continue  # the cluster executor takes k <= 4, the fused chain k <= 8
         exec_t[name] = timed_graph(fn, stream, args.warmup, args.steps, ws)
         if not torch.equal(acts[-1], y_main):
             raise RuntimeError(f"{name} and {args.exec} executors disagree")

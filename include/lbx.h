@@ -272,7 +272,12 @@ int lbx_linear_chain(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens, 
  * Every output is bit-identical to calling lbx_linear layer by layer.
  * Requirements: in/out features multiples of 256 (in <= 8192), no prologue,
  * store epilogue, 1-2 branches of at most 32 quantisation groups (128 ranks)
- * together, 1..4 tokens, one activation dtype (LBX_F32 / LBX_BF16).
+ * together, 1..8 tokens, one activation dtype (LBX_F32 / LBX_BF16).  A call
+ * of 2..8 tokens runs as two chains of ceil(k/2) and floor(k/2) tokens at
+ * once, the second on a helper stream the library keeps per device, forked
+ * from `stream` and joined back to it with events (so the call may be
+ * captured in a CUDA graph); calls on one device then come from one host
+ * thread at a time.
  * lbx_chain_prepare writes, once, a copy of the chain's sign words laid out
  * so that each CTA's share of a layer is contiguous (blob of
  * lbx_chain_prepare_size bytes, 16-byte aligned); the layers' scale vectors

@@ -749,49 +749,13 @@ extern "C" int lbx_chain_prepare(const lbx_proj *projs, int32_t n_layers, void *
   return LBX_OK;
 }
 
-extern "C" size_t lbx_chain_fused_workspace_size(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens) {
-  using namespace lbx;
-  if (fc_validate(projs, n_layers) || n_tokens < 1 || n_tokens > FC_MAXK) return 0;
-  return fc_ws_bytes(projs, n_layers, n_tokens);
-}
+namespace lbx {
 
-extern "C" int lbx_chain_fused(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens, int32_t dtype,
-                               void *const *acts, const void *blob, size_t blob_bytes, void *ws, size_t ws_bytes,
-                               cudaStream_t stream) {
-  using namespace lbx;
-  int rc = fc_validate(projs, n_layers);
-  if (rc) return rc;
-  LBX_CHECK_SUP(n_tokens >= 1 && n_tokens <= FC_MAXK, "fused chain: 1..%d tokens", FC_MAXK);
-  LBX_CHECK_ARG(dtype == LBX_F32 || dtype == LBX_BF16, "bad dtype");
-  LBX_CHECK_ARG(acts && blob, "NULL argument");
-  for (int i = 0; i <= n_layers; ++i) LBX_CHECK_ARG(acts[i], "acts[%d] is NULL", i);
-  // every layer's plan once: blob offsets (as fc_blob_words lays them out)
-  // and the partial-sum buffers (as fc_ws_bytes sizes them)
-  const int k = n_tokens;
-  std::vector<FcPlan> plan(n_layers);
-  std::vector<size_t> uo(n_layers), vo(n_layers);
-  size_t words = 0, pmax = 0;
-  for (int i = 0; i < n_layers; ++i) {
-    rc = fc_plan(projs[i], plan[i]);
-    if (rc) return rc;
-    uo[i] = words;
-    words += (plan[i].ublob_words + 63) & ~(size_t)63;
-    vo[i] = words;
-    words += (plan[i].vblob_words + 63) & ~(size_t)63;
-    pmax = std::max(pmax, (size_t)(projs[i].in_features / FC_ROWS) * k * plan[i].pcols * 4);
-  }
-  LBX_CHECK_ARG(blob_bytes >= words * 4, "blob too small (%zu < %zu)", blob_bytes, words * 4);
-  const size_t need = 2 * al256(pmax);
-  LBX_CHECK_ARG(ws && ws_bytes >= need, "workspace too small (%zu < %zu)", ws_bytes, need);
-  static DevCache<size_t> smax_cache;
-  size_t smax = 0;
-  rc = smax_cache.get(smax, [](size_t &out) {
-    const cudaError_t e = allow_max_smem(fc_kernel, &out);
-    return e != cudaSuccess ? cuda_status(e, "fused chain smem attribute") : (int)LBX_OK;
-  });
-  if (rc) return rc;
-  const uint32_t *b = reinterpret_cast<const uint32_t *>(blob);
-  float *part[2] = {reinterpret_cast<float *>(ws), reinterpret_cast<float *>(ws) + need / 8};
+// the launches of one chain for tokens [0, k) of acts (already offset to the
+// sub-batch's first token), partial sums in part[0] / part[1]
+static int fc_run(const lbx_proj *projs, int n_layers, int k, int dtype, void *const *acts, const uint32_t *b,
+                  const std::vector<FcPlan> &plan, const std::vector<size_t> &uo, const std::vector<size_t> &vo,
+                  float *const (&part)[2], size_t smax, cudaStream_t stream) {
   for (int i = -1; i < n_layers; ++i) {
     FcParams p = {};
     p.k = k;
@@ -863,4 +827,100 @@ extern "C" int lbx_chain_fused(const lbx_proj *projs, int32_t n_layers, int32_t 
     if (e != cudaSuccess) return cuda_status(e, "fused chain launch");
   }
   return LBX_OK;
+}
+
+// tokens of the first of the two sub-chains a call of k tokens runs as.  A
+// chain's cost grows faster than its token count (the sums exchange carries
+// every token, and from 3 tokens on one CTA fits per SM), so two concurrent
+// sub-chains win from 2 tokens on; measured per C2 layer: 2 tokens 14.7 us as
+// one chain, 10.4 as two; 4 tokens 31.2 and 16.0.
+static int fc_first(int k) { return k <= 1 ? k : (k + 1) / 2; }
+
+// the library's helper stream of this device (a call of more than FC_MAXK
+// tokens runs its second sub-chain there, forked from and joined back to the
+// caller's stream through two events)
+struct FcFork {
+  cudaStream_t s;
+  cudaEvent_t fork, join;
+};
+static int fc_fork(FcFork &f) {
+  static DevCache<FcFork> cache;
+  return cache.get(f, [](FcFork &o) {
+    cudaError_t e = cudaStreamCreateWithFlags(&o.s, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&o.fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&o.join, cudaEventDisableTiming);
+    return cuda_status(e, "fused chain helper stream");
+  });
+}
+
+}  // namespace lbx
+
+extern "C" size_t lbx_chain_fused_workspace_size(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens) {
+  using namespace lbx;
+  if (fc_validate(projs, n_layers) || n_tokens < 1 || n_tokens > 2 * FC_MAXK) return 0;
+  const int k1 = fc_first(n_tokens);
+  // a split call keeps both sub-chains' partial sums
+  return n_tokens == 1 ? fc_ws_bytes(projs, n_layers, 1) : 2 * fc_ws_bytes(projs, n_layers, k1);
+}
+
+extern "C" int lbx_chain_fused(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens, int32_t dtype,
+                               void *const *acts, const void *blob, size_t blob_bytes, void *ws, size_t ws_bytes,
+                               cudaStream_t stream) {
+  using namespace lbx;
+  int rc = fc_validate(projs, n_layers);
+  if (rc) return rc;
+  LBX_CHECK_SUP(n_tokens >= 1 && n_tokens <= 2 * FC_MAXK, "fused chain: 1..%d tokens", 2 * FC_MAXK);
+  LBX_CHECK_ARG(dtype == LBX_F32 || dtype == LBX_BF16, "bad dtype");
+  LBX_CHECK_ARG(acts && blob, "NULL argument");
+  for (int i = 0; i <= n_layers; ++i) LBX_CHECK_ARG(acts[i], "acts[%d] is NULL", i);
+  // every layer's plan once: blob offsets (as fc_blob_words lays them out)
+  // and the partial-sum buffers (as fc_ws_bytes sizes them)
+  const int k1 = fc_first(n_tokens), k2 = n_tokens - k1;
+  std::vector<FcPlan> plan(n_layers);
+  std::vector<size_t> uo(n_layers), vo(n_layers);
+  size_t words = 0, pmax = 0;
+  for (int i = 0; i < n_layers; ++i) {
+    rc = fc_plan(projs[i], plan[i]);
+    if (rc) return rc;
+    uo[i] = words;
+    words += (plan[i].ublob_words + 63) & ~(size_t)63;
+    vo[i] = words;
+    words += (plan[i].vblob_words + 63) & ~(size_t)63;
+    pmax = std::max(pmax, (size_t)(projs[i].in_features / FC_ROWS) * k1 * plan[i].pcols * 4);
+  }
+  LBX_CHECK_ARG(blob_bytes >= words * 4, "blob too small (%zu < %zu)", blob_bytes, words * 4);
+  const size_t one = 2 * al256(pmax);  // one sub-chain's partial sums
+  const size_t need = k2 ? 2 * one : one;
+  LBX_CHECK_ARG(ws && ws_bytes >= need, "workspace too small (%zu < %zu)", ws_bytes, need);
+  static DevCache<size_t> smax_cache;
+  size_t smax = 0;
+  rc = smax_cache.get(smax, [](size_t &out) {
+    const cudaError_t e = allow_max_smem(fc_kernel, &out);
+    return e != cudaSuccess ? cuda_status(e, "fused chain smem attribute") : (int)LBX_OK;
+  });
+  if (rc) return rc;
+  const uint32_t *b = reinterpret_cast<const uint32_t *>(blob);
+  uint8_t *w = reinterpret_cast<uint8_t *>(ws);
+  float *const part1[2] = {reinterpret_cast<float *>(w), reinterpret_cast<float *>(w + one / 2)};
+  if (!k2) return fc_run(projs, n_layers, k1, dtype, acts, b, plan, uo, vo, part1, smax, stream);
+  // 2..8 tokens: two sub-chains of k1 and k2 tokens (tokens never interact, so
+  // every token gets the bits of a chain of its own), the second on the helper
+  // stream so that both run at once
+  FcFork f;
+  rc = fc_fork(f);
+  if (rc) return rc;
+  const size_t esz = dtype == LBX_F32 ? 4 : 2;
+  std::vector<void *> acts2(n_layers + 1);
+  for (int i = 0; i <= n_layers; ++i) {
+    const size_t feat = i == 0 ? projs[0].in_features : projs[i - 1].out_features;
+    acts2[i] = reinterpret_cast<uint8_t *>(acts[i]) + (size_t)k1 * feat * esz;
+  }
+  float *const part2[2] = {reinterpret_cast<float *>(w + one), reinterpret_cast<float *>(w + one + one / 2)};
+  rc = cuda_status(cudaEventRecord(f.fork, stream), "fused chain fork");
+  if (!rc) rc = cuda_status(cudaStreamWaitEvent(f.s, f.fork, 0), "fused chain fork");
+  if (!rc) rc = fc_run(projs, n_layers, k2, dtype, acts2.data(), b, plan, uo, vo, part2, smax, f.s);
+  if (!rc) rc = fc_run(projs, n_layers, k1, dtype, acts, b, plan, uo, vo, part1, smax, stream);
+  if (!rc) rc = cuda_status(cudaEventRecord(f.join, f.s), "fused chain join");
+  if (!rc) rc = cuda_status(cudaStreamWaitEvent(stream, f.join, 0), "fused chain join");
+  return rc;
 }

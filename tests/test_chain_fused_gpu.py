@@ -33,10 +33,11 @@ def _layerwise(ops, layers, x):
     return outs
 
 
-@pytest.mark.parametrize("k", [1, 2, 4])
+@pytest.mark.parametrize("k", [1, 2, 4, 5, 8])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_fused_chain_c2_bitwise(k, dtype):
-    """C2 layers (4096 -> 4096, draft rank 208 + independent residual rank 1840)."""
+    """C2 layers (4096 -> 4096, draft rank 208 + independent residual rank 1840);
+    5 and 8 tokens run as two concurrent sub-chains."""
     from littlebit_b200 import ops
 
     layers, g = _chain([4096] * 5, [208, 1840], seed=10 + k)
@@ -74,6 +75,33 @@ def test_fused_chain_shared_factor_bias_and_widths_bitwise(k):
         assert torch.equal(acts[i].view(torch.int32), ref[i].view(torch.int32)), (k, i)
 
 
+def test_fused_chain_split_calls_in_a_graph():
+    """A 6-token call (two sub-chains on two streams) captured in a CUDA graph
+    and replayed gives the layer-by-layer bits every time."""
+    from littlebit_b200 import ops
+
+    layers, g = _chain([4096] * 4, [208, 1840], seed=80)
+    fc = ops.FusedChain(layers)
+    x = torch.randn(6, 4096, generator=g).to(DEV, torch.bfloat16)
+    ref = _layerwise(ops, layers, x)
+    acts = [x.clone()] + [torch.empty_like(r) for r in ref[1:]]
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        fc.run(acts, stream=stream)  # (workspace allocated outside the capture)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        fc.run(acts, stream=stream)
+    for _ in range(3):
+        for a in acts[1:]:
+            a.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert ops.device_error() == 0
+        for i in range(1, len(acts)):
+            assert torch.equal(acts[i].view(torch.int16), ref[i].view(torch.int16)), i
+
+
 def test_fused_chain_repeated_calls_and_single_layer():
     """Back-to-back calls reuse the partial-sum workspace; a one-layer chain is
     the head launch plus one layer launch."""
@@ -95,7 +123,7 @@ def test_fused_chain_rejects_unsupported():
 
     layers, _ = _chain([4096, 4096], [208], seed=70)
     fc = ops.FusedChain(layers)
-    x = torch.zeros(5, 4096, device=DEV)
+    x = torch.zeros(9, 4096, device=DEV)
     with pytest.raises(RuntimeError, match="tokens"):
         fc.run([x, torch.empty_like(x)])
     odd, _ = _chain([4096, 4112], [208], seed=71)   # out_features not a multiple of 256
