@@ -8,13 +8,23 @@
 // partials.  The grid is one thread-block cluster of FC_CS CTAs per 256 output
 // rows.
 //
+//  * Placement.  A launch must not put two of its CTAs on one SM: the CTAs of
+//    a cluster wait for one another, so the slowest one paces the layer.  At
+//    one CTA per SM a B200 holds 15 clusters of 8 but 22 of 6, so a 4096-row
+//    layer (16 clusters) takes clusters of 6.  The launches of a chain
+//    alternate between two builds of the kernel: FC_SMEM_SIDE (48 registers,
+//    shared memory padded past half an SM) and FC_REG_SIDE (72 registers, the
+//    shared memory it needs).  Two of either do not fit on one SM, one of each
+//    does (with the shared-memory carveout at its maximum), so the next
+//    launch's CTAs are placed under PDL beside the running ones, one per SM.
+//
 //  * V partials.  The V-stage quantises a = v2 ⊙ x with one scale per token
 //    per 256-column block and sums the blocks' exact integer products in block
 //    order (linear.cu, vstage_run).  Cluster c owns output rows [256c, 256c+256)
 //    of layer i, which are exactly block c of layer i+1's input, so it can form
 //    block c's product for every rank of layer i+1 as soon as its rows exist:
 //    P[c][t][r] = float(Σ_{j in block c} s_rj q_j) · (absmax / QMAX).  The CTAs
-//    of the cluster split the ranks (whole 128-rank groups).
+//    of the cluster split the ranks (16-rank tiles).
 //  * z.  Launch i+1 adds the blocks' partials of its ranks in the V-stage's
 //    order (for each of the 16 block positions of a 4096-column pass, the passes
 //    in order, then the positions in order) and multiplies by mid: the V-stage's
@@ -28,8 +38,9 @@
 //    exponent with the U-stage's integer shift and forms y for all 256 rows with
 //    the U-stage's epilogue expression (u_result).  Exact integers add the same
 //    in any order, so y has the bits of the two stage grids.
-//  * Each CTA stores its 32 rows of y and quantises the cluster's 256 values
-//    (one block of layer i+1's input) for the next partials.
+//  * Each CTA stores its share of the 256 rows of y and quantises the
+//    cluster's 256 values (one block of layer i+1's input) for the next
+//    partials.
 //
 // Per layer this is one grid boundary and one cluster barrier, against two grid
 // boundaries for the stage grids.  Weights are copied into shared memory from a
@@ -40,9 +51,9 @@
 
 namespace lbx {
 
-constexpr int FC_CS = 8;          // CTAs per cluster
+constexpr int FC_CS = 6;          // CTAs per cluster
 constexpr int FC_ROWS = 256;      // output rows per cluster (= one 256-column V block of the next layer)
-constexpr int FC_GMAX = 4;        // 128-rank groups per CTA, U side and V side
+constexpr int FC_GMAX = 5;        // 128-rank groups per CTA (FC_GTOT <= 32: one warp reduces over them)
 constexpr int FC_GTOT = FC_CS * FC_GMAX;
 constexpr int FC_MAXK = 4;        // tokens per launch (one MMA column block)
 constexpr int FC_NBLK = 32;       // 256-column input blocks of a layer (in_features <= 8192)
@@ -51,7 +62,10 @@ constexpr int FC_VPITCH = 8;      // words per V row in the blob (rows 4-7 and 1
                                   // two 4-word halves swapped: conflict-free fragment loads, no padding)
 constexpr int FC_UGW = FC_ROWS * 4;     // words of one U group slot (256 rows x 4 words)
 constexpr int FC_VTW = 16 * FC_VPITCH;  // words of one V tile (16 ranks x 8 words)
-constexpr int FC_VTC = 32;              // V tiles per CTA at most (two per warp)
+constexpr int FC_VTC = 40;              // V tiles per CTA at most
+constexpr int FC_SMEM_SIDE = 48;        // register caps of the two builds of the kernel
+constexpr int FC_REG_SIDE = 72;
+constexpr int FC_SMEM_PAD = 118 * 1024;  // shared memory of an FC_SMEM_SIDE CTA at least (> half an SM)
 
 struct FcGroup {  // one 128-rank quantisation group of a branch (U side)
   int b;          // branch
@@ -197,7 +211,8 @@ LBX_DEV bool mbar_poll_cta(uint64_t *bar, uint32_t parity, int code) {
 LBX_DEV void fc_vpart(const FcParams &p, int c, int k, int ws, int vs, int ve, const uint32_t *vw,
                       const uint32_t *actv, const int *vmax, const int *vsq, int lane);
 
-__global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant__ FcParams p) {
+template <int MAXR>
+__global__ void __launch_bounds__(FC_THREADS, 1) __maxnreg__(MAXR) fc_kernel(const __grid_constant__ FcParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar;
   __shared__ __align__(8) uint64_t xbar[2];  // exponents, then the CTAs' rounded sums (filled by st.async)
@@ -420,7 +435,7 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
     }
     {
       // all four lanes of a row pair store: lane q sends every token's sums
-      // (fetched from lane (g, t)) to the CTAs d = q, q + 4
+      // (fetched from lane (g, t)) to the CTAs d = q, q + 4 of the cluster
       int A[FC_MAXK][4];
 #pragma unroll
       for (int t = 0; t < FC_MAXK; ++t) {
@@ -437,8 +452,9 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
       // [source CTA][row pair][token][4]
       const int rp = warp * 8 + g;
 #pragma unroll
-      for (int dd = 0; dd < FC_CS / 4; ++dd) {
+      for (int dd = 0; dd < (FC_CS + 3) / 4; ++dd) {
         const int d = q + 4 * dd;
+        if (d >= FC_CS) break;
         const uint32_t bar = cl_addr(&xbar[1], d);
 #pragma unroll
         for (int t = 0; t < FC_MAXK; ++t)
@@ -472,10 +488,10 @@ __global__ void __launch_bounds__(FC_THREADS, 2) fc_kernel(const __grid_constant
       float xv = v;  // the next layer's input value: as stored
       const size_t off = (size_t)t * p.N + (size_t)c * FC_ROWS + r;
       if (p.adt == LBX_F32) {
-        if ((r >> 5) == j) reinterpret_cast<float *>(p.y)[off] = v;
+        if (r * FC_CS / FC_ROWS == j) reinterpret_cast<float *>(p.y)[off] = v;
       } else {
         const uint16_t hb = f32_to_bf16(v);
-        if ((r >> 5) == j) reinterpret_cast<uint16_t *>(p.y)[off] = hb;
+        if (r * FC_CS / FC_ROWS == j) reinterpret_cast<uint16_t *>(p.y)[off] = hb;
         xv = bf16_to_f32(hb);
       }
       if (p.has_v)
@@ -752,10 +768,13 @@ extern "C" int lbx_chain_prepare(const lbx_proj *projs, int32_t n_layers, void *
 namespace lbx {
 
 // the launches of one chain for tokens [0, k) of acts (already offset to the
-// sub-batch's first token), partial sums in part[0] / part[1]
+// sub-batch's first token), partial sums in part[0] / part[1].  `alt`: the
+// launches alternate between the FC_SMEM_SIDE and FC_REG_SIDE builds (one CTA
+// of a launch per SM); otherwise every launch is the 64-register build, two
+// CTAs per SM (for two chains that run at once).
 static int fc_run(const lbx_proj *projs, int n_layers, int k, int dtype, void *const *acts, const uint32_t *b,
                   const std::vector<FcPlan> &plan, const std::vector<size_t> &uo, const std::vector<size_t> &vo,
-                  float *const (&part)[2], size_t smax, cudaStream_t stream) {
+                  float *const (&part)[2], size_t smax, bool alt, cudaStream_t stream) {
   for (int i = -1; i < n_layers; ++i) {
     FcParams p = {};
     p.k = k;
@@ -813,7 +832,8 @@ static int fc_run(const lbx_proj *projs, int n_layers, int k, int dtype, void *c
     cudaLaunchAttribute attr[2];
     cfg.gridDim = dim3(nclusters * FC_CS);
     cfg.blockDim = dim3(FC_THREADS);
-    cfg.dynamicSmemBytes = Ls.total;
+    const bool sside = alt && ((i + 1) & 1) == 0;
+    cfg.dynamicSmemBytes = sside ? std::max(Ls.total, FC_SMEM_PAD) : Ls.total;
     cfg.stream = stream;
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = FC_CS;
@@ -823,7 +843,9 @@ static int fc_run(const lbx_proj *projs, int n_layers, int k, int dtype, void *c
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, fc_kernel, p);
+    const cudaError_t e = !alt   ? cudaLaunchKernelEx(&cfg, fc_kernel<64>, p)
+                          : sside ? cudaLaunchKernelEx(&cfg, fc_kernel<FC_SMEM_SIDE>, p)
+                                  : cudaLaunchKernelEx(&cfg, fc_kernel<FC_REG_SIDE>, p);
     if (e != cudaSuccess) return cuda_status(e, "fused chain launch");
   }
   return LBX_OK;
@@ -833,7 +855,7 @@ static int fc_run(const lbx_proj *projs, int n_layers, int k, int dtype, void *c
 // chain's cost grows faster than its token count (the sums exchange carries
 // every token, and from 3 tokens on one CTA fits per SM), so two concurrent
 // sub-chains win from 2 tokens on; measured per C2 layer: 2 tokens 14.7 us as
-// one chain, 10.4 as two; 4 tokens 31.2 and 16.0.
+// one chain, 9.7 as two; 4 tokens 31.2 and 14.3.
 static int fc_first(int k) { return k <= 1 ? k : (k + 1) / 2; }
 
 // the library's helper stream of this device (a call of more than FC_MAXK
@@ -895,14 +917,20 @@ extern "C" int lbx_chain_fused(const lbx_proj *projs, int32_t n_layers, int32_t 
   static DevCache<size_t> smax_cache;
   size_t smax = 0;
   rc = smax_cache.get(smax, [](size_t &out) {
-    const cudaError_t e = allow_max_smem(fc_kernel, &out);
+    // every build may take the SM's shared memory, and prefers the largest
+    // carveout, so that an FC_SMEM_SIDE CTA leaves room for an FC_REG_SIDE one
+    cudaError_t e = cudaSuccess;
+    for (auto fn : {fc_kernel<64>, fc_kernel<FC_SMEM_SIDE>, fc_kernel<FC_REG_SIDE>}) {
+      if (e == cudaSuccess) e = allow_max_smem(fn, &out);
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    }
     return e != cudaSuccess ? cuda_status(e, "fused chain smem attribute") : (int)LBX_OK;
   });
   if (rc) return rc;
   const uint32_t *b = reinterpret_cast<const uint32_t *>(blob);
   uint8_t *w = reinterpret_cast<uint8_t *>(ws);
   float *const part1[2] = {reinterpret_cast<float *>(w), reinterpret_cast<float *>(w + one / 2)};
-  if (!k2) return fc_run(projs, n_layers, k1, dtype, acts, b, plan, uo, vo, part1, smax, stream);
+  if (!k2) return fc_run(projs, n_layers, k1, dtype, acts, b, plan, uo, vo, part1, smax, true, stream);
   // 2..8 tokens: two sub-chains of k1 and k2 tokens (tokens never interact, so
   // every token gets the bits of a chain of its own), the second on the helper
   // stream so that both run at once
@@ -918,8 +946,10 @@ extern "C" int lbx_chain_fused(const lbx_proj *projs, int32_t n_layers, int32_t 
   float *const part2[2] = {reinterpret_cast<float *>(w + one), reinterpret_cast<float *>(w + one + one / 2)};
   rc = cuda_status(cudaEventRecord(f.fork, stream), "fused chain fork");
   if (!rc) rc = cuda_status(cudaStreamWaitEvent(f.s, f.fork, 0), "fused chain fork");
-  if (!rc) rc = fc_run(projs, n_layers, k2, dtype, acts2.data(), b, plan, uo, vo, part2, smax, f.s);
-  if (!rc) rc = fc_run(projs, n_layers, k1, dtype, acts, b, plan, uo, vo, part1, smax, stream);
+  // (two alternating chains would contend for the same builds' SM slots;
+  // measured per C2 layer at 2 tokens: 9.7 us plain, 10.7 alternating)
+  if (!rc) rc = fc_run(projs, n_layers, k2, dtype, acts2.data(), b, plan, uo, vo, part2, smax, false, f.s);
+  if (!rc) rc = fc_run(projs, n_layers, k1, dtype, acts, b, plan, uo, vo, part1, smax, false, stream);
   if (!rc) rc = cuda_status(cudaEventRecord(f.join, f.s), "fused chain join");
   if (!rc) rc = cuda_status(cudaStreamWaitEvent(stream, f.join, 0), "fused chain join");
   return rc;
