@@ -104,7 +104,7 @@ struct FcParams {
 // shared-memory layout of one CTA (bytes; weights first, then scratch)
 struct FcSmem {
   int uw, vw, mid, u1, bias, v2, wbytes;      // weight region
-  int actu, xs, ex, sa, actv, total;          // scratch
+  int actu, xs, stg, ex, sa, actv, total;     // scratch
 };
 
 __host__ __device__ inline FcSmem fc_smem(int k, int ng) {
@@ -120,6 +120,7 @@ __host__ __device__ inline FcSmem fc_smem(int k, int ng) {
   L.wbytes = o;
   L.actu = o; o += FC_GMAX * 4 * ws * 4;
   L.xs = o;   o += (ng ? FC_CS : 0) * FC_ROWS * k * 8;
+  L.stg = o;  o += (ng && k > 1 ? 1 : 0) * FC_ROWS * k * 8;  // the bulk build's staging buffer
   L.ex = o;   o += ((ng * k * 4 + 15) / 16) * 16;
   L.sa = o;   o += 2 * k * FC_ROWS * 4;
   L.actv = o; o += 2 * 8 * ws * 4;
@@ -156,6 +157,14 @@ LBX_DEV void st_async_v4(uint32_t addr, int a, int b, int c, int d, uint32_t bar
       "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
       "r"(a), "r"(b), "r"(c), "r"(d), "r"(bar)
       : "memory");
+}
+// bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from
+// this CTA's shared memory into a cluster CTA's, counted on that CTA's mbarrier
+LBX_DEV void bulk_s2cl(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst),
+               "r"(smem_u32(src)), "r"(bytes), "r"(bar)
+               : "memory");
 }
 // bounded wait on a phase of an mbarrier that other CTAs of the cluster
 // complete (acquire at cluster scope), polled with test_wait: the data is
@@ -211,7 +220,12 @@ LBX_DEV bool mbar_poll_cta(uint64_t *bar, uint32_t parity, int code) {
 LBX_DEV void fc_vpart(const FcParams &p, int c, int k, int ws, int vs, int ve, const uint32_t *vw,
                       const uint32_t *actv, const int *vmax, const int *vsq, int lane);
 
-template <int MAXR>
+// MAXR: the register cap of the build.  BULK: the sums exchange goes by bulk
+// copies (the build for 2-4 tokens) rather than 16-byte st.async stores (the
+// one-token builds).  They are separate builds so that the one-token kernels
+// keep their own code: with the bulk path compiled in beside it, a one-token
+// chain measured 8.1 us per C2 layer against 7.5.
+template <int MAXR, bool BULK>
 __global__ void __launch_bounds__(FC_THREADS, 1) __maxnreg__(MAXR) fc_kernel(const __grid_constant__ FcParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar;
@@ -238,7 +252,8 @@ __global__ void __launch_bounds__(FC_THREADS, 1) __maxnreg__(MAXR) fc_kernel(con
   float *sbias = reinterpret_cast<float *>(smem + L.bias);
   float *sv2 = reinterpret_cast<float *>(smem + L.v2);
   uint32_t *actu = reinterpret_cast<uint32_t *>(smem + L.actu);  // [slot][4 words][ws]
-  int *xs = reinterpret_cast<int *>(smem + L.xs);            // [cta][row][t][branch] rounded sums
+  int *xs = reinterpret_cast<int *>(smem + L.xs);            // [cta][row pair][t][4] rounded sums
+  int *stg = reinterpret_cast<int *>(smem + L.stg);          // (bulk build) this CTA's sums, [row pair][t][4]
   int *ex = reinterpret_cast<int *>(smem + L.ex);            // [group][t] exponents
   float *sa = reinterpret_cast<float *>(smem + L.sa);        // [seg][t][256] a = v2 * x of the block
   uint32_t *actv = reinterpret_cast<uint32_t *>(smem + L.actv);  // [segment][8 words][ws]
@@ -433,7 +448,7 @@ __global__ void __launch_bounds__(FC_THREADS, 1) __maxnreg__(MAXR) fc_kernel(con
         }
       }
     }
-    {
+    if constexpr (!BULK) {
       // all four lanes of a row pair store: lane q sends every token's sums
       // (fetched from lane (g, t)) to the CTAs d = q, q + 4 of the cluster
       int A[FC_MAXK][4];
@@ -462,15 +477,33 @@ __global__ void __launch_bounds__(FC_THREADS, 1) __maxnreg__(MAXR) fc_kernel(con
             st_async_v4(cl_addr(xs + ((j * (FC_ROWS / 2) + rp) * k + t) * 4, d), A[t][0], A[t][1], A[t][2],
                         A[t][3], bar);
       }
+      LBX_PROBE(24);
+      // cluster barrier C (waited at the exit): no CTA leaves before every
+      // CTA of the cluster has issued its stores into the others' shared
+      // memory.  Relaxed: the stores a CTA receives are all counted on its
+      // own barriers, which it waits for before it reaches the exit.
+      cl_arrive_relaxed();
+    } else {
+      // the sums go into this CTA's staging buffer [row pair][token][4]
+      // (lane (g, q) holds token q), then one bulk copy of the buffer into
+      // every CTA of the cluster (xs [source CTA][row pair][token][4], counted
+      // on the receiver's xbar[1]): six large copies instead of a 16-byte
+      // store per (row pair, token, destination)
+      if (q < k)
+        *reinterpret_cast<int4 *>(stg + ((warp * 8 + g) * k + q) * 4) = make_int4(I[0][0], I[0][1], I[1][0], I[1][1]);
+      fence_proxy_async();  // the staging writes, before the copies read them
+      __syncthreads();
+      if (tid < FC_CS)
+        bulk_s2cl(cl_addr(xs + j * (FC_ROWS / 2) * k * 4, tid), stg, (uint32_t)FC_ROWS * k * 8u,
+                  cl_addr(&xbar[1], tid));
+      LBX_PROBE(24);
     }
-    LBX_PROBE(24);
-    // cluster barrier C (waited at the exit): no CTA leaves before every CTA
-    // of the cluster has issued its stores into the others' shared memory.
-    // Relaxed: the stores a CTA receives are all counted on its own barriers,
-    // which it waits for before it reaches the exit.
-    cl_arrive_relaxed();
     // ---- every CTA's sums, then y for all 256 rows
     okx = __syncthreads_and(mbar_wait_cluster(&xbar[1], 0, 0x133) && okx);
+    // (bulk build) cluster barrier C, waited at the exit: every copy into this
+    // CTA has landed, so a CTA that passes C has had its staging buffer read
+    // and no copy still targets it
+    if constexpr (BULK) cl_arrive_relaxed();
     LBX_PROBE(28);
     for (int it = tid; it < FC_ROWS * k; it += FC_THREADS) {
       const int t = it / FC_ROWS, r = it - t * FC_ROWS;
@@ -768,13 +801,14 @@ extern "C" int lbx_chain_prepare(const lbx_proj *projs, int32_t n_layers, void *
 namespace lbx {
 
 // the launches of one chain for tokens [0, k) of acts (already offset to the
-// sub-batch's first token), partial sums in part[0] / part[1].  `alt`: the
-// launches alternate between the FC_SMEM_SIDE and FC_REG_SIDE builds (one CTA
-// of a launch per SM); otherwise every launch is the 64-register build, two
-// CTAs per SM (for two chains that run at once).
+// sub-batch's first token), partial sums in part[0] / part[1].  `alt` (one
+// token): the launches alternate between the FC_SMEM_SIDE and FC_REG_SIDE
+// builds (one CTA of a launch per SM); otherwise every launch is a 64-register
+// build, two CTAs per SM (for two chains that run at once).
 static int fc_run(const lbx_proj *projs, int n_layers, int k, int dtype, void *const *acts, const uint32_t *b,
                   const std::vector<FcPlan> &plan, const std::vector<size_t> &uo, const std::vector<size_t> &vo,
                   float *const (&part)[2], size_t smax, bool alt, cudaStream_t stream) {
+  alt = alt && k == 1;  // the alternating builds are one-token builds
   for (int i = -1; i < n_layers; ++i) {
     FcParams p = {};
     p.k = k;
@@ -843,9 +877,11 @@ static int fc_run(const lbx_proj *projs, int n_layers, int k, int dtype, void *c
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    const cudaError_t e = !alt   ? cudaLaunchKernelEx(&cfg, fc_kernel<64>, p)
-                          : sside ? cudaLaunchKernelEx(&cfg, fc_kernel<FC_SMEM_SIDE>, p)
-                                  : cudaLaunchKernelEx(&cfg, fc_kernel<FC_REG_SIDE>, p);
+    // (fc_smem has the staging buffer exactly when k > 1: the bulk build)
+    void (*fn)(FcParams) = alt     ? (sside ? fc_kernel<FC_SMEM_SIDE, false> : fc_kernel<FC_REG_SIDE, false>)
+                           : k > 1 ? fc_kernel<64, true>
+                                   : fc_kernel<64, false>;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, p);
     if (e != cudaSuccess) return cuda_status(e, "fused chain launch");
   }
   return LBX_OK;
@@ -855,7 +891,7 @@ static int fc_run(const lbx_proj *projs, int n_layers, int k, int dtype, void *c
 // chain's cost grows faster than its token count (the sums exchange carries
 // every token, and from 3 tokens on one CTA fits per SM), so two concurrent
 // sub-chains win from 2 tokens on; measured per C2 layer: 2 tokens 14.7 us as
-// one chain, 9.7 as two; 4 tokens 31.2 and 14.3.
+// one chain, 9.7 as two; 4 tokens 31.2 and 12.8.
 static int fc_first(int k) { return k <= 1 ? k : (k + 1) / 2; }
 
 // the library's helper stream of this device (a call of more than FC_MAXK
@@ -920,7 +956,8 @@ extern "C" int lbx_chain_fused(const lbx_proj *projs, int32_t n_layers, int32_t 
     // every build may take the SM's shared memory, and prefers the largest
     // carveout, so that an FC_SMEM_SIDE CTA leaves room for an FC_REG_SIDE one
     cudaError_t e = cudaSuccess;
-    for (auto fn : {fc_kernel<64>, fc_kernel<FC_SMEM_SIDE>, fc_kernel<FC_REG_SIDE>}) {
+    for (auto fn : {fc_kernel<64, false>, fc_kernel<64, true>, fc_kernel<FC_SMEM_SIDE, false>,
+                    fc_kernel<FC_REG_SIDE, false>}) {
       if (e == cudaSuccess) e = allow_max_smem(fn, &out);
       if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     }
