@@ -19,10 +19,13 @@ value   = algorithmic bytes of all layers of all ranks / max-over-ranks time
           (packed bits without word padding + fp32 scales + activations in/out)
 e2e     = the same metric through the C-ABI call itself: every step copies
           x from pinned host memory to the device, the host calls
-          lbx_linear_verify (ctypes) once per layer of the chain, and the
-          last layer's y is copied back to pinned host memory (8 KB each
-          way per step at k=1); no CUDA graph.  e2e_graph is the default
-          executor's step with the same copies, captured in a CUDA graph.
+          lbx_chain_fused (ctypes) once for the chain, and the last layer's y
+          is copied back to pinned host memory (8 KB each way per step at
+          k=1).  The bench captures nothing; the library replays its own
+          cached graph of a call it has seen (built during warm-up).
+          e2e_per_layer_calls makes one lbx_linear_verify call per layer
+          instead; e2e_graph is the default executor's step with the same
+          copies, captured by the bench in a CUDA graph.
 configs = the other BASELINE layer configs, each as its own chain: C1 (fp32,
           r=208), C2 verify at k=5 and k=8, the shared-factor target layer of
           config 4 (draft r=208 + residual U_R of the same rank on the draft's
@@ -1131,7 +1134,7 @@ def run_ours(args):
                      "doing no arithmetic (lbx_linear_floor): launches only, and with each unit's weight "
                      "bulk copies and their wait")
 
-    # ---- e2e through the C ABI with host buffers, no CUDA graph: every step
+    # ---- e2e through the C ABI with host buffers, no graph captured here: every step
     # copies x from pinned host memory, makes the library call(s) of the
     # chain from the host (ctypes), and copies the last y back to pinned host
     # memory.  Two forms: the chain entry point (lbx_chain_fused, one call
@@ -1168,7 +1171,8 @@ def run_ours(args):
     if fchain is not None:
         t2, t_wall = e2e_time(step_fused)
         e2e_path = (f"pinned host x -> device; the host calls lbx_chain_fused (C ABI, ctypes) once for the "
-                    f"{P}-layer chain, no CUDA graph; last y -> pinned host; every step")
+                    f"{P}-layer chain (the library replays its cached graph of the call, built on the first "
+                    f"call during warm-up); last y -> pinned host; every step")
     else:
         t2, t_wall = e2e_time(lambda: ch.run(L.LBX_EXEC_KERNELS, stream, args.pdl))
         e2e_path = (f"pinned host x -> device; the host calls lbx_linear_verify (C ABI, ctypes) for each of "

@@ -267,11 +267,11 @@ int lbx_linear_chain(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens, 
  * of single-projection layers, acts[i+1] = layer_i(acts[i]) as in
  * lbx_linear_chain, as n_layers + 1 launches instead of two per layer.  Launch
  * i runs layer i's U-stage and, from the outputs it has just formed, layer
- * i+1's V-stage partial sums (one thread-block cluster of 8 CTAs per 256
+ * i+1's V-stage partial sums (one thread-block cluster of 6 CTAs per 256
  * output rows; the first launch forms layer 0's partials from acts[0]).
  * Every output is bit-identical to calling lbx_linear layer by layer.
  * Requirements: in/out features multiples of 256 (in <= 8192), no prologue,
- * store epilogue, 1-2 branches of at most 32 quantisation groups (128 ranks)
+ * store epilogue, 1-2 branches of at most 30 quantisation groups (128 ranks)
  * together, 1..8 tokens, one activation dtype (LBX_F32 / LBX_BF16).  A call
  * of 2..8 tokens runs as two chains of ceil(k/2) and floor(k/2) tokens at
  * once, the second on a helper stream the library keeps per device, forked
@@ -282,7 +282,15 @@ int lbx_linear_chain(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens, 
  * so that each CTA's share of a layer is contiguous (blob of
  * lbx_chain_prepare_size bytes, 16-byte aligned); the layers' scale vectors
  * are read from the descriptors.  The workspace (any contents) holds the
- * partial sums between launches; calls sharing it must be ordered. */
+ * partial sums between launches; calls sharing it must be ordered.
+ * Outside stream capture the library keeps, per device, instantiated CUDA
+ * graphs of the last 16 distinct calls (keyed by the layer descriptors'
+ * fields, the buffer pointers and sizes, the token count and the dtype).  A
+ * call equal to one of them replays its graph, one host launch instead of
+ * n_layers + 1; the first such call captures the launches on a private stream
+ * (the caller's stream never enters capture mode).  Graphs read the buffers
+ * through their pointers, so new contents need no new graph.  Inside the
+ * caller's stream capture the call makes its launches directly. */
 size_t lbx_chain_prepare_size(const lbx_proj *projs, int32_t n_layers);
 int lbx_chain_prepare(const lbx_proj *projs, int32_t n_layers, void *blob, size_t blob_bytes,
                       cudaStream_t stream);

@@ -911,6 +911,67 @@ static int fc_fork(FcFork &f) {
   });
 }
 
+// Instantiated CUDA graphs of recent calls, per device.  A call outside
+// stream capture with the same arguments as a cached one (the same layers,
+// buffers, token count and dtype) replays the graph: one host launch instead
+// of n_layers + 1 cluster launches, which cost the host more than the ~7 us a
+// C2 layer takes on the device.  A miss captures the launches on a private
+// stream (the caller's stream never enters capture mode), instantiates them
+// and launches the graph on the caller's stream.  A graph reads its buffers
+// through the pointers it was built with, so new contents in the same buffers
+// need no new graph.
+constexpr int FC_GRAPHS = 16;
+struct FcGraph {
+  std::vector<uintptr_t> key;
+  cudaGraphExec_t exec = nullptr;
+  uint64_t used = 0;
+};
+struct FcGraphs {
+  cudaStream_t cap = nullptr;  // the private capture stream
+  std::vector<FcGraph> g;
+  uint64_t tick = 0;
+};
+static std::mutex &fc_graph_mu() {
+  static std::mutex m;
+  return m;
+}
+static FcGraphs g_fc_graphs[LBX_MAX_DEVICES];
+
+// every argument that the launches depend on, field by field (not the
+// descriptors' raw bytes, whose padding a caller need not keep equal)
+static std::vector<uintptr_t> fc_key(const lbx_proj *projs, int n_layers, int n_tokens, int dtype,
+                                     void *const *acts, const void *blob, size_t blob_bytes, void *ws,
+                                     size_t ws_bytes) {
+  std::vector<uintptr_t> k;
+  k.reserve(8 + 16 * (size_t)n_layers);
+  auto u = [&](const void *v) { k.push_back(reinterpret_cast<uintptr_t>(v)); };
+  k.push_back((uintptr_t)n_layers);
+  k.push_back((uintptr_t)n_tokens);
+  k.push_back((uintptr_t)dtype);
+  u(blob);
+  k.push_back((uintptr_t)blob_bytes);
+  u(ws);
+  k.push_back((uintptr_t)ws_bytes);
+  for (int i = 0; i <= n_layers; ++i) u(acts[i]);
+  for (int i = 0; i < n_layers; ++i) {
+    const lbx_proj &pr = projs[i];
+    k.push_back((uintptr_t)(uint32_t)pr.in_features);
+    k.push_back((uintptr_t)(uint32_t)pr.out_features);
+    k.push_back((uintptr_t)(uint32_t)pr.n_branches);
+    u(pr.bias);
+    for (int bb = 0; bb < 2 && bb < pr.n_branches; ++bb) {  // (not yet validated)
+      const lbx_branch &br = pr.br[bb];
+      u(br.v_sign);
+      u(br.v2);
+      u(br.mid);
+      u(br.u_sign);
+      u(br.u1);
+      k.push_back((uintptr_t)(uint32_t)br.rank);
+    }
+  }
+  return k;
+}
+
 }  // namespace lbx
 
 extern "C" size_t lbx_chain_fused_workspace_size(const lbx_proj *projs, int32_t n_layers, int32_t n_tokens) {
@@ -925,12 +986,32 @@ extern "C" int lbx_chain_fused(const lbx_proj *projs, int32_t n_layers, int32_t 
                                void *const *acts, const void *blob, size_t blob_bytes, void *ws, size_t ws_bytes,
                                cudaStream_t stream) {
   using namespace lbx;
-  int rc = fc_validate(projs, n_layers);
-  if (rc) return rc;
+  LBX_CHECK_ARG(projs && n_layers >= 1, "need at least one layer");
   LBX_CHECK_SUP(n_tokens >= 1 && n_tokens <= 2 * FC_MAXK, "fused chain: 1..%d tokens", 2 * FC_MAXK);
   LBX_CHECK_ARG(dtype == LBX_F32 || dtype == LBX_BF16, "bad dtype");
   LBX_CHECK_ARG(acts && blob, "NULL argument");
   for (int i = 0; i <= n_layers; ++i) LBX_CHECK_ARG(acts[i], "acts[%d] is NULL", i);
+  // outside the caller's stream capture, a call whose arguments equal a cached
+  // graph's replays it (the arguments were checked and planned when it was
+  // built); inside it, the call makes its launches itself
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  int rc = cuda_status(cudaStreamIsCapturing(stream, &cs), "fused chain capture query");
+  if (rc) return rc;
+  const int dev = cur_device();
+  const bool use_graph = cs == cudaStreamCaptureStatusNone && dev >= 0 && dev < LBX_MAX_DEVICES;
+  std::vector<uintptr_t> key;
+  if (use_graph) {
+    key = fc_key(projs, n_layers, n_tokens, dtype, acts, blob, blob_bytes, ws, ws_bytes);
+    std::lock_guard<std::mutex> lk(fc_graph_mu());  // (held through the launch: no eviction meanwhile)
+    FcGraphs &G = g_fc_graphs[dev];
+    for (FcGraph &e : G.g)
+      if (e.key == key) {
+        e.used = ++G.tick;
+        return cuda_status(cudaGraphLaunch(e.exec, stream), "fused chain graph launch");
+      }
+  }
+  rc = fc_validate(projs, n_layers);
+  if (rc) return rc;
   // every layer's plan once: blob offsets (as fc_blob_words lays them out)
   // and the partial-sum buffers (as fc_ws_bytes sizes them)
   const int k1 = fc_first(n_tokens), k2 = n_tokens - k1;
@@ -967,13 +1048,14 @@ extern "C" int lbx_chain_fused(const lbx_proj *projs, int32_t n_layers, int32_t 
   const uint32_t *b = reinterpret_cast<const uint32_t *>(blob);
   uint8_t *w = reinterpret_cast<uint8_t *>(ws);
   float *const part1[2] = {reinterpret_cast<float *>(w), reinterpret_cast<float *>(w + one / 2)};
-  if (!k2) return fc_run(projs, n_layers, k1, dtype, acts, b, plan, uo, vo, part1, smax, true, stream);
   // 2..8 tokens: two sub-chains of k1 and k2 tokens (tokens never interact, so
   // every token gets the bits of a chain of its own), the second on the helper
   // stream so that both run at once
-  FcFork f;
-  rc = fc_fork(f);
-  if (rc) return rc;
+  FcFork f = {};
+  if (k2) {
+    rc = fc_fork(f);
+    if (rc) return rc;
+  }
   const size_t esz = dtype == LBX_F32 ? 4 : 2;
   std::vector<void *> acts2(n_layers + 1);
   for (int i = 0; i <= n_layers; ++i) {
@@ -981,13 +1063,51 @@ extern "C" int lbx_chain_fused(const lbx_proj *projs, int32_t n_layers, int32_t 
     acts2[i] = reinterpret_cast<uint8_t *>(acts[i]) + (size_t)k1 * feat * esz;
   }
   float *const part2[2] = {reinterpret_cast<float *>(w + one), reinterpret_cast<float *>(w + one + one / 2)};
-  rc = cuda_status(cudaEventRecord(f.fork, stream), "fused chain fork");
-  if (!rc) rc = cuda_status(cudaStreamWaitEvent(f.s, f.fork, 0), "fused chain fork");
-  // (two alternating chains would contend for the same builds' SM slots;
-  // measured per C2 layer at 2 tokens: 9.7 us plain, 10.7 alternating)
-  if (!rc) rc = fc_run(projs, n_layers, k2, dtype, acts2.data(), b, plan, uo, vo, part2, smax, false, f.s);
-  if (!rc) rc = fc_run(projs, n_layers, k1, dtype, acts, b, plan, uo, vo, part1, smax, false, stream);
-  if (!rc) rc = cuda_status(cudaEventRecord(f.join, f.s), "fused chain join");
-  if (!rc) rc = cuda_status(cudaStreamWaitEvent(stream, f.join, 0), "fused chain join");
-  return rc;
+  auto launch_all = [&](cudaStream_t st) -> int {
+    if (!k2) return fc_run(projs, n_layers, k1, dtype, acts, b, plan, uo, vo, part1, smax, true, st);
+    int r = cuda_status(cudaEventRecord(f.fork, st), "fused chain fork");
+    if (!r) r = cuda_status(cudaStreamWaitEvent(f.s, f.fork, 0), "fused chain fork");
+    // (two alternating chains would contend for the same builds' SM slots;
+    // measured per C2 layer at 2 tokens: 9.7 us plain, 10.7 alternating)
+    if (!r) r = fc_run(projs, n_layers, k2, dtype, acts2.data(), b, plan, uo, vo, part2, smax, false, f.s);
+    if (!r) r = fc_run(projs, n_layers, k1, dtype, acts, b, plan, uo, vo, part1, smax, false, st);
+    if (!r) r = cuda_status(cudaEventRecord(f.join, f.s), "fused chain join");
+    if (!r) r = cuda_status(cudaStreamWaitEvent(st, f.join, 0), "fused chain join");
+    return r;
+  };
+  if (!use_graph) return launch_all(stream);
+  // this call's graph: captured now, unless another thread has just added it
+  std::lock_guard<std::mutex> lk(fc_graph_mu());
+  FcGraphs &G = g_fc_graphs[dev];
+  cudaGraphExec_t exec = nullptr;
+  for (FcGraph &e : G.g)
+    if (e.key == key) {
+      e.used = ++G.tick;
+      exec = e.exec;
+      break;
+    }
+  if (!exec) {
+    if (!G.cap) {
+      rc = cuda_status(cudaStreamCreateWithFlags(&G.cap, cudaStreamNonBlocking), "fused chain capture stream");
+      if (rc) return rc;
+    }
+    rc = cuda_status(cudaStreamBeginCapture(G.cap, cudaStreamCaptureModeThreadLocal), "fused chain capture");
+    if (rc) return rc;
+    rc = launch_all(G.cap);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t ee = cudaStreamEndCapture(G.cap, &graph);  // (always: the stream leaves capture)
+    if (!rc && ee != cudaSuccess) rc = cuda_status(ee, "fused chain capture");
+    if (!rc) rc = cuda_status(cudaGraphInstantiate(&exec, graph, 0), "fused chain graph");
+    if (graph) cudaGraphDestroy(graph);
+    if (rc) return rc;
+    if ((int)G.g.size() >= FC_GRAPHS) {  // drop the least recently used graph
+      size_t lru = 0;
+      for (size_t i = 1; i < G.g.size(); ++i)
+        if (G.g[i].used < G.g[lru].used) lru = i;
+      cudaGraphExecDestroy(G.g[lru].exec);  // (freed once any launch in flight completes)
+      G.g.erase(G.g.begin() + (long)lru);
+    }
+    G.g.push_back(FcGraph{std::move(key), exec, ++G.tick});
+  }
+  return cuda_status(cudaGraphLaunch(exec, stream), "fused chain graph launch");
 }

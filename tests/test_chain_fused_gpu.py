@@ -118,6 +118,31 @@ def test_fused_chain_repeated_calls_and_single_layer():
         assert torch.equal(acts[1].view(torch.int16), ref[1].view(torch.int16)), it
 
 
+@pytest.mark.parametrize("k", [1, 5])
+def test_fused_chain_cached_graph_replays_with_new_contents(k):
+    """Outside stream capture, a call with the same layers, buffers and token
+    count as an earlier one replays the library's cached graph of that call.
+    The graph reads the buffers through their pointers, so new input contents
+    in the same buffers must give the layer-by-layer bits on every call, and a
+    new output buffer (a new graph) must too."""
+    from littlebit_b200 import ops
+
+    layers, g = _chain([4096, 4096, 4096], [208, 1840], seed=90 + k)
+    fc = ops.FusedChain(layers)
+    x = torch.empty(k, 4096, dtype=torch.bfloat16, device=DEV)
+    acts = [x, torch.empty_like(x), torch.empty_like(x)]
+    for it in range(4):
+        if it == 3:
+            acts[2] = torch.empty_like(x)  # another output buffer: another graph
+        x.copy_(torch.randn(k, 4096, generator=g).to(DEV, torch.bfloat16))
+        fc.run(acts)
+        torch.cuda.synchronize()
+        ref = _layerwise(ops, layers, x)
+        assert ops.device_error() == 0
+        for i in (1, 2):
+            assert torch.equal(acts[i].view(torch.int16), ref[i].view(torch.int16)), (it, i)
+
+
 def test_fused_chain_rejects_unsupported():
     from littlebit_b200 import ops
 
