@@ -1199,6 +1199,9 @@ def run_ours(args):
         if r is not None:
             cpu = {"value": round(r["gbs"], 4), "unit": "GB/s", "cores": r["threads"],
                    "kind": "reference", "sample": r["sample"]}
+        else:
+            cpu = {"value": None, "unavailable": "the reference's C++ op is not built (oracle/_ref is missing: "
+                                                 "run __graft_entry__.build() where the reference sources are)"}
 
     dense = run_dense_ref(args, dev, rank, ws) if args.dense_ref and ws == 1 else None
     if dense:
