@@ -681,7 +681,8 @@ def run_decode70b(args, dev, rank, ws):
 
 def run_c5(args, dev, rank, ws):
     """BASELINE config 5 on the Llama-2-70B shape: 64 independent sequences split
-    data-parallel over the ranks (64/N per GPU), each GPU decoding its share as
+    data-parallel over the ranks (64/N per GPU, the first 64 % N ranks one
+    more when N does not divide 64), each GPU decoding its share as
     one batch (lbx_forward_multi: every packed-weight read serves all of its
     sequences).  0.1-bit draft + 0.9-bit residual target (per-layer residual),
     chain speculation with gamma 4 against batched target-only greedy decoding;
@@ -700,8 +701,10 @@ def run_c5(args, dev, rank, ws):
     for k in list(st):
         if k.endswith(".u1_r"):
             st[k] = st[k] * args.res_scale
+    from littlebit_b200 import sharded
+
     S_total, gamma, P, G = 64, 4, 512, args.c5_new
-    S = S_total // ws
+    S = len(sharded.split_requests(S_total, ws, rank))  # (rank 0 holds the largest share)
     max_seq = P + (gamma + 1) * G + 16
     dec = LittleBitDecoder(shape, st, device=dev, max_seq=16)  # weights only (the batches own the caches)
     del st
